@@ -1,0 +1,86 @@
+"""Typed ``MINISGL_*`` environment flags, parsed once at import.
+
+Same variable names and defaults as the reference (python/minisgl/env.py:58-87) plus the
+flags this engine adds for its native paths (fused collectives, timeouts).
+"""
+
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+from typing import Any, Callable
+
+
+def _as_bool(text: str) -> bool:
+    return text.strip().lower() in ("1", "true", "yes", "on")
+
+
+def _as_opt_bool(text: str) -> bool | None:
+    t = text.strip().lower()
+    if t in ("", "none", "auto"):
+        return None
+    return _as_bool(t)
+
+
+def parse_mem_bytes(text: str) -> int:
+    """Parse ``"1G"``, ``"512M"``, ``"64KB"`` or a plain integer into bytes."""
+    t = text.strip().upper()
+    if t.endswith("B") and len(t) > 1 and t[-2].isalpha():
+        t = t[:-1]
+    units = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30, "T": 1 << 40}
+    if t and t[-1] in units:
+        return int(float(t[:-1]) * units[t[-1]])
+    return int(t)
+
+
+@dataclass
+class _Flag:
+    default: Any
+    parse: Callable[[str], Any]
+
+
+_FLAGS = {
+    # interactive shell sampling defaults
+    "SHELL_MAX_TOKENS": _Flag(2048, int),
+    "SHELL_TOP_K": _Flag(-1, int),
+    "SHELL_TOP_P": _Flag(1.0, float),
+    "SHELL_TEMPERATURE": _Flag(0.6, float),
+    # runtime
+    "FLASHINFER_USE_TENSOR_CORES": _Flag(None, _as_opt_bool),  # accepted, unused (own kernels)
+    "DISABLE_OVERLAP_SCHEDULING": _Flag(False, _as_bool),
+    "PYNCCL_MAX_BUFFER_SIZE": _Flag(1 << 30, parse_mem_bytes),
+    # engine-specific
+    "COMM_MODE": _Flag("auto", str),  # auto | nccl | fused
+    "COMM_TIMEOUT_MS": _Flag(5000, int),  # bound on every device-side peer wait
+    "DEBUG_CHECK_INTEGRITY": _Flag(False, _as_bool),
+}
+
+
+class _Env:
+    """Attribute access to the parsed flags: ``ENV.DISABLE_OVERLAP_SCHEDULING``."""
+
+    PREFIX = "MINISGL_"
+
+    def __init__(self) -> None:
+        self.reload()
+
+    def reload(self) -> None:
+        for name, flag in _FLAGS.items():
+            raw = os.environ.get(self.PREFIX + name)
+            value = flag.default
+            if raw is not None:
+                try:
+                    value = flag.parse(raw)
+                except (TypeError, ValueError):
+                    value = flag.default
+            object.__setattr__(self, name, value)
+
+    def __setattr__(self, key: str, value: Any) -> None:  # tests may override flags
+        if key not in _FLAGS:
+            raise AttributeError(key)
+        object.__setattr__(self, key, value)
+
+
+ENV = _Env()
+
+__all__ = ["ENV", "parse_mem_bytes"]

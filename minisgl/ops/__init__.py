@@ -1,0 +1,128 @@
+"""Op entry points used by the layers.
+
+CUDA tensors run this engine's sm_100a kernels (``minisgl._cuda``); CPU tensors run the PyTorch
+reference in ``ops.reference`` (the oracle / CPU engine). There is no third path: on a GPU a
+missing extension raises instead of falling back.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from minisgl._native import cuda as _cuda
+
+from . import reference as ref
+from .reference import GATE_UP_BLOCK, deinterleave_gate_up, interleave_gate_up
+
+
+def _on_gpu(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+def embedding(weight, ids, vocab_start: int = 0, vocab_len: int | None = None):
+    if not _on_gpu(weight):
+        return ref.embedding(weight, ids, vocab_start, vocab_len)
+    out = torch.empty(ids.shape[0], weight.shape[1], dtype=weight.dtype, device=weight.device)
+    lo, n = (0, weight.shape[0]) if vocab_len is None else (vocab_start, vocab_len)
+    _cuda().embedding(out, weight, ids, lo, n, vocab_len is not None)
+    return out
+
+
+def rmsnorm(x, w, eps: float):
+    if not _on_gpu(x):
+        return ref.rmsnorm(x, w, eps)
+    out = torch.empty_like(x)
+    _cuda().rmsnorm(out, x, w, eps)
+    return out
+
+
+def fused_add_rmsnorm(x, residual, w, eps: float):
+    if not _on_gpu(x):
+        return ref.fused_add_rmsnorm(x, residual, w, eps)
+    _cuda().fused_add_rmsnorm(x, residual, w, eps)
+    return x, residual
+
+
+def linear(x, w, bias=None):
+    if not _on_gpu(x):
+        return ref.linear(x, w, bias)
+    out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    _cuda().gemm(out, x, w, bias, 0)
+    return out
+
+
+def gate_up_silu(x, w, act: str = "silu"):
+    if not _on_gpu(x):
+        return ref.gate_up_silu(x, w, act)
+    out = torch.empty(x.shape[0], w.shape[0] // 2, dtype=x.dtype, device=x.device)
+    _cuda().gemm(out, x, w, None, 1 if act == "silu" else 2)
+    return out
+
+
+def silu_and_mul(x):
+    if not _on_gpu(x):
+        return ref.silu_and_mul(x)
+    out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
+    _cuda().act_and_mul(out, x, 0)
+    return out
+
+
+def gelu_and_mul(x):
+    if not _on_gpu(x):
+        return ref.gelu_and_mul(x)
+    out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
+    _cuda().act_and_mul(out, x, 1)
+    return out
+
+
+def qk_norm_rope_store(qkv, positions, cos_sin, q_norm, k_norm, eps, k_cache, v_cache, out_loc, nq, nkv, hd):
+    if not _on_gpu(qkv):
+        return ref.qk_norm_rope_store(
+            qkv, positions, cos_sin, q_norm, k_norm, eps, k_cache, v_cache, out_loc, nq, nkv, hd
+        )
+    q = torch.empty(qkv.shape[0], nq, hd, dtype=qkv.dtype, device=qkv.device)
+    _cuda().qk_norm_rope_store(
+        q, qkv, positions, cos_sin, q_norm, k_norm, eps, k_cache, v_cache, out_loc, nq, nkv, hd
+    )
+    return q
+
+
+def store_kv(k, v, k_cache, v_cache, out_loc):
+    if not _on_gpu(k):
+        return ref.store_kv(k, v, k_cache, v_cache, out_loc)
+    _cuda().store_kv(k.reshape(k.shape[0], -1), v.reshape(v.shape[0], -1), k_cache, v_cache, out_loc)
+
+
+def argmax(logits):
+    if not _on_gpu(logits):
+        return ref.argmax(logits)
+    out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    _cuda().argmax(out, logits)
+    return out
+
+
+def sample(logits, temperature, top_k, top_p, seed, step):
+    if not _on_gpu(logits):
+        return ref.sample(logits, temperature, top_k, top_p, seed, step)
+    out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    _cuda().sample(out, logits, temperature, top_k, top_p, seed, step)
+    return out
+
+
+__all__ = [
+    "GATE_UP_BLOCK",
+    "interleave_gate_up",
+    "deinterleave_gate_up",
+    "embedding",
+    "rmsnorm",
+    "fused_add_rmsnorm",
+    "linear",
+    "gate_up_silu",
+    "silu_and_mul",
+    "gelu_and_mul",
+    "qk_norm_rope_store",
+    "store_kv",
+    "argmax",
+    "sample",
+    "ref",
+]

@@ -1,0 +1,40 @@
+"""Running-set manager for decode (reference: python/minisgl/scheduler/decode.py:9-39)."""
+
+from __future__ import annotations
+
+from typing import Dict, Iterable
+
+from minisgl.core import Batch, Req
+
+
+class DecodeManager:
+    def __init__(self, page_size: int):
+        self.page_size = page_size
+        self.running: Dict[int, Req] = {}  # uid -> req, insertion-ordered
+
+    def filter_reqs(self, reqs: Iterable[Req]) -> None:
+        for r in reqs:
+            self.running.setdefault(r.uid, r)
+        self.running = {u: r for u, r in self.running.items() if r.can_decode}
+
+    def remove_req(self, req: Req) -> None:
+        if self.running.get(req.uid) is req:
+            del self.running[req.uid]
+
+    def abort_req(self, uid: int) -> Req | None:
+        return self.running.pop(uid, None)
+
+    @property
+    def inflight_tokens(self) -> int:
+        """Tokens that running requests may still claim (plus one partial page each)."""
+        n = len(self.running)
+        return sum(r.remain_len for r in self.running.values()) + (self.page_size - 1) * n
+
+    def schedule_next_batch(self) -> Batch | None:
+        if not self.running:
+            return None
+        return Batch(reqs=sorted(self.running.values(), key=lambda r: r.uid), phase="decode")
+
+    @property
+    def runnable(self) -> bool:
+        return bool(self.running)

@@ -1,0 +1,131 @@
+"""FCFS prefill admission with chunking (reference: python/minisgl/scheduler/prefill.py:23-158).
+
+A request is admitted when its extend length plus its output budget fits in the KV pool (free +
+evictable) after reserving what the running decode set may still claim. A prompt that does not
+fit the per-batch token budget becomes a ``ChunkedReq``: it is computed over several prefill
+batches, is never sampled until its last chunk, and is re-queued at the head of the list.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Tuple
+
+import numpy as np
+import torch
+
+from minisgl.core import Batch, Req
+from minisgl.kvcache import BaseCacheHandle
+
+from .cache import CacheManager
+from .decode import DecodeManager
+from .table import TableManager
+from .utils import PendingReq
+
+
+class ChunkedReq(Req):
+    def append_host(self, next_token: torch.Tensor) -> None:
+        raise RuntimeError("a chunked request is not sampled")
+
+    @property
+    def can_decode(self) -> bool:
+        return False
+
+
+@dataclass
+class PrefillAdder:
+    token_budget: int
+    reserved_size: int
+    cache_manager: CacheManager
+    table_manager: TableManager
+
+    def _admit(self, p: PendingReq) -> Tuple[BaseCacheHandle, int, np.ndarray] | None:
+        if self.table_manager.available_size == 0:
+            return None
+        handle = self.cache_manager.match_req(p.input_ids).cuda_handle
+        need = p.input_len - handle.cached_len + p.output_len
+        if need + self.reserved_size > self.cache_manager.available_size:
+            return None
+        self.cache_manager.lock(handle)  # locking moves the match out of the evictable pool
+        if need + self.reserved_size > self.cache_manager.available_size:
+            self.cache_manager.unlock(handle)
+            return None
+        row = self.table_manager.allocate()
+        return handle, row, np.asarray(handle.get_matched_indices(), dtype=np.int32)
+
+    def _make(self, p: PendingReq, handle, row: int, cached_len: int, slots: np.ndarray) -> Req:
+        remain = p.input_len - cached_len
+        chunk = min(self.token_budget, remain)
+        cls = ChunkedReq if chunk < remain else Req
+        self.token_budget -= chunk
+        self.reserved_size += remain + p.output_len
+        req = cls(
+            input_ids=p.input_ids[: cached_len + chunk],
+            table_idx=row,
+            cached_len=cached_len,
+            output_len=p.output_len,
+            uid=p.uid,
+            sampling_params=p.sampling_params,
+            cache_handle=handle,
+        )
+        req.slots = slots
+        # a fresh admission with a cache hit must publish the matched slots to its page-table row
+        req.pending_prefix = cached_len if p.chunked_req is None else 0
+        return req
+
+    def try_add_one(self, p: PendingReq) -> Req | None:
+        if self.token_budget <= 0:
+            return None
+        if (c := p.chunked_req) is not None:
+            return self._make(p, c.cache_handle, c.table_idx, c.cached_len, c.slots)
+        got = self._admit(p)
+        if got is None:
+            return None
+        handle, row, slots = got
+        return self._make(p, handle, row, handle.cached_len, slots)
+
+
+@dataclass
+class PrefillManager:
+    cache_manager: CacheManager
+    table_manager: TableManager
+    decode_manager: DecodeManager
+    pending_list: List[PendingReq] = field(default_factory=list)
+
+    def add_one_req(self, msg) -> None:
+        self.pending_list.append(PendingReq(msg.uid, msg.input_ids, msg.sampling_params))
+
+    def schedule_next_batch(self, prefill_budget: int) -> Batch | None:
+        if not self.pending_list:
+            return None
+        adder = PrefillAdder(
+            token_budget=prefill_budget,
+            reserved_size=self.decode_manager.inflight_tokens,
+            cache_manager=self.cache_manager,
+            table_manager=self.table_manager,
+        )
+        reqs: List[Req] = []
+        chunked: List[PendingReq] = []
+        for p in self.pending_list:
+            r = adder.try_add_one(p)
+            if r is None:
+                break
+            p.chunked_req = r if isinstance(r, ChunkedReq) else None
+            if p.chunked_req is not None:
+                chunked.append(p)
+            reqs.append(r)
+        if not reqs:
+            return None
+        self.pending_list = chunked + self.pending_list[len(reqs) :]
+        return Batch(reqs=reqs, phase="prefill")
+
+    def abort_req(self, uid: int) -> Req | None:
+        for i, p in enumerate(self.pending_list):
+            if p.uid == uid:
+                self.pending_list.pop(i)
+                return p.chunked_req
+        return None
+
+    @property
+    def runnable(self) -> bool:
+        return bool(self.pending_list)
