@@ -1,0 +1,216 @@
+// Torch bindings for the sm_100a kernels: validate tensors (dtype / device / contiguity / shape),
+// take the current CUDA stream, and call the C ABI in kernels/api.h.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "kernels/api.h"
+
+namespace {
+
+#define CHECK(cond, ...) TORCH_CHECK(cond, "minisgl: ", __VA_ARGS__)
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_dtype(const at::Tensor& t, at::ScalarType dt, const char* name) {
+  CHECK(t.scalar_type() == dt, name, " must be ", c10::toString(dt), ", got ", t.scalar_type());
+}
+void check_contig(const at::Tensor& t, const char* name) { CHECK(t.is_contiguous(), name, " must be contiguous"); }
+void check_bf16(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  check_dtype(t, at::kBFloat16, name);
+}
+void check_i32(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  check_dtype(t, at::kInt, name);
+  check_contig(t, name);
+}
+const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// Per-device scratch for split-K partials / counters (zero-initialised once; kernels leave the
+// counters at zero). Sized generously on first use so CUDA-graph capture never reallocates it.
+at::Tensor& gemm_workspace(const at::Device& dev, int64_t bytes) {
+  static std::mutex mu;
+  static std::unordered_map<int, at::Tensor> ws;
+  std::lock_guard<std::mutex> g(mu);
+  auto& t = ws[dev.index()];
+  if (!t.defined() || t.numel() < bytes) {
+    const int64_t sz = std::max<int64_t>(bytes, 64ll << 20);
+    t = at::zeros({sz}, at::TensorOptions().dtype(at::kByte).device(dev));
+  }
+  return t;
+}
+
+void embedding(at::Tensor out, at::Tensor weight, at::Tensor ids, int64_t lo, int64_t n, bool masked) {
+  check_bf16(out, "out"); check_bf16(weight, "weight"); check_i32(ids, "ids");
+  check_contig(out, "out"); check_contig(weight, "weight");
+  const int dim = weight.size(1);
+  CHECK(dim % 8 == 0, "hidden size must be a multiple of 8");
+  CHECK(out.size(0) == ids.size(0) && out.size(1) == dim, "embedding out shape");
+  msgl_embedding(out.data_ptr(), weight.data_ptr(), ids.data_ptr<int32_t>(), ids.size(0), dim, lo, n,
+                 masked, stream());
+}
+
+void rmsnorm(at::Tensor out, at::Tensor x, at::Tensor w, double eps) {
+  check_bf16(out, "out"); check_bf16(x, "x"); check_bf16(w, "w");
+  check_contig(out, "out"); check_contig(x, "x");
+  const int dim = x.size(-1);
+  CHECK(dim % 8 == 0 && w.numel() == dim, "rmsnorm dim");
+  msgl_rmsnorm(out.data_ptr(), x.data_ptr(), w.data_ptr(), x.numel() / dim, dim, eps, stream());
+}
+
+void fused_add_rmsnorm(at::Tensor x, at::Tensor residual, at::Tensor w, double eps) {
+  check_bf16(x, "x"); check_bf16(residual, "residual"); check_bf16(w, "w");
+  check_contig(x, "x"); check_contig(residual, "residual");
+  const int dim = x.size(-1);
+  CHECK(dim % 8 == 0 && w.numel() == dim && residual.numel() == x.numel(), "fused_add_rmsnorm shapes");
+  msgl_fused_add_rmsnorm(x.data_ptr(), residual.data_ptr(), w.data_ptr(), x.numel() / dim, dim, eps, stream());
+}
+
+// epi: 0 bf16, 1 silu-mul (interleaved gate/up), 2 gelu-mul, 3 fp32 out
+void gemm(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, int64_t epi) {
+  check_bf16(x, "x"); check_bf16(w, "w"); check_cuda(out, "out");
+  check_contig(x, "x"); check_contig(w, "w");
+  CHECK(out.stride(-1) == 1, "out must have unit inner stride");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  CHECK(w.size(1) == K, "gemm K mismatch: x ", x.sizes(), " w ", w.sizes());
+  CHECK(K % 8 == 0 && N % 8 == 0, "gemm needs K and N multiples of 8");
+  if (epi == 3) check_dtype(out, at::kFloat, "out"); else check_dtype(out, at::kBFloat16, "out");
+  const int64_t n_out = (epi == 1 || epi == 2) ? N / 2 : N;
+  CHECK(out.size(0) == M && out.size(1) == n_out, "gemm out shape");
+  if (bias.has_value()) { check_bf16(*bias, "bias"); CHECK(bias->numel() == N, "bias size"); }
+  if (M == 0) return;
+  const int splits = msgl_gemm_pick_splits(M, N, K);
+  void* ws = nullptr;
+  if (splits > 1) ws = gemm_workspace(x.device(), msgl_gemm_workspace_bytes(M, N, K, splits)).data_ptr();
+  msgl_gemm(out.data_ptr(), x.data_ptr(), w.data_ptr(), opt_ptr(bias), M, N, K, out.stride(0), epi,
+            splits, ws, stream());
+}
+
+void act_and_mul(at::Tensor out, at::Tensor x, int64_t act) {
+  check_bf16(out, "out"); check_bf16(x, "x"); check_contig(out, "out"); check_contig(x, "x");
+  const int inter = x.size(1) / 2;
+  CHECK(inter % 8 == 0 && out.size(1) == inter, "act_and_mul shapes");
+  msgl_act_and_mul(out.data_ptr(), x.data_ptr(), x.size(0), inter, act, stream());
+}
+
+void store_kv(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v_cache, at::Tensor out_loc) {
+  check_bf16(k, "k"); check_bf16(v, "v"); check_bf16(k_cache, "k_cache"); check_bf16(v_cache, "v_cache");
+  check_i32(out_loc, "out_loc");
+  const int64_t row = k_cache.numel() / k_cache.size(0);
+  CHECK(k.size(1) == row && v.size(1) == row && row % 8 == 0, "store_kv row size");
+  CHECK(k.stride(1) == 1 && v.stride(1) == 1, "store_kv rows must be contiguous");
+  CHECK(k.stride(0) % 8 == 0 && v.stride(0) % 8 == 0, "store_kv row stride alignment");
+  msgl_store_kv(k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out_loc.data_ptr<int32_t>(),
+                k.size(0), row, k.stride(0), v.stride(0), row, stream());
+}
+
+void qk_norm_rope_store(at::Tensor q_out, at::Tensor qkv, at::Tensor positions, at::Tensor cos_sin,
+                        c10::optional<at::Tensor> q_norm, c10::optional<at::Tensor> k_norm, double eps,
+                        at::Tensor k_cache, at::Tensor v_cache, at::Tensor out_loc, int64_t nq, int64_t nkv,
+                        int64_t hd) {
+  check_bf16(q_out, "q_out"); check_bf16(qkv, "qkv"); check_i32(positions, "positions");
+  check_cuda(cos_sin, "cos_sin"); check_dtype(cos_sin, at::kFloat, "cos_sin"); check_contig(cos_sin, "cos_sin");
+  check_bf16(k_cache, "k_cache"); check_bf16(v_cache, "v_cache"); check_i32(out_loc, "out_loc");
+  check_contig(qkv, "qkv"); check_contig(q_out, "q_out");
+  CHECK(hd == 64 || hd == 128 || hd == 256, "head_dim must be 64, 128 or 256");
+  CHECK(qkv.size(1) == (nq + 2 * nkv) * hd, "qkv width");
+  CHECK(cos_sin.size(1) == hd, "cos_sin width");
+  CHECK(q_norm.has_value() == k_norm.has_value(), "q_norm/k_norm must both be given or both absent");
+  msgl_qk_norm_rope_store(q_out.data_ptr(), qkv.data_ptr(), positions.data_ptr<int32_t>(),
+                          cos_sin.data_ptr<float>(), opt_ptr(q_norm), opt_ptr(k_norm), eps,
+                          k_cache.data_ptr(), v_cache.data_ptr(), out_loc.data_ptr<int32_t>(),
+                          qkv.size(0), nq, nkv, hd, nkv * hd, stream());
+}
+
+void argmax(at::Tensor out, at::Tensor logits) {
+  check_i32(out, "out"); check_cuda(logits, "logits");
+  CHECK(logits.stride(-1) == 1, "logits rows must be contiguous");
+  const bool f32 = logits.scalar_type() == at::kFloat;
+  CHECK(f32 || logits.scalar_type() == at::kBFloat16, "logits must be fp32 or bf16");
+  msgl_argmax(out.data_ptr<int32_t>(), logits.data_ptr(), logits.size(0), logits.size(1), logits.stride(0), f32,
+              stream());
+}
+
+void sample(at::Tensor out, at::Tensor logits, at::Tensor temperature, at::Tensor top_k, at::Tensor top_p,
+            at::Tensor seed, at::Tensor step) {
+  check_i32(out, "out"); check_cuda(logits, "logits");
+  at::Tensor lf = logits.scalar_type() == at::kFloat ? logits : logits.to(at::kFloat);
+  CHECK(lf.stride(-1) == 1, "logits rows must be contiguous");
+  check_dtype(temperature, at::kFloat, "temperature"); check_dtype(top_p, at::kFloat, "top_p");
+  check_dtype(top_k, at::kInt, "top_k"); check_dtype(seed, at::kLong, "seed"); check_dtype(step, at::kLong, "step");
+  msgl_sample(out.data_ptr<int32_t>(), lf.data_ptr<float>(), lf.size(0), lf.size(1), lf.stride(0),
+              temperature.data_ptr<float>(), top_k.data_ptr<int32_t>(), top_p.data_ptr<float>(),
+              seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(), stream());
+}
+
+void attention_prefill(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor page_table,
+                       at::Tensor rows, at::Tensor cu_q, at::Tensor kv_lens, int64_t max_q_len, double scale,
+                       int64_t window, c10::optional<at::Tensor> sinks) {
+  check_bf16(o, "o"); check_bf16(q, "q"); check_bf16(k_cache, "k_cache"); check_bf16(v_cache, "v_cache");
+  check_i32(rows, "rows"); check_i32(cu_q, "cu_q"); check_i32(kv_lens, "kv_lens");
+  check_cuda(page_table, "page_table"); check_dtype(page_table, at::kInt, "page_table");
+  check_contig(q, "q"); check_contig(o, "o");
+  const int nq = q.size(1), hd = q.size(2), nkv = k_cache.size(1);
+  CHECK(hd == 64 || hd == 128, "attention head_dim must be 64 or 128");
+  CHECK(nq % nkv == 0, "nq must be a multiple of nkv");
+  if (sinks.has_value()) { check_dtype(*sinks, at::kFloat, "sinks"); CHECK(sinks->numel() == nq, "sinks size"); }
+  msgl_attention_prefill(o.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                         page_table.data_ptr<int32_t>(), page_table.stride(0), rows.data_ptr<int32_t>(),
+                         cu_q.data_ptr<int32_t>(), kv_lens.data_ptr<int32_t>(), rows.size(0), q.size(0),
+                         max_q_len, nq, nkv, hd, k_cache.stride(0), scale, window,
+                         sinks.has_value() ? sinks->data_ptr<float>() : nullptr, stream());
+}
+
+void attention_decode(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor page_table,
+                      at::Tensor rows, at::Tensor kv_lens, double scale, int64_t window,
+                      c10::optional<at::Tensor> sinks, int64_t num_splits, at::Tensor workspace) {
+  check_bf16(o, "o"); check_bf16(q, "q"); check_bf16(k_cache, "k_cache"); check_bf16(v_cache, "v_cache");
+  check_i32(rows, "rows"); check_i32(kv_lens, "kv_lens");
+  check_cuda(page_table, "page_table"); check_dtype(page_table, at::kInt, "page_table");
+  check_contig(q, "q"); check_contig(o, "o");
+  const int bs = q.size(0), nq = q.size(1), hd = q.size(2), nkv = k_cache.size(1);
+  CHECK(hd == 64 || hd == 128, "attention head_dim must be 64 or 128");
+  CHECK(nq % nkv == 0 && nq / nkv <= 16, "decode supports up to 16 query heads per KV head");
+  CHECK(rows.size(0) >= bs && kv_lens.size(0) >= bs, "metadata too short");
+  if (num_splits > 1)
+    CHECK(workspace.numel() >= (int64_t)bs * nq * num_splits * (hd + 2) * 4, "decode workspace too small");
+  if (sinks.has_value()) { check_dtype(*sinks, at::kFloat, "sinks"); CHECK(sinks->numel() == nq, "sinks size"); }
+  msgl_attention_decode(o.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                        page_table.data_ptr<int32_t>(), page_table.stride(0), rows.data_ptr<int32_t>(),
+                        kv_lens.data_ptr<int32_t>(), bs, nq, nkv, hd, k_cache.stride(0), scale, window,
+                        sinks.has_value() ? sinks->data_ptr<float>() : nullptr, num_splits,
+                        workspace.data_ptr(), stream());
+}
+
+std::tuple<int64_t, int64_t> get_error() {
+  int info = 0;
+  const int code = msgl_get_error(&info);
+  return {code, info};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_cuda, m) {
+  m.doc() = "minisgl sm_100a kernels";
+  m.def("embedding", &embedding);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
+  m.def("gemm", &gemm);
+  m.def("act_and_mul", &act_and_mul);
+  m.def("store_kv", &store_kv);
+  m.def("qk_norm_rope_store", &qk_norm_rope_store);
+  m.def("argmax", &argmax);
+  m.def("sample", &sample);
+  m.def("attention_prefill", &attention_prefill);
+  m.def("attention_decode", &attention_decode);
+  m.def("get_error", &get_error);
+  m.def("num_sms", []() { return msgl_num_sms(); });
+  m.def("gemm_splits", [](int64_t M, int64_t N, int64_t K) { return msgl_gemm_pick_splits(M, N, K); });
+}

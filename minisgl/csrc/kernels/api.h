@@ -1,0 +1,55 @@
+// C ABI between the torch bindings (bindings.cpp) and the CUDA translation units. Kernels take
+// raw pointers, sizes and a stream; no torch headers are included on the device side.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+extern "C" {
+
+// ----- status
+int msgl_get_error(int* info);  // returns and clears the device error word
+int msgl_num_sms();
+
+// ----- elementwise / normalization (bf16 activations)
+void msgl_embedding(void* out, const void* weight, const int32_t* ids, int n, int dim,
+                    int vocab_start, int vocab_len, int masked, cudaStream_t s);
+void msgl_rmsnorm(void* out, const void* x, const void* w, int rows, int dim, float eps,
+                  cudaStream_t s);
+void msgl_fused_add_rmsnorm(void* x, void* residual, const void* w, int rows, int dim, float eps,
+                            cudaStream_t s);
+void msgl_act_and_mul(void* out, const void* x, int rows, int inter, int act, cudaStream_t s);
+void msgl_store_kv(const void* k, const void* v, void* k_cache, void* v_cache,
+                   const int32_t* out_loc, int n, int row_elems, int64_t k_stride, int64_t v_stride,
+                   int64_t cache_stride, cudaStream_t s);
+void msgl_qk_norm_rope_store(void* q_out, const void* qkv, const int32_t* positions,
+                             const float* cos_sin, const void* q_norm, const void* k_norm,
+                             float eps, void* k_cache, void* v_cache, const int32_t* out_loc,
+                             int n, int nq, int nkv, int hd, int64_t cache_stride, cudaStream_t s);
+void msgl_argmax(int32_t* out, const void* logits, int rows, int vocab, int64_t stride,
+                 int is_fp32, cudaStream_t s);
+void msgl_sample(int32_t* out, const float* logits, int rows, int vocab, int64_t stride,
+                 const float* temperature, const int32_t* top_k, const float* top_p,
+                 const int64_t* seed, const int64_t* step, cudaStream_t s);
+
+// ----- GEMM: out[M,N] = epi(x[M,K] @ w[N,K]^T + bias)
+//   epi 0: bf16 out; 1: silu(g)*u on 64-row interleaved gate/up (out has N/2 cols);
+//   2: gelu(g)*u likewise; 3: fp32 out.
+// workspace: fp32 split-K partials + tile counters (may be null when splits == 1).
+int msgl_gemm_workspace_bytes(int M, int N, int K, int splits);
+int msgl_gemm_pick_splits(int M, int N, int K);
+void msgl_gemm(void* out, const void* x, const void* w, const void* bias, int M, int N, int K,
+               int ldo, int epi, int splits, void* workspace, cudaStream_t s);
+
+// ----- paged attention (bf16 q/kv, fp32 softmax)
+void msgl_attention_prefill(void* o, const void* q, const void* k_cache, const void* v_cache,
+                            const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
+                            const int32_t* cu_q, const int32_t* kv_lens, int num_reqs,
+                            int total_q, int max_q_len, int nq, int nkv, int hd,
+                            int64_t cache_stride, float sm_scale, int window, const float* sinks,
+                            cudaStream_t s);
+void msgl_attention_decode(void* o, const void* q, const void* k_cache, const void* v_cache,
+                           const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
+                           const int32_t* kv_lens, int bs, int nq, int nkv, int hd,
+                           int64_t cache_stride, float sm_scale, int window, const float* sinks,
+                           int num_splits, void* workspace, cudaStream_t s);
+}

@@ -1,0 +1,220 @@
+"""Numerics of every sm_100a kernel against the plain PyTorch fp32 reference (ops/reference.py)."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from minisgl.ops import reference as ref  # noqa: E402
+
+DEV = "cuda"
+
+
+def _c():
+    from minisgl._native import cuda
+
+    return cuda()
+
+
+def _assert_no_device_error():
+    code, info = _c().get_error()
+    assert code == 0, f"device error {code} ({info})"
+
+
+def _close(a, b, atol, rtol):
+    torch.testing.assert_close(a.float().cpu(), b.float().cpu(), atol=atol, rtol=rtol)
+
+
+@pytest.fixture(autouse=True)
+def _cuda_only():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    torch.manual_seed(0)
+    yield
+    torch.cuda.synchronize()
+    _assert_no_device_error()
+
+
+def test_embedding():
+    from minisgl import ops
+
+    w = torch.randn(1000, 1024, device=DEV, dtype=torch.bfloat16)
+    ids = torch.randint(0, 1000, (77,), device=DEV, dtype=torch.int32)
+    _close(ops.embedding(w, ids), ref.embedding(w.cpu(), ids.cpu()), 0, 0)
+    ids2 = torch.randint(0, 3000, (77,), device=DEV, dtype=torch.int32)
+    _close(ops.embedding(w, ids2, 1000, 1000), ref.embedding(w.cpu(), ids2.cpu(), 1000, 1000), 0, 0)
+
+
+@pytest.mark.parametrize("dim", [256, 1024, 5120, 2880])
+def test_rmsnorm(dim):
+    from minisgl import ops
+
+    x = torch.randn(37, dim, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(dim, device=DEV, dtype=torch.bfloat16)
+    _close(ops.rmsnorm(x, w, 1e-6), ref.rmsnorm(x.cpu().float(), w.cpu().float(), 1e-6), 2e-2, 2e-2)
+    r = torch.randn_like(x)
+    x1, r1 = x.clone(), r.clone()
+    ops.fused_add_rmsnorm(x1, r1, w, 1e-6)
+    x2, r2 = x.cpu().clone(), r.cpu().clone()
+    ref.fused_add_rmsnorm(x2, r2, w.cpu(), 1e-6)
+    _close(r1, r2, 0, 0)
+    _close(x1, x2, 3e-2, 2e-2)
+
+
+@pytest.mark.parametrize("M", [1, 7, 16, 33, 64, 100, 128, 200, 256, 300, 1000])
+@pytest.mark.parametrize("N,K", [(256, 1024), (4096, 1024), (1024, 3072), (136, 200)])
+def test_gemm(M, N, K):
+    from minisgl import ops
+
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    y = ops.linear(x, w)
+    torch.cuda.synchronize()
+    expect = x.float() @ w.float().t()
+    _close(y, expect, 3e-2, 2e-2)
+
+
+@pytest.mark.parametrize("M", [3, 64, 256, 777])
+def test_gemm_epilogues(M):
+    from minisgl import ops
+
+    K, N = 1024, 1024
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    b = torch.randn(N, device=DEV, dtype=torch.bfloat16)
+    _close(ops.linear(x, w, b), x.float() @ w.float().t() + b.float(), 3e-2, 2e-2)
+    out = torch.empty(M, N, device=DEV, dtype=torch.float32)
+    _c().gemm(out, x, w, None, 3)
+    _close(out, x.float() @ w.float().t(), 2e-3, 2e-3)
+    y = ops.gate_up_silu(x, w)
+    _close(y, ref.gate_up_silu(x.cpu().float(), w.cpu().float()), 3e-2, 3e-2)
+
+
+def test_gemm_large_k_split():
+    from minisgl import ops
+
+    for M, N, K in [(8, 1024, 17408), (256, 5120, 5120), (1, 2048, 4096)]:
+        x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+        w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+        for _ in range(2):  # second launch checks the split-K counters were re-armed
+            _close(ops.linear(x, w), x.float() @ w.float().t(), 3e-2, 2e-2)
+
+
+@pytest.mark.parametrize("hd,nq,nkv,norm", [(128, 16, 8, True), (64, 8, 2, False), (128, 40, 8, True)])
+def test_qk_norm_rope_store(hd, nq, nkv, norm):
+    from minisgl import ops
+
+    T, slots = 50, 300
+    qkv = torch.randn(T, (nq + 2 * nkv) * hd, device=DEV, dtype=torch.bfloat16)
+    pos = torch.randint(0, 1000, (T,), device=DEV, dtype=torch.int32)
+    cs = ref.rope_cos_sin(2048, hd, ref.default_inv_freq(hd, 1e6)).to(DEV)
+    qn = torch.randn(hd, device=DEV, dtype=torch.bfloat16) if norm else None
+    kn = torch.randn(hd, device=DEV, dtype=torch.bfloat16) if norm else None
+    loc = torch.randperm(slots, device=DEV)[:T].to(torch.int32)
+    kc = torch.zeros(slots, nkv, hd, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q = ops.qk_norm_rope_store(qkv, pos, cs, qn, kn, 1e-6, kc, vc, loc, nq, nkv, hd)
+    kc2, vc2 = kc.cpu().zero_(), vc.cpu().zero_()
+    q2 = ref.qk_norm_rope_store(qkv.cpu(), pos.cpu(), cs.cpu(), None if qn is None else qn.cpu(),
+                                None if kn is None else kn.cpu(), 1e-6, kc2, vc2, loc.cpu(), nq, nkv, hd)
+    _close(q, q2, 3e-2, 3e-2)
+    _close(kc, kc2, 3e-2, 3e-2)
+    _close(vc, vc2, 0, 0)
+
+
+def _paged_setup(lens_q, lens_kv, nq, nkv, hd, slots=4096, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    B = len(lens_kv)
+    kc = torch.randn(slots, nkv, hd, generator=g).to(DEV, torch.bfloat16)
+    vc = torch.randn(slots, nkv, hd, generator=g).to(DEV, torch.bfloat16)
+    L = max(lens_kv)
+    pt = torch.zeros(B + 3, (L + 31) // 32 * 32, dtype=torch.int32)
+    perm = torch.randperm(slots, generator=g)
+    used = 0
+    rows = torch.arange(B, dtype=torch.int32) + 2  # rows are not 0..B-1
+    for b, n in enumerate(lens_kv):
+        pt[rows[b], :n] = perm[used : used + n].to(torch.int32)
+        used += n
+    cu = torch.zeros(B + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(torch.tensor(lens_q), 0)
+    q = torch.randn(int(cu[-1]), nq, hd, generator=g).to(DEV, torch.bfloat16)
+    return q, kc, vc, pt.to(DEV), rows.to(DEV), cu.to(DEV), torch.tensor(lens_kv, dtype=torch.int32, device=DEV)
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 16, 8), (128, 40, 8), (64, 64, 8), (128, 8, 8)])
+@pytest.mark.parametrize("window,sinks", [(-1, False), (37, True)])
+def test_attention_prefill(hd, nq, nkv, window, sinks):
+    lens_q = [1, 17, 100, 64, 250]
+    lens_kv = [1, 40, 100, 300, 250]  # prefix hits: kv longer than q
+    q, kc, vc, pt, rows, cu, kvl = _paged_setup(lens_q, lens_kv, nq, nkv, hd)
+    sk = torch.randn(nq, device=DEV) if sinks else None
+    o = torch.empty_like(q)
+    scale = 1 / math.sqrt(hd)
+    _c().attention_prefill(o, q, kc, vc, pt, rows, cu, kvl, max(lens_q), scale, window, sk)
+    e = ref.paged_attention(q.cpu(), kc.cpu(), vc.cpu(), pt.cpu(), rows.cpu(), cu.cpu(), kvl.cpu(), scale,
+                            window, None if sk is None else sk.cpu())
+    _close(o, e, 2e-2, 2e-2)
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 16, 8), (128, 40, 8), (64, 64, 8), (128, 64, 8)])
+@pytest.mark.parametrize("splits", [1, 3, 8])
+@pytest.mark.parametrize("window,sinks", [(-1, False), (128, True)])
+def test_attention_decode(hd, nq, nkv, splits, window, sinks):
+    lens_kv = [1, 5, 64, 65, 300, 1000, 777]
+    B = len(lens_kv)
+    q, kc, vc, pt, rows, cu, kvl = _paged_setup([1] * B, lens_kv, nq, nkv, hd)
+    sk = torch.randn(nq, device=DEV) if sinks else None
+    o = torch.empty_like(q)
+    ws = torch.empty(B * nq * splits * (hd + 2) * 4, dtype=torch.uint8, device=DEV)
+    scale = 1 / math.sqrt(hd)
+    _c().attention_decode(o, q, kc, vc, pt, rows, kvl, scale, window, sk, splits, ws)
+    e = ref.paged_attention(q.cpu(), kc.cpu(), vc.cpu(), pt.cpu(), rows.cpu(), cu.cpu(), kvl.cpu(), scale,
+                            window, None if sk is None else sk.cpu())
+    _close(o, e, 2e-2, 2e-2)
+
+
+def test_argmax_and_greedy_sample():
+    from minisgl import ops
+
+    logits = torch.randn(33, 151936, device=DEV)
+    logits[3, 5] = logits[3, 9] = 100.0  # tie -> lowest index
+    assert torch.equal(ops.argmax(logits).cpu(), ref.argmax(logits.cpu()))
+    assert torch.equal(ops.argmax(logits.bfloat16()).cpu(), ref.argmax(logits.bfloat16().cpu()))
+
+
+def test_sampling_matches_reference():
+    from minisgl import ops
+
+    B, V = 16, 5000
+    logits = torch.randn(B, V, device=DEV) * 3
+    temp = torch.tensor([0.0, 0.7, 1.0, 1.3] * 4, device=DEV)
+    topk = torch.tensor([V, 1, 50, V] * 4, dtype=torch.int32, device=DEV)
+    topp = torch.tensor([1.0, 1.0, 0.9, 0.5] * 4, device=DEV)
+    seed = torch.arange(B, dtype=torch.int64, device=DEV) * 7 + 1
+    step = torch.arange(B, dtype=torch.int64, device=DEV) + 100
+    a = ops.sample(logits, temp, topk, topp, seed, step).cpu()
+    b = ref.sample(logits.cpu(), temp.cpu(), topk.cpu(), topp.cpu(), seed.cpu(), step.cpu())
+    assert (a == b).float().mean() >= 0.9, (a, b)
+    # kept-set property: every draw lies inside its top-k
+    for i in range(B):
+        k = int(topk[i])
+        if 0 < k < V:
+            kth = torch.topk(logits[i].cpu() / max(float(temp[i]), 1e-6), k).values[-1]
+            assert logits[i, a[i]].cpu() / max(float(temp[i]), 1e-6) >= kth
+
+
+def test_store_kv():
+    from minisgl import ops
+
+    k = torch.randn(20, 8 * 128, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn_like(k)
+    kc = torch.zeros(100, 8, 128, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    loc = torch.randperm(100, device=DEV)[:20].to(torch.int32)
+    ops.store_kv(k, v, kc, vc, loc)
+    kc2, vc2 = kc.cpu().zero_(), vc.cpu().zero_()
+    ref.store_kv(k.cpu(), v.cpu(), kc2, vc2, loc.cpu())
+    _close(kc, kc2, 0, 0)
+    _close(vc, vc2, 0, 0)
