@@ -22,12 +22,33 @@ def host():
         return importlib.import_module("minisgl._host")
 
 
+class _CountingModule:
+    """Forwards attribute access to the extension and counts kernel-launching calls."""
+
+    _NON_LAUNCH = {"get_error", "num_sms", "gemm_splits"}
+
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if name in self._NON_LAUNCH or not callable(fn):
+            return fn
+        from minisgl.engine.counters import COUNTERS
+
+        def call(*args, **kwargs):
+            COUNTERS.launches += 2 if (name == "attention_decode" and args[-2] > 1) else 1
+            return fn(*args, **kwargs)
+
+        return call
+
+
 @functools.cache
 def cuda():
     try:
         import torch  # noqa: F401  (loads libtorch before the extension)
 
-        return importlib.import_module("minisgl._cuda")
+        return _CountingModule(importlib.import_module("minisgl._cuda"))
     except ImportError as e:
         raise RuntimeError(
             "minisgl CUDA kernels are not built; run `python -m minisgl._build` "

@@ -28,6 +28,7 @@ from minisgl.parallel.info import reset_tp_info
 from minisgl.utils import div_even, init_logger, torch_dtype
 
 from .config import EngineConfig
+from .counters import COUNTERS
 from .graph import GraphRunner, determine_graph_bs
 from .sample import BatchSamplingArgs, Sampler
 
@@ -52,6 +53,7 @@ def _align32(n: int) -> int:
 class Engine:
     def __init__(self, config: EngineConfig):
         self.config = config
+        self.counters = COUNTERS
         info = config.tp_info
         set_tp_info(info.rank, info.size)
         self.device = torch.device(config.device or f"cuda:{info.rank}")
@@ -211,6 +213,7 @@ class Engine:
         host, views = plan.pack()
         if self.is_cuda:
             dev_buf = host.pin_memory().to(self.device, non_blocking=True)
+            COUNTERS.h2d_bytes += host.numel() * host.element_size()
         else:
             dev_buf = host
         dev = {k: dev_buf[s:e] for k, (s, e) in views.items()}
@@ -239,6 +242,7 @@ class Engine:
         if self.is_cuda:
             cpu = torch.empty(next_tokens.shape, dtype=torch.int32, pin_memory=True)
             cpu.copy_(next_tokens, non_blocking=True)
+            COUNTERS.d2h_bytes += cpu.numel() * cpu.element_size()
             ev = torch.cuda.Event()
             ev.record(self.stream)
         else:

@@ -40,6 +40,7 @@ class GraphRunner:
         self.max_graph_bs = max(graph_bs) if graph_bs else 0
         self.dummy_req = dummy_req
         self.graph_map: Dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: Dict[int, int] = {}
         if self.max_graph_bs and engine.device.type == "cuda":
             self._capture()
         else:
@@ -67,10 +68,14 @@ class GraphRunner:
             batch.positions = self.positions[:bs]
             batch.out_loc = self.out_loc[:bs]
             g = torch.cuda.CUDAGraph()
+            from .counters import COUNTERS
+
             with ctx.forward_batch(batch):
                 self.logits[:bs].copy_(eng.model.forward())  # warm up outside the capture
+                before = COUNTERS.launches
                 with torch.cuda.graph(g, pool=pool, stream=eng.stream):
                     self.logits[:bs].copy_(eng.model.forward())
+                self.graph_launches[bs] = COUNTERS.launches - before
             pool = pool or g.pool()
             self.graph_map[bs] = g
         torch.cuda.synchronize(dev)
@@ -94,6 +99,9 @@ class GraphRunner:
         self.out_loc[:bs].copy_(batch.out_loc)
         self.engine.attn_backend.prepare_for_replay(batch)
         self.graph_map[bs].replay()
+        from .counters import COUNTERS
+
+        COUNTERS.launches += self.graph_launches[bs]
         return self.logits[: batch.size]
 
     def destroy_cuda_graphs(self) -> None:

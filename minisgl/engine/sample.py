@@ -28,6 +28,9 @@ class BatchSamplingArgs:
 def _to_device(data: List, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
     t = torch.tensor(data, dtype=dtype)
     if device.type == "cuda":
+        from .counters import COUNTERS
+
+        COUNTERS.h2d_bytes += t.numel() * t.element_size()
         return t.pin_memory().to(device, non_blocking=True)
     return t
 
