@@ -73,24 +73,39 @@ void fused_add_rmsnorm(at::Tensor x, at::Tensor residual, at::Tensor w, double e
   msgl_fused_add_rmsnorm(x.data_ptr(), residual.data_ptr(), w.data_ptr(), x.numel() / dim, dim, eps, stream());
 }
 
-// epi: 0 bf16, 1 silu-mul (interleaved gate/up), 2 gelu-mul, 3 fp32 out
-void gemm(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, int64_t epi) {
+// epi: 0 bf16, 1 silu-mul (interleaved gate/up), 2 gelu-mul, 3 fp32 out.
+// w is [N, K] row-major, or K-block major [K/64, N, 64] (3-D tensor).
+void gemm_ex(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, int64_t epi,
+             int64_t splits, int64_t wide) {
   check_bf16(x, "x"); check_bf16(w, "w"); check_cuda(out, "out");
   check_contig(x, "x"); check_contig(w, "w");
   CHECK(out.stride(-1) == 1, "out must have unit inner stride");
-  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
-  CHECK(w.size(1) == K, "gemm K mismatch: x ", x.sizes(), " w ", w.sizes());
+  const bool blocked = w.dim() == 3;
+  const int64_t M = x.size(0), K = x.size(1);
+  const int64_t N = blocked ? w.size(1) : w.size(0);
+  if (blocked) {
+    CHECK(w.size(2) == 64 && w.size(0) * 64 == K, "blocked weight must be [K/64, N, 64], got ", w.sizes());
+  } else {
+    CHECK(w.size(1) == K, "gemm K mismatch: x ", x.sizes(), " w ", w.sizes());
+  }
   CHECK(K % 8 == 0 && N % 8 == 0, "gemm needs K and N multiples of 8");
-  if (epi == 3) check_dtype(out, at::kFloat, "out"); else check_dtype(out, at::kBFloat16, "out");
+  if (epi == 3) {
+    check_dtype(out, at::kFloat, "out");
+  } else {
+    check_dtype(out, at::kBFloat16, "out");
+  }
   const int64_t n_out = (epi == 1 || epi == 2) ? N / 2 : N;
   CHECK(out.size(0) == M && out.size(1) == n_out, "gemm out shape");
   if (bias.has_value()) { check_bf16(*bias, "bias"); CHECK(bias->numel() == N, "bias size"); }
   if (M == 0) return;
-  const int splits = msgl_gemm_pick_splits(M, N, K);
-  void* ws = nullptr;
-  if (splits > 1) ws = gemm_workspace(x.device(), msgl_gemm_workspace_bytes(M, N, K, splits)).data_ptr();
-  msgl_gemm(out.data_ptr(), x.data_ptr(), w.data_ptr(), opt_ptr(bias), M, N, K, out.stride(0), epi,
-            splits, ws, stream());
+  CHECK(out.stride(0) % (epi == 3 ? 4 : 8) == 0, "out row stride must be 16-byte aligned");
+  if (epi == 1 || epi == 2) CHECK(N % 256 == 0, "gated GEMM needs N (gate+up rows) to be a multiple of 256");
+  msgl_gemm_ex2(out.data_ptr(), x.data_ptr(), w.data_ptr(), blocked ? 1 : 0, opt_ptr(bias), M, N, K,
+                out.stride(0), epi, splits, wide, stream());
+}
+
+void gemm(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, int64_t epi) {
+  gemm_ex(out, x, w, bias, epi, -1, -1);
 }
 
 void act_and_mul(at::Tensor out, at::Tensor x, int64_t act) {
@@ -203,6 +218,7 @@ PYBIND11_MODULE(_cuda, m) {
   m.def("rmsnorm", &rmsnorm);
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
   m.def("gemm", &gemm);
+  m.def("gemm_ex", &gemm_ex);
   m.def("act_and_mul", &act_and_mul);
   m.def("store_kv", &store_kv);
   m.def("qk_norm_rope_store", &qk_norm_rope_store);

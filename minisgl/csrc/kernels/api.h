@@ -39,6 +39,13 @@ int msgl_gemm_workspace_bytes(int M, int N, int K, int splits);
 int msgl_gemm_pick_splits(int M, int N, int K);
 void msgl_gemm(void* out, const void* x, const void* w, const void* bias, int M, int N, int K,
                int ldo, int epi, int splits, void* workspace, cudaStream_t s);
+// same with explicit tiling overrides (splits > 0 forces split-K; wide 0/1 forces 128/256-row
+// weight tiles for plain outputs; -1 = automatic)
+void msgl_gemm_ex(void* out, const void* x, const void* w, const void* bias, int M, int N, int K,
+                  int ldo, int epi, int splits, int wide, void* workspace, cudaStream_t s);
+// w_blocked: weight stored K-block major as [K/64][N][64] (requires K % 64 == 0)
+void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M, int N,
+                   int K, int ldo, int epi, int splits, int wide, cudaStream_t s);
 
 // ----- paged attention (bf16 q/kv, fp32 softmax)
 void msgl_attention_prefill(void* o, const void* q, const void* k_cache, const void* v_cache,

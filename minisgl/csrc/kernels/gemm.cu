@@ -1,22 +1,31 @@
 // Persistent, warp-specialized bf16 GEMM on the 5th-generation tensor core (tcgen05 + TMEM + TMA).
 //
-//   out[M, N] = epilogue( x[M, K] @ w[N, K]^T + bias[N] )
+//   out[M, n] = epilogue( x[M, K] @ w[N, K]^T + bias )
 //
-// Orientation ("swap-AB"): the weight tile is the MMA's A operand (M = 128 weight rows) and the
-// activations are the B operand (N = BN tokens, 16..256). A decode batch of any size therefore
-// maps onto one MMA column tile, and every weight byte is streamed from HBM once per call.
+// Orientation ("swap-AB"): weight rows are the MMA's M dimension (128 per instruction) and the
+// tokens are its N dimension (BN = 16..256), so a decode batch of any size is one MMA column
+// tile and every weight byte is streamed from HBM once per call.
 //
-// Warp roles (192 threads, one CTA per SM, persistent over work units):
-//   warp 0      : TMA producer (one lane), fills a STAGES-deep ring of {A,B} tiles in smem.
-//   warp 1      : TMEM allocator + MMA issuer (one lane); accumulates a 128 x BN fp32 tile in
-//                 TMEM, double buffered so the epilogue of tile i overlaps the MMAs of tile i+1.
-//   warps 2..5  : epilogue; warp w reads TMEM lanes 32*(w%4).. via tcgen05.ld, applies bias /
-//                 activation, transposes through smem and writes 16-byte vectors.
-// Split-K (small-M decode with few weight tiles): each split writes an fp32 partial to the
-// workspace; the last split to arrive (atomic tile counter) reduces and runs the epilogue, then
-// resets the counter so the next launch (or CUDA-graph replay) starts from zero.
+// Warp roles (320 threads, one CTA per SM, persistent over work units):
+//   warp 0      TMA producer (one lane): a kStages-deep ring of {weight tile, activation tile}.
+//   warp 1      TMEM allocator + MMA issuer (one lane); fp32 accumulators live in TMEM, double
+//               buffered so the epilogue of one tile overlaps the main loop of the next.
+//   warps 2..9  epilogue: warp w reads TMEM lane quadrant (w % 4) (a hardware rule) and every
+//               other 32-token chunk; values go through a per-warp smem tile to a TMA store.
+//
+// Gated activations (gate_up projection with SiLU/GELU): the weight is stored with gate and up
+// rows interleaved in blocks of 128, so one 256-row weight tile holds 128 gate rows and their 128
+// up rows. Two MMAs per k-step write two TMEM accumulators; each epilogue thread then owns the
+// gate and up value of the same output element - no cross-warp exchange.
+//
+// Split-K (decode shapes with few weight tiles): the splits of one tile are launched as one
+// thread-block cluster (co-scheduled by hardware). Each CTA parks its fp32 partial in its own
+// shared memory (the drained operand ring), the cluster synchronizes, and every CTA reduces a
+// disjoint slice of the tile by reading its peers' partials over DSMEM (mapa +
+// ld.shared::cluster) before the epilogue. No global atomics, no workspace.
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "api.h"
@@ -25,71 +34,157 @@
 namespace msgl {
 namespace gemm {
 
-constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + kEpiWarps * 32;
 
 enum Epi : int { kBf16 = 0, kSilu = 1, kGelu = 2, kF32 = 3 };
 
-template <int BN>
+constexpr int pow2ceil(int x) {
+  int p = 32;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+template <int BN, int EPI, bool WIDE>
 struct Cfg {
-  static constexpr int kA = BM * BK * 2;
+  static constexpr bool kAct = EPI == kSilu || EPI == kGelu;
+  static constexpr bool kTwo = kAct || WIDE;           // two 128-row MMA halves per tile
+  static constexpr int kRowsA = kTwo ? 256 : 128;
+  static constexpr int kOutPerTile = kAct ? 128 : kRowsA;
+  static constexpr int kAccCols = (kTwo ? 2 : 1) * BN;
+  static constexpr int kBufs = 2 * kAccCols <= 512 ? 2 : 1;  // TMEM double buffering if it fits
+  static constexpr int kTmemCols = pow2ceil(kBufs * kAccCols);
+  static constexpr int kA = kRowsA * BK * 2;
   static constexpr int kB = BN * BK * 2;
   static constexpr int kStage = kA + kB;
-  static constexpr int kEpiBuf = 32 * 33 * 4;  // per epilogue warp: 32x32 fp32, padded
-  static constexpr int kStages = std::min(8, (220 * 1024 - kEpiWarps * kEpiBuf) / kStage);
-  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int kSmem = 1024 + kStages * kStage + kEpiWarps * kEpiBuf + 256;
+  static constexpr int kOutElem = EPI == kF32 ? 4 : 2;
+  static constexpr int kChunk = BN >= 32 ? 32 : 16;
+  static constexpr int kStageOut = kChunk * 32 * kOutElem;
+  static constexpr int kEpiSmem = kEpiWarps * kStageOut;
+  static constexpr int kStages = std::min(8, (220 * 1024 - kEpiSmem) / kStage);
+  static constexpr int kSmem = 1024 + kStages * kStage + kEpiSmem + 256;
+  // split-K partial parked in the operand ring: [rows][BN + 4] fp32 (padding spreads banks)
+  static constexpr int kPartRows = kTwo ? 256 : 128;
+  static constexpr int kPartLd = BN + 4;
+  static constexpr bool kCanSplit = kPartRows * kPartLd * 4 <= kStages * kStage;
+  static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
 };
 
 struct Params {
-  void* out;
   const __nv_bfloat16* bias;
-  float* partials;  // [units_tiles * splits, BM, BN]
-  int* counters;    // [tiles]
-  int M, N, K, ldo;
-  int n_tiles, m_tiles, splits, kblocks;
+  int w_blocked;  // weight stored [K/64][N][64] (3-D map) instead of [N][K]
+  int M, n_out, kblocks;
+  int n_tiles, m_tiles, splits;  // splits > 1: grid (splits, tiles), cluster (splits, 1, 1)
 };
 
 __device__ __forceinline__ float act_silu(float g) { return g / (1.f + __expf(-g)); }
 __device__ __forceinline__ float act_gelu(float g) {
-  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-  return 0.5f * g * (1.f + tanhf(k0 * (g + k1 * g * g * g)));
+  return 0.5f * g * (1.f + tanhf(0.7978845608028654f * (g + 0.044715f * g * g * g)));
 }
 
-// tile id -> (n_tile, m_tile); groups of 8 weight tiles sweep all token tiles so the weight
-// tiles of one wave stay resident in L2 while activations stream.
+// tile -> (weight tile, token tile): groups of 8 weight tiles sweep all token tiles so one wave's
+// weight tiles stay in L2 while activations stream.
 __device__ __forceinline__ void tile_coords(int tile, int n_tiles, int m_tiles, int& nt, int& mt) {
   constexpr int G = 8;
-  const int per_group = G * m_tiles;
-  const int g = tile / per_group;
-  const int r = tile - g * per_group;
-  const int gsize = min(G, n_tiles - g * G);
-  nt = g * G + r % gsize;
-  mt = r / gsize;
+  const int g = tile / (G * m_tiles);
+  const int r = tile - g * G * m_tiles;
+  const int gs = min(G, n_tiles - g * G);
+  nt = g * G + r % gs;
+  mt = r / gs;
 }
 
-template <int BN, int EPI>
+__device__ __forceinline__ void split_range(int split, int splits, int kblocks, int& kb0, int& kb1) {
+  kb0 = (int)((long long)split * kblocks / splits);
+  kb1 = (int)((long long)(split + 1) * kblocks / splits);
+}
+
+template <int W>
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float (&v)[32]) {
+  if constexpr (W == 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr, r);
+    tc_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  } else {
+    uint32_t r[16];
+    tmem_ld_32x32b_x16(taddr, r);
+    tc_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  }
+}
+
+// bias + activation for one (part, 32-token chunk) item of a warp's 32 accumulator rows, staged
+// in smem as [W tokens][32 cols] and written with a TMA store (rows >= M / cols >= n_out clipped)
+template <int BN, int EPI, bool WIDE>
+__device__ __forceinline__ void store_item(const float (&v)[32], const float (&g2)[32], const Params& p, int nt,
+                                           int mt, int part, int c, int q, int lane, uint8_t* stage_out,
+                                           const CUtensorMap* tmap_out) {
+  using C = Cfg<BN, EPI, WIDE>;
+  constexpr int W = C::kChunk;
+  const int nrow = q * 32 + lane;
+  const int wrow_idx = nt * C::kRowsA + part * 128 + nrow;
+  const int ocol0 = nt * C::kOutPerTile + part * 128 + q * 32;
+  float bias_a = 0.f, bias_b = 0.f;
+  if (p.bias != nullptr && ocol0 + lane < p.n_out) {
+    bias_a = __bfloat162float(p.bias[wrow_idx]);
+    if constexpr (C::kAct) bias_b = __bfloat162float(p.bias[wrow_idx + 128]);
+  }
+  float o[32];
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    if constexpr (C::kAct) {
+      const float g = v[j] + bias_a, up = g2[j] + bias_b;
+      o[j] = (EPI == kSilu ? act_silu(g) : act_gelu(g)) * up;
+    } else {
+      o[j] = v[j] + bias_a;
+    }
+  }
+  if (lane == 0) bulk_wait_read<0>();
+  __syncwarp();
+  if constexpr (EPI == kF32) {
+    float* s = reinterpret_cast<float*>(stage_out);
+#pragma unroll
+    for (int j = 0; j < W; ++j) s[j * 32 + lane] = o[j];
+  } else {
+    __nv_bfloat16* s = reinterpret_cast<__nv_bfloat16*>(stage_out);
+#pragma unroll
+    for (int j = 0; j < W; ++j) s[j * 32 + lane] = __float2bfloat16(o[j]);
+  }
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmap_out, stage_out, ocol0, mt * BN + c * W);
+    bulk_commit();
+  }
+}
+
+template <int BN, int EPI, bool WIDE>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-            Params p) {
-  using C = Cfg<BN>;
+            const __grid_constant__ CUtensorMap tmap_out, Params p) {
+  using C = Cfg<BN, EPI, WIDE>;
+  constexpr int W = C::kChunk;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* stage_base = smem;
-  float* epi_buf = reinterpret_cast<float*>(smem + C::kStages * C::kStage);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStage + kEpiWarps * C::kEpiBuf);
+  uint8_t* stages = smem;
+  uint8_t* epi_smem = smem + C::kStages * C::kStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + C::kEpiSmem);
   uint64_t* full = bars;
   uint64_t* empty = bars + C::kStages;
   uint64_t* tfull = bars + 2 * C::kStages;
-  uint64_t* tempty = tfull + 2;
+  uint64_t* tempty = tfull + 2;  // indexed by accumulator buffer (kBufs of them)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   int* flag_slot = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles = p.n_tiles * p.m_tiles;
-  const int units = tiles * p.splits;
+  const bool split = p.splits > 1;
+  // persistent over units, or exactly one unit per CTA when split (cluster rank = split index)
+  const int units = p.n_tiles * p.m_tiles * p.splits;
+  const int u_first = split ? blockIdx.y * p.splits + blockIdx.x : blockIdx.x;
+  const int u_step = split ? units : gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::kStages; ++i) {
@@ -103,6 +198,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     fence_barrier_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_out);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -119,17 +215,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int split = u % p.splits, tile = u / p.splits;
-        int nt, mt;
+      for (int u = u_first; u < units && ok; u += u_step) {
+        const int tile = u / p.splits;
+        int nt, mt, kb0, kb1;
         tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
-        const int kb0 = (int)((long long)split * p.kblocks / p.splits);
-        const int kb1 = (int)((long long)(split + 1) * p.kblocks / p.splits);
+        split_range(u % p.splits, p.splits, p.kblocks, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, 100)) { ok = false; break; }
-          uint8_t* a = stage_base + stage * C::kStage;
+          uint8_t* a = stages + stage * C::kStage;
           mbar_expect_tx(&full[stage], C::kStage);
-          tma_load_2d(a, &tmap_w, &full[stage], kb * BK, nt * BM);
+          if (p.w_blocked) tma_load_3d(a, &tmap_w, &full[stage], 0, nt * C::kRowsA, kb);
+          else tma_load_2d(a, &tmap_w, &full[stage], kb * BK, nt * C::kRowsA);
           tma_load_2d(a + C::kA, &tmap_x, &full[stage], kb * BK, mt * BN);
           if (++stage == C::kStages) { stage = 0; phase ^= 1; }
         }
@@ -138,28 +234,29 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
-      int stage = 0;
+      constexpr uint32_t idesc = idesc_bf16_f32(128, BN);
+      int stage = 0, use = 0;
       uint32_t phase = 0;
-      int use = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++use) {
-        const int split = u % p.splits;
-        const int kb0 = (int)((long long)split * p.kblocks / p.splits);
-        const int kb1 = (int)((long long)(split + 1) * p.kblocks / p.splits);
-        const int acc = use & 1;
-        if (!mbar_wait(&tempty[acc], ((use >> 1) & 1) ^ 1, 200)) break;
+      for (int u = u_first; u < units && ok; u += u_step, ++use) {
+        int kb0, kb1;
+        split_range(u % p.splits, p.splits, p.kblocks, kb0, kb1);
+        const int acc = C::kBufs == 2 ? (use & 1) : 0;
+        const uint32_t par = C::kBufs == 2 ? ((use >> 1) & 1) : (use & 1);
+        if (!mbar_wait(&tempty[acc], par ^ 1, 200)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + acc * BN;
+        const uint32_t d = tmem_base + acc * C::kAccCols;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, 201)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a = smem_u32(stage_base + stage * C::kStage);
+          const uint32_t a = smem_u32(stages + stage * C::kStage);
           const uint32_t b = a + C::kA;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            tc_mma_f16(d, smem_desc_sw128(a + k * 32), smem_desc_sw128(b + k * 32), idesc,
-                       (kb > kb0 || k > 0) ? 1u : 0u);
+            const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
+            const uint64_t bd = smem_desc_sw128(b + k * 32);
+            tc_mma_f16(d, smem_desc_sw128(a + k * 32), bd, idesc, accum);
+            if constexpr (C::kTwo) tc_mma_f16(d + BN, smem_desc_sw128(a + 128 * 128 + k * 32), bd, idesc, accum);
           }
           tc_commit(&empty[stage]);
           if (++stage == C::kStages) { stage = 0; phase ^= 1; }
@@ -169,168 +266,102 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     }
   } else {
     // ------------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const int ep_tid = threadIdx.x - 64;
-    float* buf = epi_buf + q * 32 * 33;
+    const int q = warp & 3;              // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;    // which half of the work items it takes
+    uint8_t* stage_out = epi_smem + (warp - 2) * C::kStageOut;
+    constexpr int kChunks = BN / W;
+    // work items: (part, chunk); a gated tile consumes both parts in one item
+    constexpr int kParts = (C::kTwo && !C::kAct) ? 2 : 1;
+    constexpr int kItems = kParts * kChunks;
     int use = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++use) {
-      const int split = u % p.splits, tile = u / p.splits;
+    for (int u = u_first; u < units; u += u_step, ++use) {
+      const int tile = u / p.splits;
       int nt, mt;
       tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
-      const int acc = use & 1;
-      if (!mbar_wait(&tfull[acc], (use >> 1) & 1, 300)) break;
+      const int acc = C::kBufs == 2 ? (use & 1) : 0;
+      const uint32_t par = C::kBufs == 2 ? ((use >> 1) & 1) : (use & 1);
+      if (!mbar_wait(&tfull[acc], par, 300)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
-      const int n_row = nt * BM + q * 32 + lane;  // weight row owned by this thread
-      const int m0 = mt * BN;
-
-      bool do_epilogue = true;
-      if (p.splits > 1) {
-        // write this split's partial (row-major [BM][BN] per unit), then count arrivals
-        float* part = p.partials + ((size_t)tile * p.splits + split) * BM * BN + (size_t)(q * 32 + lane) * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          if constexpr (BN >= 32) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tbase + c, r);
-            tc_wait_ld();
+      const uint32_t tb = tmem_base + acc * C::kAccCols + ((uint32_t)(q * 32) << 16);
+      const int nrow = q * 32 + lane;  // accumulator row inside a 128-row half
+      if (split) {
+        if constexpr (C::kCanSplit) {
+          // park this split's partial in the (drained) operand ring; reduce after cluster sync
+          float* part_buf = reinterpret_cast<float*>(stages);
+          for (int c = half; c < kChunks; c += 2) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(part + c + j) =
-                  make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                              __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-          } else {
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(tbase + c, r);
-            tc_wait_ld();
+            for (int pt = 0; pt < (C::kTwo ? 2 : 1); ++pt) {
+              float v[32];
+              tmem_load_cols<W>(tb + pt * BN + c * W, v);
+              float* dst = part_buf + (size_t)(pt * 128 + nrow) * C::kPartLd + c * W;
 #pragma unroll
-            for (int j = 0; j < 16; j += 4)
-              *reinterpret_cast<float4*>(part + c + j) =
-                  make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                              __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+              for (int j = 0; j < W; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
           }
         }
-        __threadfence();
-        named_bar_sync(1, kEpiWarps * 32);
-        if (ep_tid == 0) {
-          const int old = atomicAdd(&p.counters[tile], 1);
-          const int last = old == p.splits - 1;
-          if (last) p.counters[tile] = 0;  // re-arm for the next launch
-          *flag_slot = last;
-        }
-        named_bar_sync(1, kEpiWarps * 32);
-        do_epilogue = *flag_slot != 0;
-        __threadfence();
+        break;  // the reduction + epilogue run after the cluster barrier below
       }
-
-      if (do_epilogue) {
-        float bias_v = 0.f;
-        if (p.bias != nullptr && n_row < p.N) bias_v = __bfloat162float(p.bias[n_row]);
-        const bool is_act = EPI == kSilu || EPI == kGelu;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          constexpr int W = BN >= 32 ? 32 : 16;
-          float v[32];
-          if (p.splits > 1) {
-            // reduce all partials of this tile for columns [c, c + W)
-#pragma unroll
-            for (int j = 0; j < W; ++j) v[j] = 0.f;
-            for (int s = 0; s < p.splits; ++s) {
-              const float* part = p.partials + ((size_t)tile * p.splits + s) * BM * BN +
-                                  (size_t)(q * 32 + lane) * BN + c;
-#pragma unroll
-              for (int j = 0; j < W; j += 4) {
-                const float4 t = __ldcg(reinterpret_cast<const float4*>(part + j));
-                v[j] += t.x; v[j + 1] += t.y; v[j + 2] += t.z; v[j + 3] += t.w;
-              }
-            }
-          } else if constexpr (W == 32) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tbase + c, r);
-            tc_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          } else {
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(tbase + c, r);
-            tc_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-          }
-#pragma unroll
-          for (int j = 0; j < W; ++j) v[j] += bias_v;
-
-          if constexpr (is_act) {
-            // quadrants 2,3 hold "up" rows, 0,1 hold the matching "gate" rows
-            if (q >= 2) {
-#pragma unroll
-              for (int j = 0; j < W; ++j) buf[j * 33 + lane] = v[j];
-            }
-            named_bar_sync(1, kEpiWarps * 32);
-            if (q < 2) {
-              const float* up = epi_buf + (q + 2) * 32 * 33;
-#pragma unroll
-              for (int j = 0; j < W; ++j) {
-                const float g = v[j];
-                const float a = EPI == kSilu ? act_silu(g) : act_gelu(g);
-                buf[j * 33 + lane] = a * up[j * 33 + lane];
-              }
-              __syncwarp();
-              // 32 (or 16) token rows x 32 output cols bf16 = 4 x 16B per row
-              const int ncol0 = nt * (BM / 2) + q * 32;
-#pragma unroll
-              for (int i = 0; i < W / 8; ++i) {
-                const int idx = lane + 32 * i, row = idx >> 2, part = idx & 3;
-                const int m = m0 + c + row, n = ncol0 + part * 8;
-                if (m < p.M && n < p.N / 2) {
-                  const float* s = buf + row * 33 + part * 8;
-                  uint4 o;
-                  o.x = pack_bf16(s[0], s[1]); o.y = pack_bf16(s[2], s[3]);
-                  o.z = pack_bf16(s[4], s[5]); o.w = pack_bf16(s[6], s[7]);
-                  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)m * p.ldo + n) = o;
-                }
-              }
-            }
-            named_bar_sync(1, kEpiWarps * 32);
-          } else {
-#pragma unroll
-            for (int j = 0; j < W; ++j) buf[j * 33 + lane] = v[j];
-            __syncwarp();
-            const int ncol0 = nt * BM + q * 32;
-            if constexpr (EPI == kF32) {
-#pragma unroll
-              for (int i = 0; i < W / 4; ++i) {
-                const int idx = lane + 32 * i, row = idx >> 3, part = idx & 7;
-                const int m = m0 + c + row, n = ncol0 + part * 4;
-                if (m < p.M && n < p.N) {
-                  const float* s = buf + row * 33 + part * 4;
-                  *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)m * p.ldo + n) =
-                      make_float4(s[0], s[1], s[2], s[3]);
-                }
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < W / 8; ++i) {
-                const int idx = lane + 32 * i, row = idx >> 2, part = idx & 3;
-                const int m = m0 + c + row, n = ncol0 + part * 8;
-                if (m < p.M && n < p.N) {
-                  const float* s = buf + row * 33 + part * 8;
-                  uint4 o;
-                  o.x = pack_bf16(s[0], s[1]); o.y = pack_bf16(s[2], s[3]);
-                  o.z = pack_bf16(s[4], s[5]); o.w = pack_bf16(s[6], s[7]);
-                  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)m * p.ldo + n) = o;
-                }
-              }
-            }
-            __syncwarp();
-          }
-        }
+      for (int it = half; it < kItems; it += 2) {
+        const int part = it / kChunks, c = it % kChunks;
+        float v[32], g2[32];
+        tmem_load_cols<W>(tb + part * BN + c * W, v);
+        if constexpr (C::kAct) tmem_load_cols<W>(tb + BN + c * W, g2);
+        store_item<BN, EPI, WIDE>(v, g2, p, nt, mt, part, c, q, lane, stage_out, &tmap_out);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   }
+
+  if (split) {
+    if constexpr (C::kCanSplit) {
+      // ---------------------------------------------------------------- cluster split-K reduction
+      cluster_sync();  // every CTA's partial is parked
+      if (warp >= 2) {
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        const uint32_t rank = cluster_ctarank();
+        const int tile = blockIdx.y;
+        int nt, mt;
+        tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
+        uint8_t* stage_out = epi_smem + (warp - 2) * C::kStageOut;
+        constexpr int kChunks = BN / W;
+        constexpr int kParts = (C::kTwo && !C::kAct) ? 2 : 1;
+        constexpr int kItems = kParts * kChunks;
+        const float* part_buf = reinterpret_cast<const float*>(stages);
+        const int nrow = q * 32 + lane;
+        int k = 0;
+        for (int it = (int)rank; it < kItems; it += p.splits, ++k) {
+          if ((k & 1) != half) continue;
+          const int part = it / kChunks, c = it % kChunks;
+          float v[32], g2[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = g2[j] = 0.f;
+          const uint32_t la = smem_u32(part_buf + (size_t)(part * 128 + nrow) * C::kPartLd + c * W);
+          const uint32_t lb = smem_u32(part_buf + (size_t)(128 + nrow) * C::kPartLd + c * W);
+          for (int r = 0; r < p.splits; ++r) {
+            const uint32_t ra = dsmem_addr(la, r);
+#pragma unroll
+            for (int j = 0; j < W; j += 4) {
+              const float4 t = ld_dsmem_v4(ra + j * 4);
+              v[j] += t.x; v[j + 1] += t.y; v[j + 2] += t.z; v[j + 3] += t.w;
+            }
+            if constexpr (C::kAct) {
+              const uint32_t rb = dsmem_addr(lb, r);
+#pragma unroll
+              for (int j = 0; j < W; j += 4) {
+                const float4 t = ld_dsmem_v4(rb + j * 4);
+                g2[j] += t.x; g2[j + 1] += t.y; g2[j + 2] += t.z; g2[j + 3] += t.w;
+              }
+            }
+          }
+          store_item<BN, EPI, WIDE>(v, g2, p, nt, mt, part, c, q, lane, stage_out, &tmap_out);
+        }
+      }
+      cluster_sync();  // peers may still be reading this CTA's partial
+    }
+  }
+  if (warp >= 2 && lane == 0) bulk_wait<0>();
 
   tc_fence_before();
   __syncthreads();
@@ -359,23 +390,43 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D bf16 row-major [rows, cols] (cols contiguous), box [box_rows, 64], 128-byte swizzle.
-static CUtensorMap make_map(const void* base, int rows, int cols, int ld, int box_rows) {
+// 2-D row-major [rows, cols] tensor map with the given box; swizzle 128B for operand loads,
+// none for epilogue stores.
+static CUtensorMap make_map(const void* base, CUtensorMapDataType dt, int elem, int rows, int cols, int ld,
+                            int box_cols, int box_rows, bool swizzle) {
   CUtensorMap m;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
+  memset(&m, 0, sizeof(m));
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) {
     fprintf(stderr, "minisgl: cuTensorMapEncodeTiled unavailable\n");
-    memset(&m, 0, sizeof(m));
     return m;
   }
-  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * elem};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) fprintf(stderr, "minisgl: cuTensorMapEncodeTiled failed (%d)\n", (int)r);
+  return m;
+}
+
+// [K/64][N][64] weight: 3-D map (k-in-block, row, k-block), box (64, rows, 1): each weight tile is
+// one contiguous run of rows x 128 B in HBM.
+static CUtensorMap make_map_blocked(const void* base, int N, int K, int box_rows) {
+  CUtensorMap m;
+  memset(&m, 0, sizeof(m));
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return m;
+  cuuint64_t dims[3] = {(cuuint64_t)BK, (cuuint64_t)N, (cuuint64_t)(K / BK)};
+  cuuint64_t strides[2] = {(cuuint64_t)BK * 2, (cuuint64_t)N * BK * 2};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fprintf(stderr, "minisgl: cuTensorMapEncodeTiled (blocked) failed (%d)\n", (int)r);
   return m;
 }
 
@@ -390,35 +441,131 @@ static int num_sms_cached() {
   return n;
 }
 
-template <int BN, int EPI>
-static void launch(const Params& p, const CUtensorMap& mw, const CUtensorMap& mx, cudaStream_t s) {
-  using C = Cfg<BN>;
+static bool is_act(int epi) { return epi == kSilu || epi == kGelu; }
+
+struct Plan {
+  int bn;
+  bool wide;
+  int rows_a;  // weight rows per tile
+  int tiles;
+  int splits;
+};
+
+// Tile shape (chosen from graph-replay measurements on B200): plain outputs use 128-row weight
+// tiles with BN = round-up(M) <= 256 tokens; gated outputs use 256-row tiles (128 gate + 128 up)
+// with BN <= 256 for decode and 128 for prefill. Split-K (a cluster of 2 or 4 CTAs per tile,
+// reduced through DSMEM) only pays off for long K with few tiles.
+static Plan make_plan(int M, int N, int K, int epi, int force_splits, int force_wide) {
+  Plan pl;
+  const bool act = is_act(epi);
+  if (M <= 256) pl.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  else pl.bn = act ? 128 : 256;
+  pl.wide = act || force_wide == 1;
+  pl.rows_a = pl.wide ? 256 : 128;
+  pl.tiles = ((N + pl.rows_a - 1) / pl.rows_a) * ((M + pl.bn - 1) / pl.bn);
+  const int kblocks = (K + BK - 1) / BK;
+  const int sms = num_sms_cached();
+  // split-K needs the partial ([rows][bn+4] fp32) to fit the operand ring: bn <= 128 if wide
+  const bool can_split = !(pl.rows_a == 256 && pl.bn > 128);
+  int splits = 1;
+  if (force_splits > 0) splits = force_splits;
+  else if (!act && pl.tiles <= sms / 2 && kblocks >= 48) splits = (kblocks >= 192 && pl.tiles * 4 <= sms) ? 4 : 2;
+  splits = std::min(std::min(splits, 8), std::max(1, kblocks / 4));
+  pl.splits = can_split ? splits : 1;
+  return pl;
+}
+
+// Largest co-resident cluster count for a cluster size (GPCs do not divide evenly by every size).
+template <int BN, int EPI, bool WIDE>
+static int max_clusters(int size) {
+  using C = Cfg<BN, EPI, WIDE>;
+  static int cache[9] = {0};
+  if (cache[size] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(size, 64, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, EPI, WIDE>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms_cached() / size;
+    }
+    cache[size] = n;
+  }
+  return cache[size];
+}
+
+// Choose the cluster (split) size minimizing waves x k-blocks per split + a reduction charge,
+// never above `cap`.
+template <int BN, int EPI, bool WIDE>
+static int best_splits(int tiles, int kblocks, int cap) {
+  int best = 1;
+  double best_cost = 1e30;
+  for (int sz = 1; sz <= std::min(cap, 8); ++sz) {
+    const int mc = sz == 1 ? num_sms_cached() : max_clusters<BN, EPI, WIDE>(sz);
+    if (mc <= 0) continue;
+    const int waves = (tiles + mc - 1) / mc;
+    const double cost = waves * ((double)(kblocks + sz - 1) / sz + 6.0) + (sz > 1 ? 2.0 : 0.0);
+    if (cost < best_cost - 1e-9) { best_cost = cost; best = sz; }
+  }
+  return best;
+}
+
+template <int BN, int EPI, bool WIDE>
+static void launch(const Params& p, const void* x, const void* w, void* out, int N, int K, int ldo, cudaStream_t s) {
+  using C = Cfg<BN, EPI, WIDE>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    cudaFuncSetAttribute(gemm_kernel<BN, EPI, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     attr_set = true;
   }
-  const int units = p.n_tiles * p.m_tiles * p.splits;
-  const int grid = std::min(units, num_sms_cached());
-  gemm_kernel<BN, EPI><<<grid, kThreads, C::kSmem, s>>>(mw, mx, p);
-}
-
-template <int BN>
-static void dispatch_epi(int epi, const Params& p, const CUtensorMap& mw, const CUtensorMap& mx, cudaStream_t s) {
-  switch (epi) {
-    case kBf16: launch<BN, kBf16>(p, mw, mx, s); break;
-    case kSilu: launch<BN, kSilu>(p, mw, mx, s); break;
-    case kGelu: launch<BN, kGelu>(p, mw, mx, s); break;
-    default: launch<BN, kF32>(p, mw, mx, s); break;
+  const CUtensorMap mw = p.w_blocked ? make_map_blocked(w, N, K, C::kRowsA)
+                                     : make_map(w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, BK, C::kRowsA, true);
+  const CUtensorMap mx = make_map(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, K, K, BK, BN, true);
+  const CUtensorMap mo = EPI == kF32
+      ? make_map(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.M, p.n_out, ldo, 32, C::kChunk, false)
+      : make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, C::kChunk, false);
+  Params q = p;
+  if (q.splits > 1 && !C::kCanSplit) q.splits = 1;
+  if (q.splits > 1 && q.n_tiles * q.m_tiles > max_clusters<BN, EPI, WIDE>(q.splits)) q.splits = 1;
+  const int tiles = q.n_tiles * q.m_tiles;
+  if (q.splits > 1) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(q.splits, tiles, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = q.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI, WIDE>, mw, mx, mo, q);
+  } else {
+    const int grid = std::min(tiles, num_sms_cached());
+    gemm_kernel<BN, EPI, WIDE><<<grid, kThreads, C::kSmem, s>>>(mw, mx, mo, q);
   }
 }
 
-static int pick_bn(int M) {
-  if (M <= 16) return 16;
-  if (M <= 32) return 32;
-  if (M <= 64) return 64;
-  if (M <= 128) return 128;
-  return 256;
+template <int EPI, bool WIDE>
+static void dispatch_bn(int bn, const Params& p, const void* x, const void* w, void* out, int N, int K, int ldo,
+                        cudaStream_t s) {
+  switch (bn) {
+    case 16: launch<16, EPI, WIDE>(p, x, w, out, N, K, ldo, s); break;
+    case 32: launch<32, EPI, WIDE>(p, x, w, out, N, K, ldo, s); break;
+    case 64: launch<64, EPI, WIDE>(p, x, w, out, N, K, ldo, s); break;
+    case 128: launch<128, EPI, WIDE>(p, x, w, out, N, K, ldo, s); break;
+    default: launch<256, EPI, WIDE>(p, x, w, out, N, K, ldo, s); break;
+  }
 }
 
 }  // namespace gemm
@@ -427,54 +574,45 @@ static int pick_bn(int M) {
 using namespace msgl;
 using namespace msgl::gemm;
 
-extern "C" int msgl_gemm_pick_splits(int M, int N, int K) {
-  const int bn = pick_bn(M);
-  const int tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
-  const int kblocks = (K + BK - 1) / BK;
-  const int sms = num_sms_cached();
-  if (tiles >= sms / 2 || kblocks < 8) return 1;
-  int splits = std::min(sms / tiles, kblocks / 4);
-  return std::max(1, std::min(splits, 16));
+extern "C" int msgl_gemm_pick_splits(int M, int N, int K) { return make_plan(M, N, K, kBf16, -1, -1).splits; }
+
+extern "C" int msgl_gemm_workspace_bytes(int M, int N, int K, int splits) { return 0; }
+
+extern "C" void msgl_gemm_ex(void* out, const void* x, const void* w, const void* bias, int M, int N, int K,
+                             int ldo, int epi, int force_splits, int force_wide, void* workspace, cudaStream_t s) {
+  msgl_gemm_ex2(out, x, w, 0, bias, M, N, K, ldo, epi, force_splits, force_wide, s);
+  (void)workspace;
 }
 
-extern "C" int msgl_gemm_workspace_bytes(int M, int N, int K, int splits) {
-  if (splits <= 1) return 0;
-  const int bn = pick_bn(M);
-  const int tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
-  return tiles * 4 + 256 + tiles * splits * BM * bn * 4;
-}
-
-extern "C" void msgl_gemm(void* out, const void* x, const void* w, const void* bias, int M, int N,
-                          int K, int ldo, int epi, int splits, void* workspace, cudaStream_t s) {
+extern "C" void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M,
+                              int N, int K, int ldo, int epi, int force_splits, int force_wide, cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
-  const int bn = pick_bn(M);
+  Plan pl = make_plan(M, N, K, epi, force_splits, force_wide);
   Params p;
-  p.out = out;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
-  p.M = M; p.N = N; p.K = K; p.ldo = ldo;
-  p.n_tiles = (N + BM - 1) / BM;
-  p.m_tiles = (M + bn - 1) / bn;
+  p.w_blocked = w_blocked;
+  p.M = M;
+  p.n_out = is_act(epi) ? N / 2 : N;
+  p.n_tiles = (N + pl.rows_a - 1) / pl.rows_a;
+  p.m_tiles = (M + pl.bn - 1) / pl.bn;
   p.kblocks = (K + BK - 1) / BK;
-  p.splits = std::max(1, std::min(splits, p.kblocks));
-  const int tiles = p.n_tiles * p.m_tiles;
-  if (p.splits > 1) {
-    p.counters = reinterpret_cast<int*>(workspace);
-    p.partials = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + ((tiles * 4 + 255) & ~255));
-  } else {
-    p.counters = nullptr;
-    p.partials = nullptr;
-  }
-  const CUtensorMap mw = make_map(w, N, K, K, BM);
-  const CUtensorMap mx = make_map(x, M, K, K, bn);
-  switch (bn) {
-    case 16: dispatch_epi<16>(epi, p, mw, mx, s); break;
-    case 32: dispatch_epi<32>(epi, p, mw, mx, s); break;
-    case 64: dispatch_epi<64>(epi, p, mw, mx, s); break;
-    case 128: dispatch_epi<128>(epi, p, mw, mx, s); break;
-    default: dispatch_epi<256>(epi, p, mw, mx, s); break;
+  p.splits = pl.splits;
+  const bool wide = pl.wide;
+  switch (epi) {
+    case kBf16: wide ? dispatch_bn<kBf16, true>(pl.bn, p, x, w, out, N, K, ldo, s)
+                     : dispatch_bn<kBf16, false>(pl.bn, p, x, w, out, N, K, ldo, s); break;
+    case kSilu: dispatch_bn<kSilu, true>(pl.bn, p, x, w, out, N, K, ldo, s); break;
+    case kGelu: dispatch_bn<kGelu, true>(pl.bn, p, x, w, out, N, K, ldo, s); break;
+    default: wide ? dispatch_bn<kF32, true>(pl.bn, p, x, w, out, N, K, ldo, s)
+                  : dispatch_bn<kF32, false>(pl.bn, p, x, w, out, N, K, ldo, s); break;
   }
 }
 
-MSGL_ERROR_ACCESSOR(msgl_err_gemm)
+extern "C" void msgl_gemm(void* out, const void* x, const void* w, const void* bias, int M, int N, int K,
+                          int ldo, int epi, int splits, void* workspace, cudaStream_t s) {
+  msgl_gemm_ex(out, x, w, bias, M, N, K, ldo, epi, splits, -1, workspace, s);
+}
 
 extern "C" int msgl_num_sms() { return num_sms_cached(); }
+
+MSGL_ERROR_ACCESSOR(msgl_err_gemm)

@@ -148,6 +148,8 @@ class Engine:
         if not self.is_cuda or config.tp_info.size == 1:
             return
         mode = config.comm if config.comm != "auto" else os.environ.get("MINISGL_COMM_MODE", "auto")
+        if mode == "nccl":
+            return
         if mode in ("auto", "peer", "fused"):
             from minisgl.parallel.peer import enable_peer_comm
 

@@ -1,7 +1,7 @@
 """Mixture-of-experts layer (reference: python/minisgl/layers/moe.py:9-59).
 
-Expert weights are packed: ``gate_up_proj [E, 2*I/tp, H]`` (gate/up interleaved in 64-row
-blocks, like the dense MLP) and ``down_proj [E, H, I/tp]``. Tensor parallelism shards every
+Expert weights are packed: ``gate_up_proj [E, 2*I/tp, H]`` as ``[gate; up]`` halves and
+``down_proj [E, H, I/tp]``. Tensor parallelism shards every
 expert's intermediate dim; the sum over ranks follows the expert combine.
 """
 

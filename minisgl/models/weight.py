@@ -5,7 +5,8 @@ Per tensor: strip the ``language_model.`` prefix, skip vision weights, take this
 (q/k/v/gate/up and their biases split on dim 0 with KV-head replication when tp > kv heads;
 o/down split on dim 1; embed/lm_head split into ``ceil(V/tp)`` vocab rows, zero padded; sinks
 split by head), merge q,k,v -> ``qkv_proj`` and gate,up -> ``gate_up_proj`` (gate/up interleaved
-in 64-row blocks for the fused activation epilogue), and stack per-expert tensors into packed
+in 128-row blocks for the fused activation epilogue; expert weights keep plain ``[gate; up]``
+halves), and stack per-expert tensors into packed
 ``[E, ...]`` tensors. Yields ``(name, tensor)`` already on the target device.
 """
 
@@ -64,6 +65,8 @@ def _merge_slot(key: str):
 
 
 def _finish_merge(key: str, parts: Dict[str, torch.Tensor]) -> torch.Tensor:
+    if "gate_up_proj" in key and ".experts." in key:  # experts keep [gate; up] halves
+        return torch.cat([parts["gate"], parts["up"]], dim=0)
     if "gate_up_proj" in key:
         g, u = parts["gate"], parts["up"]
         if g.dim() == 1:  # bias

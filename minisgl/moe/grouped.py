@@ -26,7 +26,8 @@ def route(gating: torch.Tensor, topk: int, renormalize: bool, softmax_after_topk
 
 
 def expert_act(y: torch.Tensor, activation: str) -> torch.Tensor:
-    g, u = ref.deinterleave_gate_up(y.float())
+    """Expert gate_up output [T, 2I] laid out as [gate | up] halves -> activated [T, I]."""
+    g, u = y.float().chunk(2, dim=-1)
     if activation == "silu":
         a = F.silu(g) * u
     elif activation == "gelu":

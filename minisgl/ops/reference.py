@@ -12,7 +12,7 @@ import math
 import torch
 import torch.nn.functional as F
 
-GATE_UP_BLOCK = 64  # gate/up rows are interleaved in blocks of this many rows
+GATE_UP_BLOCK = 128  # gate/up rows are interleaved in blocks of this many rows
 
 
 def embedding(weight: torch.Tensor, ids: torch.Tensor, vocab_start: int = 0, vocab_len: int | None = None):
@@ -62,6 +62,7 @@ def deinterleave_gate_up(y: torch.Tensor):
 
 
 def gate_up_act(y: torch.Tensor, act: str = "silu") -> torch.Tensor:
+    """Activation over an interleaved gate/up projection output [T, 2I] -> [T, I]."""
     g, u = deinterleave_gate_up(y.float())
     a = F.silu(g) if act == "silu" else F.gelu(g, approximate="tanh")
     return (a * u).to(y.dtype)

@@ -218,3 +218,27 @@ def test_store_kv():
     ref.store_kv(k.cpu(), v.cpu(), kc2, vc2, loc.cpu())
     _close(kc, kc2, 0, 0)
     _close(vc, vc2, 0, 0)
+
+
+@pytest.mark.parametrize("M", [5, 130, 256, 600])
+@pytest.mark.parametrize("epi", [0, 1, 3])
+@pytest.mark.parametrize("wide,splits", [(0, 1), (1, 1), (0, 3), (1, 4), (-1, -1)])
+@pytest.mark.parametrize("blocked", [False, True])
+def test_gemm_variants(M, epi, wide, splits, blocked):
+    """Every tiling (128/256-row weight tiles, forced split-K) against the fp32 reference, run
+    twice so split-K workspace/counter re-zeroing is exercised, with bias."""
+    K, N = 1536, 768
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    b = torch.randn(N, device=DEV, dtype=torch.bfloat16)
+    if epi == 1:
+        expect = ref.gate_up_act(x.cpu().float() @ w.cpu().float().t() + b.cpu().float())
+        out = torch.empty(M, N // 2, device=DEV, dtype=torch.bfloat16)
+    else:
+        expect = x.cpu().float() @ w.cpu().float().t() + b.cpu().float()
+        out = torch.empty(M, N, device=DEV, dtype=torch.float32 if epi == 3 else torch.bfloat16)
+    wk = w.view(N, K // 64, 64).transpose(0, 1).contiguous() if blocked else w
+    for _ in range(2):
+        out.zero_()
+        _c().gemm_ex(out, x, wk, b, epi, splits, wide)
+        _close(out, expect, 3e-2, 3e-2)

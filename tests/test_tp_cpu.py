@@ -1,0 +1,63 @@
+"""Tensor parallelism on CPU: two gloo ranks (one process each, launched like torchrun) must
+produce exactly the TP1 greedy tokens of the fp32 oracle."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+from minisgl.core import SamplingParams
+from minisgl.models.synthetic import make_checkpoint
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+WORKER = r"""
+import json, os, sys
+sys.path.insert(0, {root!r})
+import torch
+from minisgl.core import SamplingParams
+from minisgl.llm import LLM
+prompts = json.loads(os.environ["TP_PROMPTS"])
+llm = LLM({path!r}, dtype=torch.float32, device="cpu", max_running_req=16, cache_type="radix",
+          max_extend_tokens=48)
+out = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=12, ignore_eos=True))]
+llm.cache_manager.check_integrity()
+if int(os.environ["RANK"]) == 0:
+    print("RESULT " + json.dumps(out), flush=True)
+llm.shutdown()
+"""
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(3)
+    return [torch.randint(0, 1024, (int(torch.randint(8, 40, (1,), generator=g)),), generator=g).tolist()
+            for _ in range(6)]
+
+
+@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-qwen3-moe"])
+def test_tp2_matches_tp1(tmp_path, preset, free_port):
+    from minisgl.llm import LLM
+
+    path = make_checkpoint(preset, str(tmp_path / preset))
+    prompts = _prompts()
+    llm = LLM(path, dtype=torch.float32, device="cpu", max_running_req=16, distributed_port=free_port,
+              max_extend_tokens=48)
+    try:
+        ref = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=12, ignore_eos=True))]
+    finally:
+        llm.shutdown()
+    script = tmp_path / "worker.py"
+    script.write_text(WORKER.format(root=ROOT, path=path))
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE="2", MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(free_port + 7), TP_PROMPTS=json.dumps(prompts), PYTHONPATH=ROOT)
+        procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    outs = [p.communicate(timeout=300)[0] for p in procs]
+    assert all(p.returncode == 0 for p in procs), outs
+    line = [l for l in outs[0].splitlines() if l.startswith("RESULT ")][0]
+    assert json.loads(line[len("RESULT "):]) == ref
