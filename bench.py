@@ -170,6 +170,8 @@ def run(args, impl: str):
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=cpu_group)
         dev_ms, wall_ms = float(t[0]), float(t[1])
     if rank != 0:
+        if impl != "reference":
+            llm.shutdown()
         return
     line = {
         "metric": "offline output tok/s Qwen3-14B @TP1/2/4/8 B200" if args.model == "qwen3-14b"

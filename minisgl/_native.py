@@ -25,7 +25,8 @@ def host():
 class _CountingModule:
     """Forwards attribute access to the extension and counts kernel-launching calls."""
 
-    _NON_LAUNCH = {"get_error", "num_sms", "gemm_splits"}
+    _NON_LAUNCH = {"get_error", "num_sms", "gemm_splits", "peer_flag_bytes", "peer_alloc", "peer_free",
+                   "ipc_handle", "ipc_open", "ipc_close", "peer_grid"}
 
     def __init__(self, mod):
         self._mod = mod

@@ -4,6 +4,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <string>
+#include <vector>
+
 #include <mutex>
 #include <unordered_map>
 
@@ -204,6 +207,49 @@ void attention_decode(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor
                         workspace.data_ptr(), stream());
 }
 
+// ----- peer-memory collectives
+int64_t peer_alloc(int64_t bytes) {
+  void* p = msgl_peer_alloc(bytes);
+  CHECK(p != nullptr, "peer buffer allocation of ", bytes, " bytes failed");
+  return reinterpret_cast<int64_t>(p);
+}
+void peer_free(int64_t p) { msgl_peer_free(reinterpret_cast<void*>(p)); }
+py::bytes ipc_handle(int64_t p) {
+  char buf[64];
+  const int rc = msgl_ipc_handle(reinterpret_cast<void*>(p), buf);
+  CHECK(rc == 0, "cudaIpcGetMemHandle failed (", rc, ")");
+  return py::bytes(buf, 64);
+}
+int64_t ipc_open(py::bytes h) {
+  std::string s = h;
+  CHECK(s.size() == 64, "bad IPC handle");
+  void* p = msgl_ipc_open(s.data());
+  CHECK(p != nullptr, "cudaIpcOpenMemHandle failed");
+  return reinterpret_cast<int64_t>(p);
+}
+void ipc_close(int64_t p) { msgl_ipc_close(reinterpret_cast<void*>(p)); }
+
+void peer_collective(int64_t mode, at::Tensor out, at::Tensor in, std::vector<int64_t> bases, int64_t rank,
+                     int64_t cap_bytes, at::Tensor state, int64_t timeout_ns) {
+  check_cuda(out, "out"); check_cuda(in, "in"); check_contig(out, "out"); check_contig(in, "in");
+  check_cuda(state, "state"); check_dtype(state, at::kInt, "state");
+  CHECK(state.numel() >= 2 * msgl_peer_grid(), "peer state tensor too small");
+  const int64_t bytes = in.numel() * in.element_size();
+  CHECK(bytes % 16 == 0, "peer collectives need a multiple of 16 bytes");
+  CHECK(bytes <= cap_bytes, "message of ", bytes, " bytes exceeds the peer buffer (", cap_bytes, ")");
+  CHECK(bases.size() >= 1 && bases.size() <= 8, "1..8 ranks supported");
+  std::vector<void*> b;
+  for (auto v : bases) b.push_back(reinterpret_cast<void*>(v));
+  if (mode == 2) {
+    CHECK(out.numel() * out.element_size() == bytes * (int64_t)b.size(), "all-gather output size");
+  } else {
+    check_dtype(in, at::kBFloat16, "in");
+    CHECK(out.numel() == in.numel(), "all-reduce output size");
+  }
+  msgl_peer_collective(b.data(), rank, b.size(), mode, out.data_ptr(), in.data_ptr(), bytes, cap_bytes,
+                       reinterpret_cast<uint32_t*>(state.data_ptr()), timeout_ns, stream());
+}
+
 std::tuple<int64_t, int64_t> get_error() {
   int info = 0;
   const int code = msgl_get_error(&info);
@@ -227,6 +273,14 @@ PYBIND11_MODULE(_cuda, m) {
   m.def("attention_prefill", &attention_prefill);
   m.def("attention_decode", &attention_decode);
   m.def("get_error", &get_error);
+  m.def("peer_flag_bytes", []() { return msgl_peer_flag_bytes(); });
+  m.def("peer_alloc", &peer_alloc);
+  m.def("peer_free", &peer_free);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("peer_grid", []() { return msgl_peer_grid(); });
+  m.def("peer_collective", &peer_collective);
   m.def("num_sms", []() { return msgl_num_sms(); });
   m.def("gemm_splits", [](int64_t M, int64_t N, int64_t K) { return msgl_gemm_pick_splits(M, N, K); });
 }

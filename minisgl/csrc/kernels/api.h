@@ -59,4 +59,16 @@ void msgl_attention_decode(void* o, const void* q, const void* k_cache, const vo
                            const int32_t* kv_lens, int bs, int nq, int nkv, int hd,
                            int64_t cache_stride, float sm_scale, int window, const float* sinks,
                            int num_splits, void* workspace, cudaStream_t s);
+
+// ----- peer-memory collectives (CUDA IPC over NVLink)
+int msgl_peer_flag_bytes();
+void* msgl_peer_alloc(int64_t bytes);
+void msgl_peer_free(void* p);
+int msgl_ipc_handle(void* p, void* out64);
+void* msgl_ipc_open(const void* in64);
+void msgl_ipc_close(void* p);
+int msgl_peer_grid();  // CTAs per collective; the state tensor holds 2 uint32 per CTA
+// mode 0: one-shot all-reduce, 1: two-shot all-reduce, 2: all-gather (dim 0)
+void msgl_peer_collective(void* const* bases, int rank, int world, int mode, void* out, const void* in,
+                          int64_t bytes, int64_t cap_bytes, uint32_t* state, int64_t timeout_ns, cudaStream_t s);
 }

@@ -5,9 +5,10 @@ extern "C" int msgl_err_gemm(int* info);
 extern "C" int msgl_err_elementwise(int* info);
 extern "C" int msgl_err_attention(int* info);
 extern "C" int msgl_err_sampling(int* info);
+extern "C" int msgl_err_comm(int* info);
 
 extern "C" int msgl_get_error(int* info) {
-  int (*fns[])(int*) = {msgl_err_gemm, msgl_err_elementwise, msgl_err_attention, msgl_err_sampling};
+  int (*fns[])(int*) = {msgl_err_gemm, msgl_err_elementwise, msgl_err_attention, msgl_err_sampling, msgl_err_comm};
   int first = 0;
   for (auto f : fns) {
     int inf = 0;

@@ -153,7 +153,12 @@ class Engine:
         if mode in ("auto", "peer", "fused"):
             from minisgl.parallel.peer import enable_peer_comm
 
-            max_bytes = config.max_forward_len * self.model_config.hidden_size * self.dtype.itemsize
+            from minisgl.env import ENV
+
+            # all-reduce messages are [tokens, hidden]; the LM-head gather is [bs, vocab/tp] fp32
+            max_bytes = max(config.max_forward_len * self.model_config.hidden_size * self.dtype.itemsize,
+                            config.max_running_req * self.model_config.vocab_size * 4 // config.tp_info.size)
+            max_bytes = min(max_bytes, int(ENV.PYNCCL_MAX_BUFFER_SIZE))
             enable_peer_comm(self.tp_cpu_group, self.device, max_bytes, strict=(mode != "auto"))
 
     def _weights(self, config: EngineConfig) -> Dict[str, torch.Tensor]:

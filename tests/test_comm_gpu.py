@@ -1,0 +1,86 @@
+"""Peer-memory collectives. Multi-GPU cases run as child processes (one per GPU) and compare
+against exact integer-valued expectations; the bounded-wait case runs on one GPU: a "peer" that
+never signals must make the kernel give up with an error status instead of hanging."""
+
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_peer_wait_times_out_and_context_survives():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from minisgl._native import cuda
+
+    c = cuda()
+    c.get_error()
+    cap = 1 << 16
+    a = c.peer_alloc(c.peer_flag_bytes() + 2 * cap)
+    b = c.peer_alloc(c.peer_flag_bytes() + 2 * cap)  # plays rank 1, which never arrives
+    try:
+        state = torch.zeros(2 * c.peer_grid(), dtype=torch.int32, device="cuda")
+        x = torch.ones(1024, dtype=torch.bfloat16, device="cuda")
+        out = torch.empty_like(x)
+        c.peer_collective(0, out, x, [a, b], 0, cap, state, 50_000_000)  # 50 ms limit
+        torch.cuda.synchronize()
+        code, _ = c.get_error()
+        assert code == 2  # kErrPeerTimeout
+        # the context is still usable
+        y = torch.randn(256, 256, device="cuda")
+        assert torch.isfinite((y @ y).sum()).item()
+    finally:
+        c.peer_free(a)
+        c.peer_free(b)
+
+
+WORKER = r"""
+import os, sys
+sys.path.insert(0, {root!r})
+import torch, torch.distributed as dist
+from datetime import timedelta
+os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("gloo", timeout=timedelta(seconds=60))
+from minisgl.parallel.comm import TorchDistributedImpl
+from minisgl.parallel.peer import PeerCommImpl
+from minisgl._native import cuda
+dev = torch.device("cuda", rank)
+impl = PeerCommImpl(dist.group.WORLD, dev, 8 << 20, TorchDistributedImpl())
+for it in range(20):
+    for n in (8, 1000, 4096 * 16, 300_000, 2 * 1024 * 1024):
+        x = torch.full((n,), float(rank + 1 + it % 3), dtype=torch.bfloat16, device=dev)
+        if it % 5 == 0 and rank == 0:
+            torch.cuda._sleep(2_000_000)  # a lagging rank
+        y = impl.all_reduce(x)
+        exp = sum(r + 1 + it % 3 for r in range(world))
+        assert torch.all(y == exp).item(), (it, n, y[:4])
+    g = impl.all_gather(torch.full((3, 8), float(rank), dtype=torch.float32, device=dev))
+    assert torch.equal(g[:, 0].cpu(), torch.arange(world, dtype=torch.float32).repeat_interleave(3))
+torch.cuda.synchronize()
+assert cuda().get_error()[0] == 0
+impl.close()
+dist.barrier()
+print("OK", rank, flush=True)
+"""
+
+
+@pytest.mark.multigpu
+def test_peer_collectives_multi_gpu(tmp_path, free_port):
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    if n < 2:
+        pytest.skip("needs 2+ GPUs")
+    world = min(n, 8)
+    script = tmp_path / "w.py"
+    script.write_text(WORKER.format(root=ROOT))
+    procs = [subprocess.Popen([sys.executable, str(script)], env=dict(
+        os.environ, RANK=str(r), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(free_port),
+        NCCL_NVLS_ENABLE="0"), stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True) for r in range(world)]
+    outs = [p.communicate(timeout=300)[0] for p in procs]
+    assert all(p.returncode == 0 for p in procs), outs
