@@ -296,6 +296,28 @@ __global__ void __launch_bounds__(kWarps * 32) prefill_kernel(AttnParams p) {
 // ================================================================================ decode
 // grid (requests, kv heads, splits). The G query heads of the group are the 16 MMA rows
 // (padded); the 4 warps take 16-key quarters of each 64-key chunk and merge at the end.
+// The KV slots of the CTA's key range are fetched into smem once up front (segments of kSlots),
+// so the cp.async ring (kDecStages deep) never waits on a dependent page-table load.
+constexpr int kDecStages = 3;
+constexpr int kSlots = 2048;
+
+template <int HD>
+__device__ __forceinline__ void load_kv_chunk_slots(uint32_t sk, uint32_t sv, const AttnParams& p,
+                                                    const int32_t* slots, int kvh, int k0, int kend, int seg0) {
+  constexpr int CH = HD / 8;
+#pragma unroll
+  for (int i = 0; i < KC * CH / (kWarps * 32); ++i) {
+    const int c = threadIdx.x + i * kWarps * 32;
+    const int key = c / CH, part = c % CH;
+    const int pos = k0 + key;
+    const bool valid = pos < kend;
+    const int64_t slot = valid ? slots[pos - seg0] : 0;
+    const int64_t off = slot * p.cache_stride + (int64_t)kvh * HD + part * 8;
+    cp_async16(sk + swz<HD>(key, part), p.k + off, valid);
+    cp_async16(sv + swz<HD>(key, part), p.v + off, valid);
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -304,6 +326,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
   const int L = p.kv_lens[b], row = p.rows[b];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int CH = HD / 8;
+  constexpr int kStageBytes = 2 * KC * HD * 2;
 
   int lo = 0;
   if (p.window > 0) lo = max(0, L - p.window);
@@ -311,13 +334,12 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
   const int per = (nchunk_total + p.num_splits - 1) / p.num_splits;
   const int kbeg = lo + split * per * KC;
   const int kend = min(L, kbeg + per * KC);
-  const int nchunks = kend > kbeg ? (kend - kbeg + KC - 1) / KC : 0;
 
   const uint32_t sq = smem_u32(smem);
-  const uint32_t sk0 = sq + 16 * HD * 2;
-  const uint32_t sv0 = sk0 + 2 * KC * HD * 2;
-  // merge scratch aliases the K/V ring, which is idle once the key loop has drained
-  float* red = reinterpret_cast<float*>(smem + 16 * HD * 2);
+  int32_t* slots = reinterpret_cast<int32_t*>(smem + 16 * HD * 2);
+  const uint32_t ring = smem_u32(smem + 16 * HD * 2 + kSlots * 4);
+  // merge scratch aliases the ring, which is idle once the key loop has drained
+  float* red = reinterpret_cast<float*>(smem + 16 * HD * 2 + kSlots * 4);
 
   for (int c = threadIdx.x; c < 16 * CH; c += kWarps * 32) {
     const int r = c / CH, part = c % CH;
@@ -326,57 +348,75 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
     cp_async16(sq + swz<HD>(r, part), src, valid);
   }
   cp_async_commit();
-  if (nchunks > 0) load_kv_chunk<HD>(sk0, sv0, p, row, kvh, kbeg, kend);
-  cp_async_commit();
-  cp_async_wait<1>();
-  __syncthreads();
-  uint32_t qf[HD / 16][4];
-#pragma unroll
-  for (int kk = 0; kk < HD / 16; ++kk) {
-    const int r = lane & 15, chunk = kk * 2 + (lane >> 4);
-    ldsm_x4(sq + swz<HD>(r, chunk), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
-  }
 
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   float o[HD / 8][4];
 #pragma unroll
   for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  uint32_t qf[HD / 16][4];
+  bool have_q = false;
+  const int32_t* pt = p.page_table + (int64_t)row * p.pt_stride;
 
-  for (int ci = 0; ci < nchunks; ++ci) {
-    const int buf = ci & 1;
-    if (ci + 1 < nchunks)
-      load_kv_chunk<HD>(sk0 + (buf ^ 1) * KC * HD * 2, sv0 + (buf ^ 1) * KC * HD * 2, p, row, kvh,
-                        kbeg + (ci + 1) * KC, kend);
-    cp_async_commit();
-    cp_async_wait<1>();
+  for (int seg0 = kbeg; seg0 < kend; seg0 += kSlots) {
+    const int seg1 = min(kend, seg0 + kSlots);
+    __syncthreads();  // previous segment's readers are done with `slots`
+    for (int i = threadIdx.x; i < seg1 - seg0; i += kWarps * 32) slots[i] = pt[seg0 + i];
     __syncthreads();
-    const uint32_t sk = sk0 + buf * KC * HD * 2, sv = sv0 + buf * KC * HD * 2;
-    const int k0 = kbeg + ci * KC + warp * 16;
-    float s[2][4];
-    qk<HD, 2>(s, qf, sk, warp * 16);
+    const int nchunks = (seg1 - seg0 + KC - 1) / KC;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int kp = k0 + nt * 8 + 2 * (lane & 3) + (e & 1);
-        s[nt][e] = kp < kend ? s[nt][e] * p.scale_log2 : -INFINITY;
-      }
-    float so[2];
-    softmax_update<2>(s, m, l, so);
-#pragma unroll
-    for (int i = 0; i < HD / 8; ++i) {
-      o[i][0] *= so[0]; o[i][1] *= so[0]; o[i][2] *= so[1]; o[i][3] *= so[1];
+    for (int s = 0; s < kDecStages - 1; ++s) {
+      if (s < nchunks)
+        load_kv_chunk_slots<HD>(ring + s * kStageBytes, ring + s * kStageBytes + KC * HD * 2, p, slots, kvh,
+                                seg0 + s * KC, seg1, seg0);
+      cp_async_commit();
     }
-    uint32_t pf[1][4];
-    pack_p<2>(pf, s);
-    pv<HD, 1>(o, pf, sv, warp * 16);
-    __syncthreads();
+    for (int ci = 0; ci < nchunks; ++ci) {
+      cp_async_wait<kDecStages - 2>();
+      __syncthreads();
+      if (!have_q) {
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const int r = lane & 15, chunk = kk * 2 + (lane >> 4);
+          ldsm_x4(sq + swz<HD>(r, chunk), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+        }
+        have_q = true;
+      }
+      {
+        const int nx = ci + kDecStages - 1;
+        const int st = nx % kDecStages;
+        if (nx < nchunks)
+          load_kv_chunk_slots<HD>(ring + st * kStageBytes, ring + st * kStageBytes + KC * HD * 2, p, slots, kvh,
+                                  seg0 + nx * KC, seg1, seg0);
+        cp_async_commit();
+      }
+      const int st = ci % kDecStages;
+      const uint32_t sk = ring + st * kStageBytes, sv = sk + KC * HD * 2;
+      const int k0 = seg0 + ci * KC + warp * 16;
+      float s[2][4];
+      qk<HD, 2>(s, qf, sk, warp * 16);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int kp = k0 + nt * 8 + 2 * (lane & 3) + (e & 1);
+          s[nt][e] = kp < seg1 ? s[nt][e] * p.scale_log2 : -INFINITY;
+        }
+      float so[2];
+      softmax_update<2>(s, m, l, so);
+#pragma unroll
+      for (int i = 0; i < HD / 8; ++i) {
+        o[i][0] *= so[0]; o[i][1] *= so[0]; o[i][2] *= so[1]; o[i][3] *= so[1];
+      }
+      uint32_t pf[1][4];
+      pack_p<2>(pf, s);
+      pv<HD, 1>(o, pf, sv, warp * 16);
+    }
+    cp_async_wait<0>();
   }
   cp_async_wait<0>();
   __syncthreads();
 
   // merge the 4 warps: rows (lane/4) and (lane/4 + 8); only rows < G matter.
-  // red layout: [warp][16 rows] m, l ; [warp][16 rows][HD] o
   float* rm = red;
   float* rl = red + kWarps * 16;
   float* ro = red + 2 * kWarps * 16;
@@ -395,7 +435,6 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
     }
   }
   __syncthreads();
-  // each thread finalizes (row, column range)
   for (int idx = threadIdx.x; idx < G * HD; idx += kWarps * 32) {
     const int r = idx / HD, col = idx % HD;
     float mx = -INFINITY;
@@ -467,8 +506,9 @@ template <int HD>
 int prefill_smem() { return 64 * HD * 2 + 4 * KC * HD * 2; }
 template <int HD>
 int decode_smem() {
-  static_assert((2 * kWarps * 16 + kWarps * 16 * HD) * 4 <= 4 * KC * HD * 2, "merge scratch must fit the K/V ring");
-  return 16 * HD * 2 + 4 * KC * HD * 2;
+  static_assert((2 * kWarps * 16 + kWarps * 16 * HD) * 4 <= kDecStages * 2 * KC * HD * 2,
+                "merge scratch must fit the K/V ring");
+  return 16 * HD * 2 + kSlots * 4 + kDecStages * 2 * KC * HD * 2;
 }
 
 template <int HD>
