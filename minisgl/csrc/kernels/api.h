@@ -60,6 +60,17 @@ void msgl_attention_decode(void* o, const void* q, const void* k_cache, const vo
                            int64_t cache_stride, float sm_scale, int window, const float* sinks,
                            int num_splits, void* workspace, cudaStream_t s);
 
+// ----- allocation-free decode attention (no counterpart in the reference; see attention.cu):
+// split-KV scratch comes from a fixed 8 MiB file-scope device array instead of a workspace
+// argument. Returns 0 on success, 1 if the problem needs more scratch than that, 2 if the
+// per-device set-up failed, 3 on bad arguments, 4 if the launch failed. Calls that overlap on the
+// GPU race on the shared scratch; the first call on a device must precede any stream capture.
+int msgl_attention_decode_noalloc(void* o, const void* q, const void* k_cache, const void* v_cache,
+                                  const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
+                                  const int32_t* kv_lens, int bs, int nq, int nkv, int hd,
+                                  int64_t cache_stride, float sm_scale, int window, const float* sinks,
+                                  int num_splits, cudaStream_t s);
+
 // ----- peer-memory collectives (CUDA IPC over NVLink)
 int msgl_peer_flag_bytes();
 void* msgl_peer_alloc(int64_t bytes);

@@ -594,3 +594,73 @@ extern "C" void msgl_attention_decode(void* o, const void* q, const void* k_cach
 }
 
 MSGL_ERROR_ACCESSOR(msgl_err_attention)
+
+// =================================================================================================
+// Allocation-free decode attention entry point (an addition of this engine: the reference has no
+// counterpart to it).
+//
+// Some callers cannot allocate device memory at all: hosts that run our kernels from inside a
+// fixed, pre-planned memory budget, plug-in environments whose callbacks may not call cudaMalloc,
+// and code that launches while a CUDA graph it does not own is being captured. For them,
+// msgl_attention_decode_noalloc takes only its inputs and outputs; the split-KV scratch that the
+// regular entry point receives as a `workspace` argument lives instead in one file-scope device
+// array of kNoAllocScratchBytes (every GPU that loads this library holds it until the process
+// exits).
+//
+//   * Host code may not use the array's name as a device address. The first call on each device
+//     looks its address up with cudaGetSymbolAddress (with that device current) and caches it;
+//     make that first call before any stream capture.
+//   * All calls share the array and it keeps the last call's contents. Calls that overlap on the
+//     GPU (other streams, concurrently replayed graphs) race on it: the caller must serialize them.
+//     Each call writes every scratch word before reading it, so nothing has to start at zero.
+//   * The problem must fit: bs * nq * num_splits * (hd + 2) * 4 bytes <= kNoAllocScratchBytes when
+//     num_splits > 1 (a single split uses no scratch). Larger requests are rejected before any launch.
+//   * Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+// Returns 0 on success, otherwise one of kNoAlloc* below (nothing is launched on error).
+// =================================================================================================
+#include <mutex>
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per GPU
+static __device__ __align__(256) unsigned char g_noalloc_decode_scratch[kNoAllocScratchBytes];
+
+enum : int { kNoAllocOk = 0, kNoAllocTooLarge = 1, kNoAllocSetupFailed = 2, kNoAllocBadArgs = 3, kNoAllocLaunch = 4 };
+
+// device address of the scratch array for the current device (looked up once per device)
+void* noalloc_scratch_for_current_device() {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> g(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_decode_scratch) != cudaSuccess || p == nullptr) return nullptr;
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int msgl_attention_decode_noalloc(
+    void* o, const void* q, const void* k_cache, const void* v_cache, const int32_t* page_table, int64_t pt_stride,
+    const int32_t* rows, const int32_t* kv_lens, int bs, int nq, int nkv, int hd, int64_t cache_stride,
+    float sm_scale, int window, const float* sinks, int num_splits, cudaStream_t s) {
+  if (bs < 0 || nkv <= 0 || nq % nkv != 0 || nq / nkv > 16 || (hd != 64 && hd != 128)) return kNoAllocBadArgs;
+  if (bs == 0) return kNoAllocOk;
+  const int splits = num_splits < 1 ? 1 : num_splits;
+  const size_t need = splits > 1 ? (size_t)bs * nq * splits * (hd + 2) * 4 : 0;
+  if (need > kNoAllocScratchBytes) return kNoAllocTooLarge;
+  void* scratch = noalloc_scratch_for_current_device();
+  if (scratch == nullptr) return kNoAllocSetupFailed;
+  AttnParams p = make_params(o, q, k_cache, v_cache, page_table, pt_stride, rows, nullptr, kv_lens, nq, nkv,
+                             cache_stride, sm_scale, window, sinks);
+  p.num_splits = splits;
+  p.ws = reinterpret_cast<float*>(scratch);
+  if (hd == 64) run_decode<64>(p, bs, s);
+  else run_decode<128>(p, bs, s);
+  return cudaPeekAtLastError() == cudaSuccess ? kNoAllocOk : kNoAllocLaunch;
+}
