@@ -177,6 +177,8 @@ __device__ __forceinline__ void pack_p(uint32_t (&pf)[NT / 2][4], const float (&
 template <int HD>
 __global__ void __launch_bounds__(kWarps * 32) prefill_kernel(AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  pdl_wait();
+  pdl_launch();
   const int qb = blockIdx.x, b = blockIdx.y, kvh = blockIdx.z;
   const int G = p.group;
   const int q0 = p.cu_q[b], n = p.cu_q[b + 1] - q0;
@@ -321,6 +323,8 @@ __device__ __forceinline__ void load_kv_chunk_slots(uint32_t sk, uint32_t sv, co
 template <int HD>
 __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  pdl_wait();
+  pdl_launch();
   const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int G = p.group;
   const int L = p.kv_lens[b], row = p.rows[b];
@@ -474,6 +478,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
 // merge split partials: one warp per (request, head)
 template <int HD>
 __global__ void decode_combine_kernel(AttnParams p, int bs) {
+  pdl_wait();
+  pdl_launch();
   const int gw = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (gw >= bs * p.nq) return;
@@ -519,7 +525,7 @@ void run_prefill(const AttnParams& p, int num_reqs, int max_q_len, cudaStream_t 
     set = true;
   }
   const dim3 grid((max_q_len * p.group + 63) / 64, num_reqs, p.nkv);
-  prefill_kernel<HD><<<grid, kWarps * 32, prefill_smem<HD>(), s>>>(p);
+  msgl_launch(prefill_kernel<HD>, grid, dim3(kWarps * 32), prefill_smem<HD>(), s, 1, p);
 }
 
 template <int HD>
@@ -530,10 +536,10 @@ void run_decode(const AttnParams& p, int bs, cudaStream_t s) {
     set = true;
   }
   const dim3 grid(bs, p.nkv, p.num_splits);
-  decode_kernel<HD><<<grid, kWarps * 32, decode_smem<HD>(), s>>>(p);
+  msgl_launch(decode_kernel<HD>, grid, dim3(kWarps * 32), decode_smem<HD>(), s, 1, p);
   if (p.num_splits > 1) {
     const int warps = bs * p.nq;
-    decode_combine_kernel<HD><<<(warps + 7) / 8, 256, 0, s>>>(p, bs);
+    msgl_launch(decode_combine_kernel<HD>, dim3((warps + 7) / 8), dim3(256), 0, s, 1, p, bs);
   }
 }
 

@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(kThreadsC) peer_collective_kernel(PeerBufs buf
                                                                     int64_t cap16, uint32_t* __restrict__ state,
                                                                     uint64_t timeout_ns) {
   const int b = blockIdx.x;
+  pdl_wait();
+  pdl_launch();
   __shared__ uint32_t s_epoch, s_calls;
   if (threadIdx.x == 0) {
     s_epoch = state[2 * b];
@@ -198,9 +200,9 @@ void msgl_peer_collective(void* const* bases, int rank, int world, int mode, voi
                           int64_t bytes, int64_t cap_bytes, uint32_t* state, int64_t timeout_ns, cudaStream_t s) {
   PeerBufs bufs;
   for (int r = 0; r < kMaxRanks; ++r) bufs.base[r] = r < world ? reinterpret_cast<uint8_t*>(bases[r]) : nullptr;
-  peer_collective_kernel<<<kGrid, kThreadsC, 0, s>>>(bufs, rank, world, mode, reinterpret_cast<uint4*>(out),
-                                                     reinterpret_cast<const uint4*>(in), bytes / 16, cap_bytes / 16,
-                                                     state, (uint64_t)timeout_ns);
+  msgl_launch(peer_collective_kernel, dim3(kGrid), dim3(kThreadsC), 0, s, 1, bufs, rank, world, mode,
+              reinterpret_cast<uint4*>(out), reinterpret_cast<const uint4*>(in), bytes / 16, cap_bytes / 16, state,
+              (uint64_t)timeout_ns);
 }
 
 }  // extern "C"

@@ -7,6 +7,9 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #define MSGL_DEVICE __device__ __forceinline__
 
@@ -280,6 +283,14 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
 }
 
 // ------------------------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with the PDL attribute may start while its
+// predecessor in the stream is still running. It must call pdl_wait() before touching any global
+// memory the predecessor (or anything earlier) reads or writes; work on static data (weights) may
+// run before. pdl_launch() lets the successor start being scheduled.
+MSGL_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MSGL_DEVICE void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ------------------------------------------------------------------------------------------
 // named barriers among a subset of warps
 MSGL_DEVICE void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -294,6 +305,44 @@ MSGL_DEVICE uint32_t pack_bf16(float a, float b) {
 }
 
 }  // namespace msgl
+
+// Launch with programmatic stream serialization (and an optional cluster shape).
+// MINISGL_PDL=0 in the environment turns the attribute off (plain stream ordering).
+inline bool msgl_pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("MINISGL_PDL");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t msgl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                               int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (msgl_pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 #define MSGL_ERROR_ACCESSOR(fn)                                                   \
   extern "C" int fn(int* info) {                                                  \

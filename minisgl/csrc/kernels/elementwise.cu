@@ -27,6 +27,8 @@ __device__ __forceinline__ uint4 f32_to_bf16x8(const float (&f)[8]) {
 __global__ void embedding_kernel(uint4* __restrict__ out, const uint4* __restrict__ w,
                                  const int32_t* __restrict__ ids, int n, int vec_per_row,
                                  int vocab_start, int vocab_len, int masked) {
+  pdl_wait();
+  pdl_launch();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= n) return;
@@ -48,6 +50,8 @@ template <int VPT, bool ADD>
 __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ out, __nv_bfloat16* __restrict__ x,
                                __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w,
                                int dim, float eps) {
+  pdl_wait();
+  pdl_launch();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int nvec = dim / 8;
@@ -98,15 +102,17 @@ void launch_rmsnorm(__nv_bfloat16* out, __nv_bfloat16* x, __nv_bfloat16* res, co
   const int nvec = dim / 8;
   int threads = std::min(1024, ((nvec + 31) / 32) * 32);
   const int vpt = (nvec + threads - 1) / threads;
-  if (vpt <= 1) rmsnorm_kernel<1, ADD><<<rows, threads, 0, s>>>(out, x, res, w, dim, eps);
-  else if (vpt <= 2) rmsnorm_kernel<2, ADD><<<rows, threads, 0, s>>>(out, x, res, w, dim, eps);
-  else rmsnorm_kernel<4, ADD><<<rows, threads, 0, s>>>(out, x, res, w, dim, eps);
+  if (vpt <= 1) msgl_launch(rmsnorm_kernel<1, ADD>, rows, threads, 0, s, 1, out, x, res, w, dim, eps);
+  else if (vpt <= 2) msgl_launch(rmsnorm_kernel<2, ADD>, rows, threads, 0, s, 1, out, x, res, w, dim, eps);
+  else msgl_launch(rmsnorm_kernel<4, ADD>, rows, threads, 0, s, 1, out, x, res, w, dim, eps);
 }
 
 // ------------------------------------------------------------------------------ act * mul
 // x = [gate | up] halves (plain layout), out = act(gate) * up
 __global__ void act_and_mul_kernel(uint4* __restrict__ out, const uint4* __restrict__ x, int rows,
                                    int inter_vec, int act) {
+  pdl_wait();
+  pdl_launch();
   const size_t total = (size_t)rows * inter_vec;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / inter_vec, c = i % inter_vec;
@@ -129,6 +135,8 @@ __global__ void store_kv_kernel(const uint4* __restrict__ k, const uint4* __rest
                                 uint4* __restrict__ kc, uint4* __restrict__ vc,
                                 const int32_t* __restrict__ loc, int n, int vec_per_row,
                                 int64_t k_stride_v, int64_t v_stride_v, int64_t c_stride_v) {
+  pdl_wait();
+  pdl_launch();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= n) return;
@@ -154,6 +162,8 @@ __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* __restrict__ q_out,
                                           __nv_bfloat16* __restrict__ v_cache,
                                           const int32_t* __restrict__ out_loc, int n, int nq,
                                           int nkv, int64_t cache_stride) {
+  pdl_wait();
+  pdl_launch();
   constexpr int HD = 64 * E;
   const int heads = nq + 2 * nkv;
   const int gw = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
@@ -211,6 +221,8 @@ __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* __restrict__ q_out,
 template <typename T>
 __global__ void argmax_kernel(int32_t* __restrict__ out, const T* __restrict__ logits, int vocab,
                               int64_t stride) {
+  pdl_wait();
+  pdl_launch();
   __shared__ float sv[32];
   __shared__ int si[32];
   const T* row = logits + (size_t)blockIdx.x * stride;
@@ -251,9 +263,8 @@ extern "C" void msgl_embedding(void* out, const void* weight, const int32_t* ids
                                int vocab_start, int vocab_len, int masked, cudaStream_t s) {
   if (n == 0) return;
   const int vec = dim / 8, wpb = 8;
-  embedding_kernel<<<(n + wpb - 1) / wpb, wpb * 32, 0, s>>>(
-      reinterpret_cast<uint4*>(out), reinterpret_cast<const uint4*>(weight), ids, n, vec,
-      vocab_start, vocab_len, masked);
+  msgl_launch(embedding_kernel, (n + wpb - 1) / wpb, wpb * 32, 0, s, 1, reinterpret_cast<uint4*>(out),
+              reinterpret_cast<const uint4*>(weight), ids, n, vec, vocab_start, vocab_len, masked);
 }
 
 extern "C" void msgl_rmsnorm(void* out, const void* x, const void* w, int rows, int dim, float eps,
@@ -276,8 +287,8 @@ extern "C" void msgl_act_and_mul(void* out, const void* x, int rows, int inter, 
   if (rows == 0) return;
   const size_t total = (size_t)rows * inter / 8;
   const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
-  act_and_mul_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<uint4*>(out), reinterpret_cast<const uint4*>(x),
-                                          rows, inter / 8, act);
+  msgl_launch(act_and_mul_kernel, grid, 256, 0, s, 1, reinterpret_cast<uint4*>(out),
+              reinterpret_cast<const uint4*>(x), rows, inter / 8, act);
 }
 
 extern "C" void msgl_store_kv(const void* k, const void* v, void* k_cache, void* v_cache,
@@ -285,10 +296,10 @@ extern "C" void msgl_store_kv(const void* k, const void* v, void* k_cache, void*
                               int64_t v_stride, int64_t cache_stride, cudaStream_t s) {
   if (n == 0) return;
   const int wpb = 8;
-  store_kv_kernel<<<(n + wpb - 1) / wpb, wpb * 32, 0, s>>>(
-      reinterpret_cast<const uint4*>(k), reinterpret_cast<const uint4*>(v),
-      reinterpret_cast<uint4*>(k_cache), reinterpret_cast<uint4*>(v_cache), out_loc, n,
-      row_elems / 8, k_stride / 8, v_stride / 8, cache_stride / 8);
+  msgl_launch(store_kv_kernel, (n + wpb - 1) / wpb, wpb * 32, 0, s, 1, reinterpret_cast<const uint4*>(k),
+              reinterpret_cast<const uint4*>(v), reinterpret_cast<uint4*>(k_cache),
+              reinterpret_cast<uint4*>(v_cache), out_loc, n, row_elems / 8, k_stride / 8, v_stride / 8,
+              cache_stride / 8);
 }
 
 extern "C" void msgl_qk_norm_rope_store(void* q_out, const void* qkv, const int32_t* positions,
@@ -306,20 +317,20 @@ extern "C" void msgl_qk_norm_rope_store(void* q_out, const void* qkv, const int3
   auto kc = reinterpret_cast<__nv_bfloat16*>(k_cache);
   auto vc = reinterpret_cast<__nv_bfloat16*>(v_cache);
   if (hd == 64)
-    qk_norm_rope_store_kernel<1><<<grid, wpb * 32, 0, s>>>(qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride);
+    msgl_launch(qk_norm_rope_store_kernel<1>, grid, wpb * 32, 0, s, 1, qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride);
   else if (hd == 128)
-    qk_norm_rope_store_kernel<2><<<grid, wpb * 32, 0, s>>>(qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride);
+    msgl_launch(qk_norm_rope_store_kernel<2>, grid, wpb * 32, 0, s, 1, qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride);
   else
-    qk_norm_rope_store_kernel<4><<<grid, wpb * 32, 0, s>>>(qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride);
+    msgl_launch(qk_norm_rope_store_kernel<4>, grid, wpb * 32, 0, s, 1, qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride);
 }
 
 extern "C" void msgl_argmax(int32_t* out, const void* logits, int rows, int vocab, int64_t stride,
                             int is_fp32, cudaStream_t s) {
   if (rows == 0) return;
   if (is_fp32)
-    argmax_kernel<float><<<rows, 1024, 0, s>>>(out, reinterpret_cast<const float*>(logits), vocab, stride);
+    msgl_launch(argmax_kernel<float>, rows, 1024, 0, s, 1, out, reinterpret_cast<const float*>(logits), vocab, stride);
   else
-    argmax_kernel<__nv_bfloat16><<<rows, 1024, 0, s>>>(out, reinterpret_cast<const __nv_bfloat16*>(logits), vocab, stride);
+    msgl_launch(argmax_kernel<__nv_bfloat16>, rows, 1024, 0, s, 1, out, reinterpret_cast<const __nv_bfloat16*>(logits), vocab, stride);
 }
 
 MSGL_ERROR_ACCESSOR(msgl_err_elementwise)

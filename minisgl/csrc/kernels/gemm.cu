@@ -204,6 +204,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
+  pdl_launch();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -214,13 +215,32 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      bool ok = true;
+      bool ok = true, waited = false;
       for (int u = u_first; u < units && ok; u += u_step) {
         const int tile = u / p.splits;
         int nt, mt, kb0, kb1;
         tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
         split_range(u % p.splits, p.splits, p.kblocks, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        int kb = kb0;
+        if (!waited) {
+          // Weights are static: fetch the first stages' weight tiles before waiting for the
+          // previous kernel (programmatic dependent launch), then the activations.
+          const int npre = min(C::kStages, kb1 - kb0);
+          for (int i = 0; i < npre; ++i) {
+            mbar_expect_tx(&full[i], C::kStage);
+            uint8_t* a = stages + i * C::kStage;
+            if (p.w_blocked) tma_load_3d(a, &tmap_w, &full[i], 0, nt * C::kRowsA, kb0 + i);
+            else tma_load_2d(a, &tmap_w, &full[i], (kb0 + i) * BK, nt * C::kRowsA);
+          }
+          pdl_wait();
+          waited = true;
+          for (int i = 0; i < npre; ++i)
+            tma_load_2d(stages + i * C::kStage + C::kA, &tmap_x, &full[i], (kb0 + i) * BK, mt * BN);
+          stage = npre % C::kStages;
+          phase = npre == C::kStages ? 1u : 0u;
+          kb = kb0 + npre;
+        }
+        for (; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, 100)) { ok = false; break; }
           uint8_t* a = stages + stage * C::kStage;
           mbar_expect_tx(&full[stage], C::kStage);
@@ -230,6 +250,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
           if (++stage == C::kStages) { stage = 0; phase ^= 1; }
         }
       }
+      if (!waited) pdl_wait();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -537,22 +558,11 @@ static void launch(const Params& p, const void* x, const void* w, void* out, int
   if (q.splits > 1 && q.n_tiles * q.m_tiles > max_clusters<BN, EPI, WIDE>(q.splits)) q.splits = 1;
   const int tiles = q.n_tiles * q.m_tiles;
   if (q.splits > 1) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(q.splits, tiles, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = C::kSmem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = q.splits;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, gemm_kernel<BN, EPI, WIDE>, mw, mx, mo, q);
+    msgl_launch(gemm_kernel<BN, EPI, WIDE>, dim3(q.splits, tiles, 1), dim3(kThreads), C::kSmem, s, q.splits, mw, mx,
+                mo, q);
   } else {
     const int grid = std::min(tiles, num_sms_cached());
-    gemm_kernel<BN, EPI, WIDE><<<grid, kThreads, C::kSmem, s>>>(mw, mx, mo, q);
+    msgl_launch(gemm_kernel<BN, EPI, WIDE>, dim3(grid), dim3(kThreads), C::kSmem, s, 1, mw, mx, mo, q);
   }
 }
 

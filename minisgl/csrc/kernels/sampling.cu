@@ -93,6 +93,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(int32_t* __restrict__ 
                                                          const int32_t* __restrict__ top_k, const float* __restrict__ top_p,
                                                          const int64_t* __restrict__ seed, const int64_t* __restrict__ step) {
   __shared__ Smem sm;
+  pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   const float* row = logits + (size_t)r * stride;
   const float t = temperature[r];
@@ -204,7 +206,8 @@ extern "C" void msgl_sample(int32_t* out, const float* logits, int rows, int voc
                             const float* temperature, const int32_t* top_k, const float* top_p,
                             const int64_t* seed, const int64_t* step, cudaStream_t s) {
   if (rows == 0) return;
-  sample_kernel<<<rows, kThreads, 0, s>>>(out, logits, vocab, stride, temperature, top_k, top_p, seed, step);
+  msgl_launch(sample_kernel, dim3(rows), dim3(kThreads), 0, s, 1, out, logits, vocab, stride, temperature, top_k,
+              top_p, seed, step);
 }
 
 MSGL_ERROR_ACCESSOR(msgl_err_sampling)
