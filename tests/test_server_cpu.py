@@ -1,0 +1,85 @@
+"""The HTTP server end to end on CPU: launcher + tokenizer/detokenizer worker + scheduler process
+(reference-op engine) + FastAPI, driven over HTTP like a client would."""
+
+import json
+import os
+import signal
+import subprocess
+import sys
+import time
+
+import pytest
+
+from minisgl.models.synthetic import make_checkpoint
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _wait_ready(port: int, proc, timeout: float = 120.0) -> None:
+    import requests
+
+    t0 = time.time()
+    while time.time() - t0 < timeout:
+        if proc.poll() is not None:
+            raise RuntimeError(proc.stdout.read())
+        try:
+            if requests.get(f"http://127.0.0.1:{port}/v1/models", timeout=1).status_code == 200:
+                return
+        except Exception:
+            time.sleep(0.5)
+    raise TimeoutError("server did not start")
+
+
+@pytest.mark.parametrize("num_tokenizer", [0, 1])
+def test_server_endpoints(tmp_path, free_port, num_tokenizer):
+    import requests
+
+    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
+    port = free_port
+    proc = subprocess.Popen(
+        [sys.executable, "-m", "minisgl", "--model", path, "--device", "cpu", "--port", str(port), "--dtype",
+         "float32", "--num-tokenizer", str(num_tokenizer), "--max-running-requests", "8"],
+        cwd=ROOT, env=dict(os.environ, PYTHONPATH=ROOT), stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+        text=True, start_new_session=True)
+    try:
+        _wait_ready(port, proc)
+        base = f"http://127.0.0.1:{port}"
+        assert requests.get(f"{base}/v1").json() == {"status": "ok"}
+        assert requests.get(f"{base}/v1/models").json()["data"][0]["id"] == path
+        r = requests.post(f"{base}/v1/chat/completions", json={
+            "model": "m", "messages": [{"role": "user", "content": "hello"}], "max_tokens": 6,
+            "temperature": 0.0, "ignore_eos": True}, timeout=60).json()
+        assert r["object"] == "chat.completion" and r["usage"]["completion_tokens"] >= 1
+        text = r["choices"][0]["message"]["content"]
+        # streaming returns the same greedy text in pieces
+        chunks = []
+        with requests.post(f"{base}/v1/chat/completions", json={
+                "model": "m", "messages": [{"role": "user", "content": "hello"}], "max_tokens": 6,
+                "temperature": 0.0, "ignore_eos": True, "stream": True}, stream=True, timeout=60) as s:
+            for line in s.iter_lines():
+                if line.startswith(b"data: ") and line != b"data: [DONE]":
+                    chunks.append(json.loads(line[6:]))
+        assert chunks[0]["choices"][0]["delta"]["role"] == "assistant"
+        assert chunks[-1]["choices"][0]["finish_reason"] == "stop"
+        assert "".join(c["choices"][0]["delta"].get("content", "") for c in chunks) == text
+        r = requests.post(f"{base}/v1/completions", json={"model": "m", "prompt": "abc", "max_tokens": 4,
+                                                          "temperature": 0.0, "ignore_eos": True}, timeout=60).json()
+        assert r["object"] == "text_completion"
+        with requests.post(f"{base}/generate", json={"prompt": "abc", "max_tokens": 4, "ignore_eos": True},
+                           stream=True, timeout=60) as g:
+            lines = [l for l in g.iter_lines() if l]
+        assert lines[-1] == b"data: [DONE]"
+        # a client that disconnects mid-stream aborts its request; the server keeps serving
+        with requests.post(f"{base}/generate", json={"prompt": "abc", "max_tokens": 2000, "ignore_eos": True},
+                           stream=True, timeout=60) as g:
+            next(g.iter_lines())
+        time.sleep(0.5)
+        r = requests.post(f"{base}/v1/completions", json={"model": "m", "prompt": "x", "max_tokens": 2,
+                                                          "temperature": 0.0}, timeout=60)
+        assert r.status_code == 200
+    finally:
+        os.killpg(proc.pid, signal.SIGTERM)
+        try:
+            proc.wait(timeout=20)
+        except subprocess.TimeoutExpired:
+            os.killpg(proc.pid, signal.SIGKILL)
