@@ -83,3 +83,34 @@ def test_server_endpoints(tmp_path, free_port, num_tokenizer):
             proc.wait(timeout=20)
         except subprocess.TimeoutExpired:
             os.killpg(proc.pid, signal.SIGKILL)
+
+
+def test_bench_client_against_server(tmp_path, free_port):
+    """The online load generator replays a small Poisson trace with shared prefixes and reports
+    TTFT / TPOT / E2E percentiles for every request."""
+    import asyncio
+
+    from minisgl.benchmark.client import run_trace, synthetic_trace
+    from minisgl.utils.hf import load_tokenizer
+
+    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
+    port = free_port
+    proc = subprocess.Popen(
+        [sys.executable, "-m", "minisgl", "--model", path, "--device", "cpu", "--port", str(port), "--dtype",
+         "float32", "--max-running-requests", "8"],
+        cwd=ROOT, env=dict(os.environ, PYTHONPATH=ROOT), stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+        text=True, start_new_session=True)
+    try:
+        _wait_ready(port, proc)
+        tok = load_tokenizer(path)
+        trace = synthetic_trace(tok, 12, rate=20.0, in_median=40, in_clip=(16, 120), out_median=6,
+                                out_clip=(2, 12), n_prefixes=2, prefix_len=20)
+        stats = asyncio.run(run_trace(f"http://127.0.0.1:{port}", trace, path))
+        assert stats["completed"] == 12
+        assert stats["ttft_p50"] > 0 and stats["tpot_p99"] >= stats["tpot_p50"] >= 0
+    finally:
+        os.killpg(proc.pid, signal.SIGTERM)
+        try:
+            proc.wait(timeout=20)
+        except subprocess.TimeoutExpired:
+            os.killpg(proc.pid, signal.SIGKILL)
