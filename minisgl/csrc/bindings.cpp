@@ -207,6 +207,60 @@ void attention_decode(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor
                         workspace.data_ptr(), stream());
 }
 
+// ----- routed experts
+void gemm_grouped(at::Tensor out, at::Tensor xs, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor tile_count,
+                  at::Tensor work, int64_t bn) {
+  check_bf16(out, "out"); check_bf16(xs, "xs"); check_bf16(w, "w");
+  check_contig(xs, "xs"); check_contig(w, "w"); check_contig(out, "out");
+  check_i32(tile_count, "tile_count"); check_i32(work, "work");
+  CHECK(w.dim() == 3, "expert weights must be [E, N, K]");
+  const int64_t E = w.size(0), N = w.size(1), K = w.size(2);
+  CHECK(xs.size(1) == K && out.size(1) == N && out.size(0) == xs.size(0), "grouped gemm shapes");
+  CHECK(K % 8 == 0 && N % 8 == 0, "grouped gemm needs K, N multiples of 8");
+  CHECK(bn == 16 || bn == 32 || bn == 64 || bn == 128, "bn must be 16/32/64/128");
+  CHECK(xs.size(0) % bn == 0, "row capacity must be a multiple of bn");
+  if (bias.has_value()) { check_bf16(*bias, "bias"); CHECK(bias->numel() == E * N, "bias must be [E, N]"); }
+  const int max_tiles = work.numel() / 2;
+  msgl_gemm_grouped(out.data_ptr(), xs.data_ptr(), w.data_ptr(), opt_ptr(bias), xs.size(0), N, K, out.stride(0), E,
+                    tile_count.data_ptr<int32_t>(), work.data_ptr(), max_tiles, bn, stream());
+}
+
+void moe_route(at::Tensor logits, int64_t topk, bool renorm, bool softmax_after, at::Tensor weights, at::Tensor ids) {
+  check_cuda(logits, "logits"); check_dtype(logits, at::kFloat, "logits"); check_contig(logits, "logits");
+  check_dtype(weights, at::kFloat, "weights"); check_i32(ids, "ids");
+  CHECK(logits.size(1) <= 512 && topk <= 16 && topk <= logits.size(1), "route: E <= 512, topk <= 16");
+  msgl_moe_route(logits.data_ptr<float>(), logits.size(0), logits.size(1), topk, renorm, softmax_after,
+                 weights.data_ptr<float>(), ids.data_ptr<int32_t>(), stream());
+}
+
+void moe_align(at::Tensor ids, int64_t E, int64_t bn, at::Tensor perm, at::Tensor inv, at::Tensor work,
+               at::Tensor tile_count) {
+  check_i32(ids, "ids"); check_i32(perm, "perm"); check_i32(inv, "inv"); check_i32(work, "work");
+  check_i32(tile_count, "tile_count");
+  CHECK(E <= 4096, "too many experts");
+  msgl_moe_align(ids.data_ptr<int32_t>(), ids.numel(), E, bn, work.numel() / 2, perm.numel(), perm.data_ptr<int32_t>(),
+                 inv.data_ptr<int32_t>(), work.data_ptr(), tile_count.data_ptr<int32_t>(), stream());
+}
+
+void moe_gather(at::Tensor xs, at::Tensor x, at::Tensor perm, int64_t topk) {
+  check_bf16(xs, "xs"); check_bf16(x, "x"); check_i32(perm, "perm"); check_contig(x, "x"); check_contig(xs, "xs");
+  CHECK(x.size(1) % 8 == 0 && xs.size(1) == x.size(1), "gather shapes");
+  msgl_moe_gather(xs.data_ptr(), x.data_ptr(), perm.data_ptr<int32_t>(), xs.size(0), x.size(1), topk, stream());
+}
+
+void moe_act(at::Tensor out, at::Tensor y, int64_t act, at::Tensor perm) {
+  check_bf16(out, "out"); check_bf16(y, "y"); check_i32(perm, "perm");
+  CHECK(y.size(1) == 2 * out.size(1) && y.size(0) == out.size(0), "act shapes");
+  msgl_moe_act(out.data_ptr(), y.data_ptr(), out.size(0), out.size(1), act, perm.data_ptr<int32_t>(), stream());
+}
+
+void moe_combine(at::Tensor out, at::Tensor y, at::Tensor w, at::Tensor inv, int64_t topk) {
+  check_bf16(out, "out"); check_bf16(y, "y"); check_dtype(w, at::kFloat, "w"); check_i32(inv, "inv");
+  CHECK(out.size(1) % 2 == 0 && y.size(1) == out.size(1), "combine shapes");
+  msgl_moe_combine(out.data_ptr(), y.data_ptr(), w.data_ptr<float>(), inv.data_ptr<int32_t>(), out.size(0),
+                   out.size(1), topk, stream());
+}
+
 // ----- peer-memory collectives
 int64_t peer_alloc(int64_t bytes) {
   void* p = msgl_peer_alloc(bytes);
@@ -273,6 +327,12 @@ PYBIND11_MODULE(_cuda, m) {
   m.def("attention_prefill", &attention_prefill);
   m.def("attention_decode", &attention_decode);
   m.def("get_error", &get_error);
+  m.def("gemm_grouped", &gemm_grouped);
+  m.def("moe_route", &moe_route);
+  m.def("moe_align", &moe_align);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_act", &moe_act);
+  m.def("moe_combine", &moe_combine);
   m.def("peer_flag_bytes", []() { return msgl_peer_flag_bytes(); });
   m.def("peer_alloc", &peer_alloc);
   m.def("peer_free", &peer_free);

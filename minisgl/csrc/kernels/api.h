@@ -47,6 +47,19 @@ void msgl_gemm_ex(void* out, const void* x, const void* w, const void* bias, int
 void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M, int N,
                    int K, int ldo, int epi, int splits, int wide, cudaStream_t s);
 
+// ----- routed experts (MoE)
+void msgl_gemm_grouped(void* out, const void* x, const void* w, const void* bias, int rows_cap, int N, int K,
+                       int ldo, int E, const int* tile_count, const void* work, int max_tiles, int bn,
+                       cudaStream_t s);
+void msgl_moe_route(const float* logits, int T, int E, int topk, int renorm, int softmax_after, float* weights,
+                    int32_t* ids, cudaStream_t s);
+void msgl_moe_align(const int32_t* ids, int pairs, int E, int bn, int max_tiles, int rows_cap, int32_t* perm,
+                    int32_t* inv, void* work, int32_t* tile_count, cudaStream_t s);
+void msgl_moe_gather(void* xs, const void* x, const int32_t* perm, int rows, int H, int topk, cudaStream_t s);
+void msgl_moe_act(void* out, const void* y, int rows, int inter, int act, const int32_t* perm, cudaStream_t s);
+void msgl_moe_combine(void* out, const void* y, const float* w, const int32_t* inv, int T, int H, int topk,
+                      cudaStream_t s);
+
 // ----- paged attention (bf16 q/kv, fp32 softmax)
 void msgl_attention_prefill(void* o, const void* q, const void* k_cache, const void* v_cache,
                             const int32_t* page_table, int64_t pt_stride, const int32_t* rows,

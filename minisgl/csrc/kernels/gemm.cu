@@ -74,6 +74,10 @@ struct Cfg {
 struct Params {
   const __nv_bfloat16* bias;
   int w_blocked;  // weight stored [K/64][N][64] (3-D map) instead of [N][K]
+  // grouped (MoE) mode: weights [E][N][K] (3-D map), token tiles from a device work list
+  const int* grp_count;   // number of valid token tiles (written by the routing kernels)
+  const int2* grp_work;   // per token tile: {expert, first row in the permuted activations}
+  int64_t bias_stride;    // per-expert bias stride (grouped)
   int M, n_out, kblocks;
   int n_tiles, m_tiles, splits;  // splits > 1: grid (splits, tiles), cluster (splits, 1, 1)
 };
@@ -99,6 +103,25 @@ __device__ __forceinline__ void split_range(int split, int splits, int kblocks, 
   kb1 = (int)((long long)(split + 1) * kblocks / splits);
 }
 
+// Work unit -> (weight tile, first token row, expert); false if the unit has no work (grouped
+// mode with fewer token tiles than the launch's capacity).
+__device__ __forceinline__ bool unit_coords(const Params& p, int tile, int bn, int& nt, int& row0, int& expert) {
+  if (p.grp_work != nullptr) {
+    const int mt = tile / p.n_tiles;
+    nt = tile - mt * p.n_tiles;
+    if (mt >= *p.grp_count) return false;
+    const int2 w = p.grp_work[mt];
+    expert = w.x;
+    row0 = w.y;
+    return true;
+  }
+  int mt;
+  tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
+  row0 = mt * bn;
+  expert = 0;
+  return true;
+}
+
 template <int W>
 __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float (&v)[32]) {
   if constexpr (W == 32) {
@@ -119,18 +142,18 @@ __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float (&v)[32]) {
 // bias + activation for one (part, 32-token chunk) item of a warp's 32 accumulator rows, staged
 // in smem as [W tokens][32 cols] and written with a TMA store (rows >= M / cols >= n_out clipped)
 template <int BN, int EPI, bool WIDE>
-__device__ __forceinline__ void store_item(const float (&v)[32], const float (&g2)[32], const Params& p, int nt,
-                                           int mt, int part, int c, int q, int lane, uint8_t* stage_out,
-                                           const CUtensorMap* tmap_out) {
+__device__ __forceinline__ void store_item(const float (&v)[32], const float (&g2)[32], const Params& p,
+                                           const __nv_bfloat16* bias, int nt, int row0, int part, int c, int q,
+                                           int lane, uint8_t* stage_out, const CUtensorMap* tmap_out) {
   using C = Cfg<BN, EPI, WIDE>;
   constexpr int W = C::kChunk;
   const int nrow = q * 32 + lane;
   const int wrow_idx = nt * C::kRowsA + part * 128 + nrow;
   const int ocol0 = nt * C::kOutPerTile + part * 128 + q * 32;
   float bias_a = 0.f, bias_b = 0.f;
-  if (p.bias != nullptr && ocol0 + lane < p.n_out) {
-    bias_a = __bfloat162float(p.bias[wrow_idx]);
-    if constexpr (C::kAct) bias_b = __bfloat162float(p.bias[wrow_idx + 128]);
+  if (bias != nullptr && ocol0 + lane < p.n_out) {
+    bias_a = __bfloat162float(bias[wrow_idx]);
+    if constexpr (C::kAct) bias_b = __bfloat162float(bias[wrow_idx + 128]);
   }
   float o[32];
 #pragma unroll
@@ -156,7 +179,7 @@ __device__ __forceinline__ void store_item(const float (&v)[32], const float (&g
   fence_async_smem();
   __syncwarp();
   if (lane == 0) {
-    tma_store_2d(tmap_out, stage_out, ocol0, mt * BN + c * W);
+    tma_store_2d(tmap_out, stage_out, ocol0, row0 + c * W);
     bulk_commit();
   }
 }
@@ -205,6 +228,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     tmem_relinquish();
   }
   pdl_launch();
+  if (p.grp_work != nullptr) pdl_wait();  // every role reads the device work list
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -216,10 +240,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, waited = false;
+      const bool grouped = p.grp_work != nullptr;
+      if (grouped) waited = true;
       for (int u = u_first; u < units && ok; u += u_step) {
         const int tile = u / p.splits;
-        int nt, mt, kb0, kb1;
-        tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
+        int nt, row0, expert, kb0, kb1;
+        if (!unit_coords(p, tile, BN, nt, row0, expert)) continue;
         split_range(u % p.splits, p.splits, p.kblocks, kb0, kb1);
         int kb = kb0;
         if (!waited) {
@@ -235,7 +261,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
           pdl_wait();
           waited = true;
           for (int i = 0; i < npre; ++i)
-            tma_load_2d(stages + i * C::kStage + C::kA, &tmap_x, &full[i], (kb0 + i) * BK, mt * BN);
+            tma_load_2d(stages + i * C::kStage + C::kA, &tmap_x, &full[i], (kb0 + i) * BK, row0);
           stage = npre % C::kStages;
           phase = npre == C::kStages ? 1u : 0u;
           kb = kb0 + npre;
@@ -244,9 +270,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
           if (!mbar_wait(&empty[stage], phase ^ 1, 100)) { ok = false; break; }
           uint8_t* a = stages + stage * C::kStage;
           mbar_expect_tx(&full[stage], C::kStage);
-          if (p.w_blocked) tma_load_3d(a, &tmap_w, &full[stage], 0, nt * C::kRowsA, kb);
+          if (grouped) tma_load_3d(a, &tmap_w, &full[stage], kb * BK, nt * C::kRowsA, expert);
+          else if (p.w_blocked) tma_load_3d(a, &tmap_w, &full[stage], 0, nt * C::kRowsA, kb);
           else tma_load_2d(a, &tmap_w, &full[stage], kb * BK, nt * C::kRowsA);
-          tma_load_2d(a + C::kA, &tmap_x, &full[stage], kb * BK, mt * BN);
+          tma_load_2d(a + C::kA, &tmap_x, &full[stage], kb * BK, row0);
           if (++stage == C::kStages) { stage = 0; phase ^= 1; }
         }
       }
@@ -259,8 +286,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       int stage = 0, use = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = u_first; u < units && ok; u += u_step, ++use) {
-        int kb0, kb1;
+      for (int u = u_first; u < units && ok; u += u_step) {
+        int kb0, kb1, nt_, row0_, ex_;
+        if (!unit_coords(p, u / p.splits, BN, nt_, row0_, ex_)) continue;
         split_range(u % p.splits, p.splits, p.kblocks, kb0, kb1);
         const int acc = C::kBufs == 2 ? (use & 1) : 0;
         const uint32_t par = C::kBufs == 2 ? ((use >> 1) & 1) : (use & 1);
@@ -283,6 +311,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
           if (++stage == C::kStages) { stage = 0; phase ^= 1; }
         }
         tc_commit(&tfull[acc]);
+        ++use;
       }
     }
   } else {
@@ -295,12 +324,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     constexpr int kParts = (C::kTwo && !C::kAct) ? 2 : 1;
     constexpr int kItems = kParts * kChunks;
     int use = 0;
-    for (int u = u_first; u < units; u += u_step, ++use) {
+    for (int u = u_first; u < units; u += u_step) {
       const int tile = u / p.splits;
-      int nt, mt;
-      tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
-      const int acc = C::kBufs == 2 ? (use & 1) : 0;
-      const uint32_t par = C::kBufs == 2 ? ((use >> 1) & 1) : (use & 1);
+      int nt, row0, expert;
+      if (!unit_coords(p, tile, BN, nt, row0, expert)) continue;
+      const __nv_bfloat16* bias = p.bias == nullptr ? nullptr : p.bias + (int64_t)expert * p.bias_stride;
+      const int use_now = use++;
+      const int acc = C::kBufs == 2 ? (use_now & 1) : 0;
+      const uint32_t par = C::kBufs == 2 ? ((use_now >> 1) & 1) : (use_now & 1);
       if (!mbar_wait(&tfull[acc], par, 300)) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + acc * C::kAccCols + ((uint32_t)(q * 32) << 16);
@@ -327,7 +358,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
         float v[32], g2[32];
         tmem_load_cols<W>(tb + part * BN + c * W, v);
         if constexpr (C::kAct) tmem_load_cols<W>(tb + BN + c * W, g2);
-        store_item<BN, EPI, WIDE>(v, g2, p, nt, mt, part, c, q, lane, stage_out, &tmap_out);
+        store_item<BN, EPI, WIDE>(v, g2, p, bias, nt, row0, part, c, q, lane, stage_out, &tmap_out);
       }
       tc_fence_before();
       __syncwarp();
@@ -345,6 +376,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
         const int tile = blockIdx.y;
         int nt, mt;
         tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
+        const int row0 = mt * BN;
         uint8_t* stage_out = epi_smem + (warp - 2) * C::kStageOut;
         constexpr int kChunks = BN / W;
         constexpr int kParts = (C::kTwo && !C::kAct) ? 2 : 1;
@@ -376,7 +408,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
               }
             }
           }
-          store_item<BN, EPI, WIDE>(v, g2, p, nt, mt, part, c, q, lane, stage_out, &tmap_out);
+          store_item<BN, EPI, WIDE>(v, g2, p, p.bias, nt, row0, part, c, q, lane, stage_out, &tmap_out);
         }
       }
       cluster_sync();  // peers may still be reading this CTA's partial
@@ -448,6 +480,23 @@ static CUtensorMap make_map_blocked(const void* base, int N, int K, int box_rows
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) fprintf(stderr, "minisgl: cuTensorMapEncodeTiled (blocked) failed (%d)\n", (int)r);
+  return m;
+}
+
+// [E][N][K] expert weights: 3-D map (k, row, expert), box (64, rows, 1)
+static CUtensorMap make_map_experts(const void* base, int E, int N, int K, int box_rows) {
+  CUtensorMap m;
+  memset(&m, 0, sizeof(m));
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return m;
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)N, (cuuint64_t)E};
+  cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)N * K * 2};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fprintf(stderr, "minisgl: cuTensorMapEncodeTiled (experts) failed (%d)\n", (int)r);
   return m;
 }
 
@@ -600,6 +649,9 @@ extern "C" void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blo
   Plan pl = make_plan(M, N, K, epi, force_splits, force_wide);
   Params p;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.grp_count = nullptr;
+  p.grp_work = nullptr;
+  p.bias_stride = 0;
   p.w_blocked = w_blocked;
   p.M = M;
   p.n_out = is_act(epi) ? N / 2 : N;
@@ -621,6 +673,50 @@ extern "C" void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blo
 extern "C" void msgl_gemm(void* out, const void* x, const void* w, const void* bias, int M, int N, int K,
                           int ldo, int epi, int splits, void* workspace, cudaStream_t s) {
   msgl_gemm_ex(out, x, w, bias, M, N, K, ldo, epi, splits, -1, workspace, s);
+}
+
+template <int BN>
+static void launch_grouped(const Params& p, const void* x, const void* w, void* out, int E, int N, int K, int ldo,
+                           cudaStream_t s) {
+  using C = Cfg<BN, kBf16, false>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_kernel<BN, kBf16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    attr_set = true;
+  }
+  const CUtensorMap mw = make_map_experts(w, E, N, K, C::kRowsA);
+  const CUtensorMap mx = make_map(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, K, K, BK, BN, true);
+  const CUtensorMap mo = make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, C::kChunk, false);
+  const int units = p.n_tiles * p.m_tiles;
+  msgl_launch(gemm_kernel<BN, kBf16, false>, dim3(std::min(units, num_sms_cached())), dim3(kThreads), C::kSmem, s,
+              1, mw, mx, mo, p);
+}
+
+// Grouped GEMM for routed experts: for every token tile t < *tile_count (device), rows
+// [work[t].y, work[t].y + bn) of x (permuted activations, [rows_cap, K]) times expert work[t].x of
+// w ([E, N, K]) -> the same rows of out ([rows_cap, N], row stride ldo), plus bias[e] if given.
+extern "C" void msgl_gemm_grouped(void* out, const void* x, const void* w, const void* bias, int rows_cap, int N,
+                                  int K, int ldo, int E, const int* tile_count, const void* work, int max_tiles,
+                                  int bn, cudaStream_t s) {
+  if (rows_cap <= 0 || N <= 0 || max_tiles <= 0) return;
+  Params p;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.bias_stride = N;
+  p.w_blocked = 0;
+  p.grp_count = tile_count;
+  p.grp_work = reinterpret_cast<const int2*>(work);
+  p.M = rows_cap;
+  p.n_out = N;
+  p.n_tiles = (N + 127) / 128;
+  p.m_tiles = max_tiles;
+  p.kblocks = (K + BK - 1) / BK;
+  p.splits = 1;
+  switch (bn) {
+    case 16: launch_grouped<16>(p, x, w, out, E, N, K, ldo, s); break;
+    case 32: launch_grouped<32>(p, x, w, out, E, N, K, ldo, s); break;
+    case 64: launch_grouped<64>(p, x, w, out, E, N, K, ldo, s); break;
+    default: launch_grouped<128>(p, x, w, out, E, N, K, ldo, s); break;
+  }
 }
 
 extern "C" int msgl_num_sms() { return num_sms_cached(); }

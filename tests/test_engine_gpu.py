@@ -33,7 +33,7 @@ def _run(path, prompts, sp, port, **kw):
     return out
 
 
-@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-llama", "tiny-qwen2"])
+@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-llama", "tiny-qwen2", "tiny-qwen3-moe"])
 def test_gpu_first_tokens_match_oracle(tmp_path, preset, free_port):
     if not torch.cuda.is_available():
         pytest.skip("no GPU")

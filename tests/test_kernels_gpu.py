@@ -242,3 +242,27 @@ def test_gemm_variants(M, epi, wide, splits, blocked):
         out.zero_()
         _c().gemm_ex(out, x, wk, b, epi, splits, wide)
         _close(out, expect, 3e-2, 3e-2)
+
+
+@pytest.mark.parametrize("T,E,topk,H,I,act,renorm,after,bias", [
+    (1, 8, 2, 256, 128, "silu", True, False, False),
+    (37, 8, 2, 256, 128, "silu", True, False, False),
+    (300, 64, 8, 1024, 384, "silu", True, False, False),
+    (64, 32, 4, 512, 360, "swiglu_oai", False, True, True),
+    (513, 128, 4, 2880, 360, "swiglu_oai", False, True, True),
+])
+def test_moe_forward(T, E, topk, H, I, act, renorm, after, bias):
+    from minisgl.moe.grouped import moe_reference
+    from minisgl.ops.moe import moe_forward
+
+    g = torch.Generator().manual_seed(T + E)
+    x = torch.randn(T, H, generator=g).to(DEV, torch.bfloat16)
+    w1 = (torch.randn(E, 2 * I, H, generator=g) / math.sqrt(H)).to(DEV, torch.bfloat16)
+    w2 = (torch.randn(E, H, I, generator=g) / math.sqrt(I)).to(DEV, torch.bfloat16)
+    gate = torch.randn(T, E, generator=g).to(DEV)
+    b1 = (torch.randn(E, 2 * I, generator=g) * 0.1).to(DEV, torch.bfloat16) if bias else None
+    b2 = (torch.randn(E, H, generator=g) * 0.1).to(DEV, torch.bfloat16) if bias else None
+    out = moe_forward(x, w1, w2, gate, topk, renorm, act, b1, b2, after)
+    exp = moe_reference(x.cpu(), w1.cpu(), w2.cpu(), gate.cpu(), topk, renorm, act,
+                        None if b1 is None else b1.cpu(), None if b2 is None else b2.cpu(), after)
+    _close(out, exp, 3e-2, 3e-2)
