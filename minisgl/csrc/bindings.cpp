@@ -103,8 +103,10 @@ void gemm_ex(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tenso
   if (M == 0) return;
   CHECK(out.stride(0) % (epi == 3 ? 4 : 8) == 0, "out row stride must be 16-byte aligned");
   if (epi == 1 || epi == 2) CHECK(N % 256 == 0, "gated GEMM needs N (gate+up rows) to be a multiple of 256");
+  const int64_t wsb = msgl_gemm_workspace_bytes(M, N, K, 0);
+  at::Tensor& ws = gemm_workspace(x.device(), wsb);
   msgl_gemm_ex2(out.data_ptr(), x.data_ptr(), w.data_ptr(), blocked ? 1 : 0, opt_ptr(bias), M, N, K,
-                out.stride(0), epi, splits, wide, stream());
+                out.stride(0), epi, splits, wide, ws.data_ptr(), ws.numel(), stream());
 }
 
 void gemm(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, int64_t epi) {
@@ -328,6 +330,7 @@ PYBIND11_MODULE(_cuda, m) {
   m.def("attention_decode", &attention_decode);
   m.def("get_error", &get_error);
   m.def("gemm_grouped", &gemm_grouped);
+
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);

@@ -34,7 +34,7 @@ void msgl_sample(int32_t* out, const float* logits, int rows, int vocab, int64_t
 // ----- GEMM: out[M,N] = epi(x[M,K] @ w[N,K]^T + bias)
 //   epi 0: bf16 out; 1: silu(g)*u on 64-row interleaved gate/up (out has N/2 cols);
 //   2: gelu(g)*u likewise; 3: fp32 out.
-// workspace: fp32 split-K partials + tile counters (may be null when splits == 1).
+// workspace: L2-resident split-K exchange buffer of the 2-SM kernel (null disables its split-K).
 int msgl_gemm_workspace_bytes(int M, int N, int K, int splits);
 int msgl_gemm_pick_splits(int M, int N, int K);
 void msgl_gemm(void* out, const void* x, const void* w, const void* bias, int M, int N, int K,
@@ -45,7 +45,8 @@ void msgl_gemm_ex(void* out, const void* x, const void* w, const void* bias, int
                   int ldo, int epi, int splits, int wide, void* workspace, cudaStream_t s);
 // w_blocked: weight stored K-block major as [K/64][N][64] (requires K % 64 == 0)
 void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M, int N,
-                   int K, int ldo, int epi, int splits, int wide, cudaStream_t s);
+                   int K, int ldo, int epi, int splits, int wide, void* workspace, int64_t ws_bytes,
+                   cudaStream_t s);
 
 // ----- routed experts (MoE)
 void msgl_gemm_grouped(void* out, const void* x, const void* w, const void* bias, int rows_cap, int N, int K,

@@ -424,6 +424,301 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   }
 }
 
+
+// =================================================================================================
+// 2-SM variant (tcgen05.mma.cta_group::2): a CTA pair computes one 256-weight-row tile. Each CTA
+// loads its own 128 weight rows (256 for gated outputs: 128 gate + 128 up) and HALF of the token
+// tile into its own smem; the loads complete on the pair leader's barrier; the leader's single MMA
+// thread issues M = 256 MMAs that read both CTAs' smem and write each CTA's TMEM (its 128 rows x
+// BN tokens). Per SM this halves the activation traffic of the 1-SM kernel, which is what limits
+// decode-sized GEMMs. Commits are multicast to both CTAs' barriers (tcgen05.commit multicast; no
+// TMA multicast). Split-K uses clusters of 2 x S CTAs (pair member = rank & 1, split = rank >> 1)
+// exchanging fp32 partials through an L2-resident buffer.
+// =================================================================================================
+template <int BN, int EPI>
+struct Cfg2 {
+  static constexpr bool kAct = EPI == kSilu || EPI == kGelu;
+  static constexpr int kRowsA = kAct ? 256 : 128;  // weight rows loaded per CTA
+  static constexpr int kTok = BN / 2;               // token rows loaded per CTA
+  static constexpr int kAccCols = (kAct ? 2 : 1) * BN;
+  static constexpr int kBufs = 2 * kAccCols <= 512 ? 2 : 1;
+  static constexpr int kTmemCols = pow2ceil(kBufs * kAccCols);
+  static constexpr int kA = kRowsA * BK * 2;
+  static constexpr int kB = kTok * BK * 2;
+  static constexpr int kStage = kA + kB;
+  static constexpr int kOutElem = EPI == kF32 ? 4 : 2;
+  static constexpr int kStageOut = 32 * 32 * kOutElem;
+  static constexpr int kEpiSmem = kEpiWarps * kStageOut;
+  static constexpr int kStages = std::min(8, (220 * 1024 - kEpiSmem) / kStage);
+  static constexpr int kSmem = 1024 + kStages * kStage + kEpiSmem + 256;
+  static constexpr int kParts = kAct ? 2 : 1;
+  // split-K exchange bytes for `tiles` pair tiles and S splits
+  static constexpr size_t ws_bytes(int tiles, int S) { return (size_t)tiles * 2 * S * kParts * 128 * BN * 4; }
+  static_assert(BN >= 64 && BN <= 256, "2-SM tiles use 64..256 tokens");
+  static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
+};
+
+struct Params2 {
+  float* ws;  // split-K exchange: [tiles][2][S][chunks][parts * 128][32] fp32
+  const __nv_bfloat16* bias;
+  int M, n_out, kblocks;
+  int n_tiles, m_tiles, splits;  // n_tiles counts pair tiles (256 weight rows, 512 if gated)
+};
+
+template <int BN, int EPI>
+__device__ __forceinline__ void store_item2(const float (&v)[32], const float (&g2)[32], const Params2& p, int nt,
+                                            int row0, int x, int c, int q, int lane, uint8_t* stage_out,
+                                            const CUtensorMap* tmap_out) {
+  using C = Cfg2<BN, EPI>;
+  const int nrow = q * 32 + lane;
+  const int ocol0 = nt * 256 + x * 128 + q * 32;
+  float bias_a = 0.f, bias_b = 0.f;
+  if (p.bias != nullptr && ocol0 + lane < p.n_out) {
+    if constexpr (C::kAct) {
+      const int grow = nt * 512 + x * 256 + nrow;
+      bias_a = __bfloat162float(p.bias[grow]);
+      bias_b = __bfloat162float(p.bias[grow + 128]);
+    } else {
+      bias_a = __bfloat162float(p.bias[ocol0 + lane]);
+    }
+  }
+  float o[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if constexpr (C::kAct) {
+      const float g = v[j] + bias_a, up = g2[j] + bias_b;
+      o[j] = (EPI == kSilu ? act_silu(g) : act_gelu(g)) * up;
+    } else {
+      o[j] = v[j] + bias_a;
+    }
+  }
+  if (lane == 0) bulk_wait_read<0>();
+  __syncwarp();
+  if constexpr (EPI == kF32) {
+    float* sp = reinterpret_cast<float*>(stage_out);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sp[j * 32 + lane] = o[j];
+  } else {
+    __nv_bfloat16* sp = reinterpret_cast<__nv_bfloat16*>(stage_out);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sp[j * 32 + lane] = __float2bfloat16(o[j]);
+  }
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmap_out, stage_out, ocol0, row0 + c * 32);
+    bulk_commit();
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+             const __grid_constant__ CUtensorMap tmap_out, Params2 p) {
+  using C = Cfg2<BN, EPI>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* epi_smem = smem + C::kStages * C::kStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + C::kEpiSmem);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::kStages;
+  uint64_t* tfull = bars + 2 * C::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int x = rank & 1, ysplit = rank >> 1;
+  const uint32_t leader = rank & ~1u;
+  const uint16_t pair_mask = (uint16_t)(3u << leader);
+  const bool split = p.splits > 1;
+  const int tiles = p.n_tiles * p.m_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 2 * kEpiWarps);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_out);
+  }
+  if (warp == 1) {
+    tmem_alloc_2sm(tmem_slot, C::kTmemCols);
+    tmem_relinquish_2sm();
+  }
+  pdl_launch();
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      pdl_wait();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.y; t < tiles; t += gridDim.y) {
+        int nt, mt, kb0, kb1;
+        tile_coords(t, p.n_tiles, p.m_tiles, nt, mt);
+        split_range(ysplit, p.splits, p.kblocks, kb0, kb1);
+        const int wrow = nt * 2 * C::kRowsA + x * C::kRowsA;
+        const int trow = mt * BN + x * C::kTok;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, 110)) { ok = false; break; }
+          if (x == 0) mbar_expect_tx(&full[stage], 2 * C::kStage);
+          uint8_t* a = stages + stage * C::kStage;
+          const uint32_t fbar = dsmem_addr(smem_u32(&full[stage]), leader);
+          tma_load_2d_2sm(a, &tmap_w, fbar, kb * BK, wrow);
+          tma_load_2d_2sm(a + C::kA, &tmap_x, fbar, kb * BK, trow);
+          if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && x == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(256, BN);
+      int stage = 0, use = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.y; t < tiles; t += gridDim.y, ++use) {
+        int kb0, kb1;
+        split_range(ysplit, p.splits, p.kblocks, kb0, kb1);
+        const int acc = C::kBufs == 2 ? (use & 1) : 0;
+        const uint32_t par = C::kBufs == 2 ? ((use >> 1) & 1) : (use & 1);
+        if (!mbar_wait(&tempty[acc], par ^ 1, 210)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * C::kAccCols;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, 211)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a = smem_u32(stages + stage * C::kStage);
+          const uint32_t b = a + C::kA;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
+            const uint64_t bd = smem_desc_sw128(b + k * 32);
+            tc_mma_f16_2sm(d, smem_desc_sw128(a + k * 32), bd, idesc, accum);
+            if constexpr (C::kAct) tc_mma_f16_2sm(d + BN, smem_desc_sw128(a + 128 * 128 + k * 32), bd, idesc, accum);
+          }
+          tc_commit_2sm_mc(&empty[stage], pair_mask);
+          if (++stage == C::kStages) { stage = 0; phase ^= 1; }
+        }
+        tc_commit_2sm_mc(&tfull[acc], pair_mask);
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* stage_out = epi_smem + (warp - 2) * C::kStageOut;
+    constexpr int kChunks = BN / 32;
+    int use = 0;
+    for (int t = blockIdx.y; t < tiles; t += gridDim.y, ++use) {
+      int nt, mt;
+      tile_coords(t, p.n_tiles, p.m_tiles, nt, mt);
+      const int acc = C::kBufs == 2 ? (use & 1) : 0;
+      const uint32_t par = C::kBufs == 2 ? ((use >> 1) & 1) : (use & 1);
+      if (!mbar_wait(&tfull[acc], par, 310)) break;
+      tc_fence_after();
+      if (split) break;  // reduced across the cluster below, straight from TMEM
+      const uint32_t tb = tmem_base + acc * C::kAccCols + ((uint32_t)(q * 32) << 16);
+      for (int c = half; c < kChunks; c += 2) {
+        float v[32], g2[32];
+        tmem_load_cols<32>(tb + c * 32, v);
+        if constexpr (C::kAct) tmem_load_cols<32>(tb + BN + c * 32, g2);
+        store_item2<BN, EPI>(v, g2, p, nt, mt * BN, x, c, q, lane, stage_out, &tmap_out);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(dsmem_addr(smem_u32(&tempty[acc]), leader));
+    }
+  }
+
+  if (split) {
+    // 2-SM split-K exchange. Chunk c (32 tokens) of this pair member's accumulator rows is owned
+    // by split (c % S). Every split writes the chunks it does not own from TMEM to the L2-resident
+    // exchange buffer with plain vector stores; after one cluster barrier (release / acquire at
+    // cluster scope) the owner adds them to its own TMEM values and runs the epilogue.
+    constexpr int kChunks = BN / 32;
+    constexpr int kParts = C::kParts;
+    const int S = p.splits;
+    const int tile = blockIdx.y;
+    float* xbase = p.ws + (size_t)((tile * 2 + x) * S) * kChunks * kParts * 128 * 32;
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    const int nrow = q * 32 + lane;
+    const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16);
+    if (warp >= 2) {
+      for (int c = half; c < kChunks; c += 2) {
+        if (c % S == ysplit) continue;
+#pragma unroll
+        for (int pt = 0; pt < kParts; ++pt) {
+          float v[32];
+          tmem_load_cols<32>(tb + pt * BN + c * 32, v);
+          float* dst = xbase + ((size_t)(ysplit * kChunks + c) * kParts * 128 + pt * 128 + nrow) * 32;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            __stcg(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+        }
+      }
+    }
+    tc_fence_before();
+    cluster_sync();  // partials of every split are visible (cluster-scope release / acquire)
+    tc_fence_after();
+    if (warp >= 2) {
+      int nt, mt;
+      tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
+      uint8_t* stage_out = epi_smem + (warp - 2) * C::kStageOut;
+      int k = 0;
+      for (int c = ysplit; c < kChunks; c += S, ++k) {
+        if ((k & 1) != half) continue;
+        float v[32], g2[32];
+        tmem_load_cols<32>(tb + c * 32, v);
+        if constexpr (C::kAct) tmem_load_cols<32>(tb + BN + c * 32, g2);
+        for (int src = 0; src < S; ++src) {
+          if (src == ysplit) continue;
+          const float* base = xbase + ((size_t)(src * kChunks + c) * kParts * 128 + nrow) * 32;
+          float4 f[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] = __ldcg(reinterpret_cast<const float4*>(base) + j);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            v[4 * j] += f[j].x; v[4 * j + 1] += f[j].y; v[4 * j + 2] += f[j].z; v[4 * j + 3] += f[j].w;
+          }
+          if constexpr (C::kAct) {
+            const float* ub = base + 128 * 32;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = __ldcg(reinterpret_cast<const float4*>(ub) + j);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              g2[4 * j] += f[j].x; g2[4 * j + 1] += f[j].y; g2[4 * j + 2] += f[j].z; g2[4 * j + 3] += f[j].w;
+            }
+          }
+        }
+        store_item2<BN, EPI>(v, g2, p, nt, mt * BN, x, c, q, lane, stage_out, &tmap_out);
+      }
+    }
+  }
+  if (warp >= 2 && lane == 0) bulk_wait<0>();
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its pair / cluster peers may still address its smem / TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_2sm(tmem_base, C::kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------------------------------ host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -539,10 +834,65 @@ static Plan make_plan(int M, int N, int K, int epi, int force_splits, int force_
   const bool can_split = !(pl.rows_a == 256 && pl.bn > 128);
   int splits = 1;
   if (force_splits > 0) splits = force_splits;
-  else if (!act && pl.tiles <= sms / 2 && kblocks >= 48) splits = (kblocks >= 192 && pl.tiles * 4 <= sms) ? 4 : 2;
+  else if (!act && M <= 128 && pl.tiles <= sms / 2 && kblocks >= 16) {
+    // weight-streaming regime: use as many K-splits as keep every SM busy in one wave
+    splits = std::max(1, std::min(sms / pl.tiles, kblocks / 8));
+  } else if (!act && pl.tiles <= sms / 2 && kblocks >= 48) {
+    splits = (kblocks >= 192 && pl.tiles * 4 <= sms) ? 4 : 2;
+  }
   splits = std::min(std::min(splits, 8), std::max(1, kblocks / 4));
   pl.splits = can_split ? splits : 1;
   return pl;
+}
+
+template <int BN, int EPI>
+static int max_clusters2(int size) {
+  using C = Cfg2<BN, EPI>;
+  static int cache[9] = {0};
+  if (cache[size] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(size, 64, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm2_kernel<BN, EPI>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms_cached() / size;
+    }
+    cache[size] = n;
+  }
+  return cache[size];
+}
+
+template <int BN, int EPI>
+static void launch2(Params2 p, const void* x, const void* w, void* out, int N, int K, int ldo, size_t ws_cap,
+                    cudaStream_t s) {
+  using C = Cfg2<BN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm2_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    attr_set = true;
+  }
+  const CUtensorMap mw = make_map(w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, BK, C::kRowsA, true);
+  const CUtensorMap mx = make_map(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, K, K, BK, C::kTok, true);
+  const CUtensorMap mo = EPI == kF32
+      ? make_map(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.M, p.n_out, ldo, 32, 32, false)
+      : make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, 32, false);
+  const int tiles = p.n_tiles * p.m_tiles;
+  while (p.splits > 1 && (p.ws == nullptr || C::ws_bytes(tiles, p.splits) > ws_cap ||
+                          tiles > max_clusters2<BN, EPI>(2 * p.splits)))
+    --p.splits;
+  int groups = tiles;
+  if (p.splits == 1) groups = std::min(tiles, std::max(1, max_clusters2<BN, EPI>(2)));
+  msgl_launch(gemm2_kernel<BN, EPI>, dim3(2 * p.splits, groups, 1), dim3(kThreads), C::kSmem, s, 2 * p.splits, mw,
+              mx, mo, p);
 }
 
 // Largest co-resident cluster count for a cluster size (GPCs do not divide evenly by every size).
@@ -604,7 +954,8 @@ static void launch(const Params& p, const void* x, const void* w, void* out, int
       : make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, C::kChunk, false);
   Params q = p;
   if (q.splits > 1 && !C::kCanSplit) q.splits = 1;
-  if (q.splits > 1 && q.n_tiles * q.m_tiles > max_clusters<BN, EPI, WIDE>(q.splits)) q.splits = 1;
+  // shrink the cluster until every tile's cluster is co-resident (GPCs do not divide evenly)
+  while (q.splits > 1 && q.n_tiles * q.m_tiles > max_clusters<BN, EPI, WIDE>(q.splits)) --q.splits;
   const int tiles = q.n_tiles * q.m_tiles;
   if (q.splits > 1) {
     msgl_launch(gemm_kernel<BN, EPI, WIDE>, dim3(q.splits, tiles, 1), dim3(kThreads), C::kSmem, s, q.splits, mw, mx,
@@ -627,6 +978,52 @@ static void dispatch_bn(int bn, const Params& p, const void* x, const void* w, v
   }
 }
 
+// 2-SM path: more than 64 tokens (larger decode batches and prefill), row-major weights.
+// force_wide == 2 forces it, 0/1 forbid it (they select the 1-SM tile shapes).
+static bool use_2sm(int M, int N, int K, int epi, int force_wide, int w_blocked) {
+  if (w_blocked) return false;
+  if (force_wide == 2) return true;
+  if (force_wide >= 0) return false;
+  if (const char* e = getenv("MINISGL_GEMM_2SM"))
+    if (e[0] == '0') return false;
+  return M > 64 && K >= 4096;
+}
+
+template <int EPI>
+static void launch_2sm_bn(int bn, Params2 p, const void* x, const void* w, void* out, int N, int K, int ldo,
+                          size_t ws_cap, cudaStream_t s) {
+  if (bn == 64) launch2<64, EPI>(p, x, w, out, N, K, ldo, ws_cap, s);
+  else if (bn == 128) launch2<128, EPI>(p, x, w, out, N, K, ldo, ws_cap, s);
+  else launch2<256, EPI>(p, x, w, out, N, K, ldo, ws_cap, s);
+}
+
+static void launch_2sm(const void* x, const void* w, const void* bias, void* out, int M, int N, int K, int ldo,
+                       int epi, int force_splits, void* ws, size_t ws_cap, cudaStream_t s) {
+  const bool act = is_act(epi);
+  Params2 p;
+  p.ws = reinterpret_cast<float*>(ws);
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.M = M;
+  p.n_out = act ? N / 2 : N;
+  p.kblocks = (K + BK - 1) / BK;
+  int bn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  if (M > 256) bn = act ? 128 : 256;
+  p.n_tiles = (N + (act ? 511 : 255)) / (act ? 512 : 256);
+  p.m_tiles = (M + bn - 1) / bn;
+  const int tiles = p.n_tiles * p.m_tiles;
+  const int sms = num_sms_cached();
+  int splits = 1;
+  if (force_splits > 0) splits = force_splits;
+  else if (2 * tiles <= sms / 2 && p.kblocks >= 32) splits = std::min(sms / (2 * tiles), p.kblocks / 16);
+  p.splits = std::max(1, std::min(splits, 4));
+  switch (epi) {
+    case kBf16: launch_2sm_bn<kBf16>(bn, p, x, w, out, N, K, ldo, ws_cap, s); break;
+    case kF32: launch_2sm_bn<kF32>(bn, p, x, w, out, N, K, ldo, ws_cap, s); break;
+    case kSilu: launch_2sm_bn<kSilu>(bn, p, x, w, out, N, K, ldo, ws_cap, s); break;
+    default: launch_2sm_bn<kGelu>(bn, p, x, w, out, N, K, ldo, ws_cap, s); break;
+  }
+}
+
 }  // namespace gemm
 }  // namespace msgl
 
@@ -635,16 +1032,21 @@ using namespace msgl::gemm;
 
 extern "C" int msgl_gemm_pick_splits(int M, int N, int K) { return make_plan(M, N, K, kBf16, -1, -1).splits; }
 
-extern "C" int msgl_gemm_workspace_bytes(int M, int N, int K, int splits) { return 0; }
+// split-K exchange buffer of the 2-SM kernel: (pair tiles) x 2 x S(<=4) x 256 rows x 256 tokens fp32
+extern "C" int msgl_gemm_workspace_bytes(int M, int N, int K, int splits) {
+  const int64_t tiles = (int64_t)((N + 255) / 256) * ((M + 63) / 64);
+  return (int)std::min<int64_t>(tiles * 2 * 4 * 256 * 256 * 4, 256ll << 20);
+}
 
 extern "C" void msgl_gemm_ex(void* out, const void* x, const void* w, const void* bias, int M, int N, int K,
                              int ldo, int epi, int force_splits, int force_wide, void* workspace, cudaStream_t s) {
-  msgl_gemm_ex2(out, x, w, 0, bias, M, N, K, ldo, epi, force_splits, force_wide, s);
-  (void)workspace;
+  msgl_gemm_ex2(out, x, w, 0, bias, M, N, K, ldo, epi, force_splits, force_wide, workspace,
+                workspace ? (int64_t)msgl_gemm_workspace_bytes(M, N, K, 0) : 0, s);
 }
 
 extern "C" void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M,
-                              int N, int K, int ldo, int epi, int force_splits, int force_wide, cudaStream_t s) {
+                              int N, int K, int ldo, int epi, int force_splits, int force_wide, void* workspace,
+                              int64_t ws_cap, cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
   Plan pl = make_plan(M, N, K, epi, force_splits, force_wide);
   Params p;
@@ -659,6 +1061,10 @@ extern "C" void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blo
   p.m_tiles = (M + pl.bn - 1) / pl.bn;
   p.kblocks = (K + BK - 1) / BK;
   p.splits = pl.splits;
+  if (use_2sm(M, N, K, epi, force_wide, w_blocked)) {
+    launch_2sm(x, w, bias, out, M, N, K, ldo, epi, force_splits, workspace, (size_t)ws_cap, s);
+    return;
+  }
   const bool wide = pl.wide;
   switch (epi) {
     case kBf16: wide ? dispatch_bn<kBf16, true>(pl.bn, p, x, w, out, N, K, ldo, s)
