@@ -325,7 +325,9 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_wait();
   pdl_launch();
-  const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  // KV heads vary fastest across the grid: the heads of one request share every 2 KB token row
+  // of the cache, so fetching them together keeps DRAM rows open.
+  const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z;
   const int G = p.group;
   const int L = p.kv_lens[b], row = p.rows[b];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -467,7 +469,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
       const int64_t slot = ((int64_t)b * p.nq + head) * p.num_splits + split;
       p.ws[slot * HD + col] = acc;
       if (col == 0) {
-        float* ml = p.ws + (int64_t)gridDim.x * p.nq * p.num_splits * HD;
+        float* ml = p.ws + (int64_t)gridDim.y * p.nq * p.num_splits * HD;
         ml[slot * 2] = mx;
         ml[slot * 2 + 1] = ll;
       }
@@ -535,7 +537,7 @@ void run_decode(const AttnParams& p, int bs, cudaStream_t s) {
     cudaFuncSetAttribute(decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<HD>());
     set = true;
   }
-  const dim3 grid(bs, p.nkv, p.num_splits);
+  const dim3 grid(p.nkv, bs, p.num_splits);
   msgl_launch(decode_kernel<HD>, grid, dim3(kWarps * 32), decode_smem<HD>(), s, 1, p);
   if (p.num_splits > 1) {
     const int warps = bs * p.nq;
