@@ -369,9 +369,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   if (split) {
     if constexpr (C::kCanSplit) {
       // ---------------------------------------------------------------- cluster split-K reduction
+      // Items are (part, 32-row quadrant, token chunk); item i belongs to cluster rank i % S and,
+      // within it, to one epilogue warp, so every warp of every split shares the reduction. A
+      // warp reads its 32 rows x W tokens from all S parked partials (local smem included) over
+      // DSMEM, one batch of loads per split, and stores the summed tile.
       cluster_sync();  // every CTA's partial is parked
       if (warp >= 2) {
-        const int q = warp & 3, half = (warp - 2) >> 2;
+        const int S = p.splits;
         const uint32_t rank = cluster_ctarank();
         const int tile = blockIdx.y;
         int nt, mt;
@@ -380,35 +384,36 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
         uint8_t* stage_out = epi_smem + (warp - 2) * C::kStageOut;
         constexpr int kChunks = BN / W;
         constexpr int kParts = (C::kTwo && !C::kAct) ? 2 : 1;
-        constexpr int kItems = kParts * kChunks;
+        constexpr int kItems = kParts * 4 * kChunks;
         const float* part_buf = reinterpret_cast<const float*>(stages);
-        const int nrow = q * 32 + lane;
-        int k = 0;
-        for (int it = (int)rank; it < kItems; it += p.splits, ++k) {
-          if ((k & 1) != half) continue;
-          const int part = it / kChunks, c = it % kChunks;
+        for (int it = (int)rank + S * (warp - 2); it < kItems; it += S * kEpiWarps) {
+          const int part = it / (4 * kChunks);
+          const int qq = (it / kChunks) & 3, c = it % kChunks;
+          const int nrow = qq * 32 + lane;
           float v[32], g2[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = g2[j] = 0.f;
           const uint32_t la = smem_u32(part_buf + (size_t)(part * 128 + nrow) * C::kPartLd + c * W);
           const uint32_t lb = smem_u32(part_buf + (size_t)(128 + nrow) * C::kPartLd + c * W);
-          for (int r = 0; r < p.splits; ++r) {
+          for (int r = 0; r < S; ++r) {
+            float4 t[W / 4], u[W / 4];
             const uint32_t ra = dsmem_addr(la, r);
 #pragma unroll
-            for (int j = 0; j < W; j += 4) {
-              const float4 t = ld_dsmem_v4(ra + j * 4);
-              v[j] += t.x; v[j + 1] += t.y; v[j + 2] += t.z; v[j + 3] += t.w;
-            }
+            for (int j = 0; j < W / 4; ++j) t[j] = ld_dsmem_v4(ra + j * 16);
             if constexpr (C::kAct) {
               const uint32_t rb = dsmem_addr(lb, r);
 #pragma unroll
-              for (int j = 0; j < W; j += 4) {
-                const float4 t = ld_dsmem_v4(rb + j * 4);
-                g2[j] += t.x; g2[j + 1] += t.y; g2[j + 2] += t.z; g2[j + 3] += t.w;
+              for (int j = 0; j < W / 4; ++j) u[j] = ld_dsmem_v4(rb + j * 16);
+            }
+#pragma unroll
+            for (int j = 0; j < W / 4; ++j) {
+              v[4 * j] += t[j].x; v[4 * j + 1] += t[j].y; v[4 * j + 2] += t[j].z; v[4 * j + 3] += t[j].w;
+              if constexpr (C::kAct) {
+                g2[4 * j] += u[j].x; g2[4 * j + 1] += u[j].y; g2[4 * j + 2] += u[j].z; g2[4 * j + 3] += u[j].w;
               }
             }
           }
-          store_item<BN, EPI, WIDE>(v, g2, p, p.bias, nt, row0, part, c, q, lane, stage_out, &tmap_out);
+          store_item<BN, EPI, WIDE>(v, g2, p, p.bias, nt, row0, part, c, qq, lane, stage_out, &tmap_out);
         }
       }
       cluster_sync();  // peers may still be reading this CTA's partial
