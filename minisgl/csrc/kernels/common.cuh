@@ -239,6 +239,14 @@ MSGL_DEVICE void st_async_v4(uint32_t remote_addr, float a, float b, float c, fl
                : "memory");
 }
 
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from this CTA's smem
+// into another cluster CTA's smem; completion is counted in bytes on that CTA's mbarrier.
+MSGL_DEVICE void bulk_push_dsmem(uint32_t remote_dst, const void* src, uint32_t bytes, uint32_t remote_bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(remote_dst), "r"(smem_u32(src)), "r"(bytes), "r"(remote_bar)
+               : "memory");
+}
+
 MSGL_DEVICE float4 ld_dsmem_v4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"

@@ -19,10 +19,11 @@
 // gate and up value of the same output element - no cross-warp exchange.
 //
 // Split-K (decode shapes with few weight tiles): the splits of one tile are launched as one
-// thread-block cluster (co-scheduled by hardware). Each CTA parks its fp32 partial in its own
-// shared memory (the drained operand ring), the cluster synchronizes, and every CTA reduces a
-// disjoint slice of the tile by reading its peers' partials over DSMEM (mapa +
-// ld.shared::cluster) before the epilogue. No global atomics, no workspace.
+// thread-block cluster (co-scheduled by hardware). The fp32 tile is divided into items with one
+// owner split each; every CTA stages the items it does not own in its drained operand ring and,
+// after one cluster barrier, pushes them with bulk shared::cluster copies into the owners'
+// receive slots. Owners add them to their TMEM accumulator and run the epilogue. No global
+// atomics, no workspace.
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -64,10 +65,17 @@ struct Cfg {
   static constexpr int kEpiSmem = kEpiWarps * kStageOut;
   static constexpr int kStages = std::min(8, (220 * 1024 - kEpiSmem) / kStage);
   static constexpr int kSmem = 1024 + kStages * kStage + kEpiSmem + 256;
-  // split-K partial parked in the operand ring: [rows][BN + 4] fp32 (padding spreads banks)
-  static constexpr int kPartRows = kTwo ? 256 : 128;
-  static constexpr int kPartLd = BN + 4;
-  static constexpr bool kCanSplit = kPartRows * kPartLd * 4 <= kStages * kStage;
+  // Split-K exchange: the fp32 tile is cut into items of 32 accumulator rows x kChunk tokens
+  // (plus the matching up rows when gated); each item has one owner split.
+  static constexpr int kItemParts = (kTwo && !kAct) ? 2 : 1;
+  static constexpr int kItems = kItemParts * 4 * (BN / kChunk);
+  static constexpr int kBlkBytes = 32 * kChunk * 4 * (kAct ? 2 : 1);
+  // operand-ring bytes the exchange needs with S splits: this CTA's non-owned items (sent) plus
+  // (S - 1) received copies of each owned item
+  static constexpr int xchg_bytes(int S) {
+    return (kItems - kItems / S + (S - 1) * ((kItems + S - 1) / S)) * kBlkBytes;
+  }
+  static constexpr bool kCanSplit = xchg_bytes(2) <= kStages * kStage;
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
 };
 
@@ -139,6 +147,26 @@ __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float (&v)[32]) {
   }
 }
 
+// Split-K exchange blocks: 32 rows x W fp32, row = lane, 16-byte groups XOR-swizzled by row so a
+// warp's vector accesses spread over all banks.
+template <int W>
+__device__ __forceinline__ void xchg_put(float* blk, int lane, const float (&v)[32]) {
+  constexpr int G = W / 4;
+#pragma unroll
+  for (int j = 0; j < G; ++j)
+    reinterpret_cast<float4*>(blk)[lane * G + (j ^ (lane & (G - 1)))] =
+        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+template <int W>
+__device__ __forceinline__ void xchg_add(const float* blk, int lane, float (&v)[32]) {
+  constexpr int G = W / 4;
+#pragma unroll
+  for (int j = 0; j < G; ++j) {
+    const float4 t = reinterpret_cast<const float4*>(blk)[lane * G + (j ^ (lane & (G - 1)))];
+    v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+  }
+}
+
 // bias + activation for one (part, 32-token chunk) item of a warp's 32 accumulator rows, staged
 // in smem as [W tokens][32 cols] and written with a TMA store (rows >= M / cols >= n_out clipped)
 template <int BN, int EPI, bool WIDE>
@@ -199,8 +227,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
   uint64_t* empty = bars + C::kStages;
   uint64_t* tfull = bars + 2 * C::kStages;
   uint64_t* tempty = tfull + 2;  // indexed by accumulator buffer (kBufs of them)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  int* flag_slot = reinterpret_cast<int*>(tmem_slot + 1);
+  uint64_t* xbar = tempty + 2;   // split-K: bytes of peers' partials received
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool split = p.splits > 1;
@@ -218,7 +246,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], kEpiWarps);
     }
+    mbar_init(xbar, 1);
     fence_barrier_init();
+    if (split) {
+      const int r = (int)cluster_ctarank();
+      const int owned = r < C::kItems ? (C::kItems - 1 - r) / p.splits + 1 : 0;
+      mbar_expect_tx(xbar, (uint32_t)(owned * (p.splits - 1) * C::kBlkBytes));
+    }
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_out);
@@ -338,18 +372,24 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       const int nrow = q * 32 + lane;  // accumulator row inside a 128-row half
       if (split) {
         if constexpr (C::kCanSplit) {
-          // park this split's partial in the (drained) operand ring; reduce after cluster sync
-          float* part_buf = reinterpret_cast<float*>(stages);
-          for (int c = half; c < kChunks; c += 2) {
-#pragma unroll
-            for (int pt = 0; pt < (C::kTwo ? 2 : 1); ++pt) {
-              float v[32];
-              tmem_load_cols<W>(tb + pt * BN + c * W, v);
-              float* dst = part_buf + (size_t)(pt * 128 + nrow) * C::kPartLd + c * W;
-#pragma unroll
-              for (int j = 0; j < W; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          // stage the items other splits own, from TMEM into the drained operand ring
+          const int S = p.splits, rank = (int)cluster_ctarank();
+          constexpr int J = C::kItemParts * kChunks;
+          for (int j = half; j < J; j += 2) {
+            const int it = q * J + j;
+            if (it % S == rank) continue;
+            const int part = j / kChunks, c = j % kChunks;
+            const int a_idx = it - (it > rank ? (it - rank - 1) / S + 1 : 0);
+            float* blk = reinterpret_cast<float*>(stages + (size_t)a_idx * C::kBlkBytes);
+            float v[32];
+            tmem_load_cols<W>(tb + part * BN + c * W, v);
+            xchg_put<W>(blk, lane, v);
+            if constexpr (C::kAct) {
+              tmem_load_cols<W>(tb + BN + c * W, v);
+              xchg_put<W>(blk + 32 * W, lane, v);
             }
           }
+          fence_async_smem();
         }
         break;  // the reduction + epilogue run after the cluster barrier below
       }
@@ -368,55 +408,64 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 
   if (split) {
     if constexpr (C::kCanSplit) {
-      // ---------------------------------------------------------------- cluster split-K reduction
-      // Items are (part, 32-row quadrant, token chunk); item i belongs to cluster rank i % S and,
-      // within it, to one epilogue warp, so every warp of every split shares the reduction. A
-      // warp reads its 32 rows x W tokens from all S parked partials (local smem included) over
-      // DSMEM, one batch of loads per split, and stores the summed tile.
-      cluster_sync();  // every CTA's partial is parked
+      // ---------------------------------------------------------------- cluster split-K exchange
+      // Item it (32 accumulator rows of one quadrant x one token chunk) is owned by split
+      // it % S. Every CTA has staged the items it does not own; after one cluster barrier (all
+      // main loops done, so every receive area in the operand ring is free) each stager pushes
+      // them with bulk shared::cluster copies into the owner's receive slots, completing on the
+      // owner's mbarrier. Owners add the received partials to their own TMEM accumulator and run
+      // the epilogue. Bulk copies move the data as a few large DMA transfers; per-lane DSMEM
+      // loads of the same bytes cost several times longer.
+      const int S = p.splits, rank = (int)cluster_ctarank();
+      constexpr int kChunks = BN / W;
+      constexpr int J = C::kItemParts * kChunks;
+      const int b_off = (C::kItems - C::kItems / S) * C::kBlkBytes;  // receive slots start
+      tc_fence_before();
+      cluster_sync();
+      tc_fence_after();
       if (warp >= 2) {
-        const int S = p.splits;
-        const uint32_t rank = cluster_ctarank();
+        const int q = warp & 3, half = (warp - 2) >> 2;
+        if (lane == 0) {
+          for (int j = half; j < J; j += 2) {
+            const int it = q * J + j, o = it % S;
+            if (o == rank) continue;
+            const int a_idx = it - (it > rank ? (it - rank - 1) / S + 1 : 0);
+            const int slot = (it / S) * (S - 1) + (rank - o - 1 + S) % S;
+            const uint32_t dst = dsmem_addr(smem_u32(stages + b_off + (size_t)slot * C::kBlkBytes), o);
+            bulk_push_dsmem(dst, stages + (size_t)a_idx * C::kBlkBytes, C::kBlkBytes, dsmem_addr(smem_u32(xbar), o));
+          }
+        }
         const int tile = blockIdx.y;
         int nt, mt;
         tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
         const int row0 = mt * BN;
         uint8_t* stage_out = epi_smem + (warp - 2) * C::kStageOut;
-        constexpr int kChunks = BN / W;
-        constexpr int kParts = (C::kTwo && !C::kAct) ? 2 : 1;
-        constexpr int kItems = kParts * 4 * kChunks;
-        const float* part_buf = reinterpret_cast<const float*>(stages);
-        for (int it = (int)rank + S * (warp - 2); it < kItems; it += S * kEpiWarps) {
-          const int part = it / (4 * kChunks);
-          const int qq = (it / kChunks) & 3, c = it % kChunks;
-          const int nrow = qq * 32 + lane;
-          float v[32], g2[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = g2[j] = 0.f;
-          const uint32_t la = smem_u32(part_buf + (size_t)(part * 128 + nrow) * C::kPartLd + c * W);
-          const uint32_t lb = smem_u32(part_buf + (size_t)(128 + nrow) * C::kPartLd + c * W);
-          for (int r = 0; r < S; ++r) {
-            float4 t[W / 4], u[W / 4];
-            const uint32_t ra = dsmem_addr(la, r);
-#pragma unroll
-            for (int j = 0; j < W / 4; ++j) t[j] = ld_dsmem_v4(ra + j * 16);
-            if constexpr (C::kAct) {
-              const uint32_t rb = dsmem_addr(lb, r);
-#pragma unroll
-              for (int j = 0; j < W / 4; ++j) u[j] = ld_dsmem_v4(rb + j * 16);
-            }
-#pragma unroll
-            for (int j = 0; j < W / 4; ++j) {
-              v[4 * j] += t[j].x; v[4 * j + 1] += t[j].y; v[4 * j + 2] += t[j].z; v[4 * j + 3] += t[j].w;
-              if constexpr (C::kAct) {
-                g2[4 * j] += u[j].x; g2[4 * j + 1] += u[j].y; g2[4 * j + 2] += u[j].z; g2[4 * j + 3] += u[j].w;
-              }
-            }
+        const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16);
+        bool have = false, ok = true;
+        for (int j = half; j < J && ok; j += 2) {
+          const int it = q * J + j;
+          if (it % S != rank) continue;
+          if (!have) {
+            ok = mbar_wait(xbar, 0, 320);
+            have = true;
+            if (!ok) break;
           }
-          store_item<BN, EPI, WIDE>(v, g2, p, p.bias, nt, row0, part, c, qq, lane, stage_out, &tmap_out);
+          const int part = j / kChunks, c = j % kChunks;
+          float v[32], g2[32];
+          tmem_load_cols<W>(tb + part * BN + c * W, v);
+          if constexpr (C::kAct) tmem_load_cols<W>(tb + BN + c * W, g2);
+          for (int src = 0; src < S - 1; ++src) {
+            const float* blk =
+                reinterpret_cast<const float*>(stages + b_off + (size_t)((it / S) * (S - 1) + src) * C::kBlkBytes);
+            xchg_add<W>(blk, lane, v);
+            if constexpr (C::kAct) xchg_add<W>(blk + 32 * W, lane, g2);
+          }
+          store_item<BN, EPI, WIDE>(v, g2, p, p.bias, nt, row0, part, c, q, lane, stage_out, &tmap_out);
         }
       }
-      cluster_sync();  // peers may still be reading this CTA's partial
+      if (warp >= 2 && lane == 0) bulk_wait<0>();
+      tc_fence_before();
+      cluster_sync();  // every push into and out of this CTA's smem has landed
     }
   }
   if (warp >= 2 && lane == 0) bulk_wait<0>();
@@ -457,14 +506,18 @@ struct Cfg2 {
   static constexpr int kStages = std::min(8, (220 * 1024 - kEpiSmem) / kStage);
   static constexpr int kSmem = 1024 + kStages * kStage + kEpiSmem + 256;
   static constexpr int kParts = kAct ? 2 : 1;
-  // split-K exchange bytes for `tiles` pair tiles and S splits
-  static constexpr size_t ws_bytes(int tiles, int S) { return (size_t)tiles * 2 * S * kParts * 128 * BN * 4; }
+  // split-K exchange among the CTAs of one pair member: items of 32 accumulator rows x 32 tokens
+  // (with the up rows when gated), staged and received in the drained operand ring
+  static constexpr int kItems = 4 * (BN / 32);
+  static constexpr int kBlkBytes = 32 * 32 * 4 * kParts;
+  static constexpr int xchg_bytes(int S) {
+    return (kItems - kItems / S + (S - 1) * ((kItems + S - 1) / S)) * kBlkBytes;
+  }
   static_assert(BN >= 64 && BN <= 256, "2-SM tiles use 64..256 tokens");
   static_assert(kTmemCols <= 512, "accumulators exceed TMEM");
 };
 
 struct Params2 {
-  float* ws;  // split-K exchange: [tiles][2][S][chunks][parts * 128][32] fp32
   const __nv_bfloat16* bias;
   int M, n_out, kblocks;
   int n_tiles, m_tiles, splits;  // n_tiles counts pair tiles (256 weight rows, 512 if gated)
@@ -530,7 +583,8 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
   uint64_t* empty = bars + C::kStages;
   uint64_t* tfull = bars + 2 * C::kStages;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* xbar = tempty + 2;  // split-K: bytes of peers' partials received
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -548,6 +602,11 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 2 * kEpiWarps);
+    }
+    mbar_init(xbar, 1);
+    if (split) {
+      const int owned = ysplit < C::kItems ? (C::kItems - 1 - ysplit) / p.splits + 1 : 0;
+      mbar_expect_tx(xbar, (uint32_t)(owned * (p.splits - 1) * C::kBlkBytes));
     }
     fence_barrier_init();
     prefetch_tmap(&tmap_w);
@@ -637,8 +696,26 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
       const uint32_t par = C::kBufs == 2 ? ((use >> 1) & 1) : (use & 1);
       if (!mbar_wait(&tfull[acc], par, 310)) break;
       tc_fence_after();
-      if (split) break;  // reduced across the cluster below, straight from TMEM
       const uint32_t tb = tmem_base + acc * C::kAccCols + ((uint32_t)(q * 32) << 16);
+      if (split) {
+        // stage the items other splits own (same pair member), from TMEM into the drained ring
+        const int S = p.splits;
+        for (int c = half; c < kChunks; c += 2) {
+          const int it = q * kChunks + c;
+          if (it % S == ysplit) continue;
+          const int a_idx = it - (it > ysplit ? (it - ysplit - 1) / S + 1 : 0);
+          float* blk = reinterpret_cast<float*>(stages + (size_t)a_idx * C::kBlkBytes);
+          float v[32];
+          tmem_load_cols<32>(tb + c * 32, v);
+          xchg_put<32>(blk, lane, v);
+          if constexpr (C::kAct) {
+            tmem_load_cols<32>(tb + BN + c * 32, v);
+            xchg_put<32>(blk + 32 * 32, lane, v);
+          }
+        }
+        fence_async_smem();
+        break;  // pushed and reduced after the cluster barrier below
+      }
       for (int c = half; c < kChunks; c += 2) {
         float v[32], g2[32];
         tmem_load_cols<32>(tb + c * 32, v);
@@ -652,64 +729,52 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
   }
 
   if (split) {
-    // 2-SM split-K exchange. Chunk c (32 tokens) of this pair member's accumulator rows is owned
-    // by split (c % S). Every split writes the chunks it does not own from TMEM to the L2-resident
-    // exchange buffer with plain vector stores; after one cluster barrier (release / acquire at
-    // cluster scope) the owner adds them to its own TMEM values and runs the epilogue.
-    constexpr int kChunks = BN / 32;
-    constexpr int kParts = C::kParts;
+    // 2-SM split-K exchange among the S CTAs holding the same pair member's rows (cluster ranks
+    // 2 * split + x). Item it (32 rows of one TMEM quadrant x 32 tokens) is owned by split
+    // it % S; stagers push their copies with bulk shared::cluster transfers into the owner's
+    // receive slots (completing on its mbarrier) once the cluster barrier shows every ring
+    // drained; the owner adds them to its TMEM accumulator and runs the epilogue.
     const int S = p.splits;
-    const int tile = blockIdx.y;
-    float* xbase = p.ws + (size_t)((tile * 2 + x) * S) * kChunks * kParts * 128 * 32;
-    const int q = warp & 3, half = (warp - 2) >> 2;
-    const int nrow = q * 32 + lane;
-    const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16);
-    if (warp >= 2) {
-      for (int c = half; c < kChunks; c += 2) {
-        if (c % S == ysplit) continue;
-#pragma unroll
-        for (int pt = 0; pt < kParts; ++pt) {
-          float v[32];
-          tmem_load_cols<32>(tb + pt * BN + c * 32, v);
-          float* dst = xbase + ((size_t)(ysplit * kChunks + c) * kParts * 128 + pt * 128 + nrow) * 32;
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            __stcg(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-        }
-      }
-    }
+    const int b_off = (C::kItems - C::kItems / S) * C::kBlkBytes;
     tc_fence_before();
-    cluster_sync();  // partials of every split are visible (cluster-scope release / acquire)
+    cluster_sync();
     tc_fence_after();
     if (warp >= 2) {
+      const int q = warp & 3, half = (warp - 2) >> 2;
+      constexpr int kChunks = BN / 32;
+      if (lane == 0) {
+        for (int c = half; c < kChunks; c += 2) {
+          const int it = q * kChunks + c, o = it % S;
+          if (o == ysplit) continue;
+          const int a_idx = it - (it > ysplit ? (it - ysplit - 1) / S + 1 : 0);
+          const int slot = (it / S) * (S - 1) + (ysplit - o - 1 + S) % S;
+          const uint32_t dst_rank = (uint32_t)(2 * o + x);
+          const uint32_t dst = dsmem_addr(smem_u32(stages + b_off + (size_t)slot * C::kBlkBytes), dst_rank);
+          bulk_push_dsmem(dst, stages + (size_t)a_idx * C::kBlkBytes, C::kBlkBytes,
+                          dsmem_addr(smem_u32(xbar), dst_rank));
+        }
+      }
+      const int tile = blockIdx.y;
       int nt, mt;
       tile_coords(tile, p.n_tiles, p.m_tiles, nt, mt);
       uint8_t* stage_out = epi_smem + (warp - 2) * C::kStageOut;
-      int k = 0;
-      for (int c = ysplit; c < kChunks; c += S, ++k) {
-        if ((k & 1) != half) continue;
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16);
+      bool have = false;
+      for (int c = half; c < kChunks; c += 2) {
+        const int it = q * kChunks + c;
+        if (it % S != ysplit) continue;
+        if (!have) {
+          if (!mbar_wait(xbar, 0, 320)) break;
+          have = true;
+        }
         float v[32], g2[32];
         tmem_load_cols<32>(tb + c * 32, v);
         if constexpr (C::kAct) tmem_load_cols<32>(tb + BN + c * 32, g2);
-        for (int src = 0; src < S; ++src) {
-          if (src == ysplit) continue;
-          const float* base = xbase + ((size_t)(src * kChunks + c) * kParts * 128 + nrow) * 32;
-          float4 f[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) f[j] = __ldcg(reinterpret_cast<const float4*>(base) + j);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            v[4 * j] += f[j].x; v[4 * j + 1] += f[j].y; v[4 * j + 2] += f[j].z; v[4 * j + 3] += f[j].w;
-          }
-          if constexpr (C::kAct) {
-            const float* ub = base + 128 * 32;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) f[j] = __ldcg(reinterpret_cast<const float4*>(ub) + j);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              g2[4 * j] += f[j].x; g2[4 * j + 1] += f[j].y; g2[4 * j + 2] += f[j].z; g2[4 * j + 3] += f[j].w;
-            }
-          }
+        for (int src = 0; src < S - 1; ++src) {
+          const float* blk =
+              reinterpret_cast<const float*>(stages + b_off + (size_t)((it / S) * (S - 1) + src) * C::kBlkBytes);
+          xchg_add<32>(blk, lane, v);
+          if constexpr (C::kAct) xchg_add<32>(blk + 32 * 32, lane, g2);
         }
         store_item2<BN, EPI>(v, g2, p, nt, mt * BN, x, c, q, lane, stage_out, &tmap_out);
       }
@@ -891,7 +956,7 @@ static void launch2(Params2 p, const void* x, const void* w, void* out, int N, i
       ? make_map(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.M, p.n_out, ldo, 32, 32, false)
       : make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, 32, false);
   const int tiles = p.n_tiles * p.m_tiles;
-  while (p.splits > 1 && (p.ws == nullptr || C::ws_bytes(tiles, p.splits) > ws_cap ||
+  while (p.splits > 1 && (C::xchg_bytes(p.splits) > C::kStages * C::kStage ||
                           tiles > max_clusters2<BN, EPI>(2 * p.splits)))
     --p.splits;
   int groups = tiles;
@@ -959,8 +1024,11 @@ static void launch(const Params& p, const void* x, const void* w, void* out, int
       : make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, C::kChunk, false);
   Params q = p;
   if (q.splits > 1 && !C::kCanSplit) q.splits = 1;
-  // shrink the cluster until every tile's cluster is co-resident (GPCs do not divide evenly)
-  while (q.splits > 1 && q.n_tiles * q.m_tiles > max_clusters<BN, EPI, WIDE>(q.splits)) --q.splits;
+  // shrink the cluster until every tile's cluster is co-resident (GPCs do not divide evenly) and
+  // the split-K exchange fits the operand ring
+  while (q.splits > 1 && (q.n_tiles * q.m_tiles > max_clusters<BN, EPI, WIDE>(q.splits) ||
+                          C::xchg_bytes(q.splits) > C::kStages * C::kStage))
+    --q.splits;
   const int tiles = q.n_tiles * q.m_tiles;
   if (q.splits > 1) {
     msgl_launch(gemm_kernel<BN, EPI, WIDE>, dim3(q.splits, tiles, 1), dim3(kThreads), C::kSmem, s, q.splits, mw, mx,
@@ -997,21 +1065,27 @@ static bool use_2sm(int M, int N, int K, int epi, int force_wide, int w_blocked)
 template <int EPI>
 static void launch_2sm_bn(int bn, Params2 p, const void* x, const void* w, void* out, int N, int K, int ldo,
                           size_t ws_cap, cudaStream_t s) {
-  if (bn == 64) launch2<64, EPI>(p, x, w, out, N, K, ldo, ws_cap, s);
-  else if (bn == 128) launch2<128, EPI>(p, x, w, out, N, K, ldo, ws_cap, s);
-  else launch2<256, EPI>(p, x, w, out, N, K, ldo, ws_cap, s);
+  switch (bn) {
+    case 64: launch2<64, EPI>(p, x, w, out, N, K, ldo, ws_cap, s); break;
+    case 128: launch2<128, EPI>(p, x, w, out, N, K, ldo, ws_cap, s); break;
+    case 160: launch2<160, EPI>(p, x, w, out, N, K, ldo, ws_cap, s); break;
+    case 192: launch2<192, EPI>(p, x, w, out, N, K, ldo, ws_cap, s); break;
+    case 224: launch2<224, EPI>(p, x, w, out, N, K, ldo, ws_cap, s); break;
+    default: launch2<256, EPI>(p, x, w, out, N, K, ldo, ws_cap, s); break;
+  }
 }
 
 static void launch_2sm(const void* x, const void* w, const void* bias, void* out, int M, int N, int K, int ldo,
                        int epi, int force_splits, void* ws, size_t ws_cap, cudaStream_t s) {
   const bool act = is_act(epi);
   Params2 p;
-  p.ws = reinterpret_cast<float*>(ws);
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   p.M = M;
   p.n_out = act ? N / 2 : N;
   p.kblocks = (K + BK - 1) / BK;
-  int bn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  // token tile = the batch rounded up to a multiple of 32 (MMA N up to 256), so little tensor
+  // work is spent on padding; prefill-sized batches use 128 (gated) or 256 token tiles
+  int bn = M <= 64 ? 64 : M <= 128 ? 128 : ((M + 31) / 32) * 32;
   if (M > 256) bn = act ? 128 : 256;
   p.n_tiles = (N + (act ? 511 : 255)) / (act ? 512 : 256);
   p.m_tiles = (M + bn - 1) / bn;

@@ -220,13 +220,13 @@ def test_store_kv():
     _close(vc, vc2, 0, 0)
 
 
-@pytest.mark.parametrize("M", [5, 130, 256, 600])
+@pytest.mark.parametrize("M", [5, 130, 190, 220, 256, 600])
 @pytest.mark.parametrize("epi", [0, 1, 3])
 @pytest.mark.parametrize("wide,splits", [(0, 1), (1, 1), (0, 3), (1, 4), (-1, -1), (2, 1), (2, 2), (2, 3)])
 @pytest.mark.parametrize("blocked", [False, True])
 def test_gemm_variants(M, epi, wide, splits, blocked):
-    """Every tiling (128/256-row weight tiles, 2-SM pairs (wide=2), forced split-K) against the fp32 reference, run
-    twice so split-K workspace/counter re-zeroing is exercised, with bias."""
+    """Every tiling (128/256-row weight tiles, 2-SM pairs (wide=2) with 64..256-token tiles, forced split-K with
+    the cluster exchange) against the fp32 reference, run twice, with bias."""
     K, N = 1536, 768
     x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
     w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
