@@ -209,6 +209,38 @@ void attention_decode(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor
                         workspace.data_ptr(), stream());
 }
 
+// Paged decode attention over a host-built work list (page size 16/32/64). work: int32 [>= 8 * entries]
+// (two int4 per entry), n_work: int32 [1] = entries, ws: fp32 partials for ws_slots chunk slots,
+// counters: int32 [>= bs * nkv], zero on entry and left at zero.
+void attention_decode_paged(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor page_table,
+                            at::Tensor rows, at::Tensor kv_lens, at::Tensor work, at::Tensor n_work, at::Tensor ws,
+                            int64_t ws_slots, at::Tensor counters, double scale, int64_t window,
+                            c10::optional<at::Tensor> sinks, int64_t page) {
+  check_bf16(o, "o"); check_bf16(q, "q"); check_bf16(k_cache, "k_cache"); check_bf16(v_cache, "v_cache");
+  check_i32(rows, "rows"); check_i32(kv_lens, "kv_lens"); check_i32(work, "work"); check_i32(n_work, "n_work");
+  check_i32(counters, "counters");
+  check_cuda(ws, "ws"); check_dtype(ws, at::kFloat, "ws");
+  check_cuda(page_table, "page_table"); check_dtype(page_table, at::kInt, "page_table");
+  check_contig(q, "q"); check_contig(o, "o"); check_contig(work, "work");
+  const int64_t T = q.size(0), nq = q.size(1), hd = q.size(2), nkv = k_cache.size(1);
+  CHECK(hd == 64 || hd == 128, "attention head_dim must be 64 or 128");
+  CHECK(nq % nkv == 0 && nq / nkv <= 16, "decode supports up to 16 query heads per KV head");
+  CHECK(page == 16 || page == 32 || page == 64, "paged decode needs a page size of 16, 32 or 64");
+  CHECK(k_cache.stride(2) == 1 && k_cache.stride(1) == hd && k_cache.stride(0) % 8 == 0, "k_cache layout");
+  CHECK(v_cache.strides() == k_cache.strides() && v_cache.sizes() == k_cache.sizes(), "v_cache layout");
+  CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(k_cache.data_ptr()) % 16 == 0 &&
+            reinterpret_cast<uintptr_t>(v_cache.data_ptr()) % 16 == 0, "attention tensors must be 16-byte aligned");
+  CHECK(ws.numel() >= ws_slots * nkv * (nq / nkv) * (hd + 2), "decode partial workspace too small");
+  if (sinks.has_value()) { check_dtype(*sinks, at::kFloat, "sinks"); CHECK(sinks->numel() == nq, "sinks size"); }
+  const int rc = msgl_attention_decode_paged(
+      o.data_ptr(), q.data_ptr(), (int)(T * nq), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.size(0),
+      k_cache.stride(0), page_table.data_ptr<int32_t>(), page_table.stride(0), rows.data_ptr<int32_t>(),
+      kv_lens.data_ptr<int32_t>(), work.data_ptr<int32_t>(), n_work.data_ptr<int32_t>(), ws.data_ptr<float>(),
+      (int)ws_slots, counters.data_ptr<int32_t>(), nq, nkv, hd, page, scale, window,
+      sinks.has_value() ? sinks->data_ptr<float>() : nullptr, stream());
+  CHECK(rc == 0, "paged decode attention failed to launch (code ", rc, ")");
+}
+
 // ----- routed experts
 void gemm_grouped(at::Tensor out, at::Tensor xs, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor tile_count,
                   at::Tensor work, int64_t bn) {
@@ -320,6 +352,7 @@ PYBIND11_MODULE(_cuda, m) {
   m.def("rmsnorm", &rmsnorm);
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
   m.def("gemm", &gemm);
+  m.def("attention_decode_paged", &attention_decode_paged);
   m.def("gemm_ex", &gemm_ex);
   m.def("act_and_mul", &act_and_mul);
   m.def("store_kv", &store_kv);

@@ -10,10 +10,14 @@
 // K/V tiles of 64 keys are gathered through the page table with cp.async (double buffered, zero
 // fill past the end) into 128-byte-swizzled shared memory; QK^T and PV run on mma.sync bf16 with
 // an fp32 online softmax in the log2 domain.
+#include <algorithm>
 #include <cfloat>
 
 #include "api.h"
 #include "common.cuh"
+
+#include <cstring>
+#include <mutex>
 
 using namespace msgl;
 
@@ -602,6 +606,505 @@ extern "C" void msgl_attention_decode(void* o, const void* q, const void* k_cach
 }
 
 MSGL_ERROR_ACCESSOR(msgl_err_attention)
+
+// ================================================================================ decode (paged)
+// Persistent decode attention over a host-built work list, for page sizes of 16, 32 or 64 tokens.
+//
+// Work: each request's keys are cut into chunks of whole 64-key blocks; an entry is one chunk
+// (request b, blocks [blk0, blk1), chunk j of nchunks, partial slot base), and an item is an
+// (entry, kv head) pair. The host sorts entries longest first; CTA c of P takes items in snake
+// order (c, 2P-1-c, 2P+c, ...), which balances variable context lengths without atomics.
+//
+// Warp roles (192 threads, one CTA per SM):
+//   warp 5     scheduler: resolves items ahead of use (work entry, length, page-table row and the
+//              first slot of every page of the chunk) into a ring of kPdDesc smem descriptors, so
+//              the dependent global loads never stall the data path.
+//   warp 0     TMA producer: per item the query tile (16 rows, G valid), then per page one 3-D box
+//              (64 head dims x 1 head x page) per column half of K and of V from the
+//              [slots, kv heads, head dim] cache into a 128-byte-swizzled ring of kPdStages
+//              64-key stages.
+//   warps 1-4  each take 16 keys of every block (mma.sync m16n8k16 with the G query heads as MMA
+//              rows, online softmax in the log2 domain) and merge at the end of the item.
+// A single-chunk request writes its output directly; otherwise each chunk writes an fp32 partial,
+// and the last chunk of the (request, head) to arrive (gpu-scope acq_rel counter) combines them.
+namespace {
+
+constexpr int kPdStages = 5;
+constexpr int kPdConsumers = 4;
+constexpr int kPdDesc = 4;          // descriptor ring depth (items resolved ahead)
+constexpr int kPdMaxGroups = 256;   // pages per item (64 blocks of 16-token pages)
+constexpr int kPdMaxChunks = 128;   // chunks per request (combine scratch)
+constexpr int kPdThreads = 32 * (2 + kPdConsumers);
+
+struct PagedDecodeParams {
+  __nv_bfloat16* o;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  const int32_t* rows;
+  const int32_t* kv_lens;
+  const int4* work;       // per entry two int4: {b, blk0, blk1, j}, {nchunks, slot0, -, -}
+  const int32_t* n_work;  // number of entries (device scalar)
+  float* ws;              // partial o [slot][nkv][G][HD], then (m, l) [slot][nkv][G][2]
+  int ws_slots;
+  int32_t* counters;      // [bs][nkv] arrivals; every launch leaves them at zero
+  const float* sinks;
+  int nq, nkv, group, page;
+  float scale_log2;
+  int window;
+};
+
+// one resolved item
+struct PdDesc {
+  int b, kvh, first, blk1, j, nchunks, slot0, L, lo, valid, pad[6];
+  int slots[kPdMaxGroups];  // first cache slot of each page of blocks [first, blk1)
+};
+
+template <int HD>
+struct PdCfg {
+  static constexpr int kHalfTile = 64 * 128;            // 64 rows x 64 head dims (bf16)
+  static constexpr int kTile = 64 * HD * 2;             // one 64-key K or V block
+  static constexpr int kStage = 2 * kTile;
+  static constexpr int kQ = 16 * HD * 2;                // 16 query rows (G <= 16, padded)
+  // merge scratch (4 warps' m, l, o rows), reused by the combine ([chunks][16] m and weights + [16])
+  static constexpr int kMerge = std::max((kPdConsumers * 16 * HD + 2 * kPdConsumers * 16) * 4,
+                                         (2 * kPdMaxChunks * 16 + 16) * 4);
+  static constexpr int kSmem = 1024 + kPdStages * kStage + 2 * kQ + kMerge + kPdDesc * (int)sizeof(PdDesc) + 256;
+};
+
+// byte offset of (row, 16-byte chunk c) in a [rows][HD] bf16 tile stored as HD/64 column halves
+// of [rows][128 B] with the TMA 128-byte swizzle (chunk XOR row % 8)
+__device__ __forceinline__ uint32_t swz_tma(int row, int c, int rows) {
+  return (uint32_t)((c >> 3) * rows * 128 + row * 128 + (((c & 7) ^ (row & 7)) << 4));
+}
+
+template <int HD>
+__device__ __forceinline__ void qk_tma(float (&s)[2][4], const uint32_t (&qf)[HD / 16][4], uint32_t sk, int key0) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int n = 0; n < 2; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < HD / 16; ++kk) {
+    const int idx = lane >> 3;
+    const int key = key0 + (idx >> 1) * 8 + (lane & 7);
+    const int chunk = kk * 2 + (idx & 1);
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4(sk + swz_tma(key, chunk, 64), b0, b1, b2, b3);
+    mma_bf16(s[0], qf[kk], b0, b1);
+    mma_bf16(s[1], qf[kk], b2, b3);
+  }
+}
+
+template <int HD>
+__device__ __forceinline__ void pv_tma(float (&o)[HD / 8][4], const uint32_t (&pf)[4], uint32_t sv, int key0) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int n = 0; n < HD / 8; n += 2) {
+    const int idx = lane >> 3;
+    const int key = key0 + (idx & 1) * 8 + (lane & 7);
+    const int chunk = n + (idx >> 1);
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4_t(sv + swz_tma(key, chunk, 64), b0, b1, b2, b3);
+    mma_bf16(o[n], pf, b0, b1);
+    mma_bf16(o[n + 1], pf, b2, b3);
+  }
+}
+
+__device__ __forceinline__ void pd_consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kPdConsumers * 32) : "memory"); }
+
+// item r of this CTA in snake order; false when the CTA has no more work
+__device__ __forceinline__ bool pd_item(const PagedDecodeParams& p, int n_items, int r, int& e, int& kvh) {
+  const int P = gridDim.x, c = blockIdx.x;
+  const int idx = r * P + ((r & 1) ? (P - 1 - c) : c);
+  if (idx >= n_items) return false;
+  e = idx / p.nkv;
+  kvh = idx - e * p.nkv;
+  return true;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kPdThreads, 1)
+paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                    const __grid_constant__ CUtensorMap tq, PagedDecodeParams p) {
+  using C = PdCfg<HD>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint8_t* sq = ring + kPdStages * C::kStage;
+  float* red = reinterpret_cast<float*>(sq + 2 * C::kQ);
+  PdDesc* desc = reinterpret_cast<PdDesc*>(reinterpret_cast<uint8_t*>(red) + C::kMerge);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(desc + kPdDesc);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kPdStages;
+  uint64_t* qfull = bars + 2 * kPdStages;
+  uint64_t* qempty = qfull + 2;
+  uint64_t* dfull = qempty + 2;
+  uint64_t* dempty = dfull + kPdDesc;
+  int* flag = reinterpret_cast<int*>(dempty + kPdDesc);
+  volatile int* abort_flag = flag + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPdStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kPdConsumers);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qfull[i], 1);
+      mbar_init(&qempty[i], kPdConsumers);
+    }
+    for (int i = 0; i < kPdDesc; ++i) {
+      mbar_init(&dfull[i], 1);
+      mbar_init(&dempty[i], 1 + kPdConsumers);  // producer + consumer warps
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+    prefetch_tmap(&tq);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch();
+  const int n_items = *p.n_work * p.nkv;
+  const int G = p.group;
+
+  if (warp == 5) {
+    // ------------------------------------------------------------------ scheduler
+    const int g = p.page, gpb = 64 / g;
+    int e, kvh;
+    for (int r = 0;; ++r) {
+      const bool valid = pd_item(p, n_items, r, e, kvh);
+      const int d = r % kPdDesc;
+      if (lane == 0 && !mbar_wait(&dempty[d], ((r / kPdDesc) & 1) ^ 1, 430)) break;
+      __syncwarp();
+      PdDesc& D = desc[d];
+      if (valid) {
+        const int4 w0 = p.work[2 * e];
+        const int4 w1 = p.work[2 * e + 1];
+        const int b = w0.x;
+        const int L = p.kv_lens[b];
+        const int lo = p.window > 0 ? max(0, L - p.window) : 0;
+        const int first = max(w0.y, lo / 64), blk1 = w0.z;
+        const int32_t* pt = p.page_table + (int64_t)p.rows[b] * p.pt_stride;
+        const int ngroups = min(kPdMaxGroups, max(0, blk1 - first) * gpb);
+        for (int gi = lane; gi < ngroups; gi += 32) {
+          const int pos = first * 64 + gi * g;
+          D.slots[gi] = pos < L ? pt[pos] : 0;
+        }
+        if (lane == 0) {
+          D.b = b; D.kvh = kvh; D.first = first; D.blk1 = first + ngroups / gpb; D.j = w0.w;
+          D.nchunks = w1.x; D.slot0 = w1.y; D.L = L; D.lo = lo; D.valid = 1;
+        }
+      } else if (lane == 0) {
+        D.valid = 0;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dfull[d]);  // release: the descriptor writes above
+      if (!valid) break;
+    }
+  } else if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    const int g = p.page, gpb = 64 / g;
+    int stage = 0;
+    uint32_t phase = 0;
+    if (lane == 0) {
+      for (int r = 0;; ++r) {
+        const int d = r % kPdDesc;
+        if (!mbar_wait(&dfull[d], (r / kPdDesc) & 1, 440)) break;
+        const PdDesc& D = desc[d];
+        if (!D.valid) break;
+        const int qb = r & 1;
+        bool ok = mbar_wait(&qempty[qb], ((r >> 1) & 1) ^ 1, 441);
+        if (ok) {
+          mbar_expect_tx(&qfull[qb], C::kQ);
+#pragma unroll
+          for (int h = 0; h < HD / 64; ++h)
+            tma_load_2d(sq + qb * C::kQ + h * 16 * 128, &tq, &qfull[qb], h * 64, D.b * p.nq + D.kvh * G);
+        }
+        const int ngroups = (D.blk1 - D.first) * gpb;
+        for (int gi = 0; ok && gi < ngroups; ++gi) {
+          const int sub = gi % gpb;
+          if (sub == 0) {
+            if (!mbar_wait(&empty[stage], phase ^ 1, 442)) { ok = false; break; }
+            mbar_expect_tx(&full[stage], C::kStage);
+          }
+          const int s0 = D.slots[gi];
+          uint8_t* kt = ring + stage * C::kStage;
+#pragma unroll
+          for (int h = 0; h < HD / 64; ++h) {
+            tma_load_3d(kt + h * C::kHalfTile + sub * g * 128, &tk, &full[stage], h * 64, D.kvh, s0);
+            tma_load_3d(kt + C::kTile + h * C::kHalfTile + sub * g * 128, &tv, &full[stage], h * 64, D.kvh, s0);
+          }
+          if (sub == gpb - 1 && ++stage == kPdStages) { stage = 0; phase ^= 1; }
+        }
+        mbar_arrive(&dempty[d]);
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ consumers
+    const int cw = warp - 1;
+    const int ctid = threadIdx.x - 32;
+    float* rm = red;
+    float* rl = red + kPdConsumers * 16;
+    float* ro = red + 2 * kPdConsumers * 16;
+    int stage = 0;
+    uint32_t phase = 0;
+    // A warp whose wait times out (error recorded) raises abort_flag, skips the rest of the item
+    // and still reaches the item's first consumer barrier, after which all consumer warps leave
+    // together; so the named barriers never wait for a warp that has gone.
+    bool dead = false;
+    for (int r = 0;; ++r) {
+      const int d = r % kPdDesc;
+      if (!dead && !mbar_wait(&dfull[d], (r / kPdDesc) & 1, 450)) { dead = true; *abort_flag = 1; }
+      const PdDesc& D = desc[d];
+      if (!dead && !D.valid) break;  // end of work: every consumer warp reads the same descriptor
+      const int b = D.b, kvh = D.kvh, first = D.first, blk1 = D.blk1, j = D.j, nchunks = D.nchunks;
+      const int slot0 = D.slot0, L = D.L, lo = D.lo;
+
+      const int qb = r & 1;
+      if (!dead && !mbar_wait(&qfull[qb], (r >> 1) & 1, 451)) { dead = true; *abort_flag = 1; }
+      uint32_t qf[HD / 16][4];
+      const uint32_t qbase = smem_u32(sq + qb * C::kQ);
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; ++kk)
+        ldsm_x4(qbase + swz_tma(lane & 15, kk * 2 + (lane >> 4), 16), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&qempty[qb]);
+
+      float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+      float o[HD / 8][4];
+#pragma unroll
+      for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      for (int blk = first; blk < blk1 && !dead; ++blk) {
+        if (!mbar_wait(&full[stage], phase, 452)) { dead = true; *abort_flag = 1; break; }
+        const uint32_t sk = smem_u32(ring + stage * C::kStage), sv = sk + C::kTile;
+        float s[2][4];
+        qk_tma<HD>(s, qf, sk, cw * 16);
+        const int k0 = blk * 64 + cw * 16;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const int kp = k0 + nt * 8 + 2 * (lane & 3) + (x & 1);
+            s[nt][x] = (kp >= lo && kp < L) ? s[nt][x] * p.scale_log2 : -INFINITY;
+          }
+        float so[2];
+        softmax_update<2>(s, m, l, so);
+#pragma unroll
+        for (int i = 0; i < HD / 8; ++i) {
+          o[i][0] *= so[0]; o[i][1] *= so[0]; o[i][2] *= so[1]; o[i][3] *= so[1];
+        }
+        uint32_t pf[1][4];
+        pack_p<2>(pf, s);
+        pv_tma<HD>(o, pf[0], sv, cw * 16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == kPdStages) { stage = 0; phase ^= 1; }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dempty[d]);  // descriptor fields are in registers now
+
+      // merge the 4 warps' rows (lane/4 and lane/4 + 8)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int rr = (lane >> 2) + 8 * h;
+        if ((lane & 3) == 0) {
+          rm[cw * 16 + rr] = m[h];
+          rl[cw * 16 + rr] = l[h];
+        }
+#pragma unroll
+        for (int i = 0; i < HD / 8; ++i) {
+          const int col = i * 8 + 2 * (lane & 3);
+          *reinterpret_cast<float2*>(&ro[(cw * 16 + rr) * HD + col]) = make_float2(o[i][2 * h], o[i][2 * h + 1]);
+        }
+      }
+      pd_consumer_sync();
+      if (*abort_flag) break;
+      const int64_t pslot = ((int64_t)(slot0 + j) * p.nkv + kvh) * G;  // partial row base
+      float* ws_o = p.ws;
+      float* ws_ml = p.ws + (int64_t)p.ws_slots * p.nkv * G * HD;
+      for (int idx = ctid; idx < G * HD; idx += kPdConsumers * 32) {
+        const int rr = idx / HD, col = idx - rr * HD;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kPdConsumers; ++w) mx = fmaxf(mx, rm[w * 16 + rr]);
+        const float base = mx == -INFINITY ? 0.f : mx;
+        float ll = 0.f, acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < kPdConsumers; ++w) {
+          const float f = exp2f(rm[w * 16 + rr] - base);
+          ll += rl[w * 16 + rr] * f;
+          acc += ro[(w * 16 + rr) * HD + col] * f;
+        }
+        const int head = kvh * G + rr;
+        if (nchunks == 1) {
+          float f = 1.f;
+          if (p.sinks != nullptr) {
+            const float skv = p.sinks[head] * kLog2e;
+            const float mn = fmaxf(mx, skv);
+            f = exp2f(base - mn);
+            ll = ll * f + exp2f(skv - mn);
+          }
+          p.o[((int64_t)b * p.nq + head) * HD + col] = __float2bfloat16(ll > 0.f ? acc * f / ll : 0.f);
+        } else {
+          ws_o[(pslot + rr) * HD + col] = acc;
+          if (col == 0) {
+            ws_ml[(pslot + rr) * 2] = mx;
+            ws_ml[(pslot + rr) * 2 + 1] = ll;
+          }
+        }
+      }
+      if (nchunks > 1) {
+        // Publish: the barrier orders every consumer thread's partial stores before thread 0's
+        // release (cumulative) add; the last arriver's acquire plus the next barrier orders the
+        // other chunks' partials before this CTA's combine loads.
+        pd_consumer_sync();
+        if (ctid == 0) {
+          int32_t* cnt = p.counters + (int64_t)b * p.nkv + kvh;
+          int old;
+          asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(old) : "l"(cnt) : "memory");
+          const int last = old == nchunks - 1;
+          if (last) *cnt = 0;
+          *flag = last;
+        }
+        pd_consumer_sync();
+        if (*flag) {
+          // combine every chunk's partial of (b, kvh): (m, l) of all chunks into smem in one round
+          // of loads, per-row weights, then each thread sums 4 columns over the chunks
+          float* cm = red;                                  // [nchunks][G]
+          float* cwt = red + kPdMaxChunks * 16;             // [nchunks][G] weights
+          float* cinv = red + 2 * kPdMaxChunks * 16;        // [G]
+          const int nc = min(nchunks, kPdMaxChunks);
+          for (int i = ctid; i < nc * G; i += kPdConsumers * 32) {
+            const int c = i / G, rr = i - c * G;
+            const int64_t rowi = ((int64_t)(slot0 + c) * p.nkv + kvh) * G + rr;
+            const float2 ml = __ldcg(reinterpret_cast<const float2*>(ws_ml) + rowi);
+            cm[i] = ml.x;
+            cwt[i] = ml.y;
+          }
+          pd_consumer_sync();
+          for (int rr = ctid; rr < G; rr += kPdConsumers * 32) {
+            float mx = p.sinks != nullptr ? p.sinks[kvh * G + rr] * kLog2e : -INFINITY;
+            const float sink = mx;
+            for (int c = 0; c < nc; ++c) mx = fmaxf(mx, cm[c * G + rr]);
+            const float base = mx == -INFINITY ? 0.f : mx;
+            float ll = p.sinks != nullptr ? exp2f(sink - base) : 0.f;
+            for (int c = 0; c < nc; ++c) {
+              const float f = exp2f(cm[c * G + rr] - base);
+              ll += cwt[c * G + rr] * f;
+              cwt[c * G + rr] = f;
+            }
+            cinv[rr] = ll > 0.f ? 1.f / ll : 0.f;
+          }
+          pd_consumer_sync();
+          for (int i = ctid; i < G * HD / 4; i += kPdConsumers * 32) {
+            const int rr = i / (HD / 4), c4 = i - rr * (HD / 4);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+            for (int c = 0; c < nc; ++c) {
+              const int64_t rowi = ((int64_t)(slot0 + c) * p.nkv + kvh) * G + rr;
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(ws_o + rowi * HD) + c4);
+              const float f = cwt[c * G + rr];
+              acc.x += v.x * f; acc.y += v.y * f; acc.z += v.z * f; acc.w += v.w * f;
+            }
+            const float inv = cinv[rr];
+            __nv_bfloat16* dst = p.o + ((int64_t)b * p.nq + kvh * G + rr) * HD + c4 * 4;
+            *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16(acc.x * inv, acc.y * inv), pack_bf16(acc.z * inv, acc.w * inv));
+          }
+        }
+      }
+      pd_consumer_sync();  // merge scratch and flag are reused by the next item
+    }
+  }
+}
+
+typedef CUresult (*PdEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PdEncodeFn pd_encode_fn() {
+  static PdEncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PdEncodeFn>(ptr);
+  });
+  return fn;
+}
+
+bool pd_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+               const cuuint32_t* box) {
+  memset(m, 0, sizeof(*m));
+  PdEncodeFn fn = pd_encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int HD>
+int run_paged_decode(const PagedDecodeParams& p, const void* q, int q_rows, const void* k, const void* v,
+                     int64_t num_slots, int64_t cache_stride, cudaStream_t s) {
+  using C = PdCfg<HD>;
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(paged_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    set = true;
+  }
+  CUtensorMap tk, tv, tq;
+  const cuuint64_t kdims[3] = {(cuuint64_t)HD, (cuuint64_t)p.nkv, (cuuint64_t)num_slots};
+  const cuuint64_t kstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)cache_stride * 2};
+  const cuuint32_t kbox[3] = {64, 1, (cuuint32_t)p.page};
+  const cuuint64_t qdims[2] = {(cuuint64_t)HD, (cuuint64_t)q_rows};
+  const cuuint64_t qstr[1] = {(cuuint64_t)HD * 2};
+  const cuuint32_t qbox[2] = {64, 16};
+  if (!pd_encode(&tk, k, 3, kdims, kstr, kbox) || !pd_encode(&tv, v, 3, kdims, kstr, kbox) ||
+      !pd_encode(&tq, q, 2, qdims, qstr, qbox))
+    return 2;
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  msgl_launch(paged_decode_kernel<HD>, dim3(sms), dim3(kPdThreads), C::kSmem, s, 1, tk, tv, tq, p);
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int msgl_attention_decode_paged(void* o, const void* q, int q_rows, const void* k_cache,
+                                           const void* v_cache, int64_t num_slots, int64_t cache_stride,
+                                           const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
+                                           const int32_t* kv_lens, const int32_t* work, const int32_t* n_work,
+                                           float* ws, int ws_slots, int32_t* counters, int nq, int nkv, int hd,
+                                           int page, float sm_scale, int window, const float* sinks,
+                                           cudaStream_t s) {
+  if (nq % nkv != 0 || nq / nkv > 16 || (hd != 64 && hd != 128) || (page != 16 && page != 32 && page != 64))
+    return 3;
+  PagedDecodeParams p;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.page_table = page_table;
+  p.pt_stride = pt_stride;
+  p.rows = rows;
+  p.kv_lens = kv_lens;
+  p.work = reinterpret_cast<const int4*>(work);
+  p.n_work = n_work;
+  p.ws = ws;
+  p.ws_slots = ws_slots;
+  p.counters = counters;
+  p.sinks = sinks;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.group = nq / nkv;
+  p.page = page;
+  p.scale_log2 = sm_scale * kLog2e;
+  p.window = window;
+  return hd == 64 ? run_paged_decode<64>(p, q, q_rows, k_cache, v_cache, num_slots, cache_stride, s)
+                  : run_paged_decode<128>(p, q, q_rows, k_cache, v_cache, num_slots, cache_stride, s);
+}
 
 // =================================================================================================
 // Allocation-free decode attention entry point (an addition of this engine: the reference has no

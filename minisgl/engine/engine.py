@@ -19,6 +19,7 @@ import torch
 import torch.distributed as dist
 
 from minisgl.attention import create_attention_backend
+from minisgl.attention.paged import PAGED_DECODE_PAGES
 from minisgl.core import Batch, Context, Req, get_global_ctx, reset_global_ctx, set_global_ctx
 from minisgl.kvcache import create_kvcache_pool
 from minisgl.layers import set_rope_device
@@ -58,6 +59,12 @@ class Engine:
         set_tp_info(info.rank, info.size)
         self.device = torch.device(config.device or f"cuda:{info.rank}")
         self.is_cuda = self.device.type == "cuda"
+        if self.is_cuda and config.page_size not in PAGED_DECODE_PAGES:
+            # The decode kernel streams whole pages with TMA, so CUDA runs use 16/32/64-token pages
+            # (the reference applies the same rule to its B200 backend:
+            # python/minisgl/engine/engine.py, _adjust_config).
+            logger.warning_rank0(f"page size {config.page_size} overridden to 64 (CUDA decode needs 16, 32 or 64)")
+            object.__setattr__(config, "page_size", 64)
         torch.manual_seed(config.seed)
         if self.is_cuda:
             torch.cuda.set_device(self.device)
@@ -217,6 +224,9 @@ class Engine:
     def upload_plan(self, batch: Batch, plan: "BatchPlan") -> dict:
         """Copy the packed plan to the device, apply page-table writes, derive out_loc and the
         attention metadata. Runs on the current (scheduler) stream."""
+        plan_arrays = getattr(self.attn_backend, "plan_arrays", None)
+        if plan_arrays is not None:
+            plan.extra.update(plan_arrays(batch, plan.kv_lens))
         host, views = plan.pack()
         if self.is_cuda:
             dev_buf = host.pin_memory().to(self.device, non_blocking=True)
@@ -299,14 +309,15 @@ class BatchPlan:
         )
         self.max_q_len = max(ext) if ext else 0
         self.max_kv_len = int(self.kv_lens.max()) if len(reqs) else 0
+        self.extra: Dict[str, np.ndarray] = {}  # backend-owned segments appended to the upload
 
     _ORDER = ("positions", "tok_rows", "input_ids", "pt_rows", "pt_pos", "pt_slots",
               "req_rows", "kv_lens", "cu_q", "sample_rows")
 
     def pack(self):
         parts, views, off = [], {}, 0
-        for name in self._ORDER:
-            a = getattr(self, name)
+        for name in self._ORDER + tuple(self.extra):
+            a = self.extra[name] if name in self.extra else getattr(self, name)
             n = len(a)
             views[name] = (off, off + n)
             pad = (-n) % 4  # keep every segment 16-byte aligned on the device

@@ -175,6 +175,61 @@ def test_attention_decode(hd, nq, nkv, splits, window, sinks):
     _close(o, e, 2e-2, 2e-2)
 
 
+def _paged_pages_setup(lens_kv, nq, nkv, hd, page, seed=0):
+    """Page-granular cache layout (what the engine allocates): each request owns whole pages of `page`
+    consecutive slots, in shuffled page order; the page table stays token-granular."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    B = len(lens_kv)
+    npages = sum((n + page - 1) // page for n in lens_kv) + 3
+    slots = npages * page
+    kc = torch.randn(slots, nkv, hd, generator=g).to(DEV, torch.bfloat16)
+    vc = torch.randn(slots, nkv, hd, generator=g).to(DEV, torch.bfloat16)
+    L = max(lens_kv)
+    pt = torch.full((B + 3, (L + 63) // 64 * 64 + 64), 7, dtype=torch.int32)  # stale entries past the end
+    perm = torch.randperm(npages, generator=g)
+    used = 0
+    rows = torch.arange(B, dtype=torch.int32) + 2
+    for b, n in enumerate(lens_kv):
+        for j in range((n + page - 1) // page):
+            pt[rows[b], j * page : (j + 1) * page] = int(perm[used]) * page + torch.arange(page, dtype=torch.int32)
+            used += 1
+    q = torch.randn(B, nq, hd, generator=g).to(DEV, torch.bfloat16)
+    cu = torch.arange(B + 1, dtype=torch.int32)
+    return q, kc, vc, pt.to(DEV), rows.to(DEV), cu.to(DEV), torch.tensor(lens_kv, dtype=torch.int32, device=DEV)
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 40, 8), (64, 64, 8), (128, 8, 8), (128, 16, 1)])
+@pytest.mark.parametrize("page", [16, 32, 64])
+@pytest.mark.parametrize("window,sinks", [(-1, False), (100, True)])
+@pytest.mark.parametrize("num_ctas", [148, 3])
+def test_attention_decode_paged(hd, nq, nkv, page, window, sinks, num_ctas):
+    """Persistent paged decode (work list, TMA page loads, last-arriver combine) against the fp32
+    reference; few CTAs force multi-chunk requests; run twice to check the counters return to zero."""
+    from minisgl.attention.paged import decode_work_list
+    import numpy as np
+
+    lens_kv = [1, 5, 64, 65, 300, 1000, 777, 4000, 129]
+    B = len(lens_kv)
+    q, kc, vc, pt, rows, cu, kvl = _paged_pages_setup(lens_kv, nq, nkv, hd, page)
+    sk = torch.randn(nq, device=DEV) if sinks else None
+    work, n = decode_work_list(np.array(lens_kv), nkv, num_ctas)
+    work_d = torch.from_numpy(work).to(DEV)
+    n_d = torch.tensor([n], dtype=torch.int32, device=DEV)
+    G = nq // nkv
+    ws = torch.empty(n * nkv * G * (hd + 2), dtype=torch.float32, device=DEV)
+    counters = torch.zeros(B * nkv, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(hd)
+    e = ref.paged_attention(q.cpu(), kc.cpu(), vc.cpu(), pt.cpu(), rows.cpu(), cu.cpu(), kvl.cpu(), scale,
+                            window, None if sk is None else sk.cpu())
+    for _ in range(2):
+        o = torch.full_like(q, float("nan"))
+        _c().attention_decode_paged(o, q, kc, vc, pt, rows, kvl, work_d, n_d, ws, n, counters, scale, window, sk,
+                                    page)
+        _close(o, e, 2e-2, 2e-2)
+        assert int(counters.abs().sum()) == 0
+    assert _c().get_error() == (0, 0)
+
+
 def test_argmax_and_greedy_sample():
     from minisgl import ops
 
