@@ -338,6 +338,24 @@ void peer_collective(int64_t mode, at::Tensor out, at::Tensor in, std::vector<in
                        reinterpret_cast<uint32_t*>(state.data_ptr()), timeout_ns, stream());
 }
 
+// NVLS all-reduce + residual add + RMSNorm over a multicast-bound symmetric buffer (uc/mc: this
+// rank's and the multicast address of the same allocation).
+void nvls_allreduce_rmsnorm(int64_t uc, int64_t mc, int64_t rank, int64_t world, at::Tensor x, at::Tensor residual, at::Tensor w,
+                            at::Tensor out, double eps, int64_t cap_bytes, at::Tensor state, int64_t timeout_ns,
+                            bool first) {
+  check_bf16(x, "x"); check_bf16(residual, "residual"); check_bf16(w, "w"); check_bf16(out, "out");
+  check_contig(x, "x"); check_contig(residual, "residual"); check_contig(out, "out"); check_contig(w, "w");
+  check_cuda(state, "state"); check_dtype(state, at::kInt, "state");
+  CHECK(state.numel() >= 2 * msgl_nvls_grid(), "nvls state tensor too small");
+  const int64_t H = x.size(-1), T = x.numel() / H;
+  CHECK(residual.numel() == x.numel() && out.numel() == x.numel() && w.numel() == H, "nvls norm shapes");
+  const int rc = msgl_nvls_allreduce_rmsnorm(reinterpret_cast<void*>(uc), reinterpret_cast<void*>(mc), rank, world,
+                                             x.data_ptr(), residual.data_ptr(), w.data_ptr(), out.data_ptr(), T, H,
+                                             eps, cap_bytes, reinterpret_cast<uint32_t*>(state.data_ptr()),
+                                             timeout_ns, first ? 1 : 0, stream());
+  CHECK(rc == 0, "nvls all-reduce rejected its arguments (code ", rc, ")");
+}
+
 std::tuple<int64_t, int64_t> get_error() {
   int info = 0;
   const int code = msgl_get_error(&info);
@@ -377,6 +395,9 @@ PYBIND11_MODULE(_cuda, m) {
   m.def("ipc_close", &ipc_close);
   m.def("peer_grid", []() { return msgl_peer_grid(); });
   m.def("peer_collective", &peer_collective);
+  m.def("nvls_grid", []() { return msgl_nvls_grid(); });
+  m.def("nvls_flag_bytes", []() { return msgl_nvls_flag_bytes(); });
+  m.def("nvls_allreduce_rmsnorm", &nvls_allreduce_rmsnorm);
   m.def("num_sms", []() { return msgl_num_sms(); });
   m.def("gemm_splits", [](int64_t M, int64_t N, int64_t K) { return msgl_gemm_pick_splits(M, N, K); });
 }

@@ -94,6 +94,13 @@ int msgl_attention_decode_noalloc(void* o, const void* q, const void* k_cache, c
                                   int64_t cache_stride, float sm_scale, int window, const float* sinks,
                                   int num_splits, cudaStream_t s);
 
+// ----- NVLS (multicast) all-reduce fused with residual add + RMSNorm (see comm.cu)
+int msgl_nvls_grid();
+int msgl_nvls_flag_bytes();
+int msgl_nvls_allreduce_rmsnorm(void* uc, void* mc, int rank, int world, const void* x, void* residual, const void* w,
+                                void* out, int T, int H, float eps, int64_t cap_bytes, uint32_t* state,
+                                int64_t timeout_ns, int first, cudaStream_t s);
+
 // ----- peer-memory collectives (CUDA IPC over NVLink)
 int msgl_peer_flag_bytes();
 void* msgl_peer_alloc(int64_t bytes);

@@ -12,6 +12,7 @@
 // per rank for large ones; all-gather copies every peer's slice. Waits never exceed a time limit: on expiry the kernel
 // records kErrPeerTimeout and returns, leaving the context usable. No multicast is used.
 #include <cstdio>
+#include <cstdlib>
 
 #include "api.h"
 #include "common.cuh"
@@ -22,7 +23,8 @@ namespace {
 
 constexpr int kMaxRanks = 8;
 constexpr int kMaxBlocks = 256;
-constexpr int kFlagBytes = kMaxBlocks * kMaxRanks * 4;  // flags[b][src]
+constexpr int kFlagLine = 128;                          // flags[b][0..kMaxRanks) share one line per CTA
+constexpr int kFlagBytes = kMaxBlocks * kFlagLine;      // flags[b][src]
 
 struct PeerBufs {
   uint8_t* base[kMaxRanks];  // symmetric buffer of every rank (own included)
@@ -44,9 +46,9 @@ __device__ bool block_barrier(const PeerBufs& bufs, int rank, int world, int b, 
   bool ok = true;
   if (threadIdx.x < world) {
     __threadfence_system();
-    uint32_t* remote = reinterpret_cast<uint32_t*>(bufs.base[threadIdx.x]) + b * kMaxRanks + rank;
+    uint32_t* remote = reinterpret_cast<uint32_t*>(bufs.base[threadIdx.x] + b * kFlagLine) + rank;
     st_release_sys(remote, epoch);
-    const uint32_t* mine = reinterpret_cast<const uint32_t*>(bufs.base[rank]) + b * kMaxRanks + threadIdx.x;
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(bufs.base[rank] + b * kFlagLine) + threadIdx.x;
     const uint64_t t0 = globaltimer_ns();
     while ((int)(ld_acquire_sys(mine) - epoch) < 0) {
       if (globaltimer_ns() - t0 > timeout_ns) {
@@ -206,5 +208,256 @@ void msgl_peer_collective(void* const* bases, int rank, int world, int mode, voi
 }
 
 }  // extern "C"
+
+
+// =================================================================================================
+// NVLink SHARP (NVLS) all-reduce fused with residual add + RMSNorm for decode-sized activations.
+// Every rank's symmetric buffer is bound to one NVLink multicast object; a multimem store or
+// reduction on the multicast address reaches the same offset on every GPU through the switch.
+// Buffer: [flags: kNvlsGrid x 128 B | data parity 0 | data parity 1], cap bytes per parity.
+// CTA b owns rows b, b + kNvlsGrid, ... of the [T, H] activation on every rank; a per-CTA call
+// counter in device memory (CUDA-graph replays stay in lockstep) gives the parity and the epoch.
+//
+// Small messages (world x T x H x 4 <= 2 MiB), "LL" form, no barrier: every rank stores its rows
+// with multimem.st as 8-byte {bf16x2 data, epoch} words into its own slot on every GPU; a reader
+// spins on its local copy until every word carries the epoch (an aligned 8-byte store lands
+// whole), so data and synchronisation arrive together in one one-way NVLink trip.
+// Larger messages, "reduce" form: stage the rows locally, one barrier per CTA (multimem.red of a
+// per-CTA counter on every GPU, bounded spin on the local copy), then multimem.ld_reduce returns
+// the sum over all ranks (fp32 accumulation in the switch).
+// Both then add the residual, store the new residual (bf16) and the RMS-normalised row (bf16).
+// Parity reuse is safe: a CTA writes parity p again only in the call after next, which it starts
+// after seeing every peer's data of the next call, which each peer sends after finishing its reads
+// of parity p.
+// Virtual aliases: staging stores (unicast address) and switch reads (multicast address) meet in
+// the owning GPU's L2 after the sys-scope release, so no proxy fence is issued per access.
+namespace {
+
+constexpr int kNvlsGrid = 128;
+constexpr int kNvlsThreads = 256;
+constexpr int kNvlsFlagStride = 128;  // one flag per 128-byte line: the per-CTA atomics never share a line
+constexpr int kNvlsFlagBytes = kNvlsGrid * kNvlsFlagStride;
+constexpr int kNvlsMaxVec = 8;  // 16-byte vectors per thread per row: H <= 8 * 8 * 256 = 16384
+
+struct NvlsParams {
+  uint8_t* uc;        // this rank's symmetric buffer
+  uint8_t* mc;        // multicast address of the same buffer
+  int rank, world;
+  const uint4* x;     // [T, H] partial (bf16)
+  uint4* residual;    // [T, H] bf16, updated in place (residual += sum)
+  const uint4* w;     // [H] bf16 norm weight
+  uint4* out;         // [T, H] bf16 normalised
+  int T, H;
+  float eps;
+  int64_t cap;
+  uint32_t* state;    // [kNvlsGrid][2] per CTA: calls (parity, LL epoch), reduce-form calls (barrier target)
+  uint64_t timeout_ns;
+  int first;          // 1: residual is not read (it becomes the sum)
+  int ll;             // 1: LL form (see above), 0: reduce form
+};
+
+__device__ __forceinline__ void mm_red_release_add(uint8_t* mc_addr, uint32_t v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc_addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const uint8_t* mc_addr) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc_addr)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ void mm_st_b64(uint8_t* mc_addr, uint64_t v) {
+  asm volatile("multimem.st.relaxed.sys.global.b64 [%0], %1;" ::"l"(mc_addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ void ld_relaxed_v2_u64(const uint8_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  f[0] = bf16_lo(u.x); f[1] = bf16_hi(u.x); f[2] = bf16_lo(u.y); f[3] = bf16_hi(u.y);
+  f[4] = bf16_lo(u.z); f[5] = bf16_hi(u.z); f[6] = bf16_lo(u.w); f[7] = bf16_hi(u.w);
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
+}
+
+// LL form: sum over every rank's slot of one 8-element group (4 words {bf16x2, epoch}); spins on
+// the local copy until all words carry `epoch`. Returns false on timeout.
+__device__ __forceinline__ bool ll_gather8(const uint8_t* base, int64_t slot_bytes, int world, int64_t goff,
+                                           uint32_t epoch, uint64_t timeout_ns, float (&f)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = 0.f;
+  uint64_t t0 = 0;
+  for (int r = 0; r < world; ++r) {
+    const uint8_t* src = base + r * slot_bytes + goff;
+    uint64_t w0, w1, w2, w3;
+    while (true) {
+      ld_relaxed_v2_u64(src, w0, w1);
+      ld_relaxed_v2_u64(src + 16, w2, w3);
+      if ((uint32_t)(w0 >> 32) == epoch && (uint32_t)(w1 >> 32) == epoch && (uint32_t)(w2 >> 32) == epoch &&
+          (uint32_t)(w3 >> 32) == epoch)
+        break;
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > timeout_ns) return false;
+    }
+    const uint32_t d[4] = {(uint32_t)w0, (uint32_t)w1, (uint32_t)w2, (uint32_t)w3};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      f[2 * j] += bf16_lo(d[j]);
+      f[2 * j + 1] += bf16_hi(d[j]);
+    }
+  }
+  // the all-reduce result is bf16, as with the reduce form
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    const uint32_t q = pack_bf16(f[j], f[j + 1]);
+    f[j] = bf16_lo(q);
+    f[j + 1] = bf16_hi(q);
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParams p) {
+  const int b = blockIdx.x, tid = threadIdx.x;
+  pdl_wait();
+  pdl_launch();
+  __shared__ uint32_t s_calls, s_rcalls;
+  __shared__ float s_red[kNvlsThreads / 32];
+  if (tid == 0) {
+    s_calls = p.state[2 * b] + 1;
+    s_rcalls = p.state[2 * b + 1] + (p.ll ? 0 : 1);
+  }
+  __syncthreads();
+  const uint32_t calls = s_calls, rcalls = s_rcalls;
+  const size_t off = kNvlsFlagBytes + (size_t)(calls & 1) * p.cap;
+  const int nv = p.H / 8;
+  const int64_t slot_bytes = (int64_t)p.T * p.H * 4;  // LL: 8 bytes per bf16 pair
+  bool ok = true;
+  if (p.ll) {
+    // 1. send: my rows into my slot on every GPU, each bf16 pair tagged with the epoch
+    uint8_t* my_slot = p.mc + off + p.rank * slot_bytes;
+    const uint64_t tag = (uint64_t)calls << 32;
+    for (int row = b; row < p.T; row += kNvlsGrid)
+      for (int v = tid; v < nv; v += kNvlsThreads) {
+        const uint4 u = p.x[(int64_t)row * nv + v];
+        uint8_t* dst = my_slot + ((int64_t)row * nv + v) * 32;
+        mm_st_b64(dst, tag | u.x);
+        mm_st_b64(dst + 8, tag | u.y);
+        mm_st_b64(dst + 16, tag | u.z);
+        mm_st_b64(dst + 24, tag | u.w);
+      }
+  } else {
+    // 1. stage this CTA's rows, 2. barrier across ranks for them
+    uint4* mine = reinterpret_cast<uint4*>(p.uc + off);
+    for (int row = b; row < p.T; row += kNvlsGrid)
+      for (int v = tid; v < nv; v += kNvlsThreads) mine[(int64_t)row * nv + v] = p.x[(int64_t)row * nv + v];
+    __syncthreads();
+    if (tid == 0) {
+      mm_red_release_add(p.mc + b * kNvlsFlagStride, 1u);
+      const uint32_t* flag = reinterpret_cast<const uint32_t*>(p.uc + b * kNvlsFlagStride);
+      const uint32_t target = rcalls * (uint32_t)p.world;  // flags count reduce-form calls only
+      const uint64_t t0 = globaltimer_ns();
+      while ((int)(ld_acquire_sys(flag) - target) < 0) {
+        if (globaltimer_ns() - t0 > p.timeout_ns) {
+          report_error(kErrPeerTimeout, 1000 + b);
+          ok = false;
+          break;
+        }
+      }
+    }
+    ok = __syncthreads_and(ok) != 0;
+  }
+  // 3. sum over ranks, add residual, normalise
+  if (ok) {
+    const uint8_t* mdata = p.mc + off;
+    const uint8_t* ldata = p.uc + off;
+    for (int row = b; row < p.T; row += kNvlsGrid) {
+      float vals[kNvlsMaxVec][8];
+      float ss = 0.f;
+      bool good = true;
+#pragma unroll
+      for (int k = 0; k < kNvlsMaxVec; ++k) {
+        const int v = tid + k * kNvlsThreads;
+        if (v < nv) {
+          const int64_t idx = (int64_t)row * nv + v;
+          if (p.ll) good &= ll_gather8(ldata, slot_bytes, p.world, idx * 32, calls, p.timeout_ns, vals[k]);
+          else unpack8(mm_ld_reduce_bf16x8(mdata + idx * 16), vals[k]);
+          if (!p.first) {
+            float r[8];
+            unpack8(p.residual[idx], r);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) vals[k][j] += r[j];
+          }
+          const uint4 packed = pack8(vals[k]);
+          p.residual[idx] = packed;
+          unpack8(packed, vals[k]);  // normalise the stored (bf16) residual
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += vals[k][j] * vals[k][j];
+        }
+      }
+      if (!good) report_error(kErrPeerTimeout, 2000 + b);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < kNvlsThreads / 32; ++i) tot += s_red[i];
+      const float rstd = rsqrtf(tot / (float)p.H + p.eps);
+#pragma unroll
+      for (int k = 0; k < kNvlsMaxVec; ++k) {
+        const int v = tid + k * kNvlsThreads;
+        if (v < nv) {
+          float wf[8];
+          unpack8(p.w[v], wf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) vals[k][j] = vals[k][j] * rstd * wf[j];
+          p.out[(int64_t)row * nv + v] = pack8(vals[k]);
+        }
+      }
+      __syncthreads();  // s_red reuse
+    }
+  }
+  if (tid == 0) {
+    p.state[2 * b] = calls;
+    p.state[2 * b + 1] = rcalls;
+  }
+}
+
+}  // namespace
+
+extern "C" int msgl_nvls_grid() { return kNvlsGrid; }
+extern "C" int msgl_nvls_flag_bytes() { return kNvlsFlagBytes; }
+
+extern "C" int msgl_nvls_allreduce_rmsnorm(void* uc, void* mc, int rank, int world, const void* x, void* residual,
+                                           const void* w, void* out, int T, int H, float eps, int64_t cap_bytes,
+                                           uint32_t* state, int64_t timeout_ns, int first, cudaStream_t s) {
+  if (H % 8 != 0 || H > 8 * kNvlsMaxVec * kNvlsThreads || (int64_t)T * H * 2 > cap_bytes) return 3;
+  NvlsParams p;
+  p.uc = reinterpret_cast<uint8_t*>(uc);
+  p.mc = reinterpret_cast<uint8_t*>(mc);
+  p.rank = rank;
+  p.world = world;
+  // LL while every rank's tagged copy is small (its 8-byte multicast stores cost more per byte than
+  // ld_reduce, but it needs no barrier); MINISGL_NVLS_LL_BYTES overrides the limit
+  static const int64_t ll_limit = getenv("MINISGL_NVLS_LL_BYTES") ? atoll(getenv("MINISGL_NVLS_LL_BYTES")) : (2 << 20);
+  const int64_t ll_bytes = (int64_t)world * T * H * 4;
+  p.ll = (ll_bytes <= cap_bytes && ll_bytes <= ll_limit) ? 1 : 0;
+  p.x = reinterpret_cast<const uint4*>(x);
+  p.residual = reinterpret_cast<uint4*>(residual);
+  p.w = reinterpret_cast<const uint4*>(w);
+  p.out = reinterpret_cast<uint4*>(out);
+  p.T = T;
+  p.H = H;
+  p.eps = eps;
+  p.cap = cap_bytes;
+  p.state = state;
+  p.timeout_ns = (uint64_t)timeout_ns;
+  p.first = first;
+  msgl_launch(nvls_ar_rmsnorm_kernel, dim3(kNvlsGrid), dim3(kNvlsThreads), 0, s, 1, p);
+  return 0;
+}
 
 MSGL_ERROR_ACCESSOR(msgl_err_comm)

@@ -166,7 +166,14 @@ class Engine:
             max_bytes = max(config.max_forward_len * self.model_config.hidden_size * self.dtype.itemsize,
                             config.max_running_req * self.model_config.vocab_size * 4 // config.tp_info.size)
             max_bytes = min(max_bytes, int(ENV.PYNCCL_MAX_BUFFER_SIZE))
-            enable_peer_comm(self.tp_cpu_group, self.device, max_bytes, strict=(mode != "auto"))
+            enable_peer_comm(self.tp_cpu_group, self.device, max_bytes, strict=(mode == "peer"))
+        if mode in ("auto", "fused"):
+            from minisgl.parallel.nvls import enable_nvls_norm
+
+            # decode-sized activations (and short prefill chunks): [tokens, hidden] bf16
+            rows = max(config.max_running_req, 1024)
+            enable_nvls_norm(dist.group.WORLD, self.tp_cpu_group, self.device,
+                             rows * self.model_config.hidden_size * self.dtype.itemsize, strict=(mode == "fused"))
 
     def _weights(self, config: EngineConfig) -> Dict[str, torch.Tensor]:
         if config.use_dummy_weight:

@@ -56,6 +56,11 @@ class LinearRowParallel(_Linear):
         self._tp = info.size
         self._reduce = reduce
         self._comm = DistributedCommunicator()
+        # set by blocks whose next op is an RMSNorm that can take the unreduced partial sum (the
+        # norm then runs the fused all-reduce + residual add + RMSNorm); `deferred` tells the block
+        # whether the last forward did so
+        self.defer_to_norm = False
+        self.deferred = False
         super().__init__(div_even(in_features, info.size), out_features, has_bias)
         if has_bias and info.rank != 0:
             self._bias_scale = 0.0  # only rank 0 adds the bias before the sum
@@ -65,8 +70,13 @@ class LinearRowParallel(_Linear):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         bias = self.bias if (self.bias is not None and self._bias_scale) else None
         y = ops.linear(x, self.weight, bias)
+        self.deferred = False
         if self._tp > 1 and self._reduce:
-            y = self._comm.all_reduce(y)
+            fused = DistributedCommunicator.norm_impl
+            if self.defer_to_norm and fused is not None and fused.fits(y):
+                self.deferred = True
+            else:
+                y = self._comm.all_reduce(y)
         return y
 
 

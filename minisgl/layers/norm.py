@@ -32,3 +32,10 @@ class RMSNormFused(RMSNorm):
         if residual is None:
             return ops.rmsnorm(x, self.weight, self._eps), x
         return ops.fused_add_rmsnorm(x, residual, self.weight, self._eps)
+
+    def forward_unreduced(self, x: torch.Tensor, residual: torch.Tensor | None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """``x`` is this rank's partial sum of a row-parallel linear: all-reduce it, add the
+        residual and normalise, in one fused collective kernel."""
+        from minisgl.parallel.comm import DistributedCommunicator
+
+        return DistributedCommunicator.norm_impl.all_reduce_add_rmsnorm(x, residual, self.weight, self._eps)

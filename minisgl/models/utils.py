@@ -47,6 +47,10 @@ class GatedMLP(BaseOP):
         y = ops.gate_up_silu(x, self.gate_up_proj.weight, self._act)
         return self.down_proj.forward(y)
 
+    @property
+    def output_unreduced(self) -> bool:
+        return self.down_proj.deferred
+
 
 class MoEMLP(BaseOP):
     def __init__(self, config: ModelConfig, router_name: str = "gate", activation: str = "silu",
@@ -68,6 +72,8 @@ class MoEMLP(BaseOP):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         logits = getattr(self, self._router_name).forward(x)
         return self.experts.forward(x, logits)
+
+    output_unreduced = False
 
 
 class RopeAttn(BaseOP):
@@ -109,13 +115,25 @@ class DecoderLayer(BaseOP):
         self.input_layernorm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
         self.post_attention_layernorm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
         self._layer_id = layer_id
+        # at TP > 1 the row-parallel outputs are reduced by the norms that follow them (fused)
+        self.self_attn.o_proj.defer_to_norm = True
+        if isinstance(self.mlp, GatedMLP):
+            self.mlp.down_proj.defer_to_norm = True
 
-    def forward(self, x: torch.Tensor, residual: torch.Tensor | None) -> Tuple[torch.Tensor, torch.Tensor]:
-        x, residual = self.input_layernorm.forward(x, residual)
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None,
+                unreduced: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+        """``unreduced``: x is the previous layer's partial sum (see LinearRowParallel).
+        Returns the MLP output and whether it is still a partial sum."""
+        norm = self.input_layernorm
+        x, residual = norm.forward_unreduced(x, residual) if unreduced else norm.forward(x, residual)
         x = self.self_attn.forward(x)
-        x, residual = self.post_attention_layernorm.forward(x, residual)
+        norm = self.post_attention_layernorm
+        if self.self_attn.o_proj.deferred:
+            x, residual = norm.forward_unreduced(x, residual)
+        else:
+            x, residual = norm.forward(x, residual)
         x = self.mlp.forward(x)
-        return x, residual
+        return x, residual, self.mlp.output_unreduced
 
 
 class DecoderModel(BaseOP):
@@ -127,8 +145,11 @@ class DecoderModel(BaseOP):
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
         x = self.embed_tokens.forward(input_ids)
         residual = None
+        unreduced = False
         for layer in self.layers.op_list:
-            x, residual = layer.forward(x, residual)
+            x, residual, unreduced = layer.forward(x, residual, unreduced)
+        if unreduced:
+            return self.norm.forward_unreduced(x, residual)[0]
         return self.norm.forward(x, residual)[0]
 
 

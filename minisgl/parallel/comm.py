@@ -41,6 +41,9 @@ class TorchDistributedImpl(CommImpl):
 
 class DistributedCommunicator:
     _stack: List[CommImpl] = [TorchDistributedImpl()]
+    # fused all-reduce + residual add + RMSNorm (NVLS), used by the norms that follow row-parallel
+    # linears; None when unavailable
+    norm_impl = None
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         return self._stack[-1].all_reduce(x)
@@ -55,6 +58,7 @@ class DistributedCommunicator:
     @classmethod
     def reset(cls) -> None:
         cls._stack = [TorchDistributedImpl()]
+        cls.norm_impl = None
 
     @classmethod
     def active(cls) -> CommImpl:
@@ -66,7 +70,7 @@ def set_torch_group(group) -> None:
 
 
 def destroy_distributed() -> None:
-    for impl in DistributedCommunicator._stack:
+    for impl in DistributedCommunicator._stack + [DistributedCommunicator.norm_impl]:
         close = getattr(impl, "close", None)
         if close is not None:
             close()

@@ -84,3 +84,71 @@ def test_peer_collectives_multi_gpu(tmp_path, free_port):
         NCCL_NVLS_ENABLE="0"), stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True) for r in range(world)]
     outs = [p.communicate(timeout=300)[0] for p in procs]
     assert all(p.returncode == 0 for p in procs), outs
+
+
+NVLS_WORKER = r"""
+import os, sys
+sys.path.insert(0, {root!r})
+import torch, torch.distributed as dist
+from datetime import timedelta
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dev = torch.device("cuda", rank)
+dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=60))
+from minisgl._native import cuda
+from minisgl.parallel.nvls import NvlsNormComm
+try:
+    impl = NvlsNormComm(dist.group.WORLD, cpu, dev, 8 << 20)
+except RuntimeError as e:
+    print("SKIP", e, flush=True)
+    dist.barrier(group=cpu)
+    dist.destroy_process_group()
+    sys.exit(0)
+H, eps = 5120, 1e-6
+g = torch.Generator(device="cpu").manual_seed(1234)
+w = (torch.rand(H, generator=g) + 0.5).to(dev, torch.bfloat16)
+# T x world x H x 4 <= 2 MiB uses the LL form (T <= 51 at 2 ranks), larger T the reduce form; alternate them
+for it, T in enumerate([1, 7, 128, 256, 129, 800, 3, 256, 1, 400, 2, 64]):
+    gp = torch.Generator(device="cpu").manual_seed(100 * it + rank)
+    x = torch.randn(T, H, generator=gp).to(dev, torch.bfloat16)
+    gr = torch.Generator(device="cpu").manual_seed(100 * it + 77)
+    first = it % 4 == 0
+    res0 = None if first else torch.randn(T, H, generator=gr).to(dev, torch.bfloat16)
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x)
+    s = torch.stack([p.float() for p in parts]).sum(0)
+    if res0 is not None:
+        s = s + res0.float()
+    exp_res = s.to(torch.bfloat16)
+    r32 = exp_res.float()
+    exp_out = (r32 * torch.rsqrt(r32.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(torch.bfloat16)
+    if it == 2 and rank == 0:
+        torch.cuda._sleep(5_000_000)  # a lagging rank
+    res = None if first else res0.clone()
+    out, res = impl.all_reduce_add_rmsnorm(x, res, w, eps)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(res.float(), exp_res.float(), atol=3e-2, rtol=2e-2)
+    torch.testing.assert_close(out.float(), exp_out.float(), atol=3e-2, rtol=2e-2)
+assert cuda().get_error()[0] == 0
+dist.barrier(group=cpu)
+impl.close()
+dist.destroy_process_group()
+print("OK", rank, flush=True)
+"""
+
+
+@pytest.mark.multigpu
+def test_nvls_allreduce_rmsnorm_multi_gpu(tmp_path, free_port):
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    if n < 2:
+        pytest.skip("needs 2+ GPUs")
+    world = min(n, 8)
+    script = tmp_path / "nvls.py"
+    script.write_text(NVLS_WORKER.format(root=ROOT))
+    procs = [subprocess.Popen([sys.executable, str(script)], env=dict(
+        os.environ, RANK=str(r), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(free_port),
+        LOCAL_RANK=str(r)), stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True) for r in range(world)]
+    outs = [p.communicate(timeout=300)[0] for p in procs]
+    assert all(p.returncode == 0 for p in procs), outs
+    assert all(("OK" in o) or ("SKIP" in o) for o in outs), outs
