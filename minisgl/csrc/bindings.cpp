@@ -149,13 +149,20 @@ void qk_norm_rope_store(at::Tensor q_out, at::Tensor qkv, at::Tensor positions, 
                           qkv.size(0), nq, nkv, hd, nkv * hd, stream());
 }
 
-void argmax(at::Tensor out, at::Tensor logits) {
+// values (optional, fp32 [rows]) receives each row's maximum; vocab < 0 means all columns
+void argmax(at::Tensor out, at::Tensor logits, c10::optional<at::Tensor> values, int64_t vocab) {
   check_i32(out, "out"); check_cuda(logits, "logits");
   CHECK(logits.stride(-1) == 1, "logits rows must be contiguous");
   const bool f32 = logits.scalar_type() == at::kFloat;
   CHECK(f32 || logits.scalar_type() == at::kBFloat16, "logits must be fp32 or bf16");
-  msgl_argmax(out.data_ptr<int32_t>(), logits.data_ptr(), logits.size(0), logits.size(1), logits.stride(0), f32,
-              stream());
+  const int64_t v = vocab < 0 ? logits.size(1) : std::min<int64_t>(vocab, logits.size(1));
+  float* vp = nullptr;
+  if (values.has_value()) {
+    check_cuda(*values, "values"); check_dtype(*values, at::kFloat, "values");
+    CHECK(values->numel() >= logits.size(0), "values too short");
+    vp = values->data_ptr<float>();
+  }
+  msgl_argmax(out.data_ptr<int32_t>(), vp, logits.data_ptr(), logits.size(0), v, logits.stride(0), f32, stream());
 }
 
 void sample(at::Tensor out, at::Tensor logits, at::Tensor temperature, at::Tensor top_k, at::Tensor top_p,
@@ -375,7 +382,8 @@ PYBIND11_MODULE(_cuda, m) {
   m.def("act_and_mul", &act_and_mul);
   m.def("store_kv", &store_kv);
   m.def("qk_norm_rope_store", &qk_norm_rope_store);
-  m.def("argmax", &argmax);
+  m.def("argmax", &argmax, py::arg("out"), py::arg("logits"), py::arg("values") = py::none(),
+        py::arg("vocab") = -1);
   m.def("sample", &sample);
   m.def("attention_prefill", &attention_prefill);
   m.def("attention_decode", &attention_decode);

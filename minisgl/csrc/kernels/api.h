@@ -25,7 +25,8 @@ void msgl_qk_norm_rope_store(void* q_out, const void* qkv, const int32_t* positi
                              const float* cos_sin, const void* q_norm, const void* k_norm,
                              float eps, void* k_cache, void* v_cache, const int32_t* out_loc,
                              int n, int nq, int nkv, int hd, int64_t cache_stride, cudaStream_t s);
-void msgl_argmax(int32_t* out, const void* logits, int rows, int vocab, int64_t stride,
+// row argmax over the first `vocab` columns; out_val (optional) receives the maximum
+void msgl_argmax(int32_t* out, float* out_val, const void* logits, int rows, int vocab, int64_t stride,
                  int is_fp32, cudaStream_t s);
 void msgl_sample(int32_t* out, const float* logits, int rows, int vocab, int64_t stride,
                  const float* temperature, const int32_t* top_k, const float* top_p,

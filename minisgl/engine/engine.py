@@ -115,6 +115,13 @@ class Engine:
             self.ctx.moe_backend = self.moe_backend = create_moe_backend(config.moe_backend)
         self.sampler = Sampler(self.device, self.model_config.vocab_size)
         self._init_peer_comm(config)
+        self._lm_shard = None
+        lm_head = getattr(self.model, "lm_head", None)
+        if config.tp_info.size > 1 and hasattr(lm_head, "return_local"):
+            from minisgl.parallel import DistributedCommunicator
+
+            lm_head.return_local = True
+            self._lm_shard = (lm_head.vocab_shard, config.tp_info.size, DistributedCommunicator())
 
         # ----------------------------------------------------------------- graphs
         self.dummy_req = Req(
@@ -261,7 +268,12 @@ class Engine:
                 logits = self.model.forward()
         for req in batch.reqs:
             req.complete_one()
-        next_tokens = self.sampler.sample(logits[: batch.size], args).to(torch.int32)
+        if self._lm_shard is not None:
+            shard, tp, comm = self._lm_shard
+            next_tokens = self.sampler.sample_sharded(logits[: batch.size], args, shard, tp, comm)
+        else:
+            next_tokens = self.sampler.sample(logits[: batch.size], args)
+        next_tokens = next_tokens.to(torch.int32)
         self.last_tokens[dev["sample_rows"].long()] = next_tokens
         if self.is_cuda:
             cpu = torch.empty(next_tokens.shape, dtype=torch.int32, pin_memory=True)

@@ -1,7 +1,8 @@
 """Decode CUDA graphs (reference: python/minisgl/engine/graph.py:20-171).
 
 One graph per padded batch size in ``[1, 2, 4, 8, 16, ..., max]`` sharing one memory pool.
-Static buffers hold input ids, positions, out_loc and fp32 logits; batches are padded with a dummy
+Static buffers hold input ids, positions and out_loc; each graph keeps its own output (fp32 logits,
+this rank's vocab shard at TP > 1). Batches are padded with a dummy
 request whose page-table row points at a dummy KV slot.
 """
 
@@ -41,6 +42,7 @@ class GraphRunner:
         self.dummy_req = dummy_req
         self.graph_map: Dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_launches: Dict[int, int] = {}
+        self.outputs: Dict[int, torch.Tensor] = {}  # each graph's own logits tensor (no copy-out)
         if self.max_graph_bs and engine.device.type == "cuda":
             self._capture()
         else:
@@ -54,7 +56,6 @@ class GraphRunner:
         self.input_ids = torch.zeros(mx, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(mx, dtype=torch.int32, device=dev)
         self.out_loc = torch.full((mx,), eng.dummy_slot, dtype=torch.int32, device=dev)
-        self.logits = torch.empty(mx, eng.model_config.vocab_size, dtype=torch.float32, device=dev)
         torch.cuda.synchronize(dev)
         free0 = torch.cuda.mem_get_info(dev)[0]
         logger.info_rank0(f"Capturing CUDA graphs for bs={self.graph_bs_list}")
@@ -71,10 +72,10 @@ class GraphRunner:
             from .counters import COUNTERS
 
             with ctx.forward_batch(batch):
-                self.logits[:bs].copy_(eng.model.forward())  # warm up outside the capture
+                eng.model.forward()  # warm up outside the capture
                 before = COUNTERS.launches
                 with torch.cuda.graph(g, pool=pool, stream=eng.stream):
-                    self.logits[:bs].copy_(eng.model.forward())
+                    self.outputs[bs] = eng.model.forward()
                 self.graph_launches[bs] = COUNTERS.launches - before
             pool = pool or g.pool()
             self.graph_map[bs] = g
@@ -102,8 +103,11 @@ class GraphRunner:
         from .counters import COUNTERS
 
         COUNTERS.launches += self.graph_launches[bs]
-        return self.logits[: batch.size]
+        # The graphs share one memory pool, so this tensor may alias another graph's buffers: it is
+        # consumed (sampled) on the same stream before the next replay.
+        return self.outputs[bs][: batch.size]
 
     def destroy_cuda_graphs(self) -> None:
         self.graph_map.clear()
+        self.outputs.clear()
         gc.collect()

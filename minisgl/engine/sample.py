@@ -63,3 +63,22 @@ class Sampler:
         if args.temperatures is None:
             return ops.argmax(logits)
         return ops.sample(logits, args.temperatures, args.top_k, args.top_p, args.seeds, args.steps)
+
+    def sample_sharded(self, local: torch.Tensor, args: BatchSamplingArgs, shard: tuple, tp: int,
+                       comm) -> torch.Tensor:
+        """``local``: this rank's logits for vocab ids [start, start + valid) (row stride = the
+        padded shard width). Greedy batches exchange one (max, global argmax) pair per row and
+        rank instead of the logits (the reference gathers all of them,
+        python/minisgl/layers/embedding.py:87-110); ties resolve to the lowest id as in the
+        unsharded argmax. Other batches gather the full logits and run the sampling kernel."""
+        start, valid = shard
+        rows, width = local.shape
+        if args.temperatures is None:
+            idx, val = ops.argmax(local, vocab=valid, with_values=True)
+            pair = torch.stack([val, (idx + start).view(torch.float32)], dim=1)  # id bit-cast into fp32
+            allp = comm.all_gather(pair.contiguous()).view(tp, rows, 2)
+            best = torch.argmax(allp[:, :, 0], dim=0)  # first maximal rank = lowest id among ties
+            ids = allp[:, :, 1].contiguous().view(torch.int32)
+            return ids.gather(0, best.view(1, rows)).view(rows)
+        full = comm.all_gather(local.contiguous()).view(tp, rows, width).permute(1, 0, 2).reshape(rows, tp * width)
+        return self.sample(full[:, : self.vocab_size], args)

@@ -69,12 +69,21 @@ class ParallelLMHead(VocabParallelEmbedding):
     def lm_weight(self) -> torch.Tensor:
         return self._tied.weight if self._tied is not None else self.weight
 
+    # At TP > 1 the engine sets this: forward returns this rank's vocab shard and the sampler
+    # combines shards (greedy: per-rank (max, argmax) pairs instead of gathering all logits).
+    return_local = False
+
+    @property
+    def vocab_shard(self) -> tuple:
+        """(first vocab id of this rank's shard, number of valid ids in it)."""
+        return self._vocab_range
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         batch = get_global_ctx().batch
         if batch.is_prefill:
             x = x.index_select(0, batch.attn_metadata.get_last_indices(batch.size))
         logits = ops.linear(x, self.lm_weight, self.bias)
-        if self._tp == 1:
+        if self._tp == 1 or self.return_local:
             return logits
         rows, vl = logits.shape
         full = self._comm.all_gather(logits)  # [tp * rows, V/tp]

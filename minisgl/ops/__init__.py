@@ -93,12 +93,18 @@ def store_kv(k, v, k_cache, v_cache, out_loc):
     _cuda().store_kv(k.reshape(k.shape[0], -1), v.reshape(v.shape[0], -1), k_cache, v_cache, out_loc)
 
 
-def argmax(logits):
+def argmax(logits, vocab: int | None = None, with_values: bool = False):
+    """Row argmax over the first ``vocab`` columns (all by default); ties to the lowest index.
+    ``with_values`` also returns each row's maximum (fp32)."""
     if not _on_gpu(logits):
-        return ref.argmax(logits)
+        lf = logits[:, :vocab].float() if vocab is not None else logits.float()
+        vals, idx = lf.max(dim=-1)  # first maximal index
+        idx = idx.to(torch.int32)
+        return (idx, vals) if with_values else idx
     out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
-    _cuda().argmax(out, logits)
-    return out
+    vals = torch.empty(logits.shape[0], dtype=torch.float32, device=logits.device) if with_values else None
+    _cuda().argmax(out, logits, vals, -1 if vocab is None else vocab)
+    return (out, vals) if with_values else out
 
 
 def sample(logits, temperature, top_k, top_p, seed, step):

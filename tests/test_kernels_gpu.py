@@ -237,6 +237,15 @@ def test_argmax_and_greedy_sample():
     logits[3, 5] = logits[3, 9] = 100.0  # tie -> lowest index
     assert torch.equal(ops.argmax(logits).cpu(), ref.argmax(logits.cpu()))
     assert torch.equal(ops.argmax(logits.bfloat16()).cpu(), ref.argmax(logits.bfloat16().cpu()))
+    # shard form: first `vocab` columns, with the maxima (what vocab-parallel greedy sampling exchanges)
+    for v in (151936, 75968, 75965, 37):
+        idx, val = ops.argmax(logits, vocab=v, with_values=True)
+        ev, ei = logits[:, :v].cpu().max(dim=-1)
+        assert torch.equal(idx.cpu(), ei.to(torch.int32)), v
+        assert torch.equal(val.cpu(), ev), v
+    # an unaligned row start takes the scalar path
+    sub = logits[:, 1:]
+    assert torch.equal(ops.argmax(sub).cpu(), ref.argmax(sub.cpu()))
 
 
 def test_sampling_matches_reference():
