@@ -36,11 +36,18 @@ class VocabParallelEmbedding(BaseOP):
             if k not in ("num_embeddings", "num_embeddings_tp"):
                 yield k, v
 
+    # set by the model when the first layer's input norm can take the unreduced per-rank rows
+    # (fused all-reduce + RMSNorm); `deferred` tells whether the last forward left them unreduced
+    defer_to_norm = False
+    deferred = False
+
     def forward(self, ids: torch.Tensor) -> torch.Tensor:
         if self._tp == 1:
             return ops.embedding(self.weight, ids)
         y = ops.embedding(self.weight, ids, *self._vocab_range)
-        return self._comm.all_reduce(y)
+        fused = DistributedCommunicator.norm_impl
+        self.deferred = self.defer_to_norm and fused is not None and fused.fits(y)
+        return y if self.deferred else self._comm.all_reduce(y)
 
 
 class ParallelLMHead(VocabParallelEmbedding):

@@ -139,13 +139,14 @@ class DecoderLayer(BaseOP):
 class DecoderModel(BaseOP):
     def __init__(self, config: ModelConfig, **layer_kwargs):
         self.embed_tokens = VocabParallelEmbedding(config.vocab_size, config.hidden_size)
+        self.embed_tokens.defer_to_norm = True  # reduced by the first layer's input norm (TP > 1)
         self.layers = OPList([DecoderLayer(config, i, **layer_kwargs) for i in range(config.num_layers)])
         self.norm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
 
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
         x = self.embed_tokens.forward(input_ids)
         residual = None
-        unreduced = False
+        unreduced = self.embed_tokens.deferred
         for layer in self.layers.op_list:
             x, residual, unreduced = layer.forward(x, residual, unreduced)
         if unreduced:
