@@ -20,13 +20,14 @@ def perf_cuda(fn: Callable[[], object], *, warmup: int = 3, reps: int = 20, grap
     with torch.cuda.graph(g, stream=s):
         for _ in range(graph_calls):
             fn()
-    g.replay()
-    torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(s)
-    for _ in range(reps):
+    with torch.cuda.stream(s):  # replays and both events on one stream
         g.replay()
-    b.record(s)
+        torch.cuda.synchronize()
+        a.record(s)
+        for _ in range(reps):
+            g.replay()
+        b.record(s)
     torch.cuda.synchronize()
     return a.elapsed_time(b) / (reps * graph_calls)
 
