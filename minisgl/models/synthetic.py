@@ -44,7 +44,7 @@ PRESETS: Dict[str, dict] = {
         hidden_size=256, num_attention_heads=4, num_key_value_heads=2, head_dim=64,
         intermediate_size=128, num_local_experts=8, num_experts_per_tok=2, experts_per_token=2,
         vocab_size=1024, rope_theta=150000.0, tie_word_embeddings=False, max_position_embeddings=4096,
-        sliding_window=16, layer_types=["sliding_attention", "full_attention"],
+        sliding_window=16, layer_types=["sliding_attention", "full_attention"], attention_bias=True,
         rope_scaling=dict(rope_type="yarn", factor=32.0, beta_fast=32.0, beta_slow=1.0,
                           original_max_position_embeddings=4096, truncate=False),
     ),
@@ -68,7 +68,7 @@ PRESETS: Dict[str, dict] = {
         hidden_size=2880, num_attention_heads=64, num_key_value_heads=8, head_dim=64,
         intermediate_size=2880, num_local_experts=128, num_experts_per_tok=4, experts_per_token=4,
         vocab_size=201088, rope_theta=150000.0, tie_word_embeddings=False,
-        max_position_embeddings=131072, sliding_window=128,
+        max_position_embeddings=131072, sliding_window=128, attention_bias=True,
         layer_types=["sliding_attention", "full_attention"] * 18,
         rope_scaling=dict(rope_type="yarn", factor=32.0, beta_fast=32.0, beta_slow=1.0,
                           original_max_position_embeddings=4096, truncate=False),
@@ -112,8 +112,48 @@ def hf_config(preset: str) -> dict:
     return cfg
 
 
-def random_state_dict(preset: str, seed: int = 0, std: float = 0.02, dtype=torch.float32) -> Dict[str, torch.Tensor]:
-    """HF-named random weights (per-expert keys for MoE). Norm weights are ones."""
+def quant_mxfp4(w: torch.Tensor):
+    """OCP MX fp4 quantisation along the last dim (a multiple of 32): per 32-value block the e8m0
+    scale 2^e is the smallest power of two with max|w| / 2^e <= 6, values round to the nearest e2m1
+    code. Returns (blocks [..., K/32, 16] uint8, low nibble first; scales [..., K/32] uint8, bias 127)."""
+    x = w.float().reshape(*w.shape[:-1], -1, 32)
+    amax = x.abs().amax(-1)
+    e = torch.ceil(torch.log2(amax.clamp(min=2.0 ** -126) / 6.0)).clamp(-127, 127)
+    q = x / torch.exp2(e).unsqueeze(-1)
+    mags = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+    code = (q.abs().unsqueeze(-1) - mags).abs().argmin(-1) | ((q < 0).long() << 3)
+    code = code.to(torch.uint8)
+    blocks = code[..., 0::2] | (code[..., 1::2] << 4)
+    return blocks.contiguous(), (e + 127).to(torch.uint8).contiguous()
+
+
+def _gpt_oss_fused_experts(per_expert: Dict[str, torch.Tensor], prefix: str, ne: int, fmt: str, dtype):
+    """Per-expert gate/up/down (+ biases) of one layer -> the gpt-oss checkpoint layout: fused
+    ``gate_up_proj [E, H, 2I]`` (gate / up interleaved) and ``down_proj [E, I, H]`` ("fused"), or
+    their MXFP4 blocks / scales over the input dim ("mxfp4")."""
+    q = prefix + "mlp.experts."
+    g = torch.stack([per_expert[f"{q}{e}.gate_proj.weight"] for e in range(ne)]).float()  # [E, I, H]
+    u = torch.stack([per_expert[f"{q}{e}.up_proj.weight"] for e in range(ne)]).float()
+    d = torch.stack([per_expert[f"{q}{e}.down_proj.weight"] for e in range(ne)]).float()  # [E, H, I]
+    gu = torch.stack([g, u], dim=2).reshape(ne, -1, g.shape[-1])  # rows interleaved: [E, 2I, H]
+    out = {}
+    if fmt == "mxfp4":
+        out[q + "gate_up_proj_blocks"], out[q + "gate_up_proj_scales"] = quant_mxfp4(gu)
+        out[q + "down_proj_blocks"], out[q + "down_proj_scales"] = quant_mxfp4(d)
+    else:
+        out[q + "gate_up_proj"] = gu.transpose(1, 2).contiguous().to(dtype)
+        out[q + "down_proj"] = d.transpose(1, 2).contiguous().to(dtype)
+    gb = torch.stack([per_expert[f"{q}{e}.gate_proj.bias"] for e in range(ne)])
+    ub = torch.stack([per_expert[f"{q}{e}.up_proj.bias"] for e in range(ne)])
+    out[q + "gate_up_proj_bias"] = torch.stack([gb, ub], dim=2).reshape(ne, -1).contiguous()
+    out[q + "down_proj_bias"] = torch.stack([per_expert[f"{q}{e}.down_proj.bias"] for e in range(ne)])
+    return out
+
+
+def random_state_dict(preset: str, seed: int = 0, std: float = 0.02, dtype=torch.float32,
+                      expert_format: str = "per_expert") -> Dict[str, torch.Tensor]:
+    """HF-named random weights. MoE experts as per-expert keys, or for gpt-oss its own fused
+    ("fused") or MXFP4 ("mxfp4") layout. Norm weights are ones."""
     c = hf_config(preset)
     g = torch.Generator().manual_seed(seed)
     H, L = c["hidden_size"], c["num_hidden_layers"]
@@ -150,15 +190,20 @@ def random_state_dict(preset: str, seed: int = 0, std: float = 0.02, dtype=torch
             out[p + f"mlp.{router}.weight"] = rnd(ne, H)
             if c["model_type"] == "gpt_oss":
                 out[p + "mlp.router.bias"] = rnd(ne)
+            layer_experts: Dict[str, torch.Tensor] = {}
             for e in range(ne):
                 q = p + f"mlp.experts.{e}."
-                out[q + "gate_proj.weight"] = rnd(inter, H)
-                out[q + "up_proj.weight"] = rnd(inter, H)
-                out[q + "down_proj.weight"] = rnd(H, inter)
+                layer_experts[q + "gate_proj.weight"] = rnd(inter, H)
+                layer_experts[q + "up_proj.weight"] = rnd(inter, H)
+                layer_experts[q + "down_proj.weight"] = rnd(H, inter)
                 if c["model_type"] == "gpt_oss":
-                    out[q + "gate_proj.bias"] = rnd(inter)
-                    out[q + "up_proj.bias"] = rnd(inter)
-                    out[q + "down_proj.bias"] = rnd(H)
+                    layer_experts[q + "gate_proj.bias"] = rnd(inter)
+                    layer_experts[q + "up_proj.bias"] = rnd(inter)
+                    layer_experts[q + "down_proj.bias"] = rnd(H)
+            if expert_format != "per_expert" and c["model_type"] == "gpt_oss":
+                out.update(_gpt_oss_fused_experts(layer_experts, p, ne, expert_format, dtype))
+            else:
+                out.update(layer_experts)
         else:
             I = c["intermediate_size"]
             out[p + "mlp.gate_proj.weight"] = rnd(I, H)
@@ -171,7 +216,7 @@ def random_state_dict(preset: str, seed: int = 0, std: float = 0.02, dtype=torch
 
 
 def make_checkpoint(preset: str, path: str, *, weights: bool = True, seed: int = 0, std: float = 0.02,
-                    dtype: torch.dtype = torch.float32) -> str:
+                    dtype: torch.dtype = torch.float32, expert_format: str = "per_expert") -> str:
     os.makedirs(path, exist_ok=True)
     cfg = hf_config(preset)
     cfg["torch_dtype"] = {torch.float32: "float32", torch.bfloat16: "bfloat16"}[dtype]
@@ -182,7 +227,7 @@ def make_checkpoint(preset: str, path: str, *, weights: bool = True, seed: int =
     if weights:
         from safetensors.torch import save_file
 
-        sd = random_state_dict(preset, seed=seed, std=std, dtype=dtype)
+        sd = random_state_dict(preset, seed=seed, std=std, dtype=dtype, expert_format=expert_format)
         save_file({k: v.contiguous() for k, v in sd.items()}, os.path.join(path, "model.safetensors"))
     return path
 
@@ -195,5 +240,8 @@ if __name__ == "__main__":
     ap.add_argument("path")
     ap.add_argument("--weights", action="store_true")
     ap.add_argument("--bf16", action="store_true")
+    ap.add_argument("--expert-format", default="per_expert", choices=["per_expert", "fused", "mxfp4"],
+                    help="gpt-oss experts: per-expert keys, the fused bf16 layout or MXFP4 blocks/scales")
     a = ap.parse_args()
-    make_checkpoint(a.preset, a.path, weights=a.weights, dtype=torch.bfloat16 if a.bf16 else torch.float32)
+    make_checkpoint(a.preset, a.path, weights=a.weights, dtype=torch.bfloat16 if a.bf16 else torch.float32,
+                    expert_format=a.expert_format)

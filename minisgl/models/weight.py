@@ -8,6 +8,14 @@ split by head), merge q,k,v -> ``qkv_proj`` and gate,up -> ``gate_up_proj`` (gat
 in 128-row blocks for the fused activation epilogue; expert weights keep plain ``[gate; up]``
 halves), and stack per-expert tensors into packed
 ``[E, ...]`` tensors. Yields ``(name, tensor)`` already on the target device.
+
+gpt-oss checkpoints store each MoE layer's experts fused: ``experts.gate_up_proj`` ``[E, H, 2I]``
+(gate / up interleaved along the last dim), ``experts.down_proj`` ``[E, I, H]`` and their biases, or
+the MXFP4 form ``experts.{gate_up,down}_proj_{blocks,scales}``: e2m1 values two per byte (low
+nibble first) in blocks of 32 along the input dim, one e8m0 scale (bias 127) per block. Both are
+converted here to this engine's ``[E, rows, K]`` row-major experts with ``[gate; up]`` halves,
+dequantising MXFP4 to the model dtype (reference format: transformers' gpt-oss modeling and mxfp4
+integration; mini-sglang itself has no gpt-oss).
 """
 
 from __future__ import annotations
@@ -29,6 +37,60 @@ _QKV = {".q_proj.": "q", ".k_proj.": "k", ".v_proj.": "v"}
 _GU = {".gate_proj.": "gate", ".up_proj.": "up"}
 _EXPERT = re.compile(r"^(?P<pre>.+\.experts)\.(?P<idx>\d+)\.(?P<name>.+)$")
 
+# e2m1 code -> value (sign bit 3, exponent bits 2..1, mantissa bit 0)
+_E2M1 = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0)
+
+
+def dequant_mxfp4(blocks: torch.Tensor, scales: torch.Tensor, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """``blocks [..., G, 16]`` uint8 (32 e2m1 values per block, low nibble first), ``scales [..., G]``
+    uint8 e8m0 -> ``[..., G * 32]``. Processed one leading index at a time to bound temporaries."""
+    if blocks.shape[:-1] != scales.shape or blocks.shape[-1] != 16:
+        raise ValueError(f"mxfp4 blocks {tuple(blocks.shape)} / scales {tuple(scales.shape)} mismatch")
+    lut = torch.tensor(_E2M1, dtype=torch.float32, device=blocks.device)
+    out = torch.empty(blocks.shape[:-2] + (blocks.shape[-2] * 32,), dtype=dtype, device=blocks.device)
+    flat_b = blocks.reshape(-1, *blocks.shape[-2:])
+    flat_s = scales.reshape(-1, scales.shape[-1])
+    flat_o = out.view(-1, out.shape[-1])
+    for i in range(flat_b.shape[0]):
+        b = flat_b[i].to(torch.uint8)
+        v = torch.stack([lut[(b & 0x0F).long()], lut[(b >> 4).long()]], dim=-1).reshape(b.shape[0], 32)
+        v = torch.ldexp(v, (flat_s[i].to(torch.int32) - 127).unsqueeze(-1).to(torch.float32))
+        flat_o[i] = v.reshape(-1).to(dtype)
+    return out
+
+
+def _split_gate_up_rows(w: torch.Tensor, rank: int, size: int) -> torch.Tensor:
+    """``[E, 2I, ...]`` with gate / up rows interleaved -> this rank's ``[E, 2I/tp, ...]`` as
+    ``[gate; up]`` halves."""
+    gate, up = w[:, 0::2], w[:, 1::2]
+    if size > 1:
+        gate, up = gate.chunk(size, dim=1)[rank], up.chunk(size, dim=1)[rank]
+    return torch.cat([gate, up], dim=1).contiguous()
+
+
+def _fused_expert(key: str, t: torch.Tensor, pending: Dict[str, torch.Tensor], rank: int, size: int, dtype):
+    """Convert one gpt-oss fused-expert tensor; returns ``(name, tensor)``, ``None`` while an MXFP4
+    blocks / scales pair is incomplete, or ``False`` if ``key`` is not such a tensor."""
+    for proj in ("gate_up_proj", "down_proj"):
+        for part in ("_blocks", "_scales"):
+            if key.endswith(f".experts.{proj}{part}"):
+                base = key[: -len(part)]
+                pending[key] = t
+                if f"{base}_blocks" not in pending or f"{base}_scales" not in pending:
+                    return None
+                w = dequant_mxfp4(pending.pop(f"{base}_blocks"), pending.pop(f"{base}_scales"), dtype)
+                if proj == "gate_up_proj":  # [E, 2I, H], rows interleaved
+                    return base, _split_gate_up_rows(w, rank, size)
+                return base, (w.chunk(size, dim=-1)[rank] if size > 1 else w).contiguous()  # [E, H, I]
+    if key.endswith(".experts.gate_up_proj") and t.dim() == 3:  # [E, H, 2I]
+        return key, _split_gate_up_rows(t.transpose(1, 2), rank, size)
+    if key.endswith(".experts.gate_up_proj_bias") and t.dim() == 2:  # [E, 2I]
+        return key, _split_gate_up_rows(t, rank, size)
+    if key.endswith(".experts.down_proj") and t.dim() == 3:  # [E, I, H]
+        w = t.transpose(1, 2)
+        return key, (w.chunk(size, dim=-1)[rank] if size > 1 else w).contiguous()
+    return False
+
 
 def shard_tensor(key: str, t: torch.Tensor, rank: int, size: int, num_kv_heads: int, head_dim: int) -> torch.Tensor:
     if size == 1:
@@ -39,8 +101,6 @@ def shard_tensor(key: str, t: torch.Tensor, rank: int, size: int, num_kv_heads: 
             return t[h * head_dim : (h + 1) * head_dim].clone()
         return t.chunk(size, dim=0)[rank].clone()
     if any(key.endswith(s) for s in _DIM1):
-        return t.chunk(size, dim=-1)[rank].clone()
-    if "experts" in key and key.endswith("down_proj") and t.dim() == 3:
         return t.chunk(size, dim=-1)[rank].clone()
     if key.endswith(".sinks"):
         return t.chunk(size, dim=0)[rank].clone()
@@ -80,6 +140,8 @@ def _expert_key(key: str):
     if m is None:
         return None
     name = m.group("name").removesuffix(".weight")
+    if name.endswith(".bias"):  # stacked expert biases are `<proj>_bias` tensors of the MoE layer
+        name = name[: -len(".bias")] + "_bias"
     return f"{m.group('pre')}.{name}", int(m.group("idx"))
 
 
@@ -99,6 +161,8 @@ def load_weight(model_path: str, device: torch.device, config=None) -> Iterator[
     info = get_tp_info()
     merge: Dict[str, Dict[str, torch.Tensor]] = {}
     experts: Dict[str, Dict[int, torch.Tensor]] = {}
+    pending: Dict[str, torch.Tensor] = {}  # gpt-oss MXFP4 blocks / scales awaiting their pair
+    dtype = getattr(config, "dtype", None) or torch.bfloat16
     for path in files:
         with safetensors.safe_open(path, framework="pt", device=str(device)) as f:
             for name in f.keys():
@@ -106,6 +170,13 @@ def load_weight(model_path: str, device: torch.device, config=None) -> Iterator[
                     continue
                 raw = f.get_tensor(name)
                 key = name.removeprefix("language_model.")
+                if ".experts." in key and not _EXPERT.match(key):
+                    conv = _fused_expert(key, raw, pending, info.rank, info.size, dtype)
+                    if conv is None:
+                        continue
+                    if conv is not False:
+                        yield conv
+                        continue
                 t = shard_tensor(key, raw, info.rank, info.size, config.num_kv_heads, config.head_dim)
                 del raw
                 mi = _merge_slot(key)
@@ -126,5 +197,5 @@ def load_weight(model_path: str, device: torch.device, config=None) -> Iterator[
                     yield pkey, torch.stack([bucket[i] for i in range(config.num_experts)])
                 else:
                     yield key, t
-    if merge or experts:
-        raise RuntimeError(f"incomplete checkpoint groups: {list(merge) + list(experts)}")
+    if merge or experts or pending:
+        raise RuntimeError(f"incomplete checkpoint groups: {list(merge) + list(experts) + list(pending)}")

@@ -36,11 +36,15 @@ def _hf_greedy(path, prompts, n_new):
     return outs
 
 
-@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-llama", "tiny-qwen2", "tiny-qwen3-moe"])
+@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-llama", "tiny-qwen2", "tiny-qwen3-moe", "tiny-gpt-oss"])
 def test_greedy_matches_hf(tmp_path, preset, free_port):
+    """gpt-oss: checkpoint in its own fused-expert layout (what transformers loads); covers biased
+    attention with sinks, alternating sliding-window layers, YaRN RoPE, top-k-then-softmax routing
+    and the clamped SwiGLU experts."""
     from minisgl.llm import LLM
 
-    path = make_checkpoint(preset, str(tmp_path / preset))
+    fmt = "fused" if preset == "tiny-gpt-oss" else "per_expert"
+    path = make_checkpoint(preset, str(tmp_path / preset), expert_format=fmt)
     prompts = _prompts()
     n_new = 8
     llm = LLM(path, dtype=torch.float32, device="cpu", max_running_req=16, distributed_port=free_port,
@@ -81,3 +85,43 @@ def test_tiny_config_full_workload(tmp_path, free_port):
     finally:
         llm2.shutdown()
     assert a == c
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_gpt_oss_mxfp4_checkpoint_loads_like_dequantized(tmp_path, tp):
+    """MXFP4 experts (e2m1 blocks + e8m0 scales) load to exactly the tensors of the same values
+    stored in the fused bf16 layout and in per-expert keys, on every TP rank."""
+    from safetensors.torch import save_file
+
+    from minisgl.models.synthetic import _gpt_oss_fused_experts, hf_config, quant_mxfp4, random_state_dict
+    from minisgl.models.weight import dequant_mxfp4, load_weight
+    from minisgl.parallel import set_tp_info
+    from minisgl.parallel.info import reset_tp_info
+
+    base = random_state_dict("tiny-gpt-oss")
+    for k in list(base):  # snap expert weights to MXFP4-representable values
+        if ".experts." in k and k.endswith(("gate_proj.weight", "up_proj.weight", "down_proj.weight")):
+            base[k] = dequant_mxfp4(*quant_mxfp4(base[k]), torch.float32)
+    ne = hf_config("tiny-gpt-oss")["num_local_experts"]
+    layers = hf_config("tiny-gpt-oss")["num_hidden_layers"]
+    dirs = {}
+    for fmt in ("per_expert", "fused", "mxfp4"):
+        sd = {k: v for k, v in base.items() if ".experts." not in k}
+        for i in range(layers):
+            p = f"model.layers.{i}."
+            layer = {k: v for k, v in base.items() if k.startswith(p + "mlp.experts.")}
+            sd.update(layer if fmt == "per_expert" else _gpt_oss_fused_experts(layer, p, ne, fmt, torch.float32))
+        d = make_checkpoint("tiny-gpt-oss", str(tmp_path / fmt), weights=False)
+        save_file({k: v.contiguous() for k, v in sd.items()}, str(tmp_path / fmt / "model.safetensors"))
+        dirs[fmt] = d
+    for rank in range(tp):
+        set_tp_info(rank, tp)
+        try:
+            loaded = {f: {k: v.float() for k, v in load_weight(d, torch.device("cpu"))} for f, d in dirs.items()}
+        finally:
+            reset_tp_info()
+        ref = loaded["per_expert"]
+        for f in ("fused", "mxfp4"):
+            assert loaded[f].keys() == ref.keys(), f
+            for k in ref:
+                assert torch.equal(loaded[f][k], ref[k]), (f, k, rank)
