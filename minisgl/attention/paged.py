@@ -232,6 +232,9 @@ class PagedAttentionBackend(BaseAttnBackend):
             ws = self._workspace(t * self.nq * m.num_splits * (self.hd + 2) * 4)
             _cuda().attention_decode(o, q, kc, vc, ctx.page_table, m.rows, m.kv_lens, self.scale,
                                      window, sinks, m.num_splits, ws)
+        elif self.page and self.hd == 128:
+            _cuda().attention_prefill_fmha(o, q, kc, vc, ctx.page_table, m.rows, m.cu_q, m.kv_lens, m.max_q_len,
+                                           self.scale, window, sinks, self.page)
         else:
             _cuda().attention_prefill(o, q, kc, vc, ctx.page_table, m.rows, m.cu_q, m.kv_lens,
                                       m.max_q_len, self.scale, window, sinks)

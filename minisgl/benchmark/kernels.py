@@ -8,7 +8,7 @@ times without timing, which is the form to wrap in a profiler.
 
   gemm          bf16 GEMM  out[M, N] = x[M, K] @ w[N, K]^T  (--epi 0 bf16, 1 SiLU-gated, 3 fp32)
   decode-attn   paged decode attention over a longest-first work list (page size 64)
-  prefill-attn  ragged causal prefill attention (requests of 100..1024 tokens)
+  prefill-attn  ragged causal prefill attention (requests of 100..1024 tokens; --impl tcgen05 | mma)
 """
 
 from __future__ import annotations
@@ -133,7 +133,10 @@ def _prefill_attn(a, c) -> None:
     o = torch.empty_like(q)
 
     def run():
-        c.attention_prefill(o, q, kc, vc, pt, rows, cu, kvl, max(lens), 1 / math.sqrt(hd), -1, None)
+        if a.impl == "tcgen05":
+            c.attention_prefill_fmha(o, q, kc, vc, pt, rows, cu, kvl, max(lens), 1 / math.sqrt(hd), -1, None, 64)
+        else:
+            c.attention_prefill(o, q, kc, vc, pt, rows, cu, kvl, max(lens), 1 / math.sqrt(hd), -1, None)
 
     if a.once:
         for _ in range(3):
@@ -144,7 +147,7 @@ def _prefill_attn(a, c) -> None:
     ms = perf_cuda(run, reps=5, graph_calls=3)
     _, tf = _peaks()
     flops = sum(n * (n + 1) / 2 for n in lens) * nq * hd * 4
-    print(f"prefill-attn tokens={tot} seqs={bs} nq={nq} nkv={nkv}: {ms * 1e3:.1f} us, {flops / ms / 1e9:.0f} TFLOP/s "
+    print(f"prefill-attn[{a.impl}] tokens={tot} seqs={bs} nq={nq} nkv={nkv}: {ms * 1e3:.1f} us, {flops / ms / 1e9:.0f} TFLOP/s "
           f"({flops / ms * 1e3 / tf:.2f} of measured)")
 
 
@@ -159,6 +162,7 @@ def main(argv=None) -> None:
     p.add_argument("--nq", type=int, default=40)
     p.add_argument("--nkv", type=int, default=8)
     p.add_argument("--tokens", type=int, default=16384)
+    p.add_argument("--impl", default="tcgen05", choices=["tcgen05", "mma"], help="prefill-attn kernel")
     p.add_argument("--once", action="store_true", help="run a few times untimed (for profilers)")
     a = p.parse_args(argv)
     from minisgl._native import cuda

@@ -216,6 +216,31 @@ void attention_decode(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor
                         workspace.data_ptr(), stream());
 }
 
+// tcgen05 prefill attention for head_dim 128 and page sizes 16/32/64 (pages of `page` consecutive slots).
+void attention_prefill_fmha(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor page_table,
+                            at::Tensor rows, at::Tensor cu_q, at::Tensor kv_lens, int64_t max_q_len, double scale,
+                            int64_t window, c10::optional<at::Tensor> sinks, int64_t page) {
+  check_bf16(o, "o"); check_bf16(q, "q"); check_bf16(k_cache, "k_cache"); check_bf16(v_cache, "v_cache");
+  check_i32(rows, "rows"); check_i32(cu_q, "cu_q"); check_i32(kv_lens, "kv_lens");
+  check_cuda(page_table, "page_table"); check_dtype(page_table, at::kInt, "page_table");
+  check_contig(q, "q"); check_contig(o, "o");
+  const int64_t T = q.size(0), nq = q.size(1), hd = q.size(2), nkv = k_cache.size(1);
+  CHECK(hd == 128, "tcgen05 prefill attention needs head_dim 128");
+  CHECK(nq % nkv == 0, "query heads must be a multiple of kv heads");
+  CHECK(page == 16 || page == 32 || page == 64, "tcgen05 prefill attention needs a page size of 16, 32 or 64");
+  CHECK(k_cache.stride(2) == 1 && k_cache.stride(1) == hd && k_cache.stride(0) % 8 == 0, "k_cache layout");
+  CHECK(v_cache.strides() == k_cache.strides() && v_cache.sizes() == k_cache.sizes(), "v_cache layout");
+  CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(k_cache.data_ptr()) % 16 == 0 &&
+            reinterpret_cast<uintptr_t>(v_cache.data_ptr()) % 16 == 0, "attention tensors must be 16-byte aligned");
+  if (sinks.has_value()) { check_dtype(*sinks, at::kFloat, "sinks"); CHECK(sinks->numel() == nq, "sinks size"); }
+  const int rc = msgl_attention_prefill_fmha(
+      o.data_ptr(), q.data_ptr(), T, k_cache.data_ptr(), v_cache.data_ptr(), k_cache.size(0), k_cache.stride(0),
+      page_table.data_ptr<int32_t>(), page_table.stride(0), rows.data_ptr<int32_t>(), cu_q.data_ptr<int32_t>(),
+      kv_lens.data_ptr<int32_t>(), cu_q.size(0) - 1, max_q_len, nq, nkv, hd, page, scale, window,
+      sinks.has_value() ? sinks->data_ptr<float>() : nullptr, stream());
+  CHECK(rc == 0, "tcgen05 prefill attention failed to launch (code ", rc, ")");
+}
+
 // Paged decode attention over a host-built work list (page size 16/32/64). work: int32 [>= 8 * entries]
 // (two int4 per entry), n_work: int32 [1] = entries, ws: fp32 partials for ws_slots chunk slots,
 // counters: int32 [>= bs * nkv], zero on entry and left at zero.
@@ -378,6 +403,7 @@ PYBIND11_MODULE(_cuda, m) {
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
   m.def("gemm", &gemm);
   m.def("attention_decode_paged", &attention_decode_paged);
+  m.def("attention_prefill_fmha", &attention_prefill_fmha);
   m.def("gemm_ex", &gemm_ex);
   m.def("act_and_mul", &act_and_mul);
   m.def("store_kv", &store_kv);

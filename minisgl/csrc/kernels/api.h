@@ -75,6 +75,14 @@ void msgl_attention_decode(void* o, const void* q, const void* k_cache, const vo
                            int64_t cache_stride, float sm_scale, int window, const float* sinks,
                            int num_splits, void* workspace, cudaStream_t s);
 
+// tcgen05 ragged causal prefill attention (head_dim 128, page size 16/32/64; see attention.cu).
+// Returns 0 on success, 2 if a tensor map could not be encoded, 3 on unsupported arguments.
+int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total_q, const void* k_cache, const void* v_cache,
+                                int64_t num_slots, int64_t cache_stride, const int32_t* page_table, int64_t pt_stride,
+                                const int32_t* rows, const int32_t* cu_q, const int32_t* kv_lens, int num_reqs,
+                                int max_q_len, int nq, int nkv, int hd, int page, float sm_scale, int window,
+                                const float* sinks, cudaStream_t s);
+
 // Persistent paged decode over a host-built work list (page size 16/32/64; see attention.cu).
 // Returns 0 on success, 2 if a tensor map could not be encoded, 3 on unsupported arguments.
 int msgl_attention_decode_paged(void* o, const void* q, int q_rows, const void* k_cache, const void* v_cache,

@@ -1075,6 +1075,356 @@ int run_paged_decode(const PagedDecodeParams& p, const void* q, int q_rows, cons
 
 }  // namespace
 
+// ================================================================================ prefill (tcgen05)
+// Ragged causal prefill attention on the 5th-generation tensor core, for head_dim 128 and page
+// sizes of 16 / 32 / 64 tokens. One CTA per (request, kv head, tile of TT = 128 / G query tokens):
+// the tile's TT x G packed (token, head) rows are the MMA M = 128 rows (G = query heads per kv head).
+//
+//   warp 0     TMA: the Q tile once (3-D box 64 dims x G heads x TT tokens, per 64-dim half), then
+//              per 128-key block the K and V pages (3-D boxes over [slots, kv heads, head dim])
+//              into a 2-stage ring; page-table entries are fetched by the warp's lanes in batches.
+//   warp 1     MMA: S_i = Q K_i^T into one of two TMEM S buffers, then O += P_{i-1} V_{i-1} once
+//              the softmax warps have written P_{i-1} (V is an MN-major operand: its 128-byte rows
+//              are keys), so QK of block i overlaps the softmax of block i - 1.
+//   warps 2-5  softmax, one thread per row (TMEM lane): read the S row, mask (causal / length /
+//              window), online max and sum in the log2 domain, P row as bf16 into a 128B-swizzled
+//              smem tile (the A operand of the PV MMA). O is rescaled in TMEM only when a row's
+//              max grows by more than 2^8 (lazy rescaling: P then stays <= 256), and always before
+//              the PV that follows. Epilogue: O / l (with the sink term) stored as bf16.
+// TMEM: S buffers at columns 0 and 128, O at 256 (512 allocated).
+namespace {
+
+constexpr int kFmKB = 128;  // keys per block
+constexpr int kFmThreads = 192;
+
+struct FmhaParams {
+  __nv_bfloat16* o;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  const int32_t* rows;
+  const int32_t* cu_q;
+  const int32_t* kv_lens;
+  const float* sinks;
+  int nq, nkv, group, tt, page;
+  float scale_log2;
+  int window;
+};
+
+struct FmSmem {
+  static constexpr int kQ = 2 * 128 * 128;           // two 64-dim halves x 128 rows x 128 B
+  static constexpr int kHalf = 128 * 128;            // one 64-dim half of a 128-key block
+  static constexpr int kKV = 4 * kHalf;              // K (2 halves) + V (2 halves)
+  static constexpr int kP = 2 * 128 * 128;           // P: two 64-key halves x 128 rows x 128 B
+  static constexpr int kOffKV = kQ;
+  static constexpr int kOffP = kQ + 2 * kKV;
+  static constexpr int kOffBar = kOffP + kP;
+  static constexpr int kBytes = 1024 + kOffBar + 256;
+};
+
+__device__ __forceinline__ uint32_t fm_swz(int row, int chunk) {  // 128B swizzle within a half tile
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kFmThreads, 1)
+fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, FmhaParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = smem + FmSmem::kOffKV;
+  uint8_t* sP = smem + FmSmem::kOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FmSmem::kOffBar);
+  uint64_t* qfull = bars;
+  uint64_t* kvfull = bars + 1;   // [2]
+  uint64_t* kvempty = bars + 3;  // [2]
+  uint64_t* sfull = bars + 5;    // [2]
+  uint64_t* sempty = bars + 7;   // [2]
+  uint64_t* pfull = bars + 9;
+  uint64_t* pvdone = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+
+  const int qb = blockIdx.x, b = blockIdx.y, kvh = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.group, TT = p.tt;
+  pdl_wait();
+  pdl_launch();
+  const int q0 = p.cu_q[b], n = p.cu_q[b + 1] - q0;
+  const int t0 = qb * TT;
+  if (t0 >= n) return;
+  const int t1 = min(n, t0 + TT);
+  const int L = p.kv_lens[b];
+  const int qpos0 = L - n;
+  const int kend = qpos0 + t1;  // exclusive
+  int kbeg = 0;
+  if (p.window > 0) kbeg = max(0, qpos0 + t0 - p.window + 1);
+  const int blk0 = kbeg / kFmKB, blk1 = (kend + kFmKB - 1) / kFmKB;
+  const int nb = blk1 - blk0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qfull, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kvfull[i], 1);
+      mbar_init(&kvempty[i], 1);
+      mbar_init(&sfull[i], 1);
+      mbar_init(&sempty[i], 4);
+    }
+    mbar_init(pfull, 4);
+    mbar_init(pvdone, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    const int g = p.page, gpb = kFmKB / g;
+    if (lane == 0) {
+      mbar_expect_tx(qfull, 2 * TT * G * 128);
+      for (int h = 0; h < 2; ++h) tma_load_3d(sQ + h * 128 * 128, &tq, qfull, h * 64, kvh * G, q0 + t0);
+    }
+    const int32_t* pt = p.page_table + (int64_t)p.rows[b] * p.pt_stride;
+    const int ngroups = nb * gpb;
+    bool ok = true;
+    for (int g0 = 0; ok && g0 < ngroups; g0 += 32) {
+      int slot = 0;
+      if (g0 + lane < ngroups) {
+        const int pos = blk0 * kFmKB + (g0 + lane) * g;
+        slot = pos < L ? pt[pos] : 0;
+      }
+      const int gend = min(32, ngroups - g0);
+      for (int k = 0; k < gend; ++k) {
+        const int s0 = __shfl_sync(0xffffffffu, slot, k);
+        const int gi = g0 + k, i = gi / gpb, sub = gi % gpb, st = i & 1;
+        if (lane == 0 && ok) {
+          if (sub == 0) {
+            if (!mbar_wait(&kvempty[st], ((i >> 1) & 1) ^ 1, 500)) ok = false;
+            else mbar_expect_tx(&kvfull[st], FmSmem::kKV);
+          }
+          if (ok) {
+            uint8_t* kt = sKV + st * FmSmem::kKV;
+            for (int h = 0; h < 2; ++h) {
+              tma_load_3d(kt + h * FmSmem::kHalf + sub * g * 128, &tk, &kvfull[st], h * 64, kvh, s0);
+              tma_load_3d(kt + (2 + h) * FmSmem::kHalf + sub * g * 128, &tv, &kvfull[st], h * 64, kvh, s0);
+            }
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, kFmKB);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128) | kIdescBMajorMN;
+      const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
+      bool ok = mbar_wait(qfull, 0, 510);
+      auto issue_pv = [&](int j) {
+        const int st = j & 1;
+        const uint32_t v_base = smem_u32(sKV + st * FmSmem::kKV + 2 * FmSmem::kHalf);
+#pragma unroll
+        for (int k = 0; k < kFmKB / 16; ++k) {  // 16 keys per MMA
+          const uint64_t a = smem_desc_sw128(p_base + (k >> 2) * 128 * 128 + (k & 3) * 32);
+          const uint64_t bd = smem_desc_sw128_mn(v_base + k * 16 * 128, FmSmem::kHalf);
+          tc_mma_f16(tmem + 256, a, bd, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(&kvempty[st]);
+        tc_commit(pvdone);
+      };
+      for (int i = 0; ok && i < nb; ++i) {
+        const int st = i & 1, sb = i & 1;
+        if (!mbar_wait(&kvfull[st], (i >> 1) & 1, 511)) { ok = false; break; }
+        if (!mbar_wait(&sempty[sb], ((i >> 1) & 1) ^ 1, 512)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_base = smem_u32(sKV + st * FmSmem::kKV);
+#pragma unroll
+        for (int k = 0; k < 128 / 16; ++k) {  // head dim, 16 per MMA
+          const uint32_t off = (k >> 2) * 128 * 128 + (k & 3) * 32;
+          tc_mma_f16(tmem + sb * kFmKB, smem_desc_sw128(q_base + off), smem_desc_sw128(k_base + off), idesc_s,
+                     k > 0 ? 1u : 0u);
+        }
+        tc_commit(&sfull[sb]);
+        if (i > 0) {
+          if (!mbar_wait(pfull, (i - 1) & 1, 513)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(i - 1);
+        }
+      }
+      if (ok && nb > 0 && mbar_wait(pfull, (nb - 1) & 1, 514)) {
+        tc_fence_after();
+        issue_pv(nb - 1);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // accumulator row == TMEM lane
+    const int t = r / G, gh = r - t * G;
+    const bool row_ok = r < TT * G && t0 + t < t1;
+    const int qpos = qpos0 + t0 + t;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    float m = -INFINITY, l = 0.f;
+    bool dead = false;
+    for (int i = 0; i < nb; ++i) {
+      const int sb = i & 1;
+      if (!dead && !mbar_wait(&sfull[sb], (i >> 1) & 1, 520)) dead = true;
+      tc_fence_after();
+      float s[kFmKB];
+#pragma unroll
+      for (int c = 0; c < kFmKB / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_base + sb * kFmKB + c * 32, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(v[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[sb]);
+      const int k0 = (blk0 + i) * kFmKB;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kFmKB; ++j) {
+        const int kp = k0 + j;
+        bool valid = row_ok && kp <= qpos && kp < L;
+        if (p.window > 0) valid = valid && kp > qpos - p.window;
+        s[j] = valid ? s[j] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[j]);
+      }
+      // P buffer and O are free once the previous PV has completed
+      if (i > 0 && !dead && !mbar_wait(pvdone, (i - 1) & 1, 521)) dead = true;
+      tc_fence_after();
+      const bool grow = mx > m + 8.f;  // lazy rescale threshold (log2 domain)
+      float alpha = 1.f;
+      if (grow) {
+        alpha = m == -INFINITY ? 0.f : exp2f(m - mx);
+        l *= alpha;
+        m = mx;
+      }
+      if (i > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(lane_base + 256 + c * 32, v);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
+          tmem_st_32x32b_x32(lane_base + 256 + c * 32, v);
+        }
+        tc_wait_st();
+      }
+      const float base = m == -INFINITY ? 0.f : m;
+      float sum = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint8_t* ph = sP + h * 128 * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float e[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            e[j] = exp2f(s[h * 64 + c * 8 + j] - base);
+            sum += e[j];
+          }
+          *reinterpret_cast<uint4*>(ph + fm_swz(r, c)) =
+              make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]), pack_bf16(e[4], e[5]), pack_bf16(e[6], e[7]));
+        }
+      }
+      l += sum;
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pfull);
+    }
+    // epilogue: wait for the last PV, normalise, store
+    if (nb > 0 && !dead) mbar_wait(pvdone, (nb - 1) & 1, 522);
+    tc_fence_after();
+    float f = 1.f, ll = l;
+    if (p.sinks != nullptr) {
+      const float sk = p.sinks[kvh * G + gh] * kLog2e;
+      const float mn = fmaxf(m, sk);
+      f = exp2f(m - mn);
+      ll = l * f + exp2f(sk - mn);
+    }
+    const float inv = ll > 0.f ? f / ll : 0.f;
+    __nv_bfloat16* dst = p.o + ((int64_t)(q0 + t0 + t) * p.nq + kvh * G + gh) * 128;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(lane_base + 256 + c * 32, v);
+      tc_wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8)
+          *reinterpret_cast<uint4*>(dst + c * 32 + j) = make_uint4(
+              pack_bf16(__uint_as_float(v[j]) * inv, __uint_as_float(v[j + 1]) * inv),
+              pack_bf16(__uint_as_float(v[j + 2]) * inv, __uint_as_float(v[j + 3]) * inv),
+              pack_bf16(__uint_as_float(v[j + 4]) * inv, __uint_as_float(v[j + 5]) * inv),
+              pack_bf16(__uint_as_float(v[j + 6]) * inv, __uint_as_float(v[j + 7]) * inv));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total_q, const void* k_cache,
+                                           const void* v_cache, int64_t num_slots, int64_t cache_stride,
+                                           const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
+                                           const int32_t* cu_q, const int32_t* kv_lens, int num_reqs, int max_q_len,
+                                           int nq, int nkv, int hd, int page, float sm_scale, int window,
+                                           const float* sinks, cudaStream_t s) {
+  if (num_reqs == 0 || total_q == 0) return 0;
+  if (hd != 128 || nq % nkv != 0 || nq / nkv > 128 || (page != 16 && page != 32 && page != 64)) return 3;
+  FmhaParams p;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.page_table = page_table;
+  p.pt_stride = pt_stride;
+  p.rows = rows;
+  p.cu_q = cu_q;
+  p.kv_lens = kv_lens;
+  p.sinks = sinks;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.group = nq / nkv;
+  p.tt = 128 / p.group;
+  p.page = page;
+  p.scale_log2 = sm_scale * kLog2e;
+  p.window = window;
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(fmha_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FmSmem::kBytes);
+    set = true;
+  }
+  CUtensorMap tq, tk, tv;
+  const cuuint64_t qdims[3] = {(cuuint64_t)hd, (cuuint64_t)nq, (cuuint64_t)total_q};
+  const cuuint64_t qstr[2] = {(cuuint64_t)hd * 2, (cuuint64_t)nq * hd * 2};
+  const cuuint32_t qbox[3] = {64, (cuuint32_t)p.group, (cuuint32_t)p.tt};
+  const cuuint64_t kdims[3] = {(cuuint64_t)hd, (cuuint64_t)nkv, (cuuint64_t)num_slots};
+  const cuuint64_t kstr[2] = {(cuuint64_t)hd * 2, (cuuint64_t)cache_stride * 2};
+  const cuuint32_t kbox[3] = {64, 1, (cuuint32_t)page};
+  if (!pd_encode(&tq, q, 3, qdims, qstr, qbox) || !pd_encode(&tk, k_cache, 3, kdims, kstr, kbox) ||
+      !pd_encode(&tv, v_cache, 3, kdims, kstr, kbox))
+    return 2;
+  const dim3 grid((max_q_len + p.tt - 1) / p.tt, num_reqs, nkv);
+  msgl_launch(fmha_prefill_kernel, grid, dim3(kFmThreads), FmSmem::kBytes, s, 1, tq, tk, tv, p);
+  return 0;
+}
+
 extern "C" int msgl_attention_decode_paged(void* o, const void* q, int q_rows, const void* k_cache,
                                            const void* v_cache, int64_t num_slots, int64_t cache_stride,
                                            const int32_t* page_table, int64_t pt_stride, const int32_t* rows,

@@ -336,6 +336,33 @@ MSGL_DEVICE uint64_t smem_desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// Descriptor for an MN-major operand tile with the 128-byte swizzle: each 128-byte row holds 64
+// consecutive MN elements of one K index; 8-row (K) groups are 1024 B apart (stride byte offset)
+// and consecutive 64-element MN groups `lbo_bytes` apart (leading byte offset).
+MSGL_DEVICE uint64_t smem_desc_sw128_mn(uint32_t saddr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// 32 lanes x 32 consecutive 32-bit columns from registers (thread i writes lane base + i).
+MSGL_DEVICE void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+MSGL_DEVICE void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Instruction descriptor for kind::f16 with bf16 A/B, fp32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4)                       // D format: f32
@@ -344,6 +371,8 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          | ((uint32_t)(N >> 3) << 17)    // N >> 3
          | ((uint32_t)(M >> 4) << 24);   // M >> 4
 }
+// bit 16 of the kind::f16 instruction descriptor: B operand MN-major
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
 
 // ------------------------------------------------------------------------------------------
 // Programmatic dependent launch: a kernel launched with the PDL attribute may start while its

@@ -230,6 +230,31 @@ def test_attention_decode_paged(hd, nq, nkv, page, window, sinks, num_ctas):
     assert _c().get_error() == (0, 0)
 
 
+@pytest.mark.parametrize("nq,nkv", [(40, 8), (64, 8), (8, 8), (32, 2)])
+@pytest.mark.parametrize("page", [16, 64])
+@pytest.mark.parametrize("window,sinks", [(-1, False), (100, True)])
+def test_attention_prefill_tcgen05(nq, nkv, page, window, sinks):
+    """tcgen05 prefill attention (S / O in TMEM, MN-major V operand, lazy O rescaling) against the
+    fp32 reference: ragged requests, prefix hits (kv longer than q), partial last tiles."""
+    hd = 128
+    lens_q = [1, 17, 300, 64, 129, 700]
+    lens_kv = [1, 40, 300, 400, 129, 1000]
+    _, kc, vc, pt, rows, _, kvl = _paged_pages_setup(lens_kv, nq, nkv, hd, page, seed=3)
+    g = torch.Generator(device="cpu").manual_seed(4)
+    q = (torch.randn(sum(lens_q), nq, hd, generator=g) * 2).to(DEV, torch.bfloat16)
+    cu = torch.zeros(len(lens_q) + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(torch.tensor(lens_q), 0)
+    cu = cu.to(DEV)
+    sk = torch.randn(nq, device=DEV) if sinks else None
+    o = torch.full_like(q, float("nan"))
+    scale = 1 / math.sqrt(hd)
+    _c().attention_prefill_fmha(o, q, kc, vc, pt, rows, cu, kvl, max(lens_q), scale, window, sk, page)
+    e = ref.paged_attention(q.cpu(), kc.cpu(), vc.cpu(), pt.cpu(), rows.cpu(), cu.cpu(), kvl.cpu(), scale, window,
+                            None if sk is None else sk.cpu())
+    _close(o, e, 2e-2, 2e-2)
+    assert _c().get_error() == (0, 0)
+
+
 def test_argmax_and_greedy_sample():
     from minisgl import ops
 
