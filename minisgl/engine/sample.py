@@ -14,6 +14,7 @@ from typing import List
 import torch
 
 from minisgl import ops
+from minisgl.utils import nvtx_annotate
 
 
 @dataclass
@@ -59,6 +60,7 @@ class Sampler:
             steps=_to_device(steps, torch.int64, d),
         )
 
+    @nvtx_annotate("Sampler")
     def sample(self, logits: torch.Tensor, args: BatchSamplingArgs) -> torch.Tensor:
         if args.temperatures is None:
             return ops.argmax(logits)

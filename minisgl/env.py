@@ -53,6 +53,7 @@ _FLAGS = {
     "COMM_MODE": _Flag("auto", str),  # auto | nccl | fused
     "COMM_TIMEOUT_MS": _Flag(5000, int),  # bound on every device-side peer wait
     "DEBUG_CHECK_INTEGRITY": _Flag(False, _as_bool),
+    "NVTX": _Flag(False, _as_bool),  # NVTX ranges around layers / attention / MLP / LM head / sampler
 }
 
 

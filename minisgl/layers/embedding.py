@@ -14,7 +14,7 @@ import torch
 from minisgl import ops
 from minisgl.core import get_global_ctx
 from minisgl.parallel import DistributedCommunicator, get_tp_info
-from minisgl.utils import div_ceil
+from minisgl.utils import div_ceil, nvtx_annotate
 
 from .base import BaseOP
 
@@ -41,6 +41,7 @@ class VocabParallelEmbedding(BaseOP):
     defer_to_norm = False
     deferred = False
 
+    @nvtx_annotate("Embedding")
     def forward(self, ids: torch.Tensor) -> torch.Tensor:
         if self._tp == 1:
             return ops.embedding(self.weight, ids)
@@ -85,6 +86,7 @@ class ParallelLMHead(VocabParallelEmbedding):
         """(first vocab id of this rank's shard, number of valid ids in it)."""
         return self._vocab_range
 
+    @nvtx_annotate("LMHead")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         batch = get_global_ctx().batch
         if batch.is_prefill:

@@ -29,6 +29,7 @@ from minisgl.layers import (
 )
 from minisgl.layers.base import BaseOP
 from minisgl.core import get_global_ctx
+from minisgl.utils import nvtx_annotate
 
 from .base import BaseLLMModel
 from .config import ModelConfig
@@ -43,6 +44,7 @@ class GatedMLP(BaseOP):
         self._act = "silu" if config.hidden_act == "silu" else "gelu"
         self.down_proj = LinearRowParallel(inter, config.hidden_size, has_bias=False)
 
+    @nvtx_annotate("MLP")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         y = ops.gate_up_silu(x, self.gate_up_proj.weight, self._act)
         return self.down_proj.forward(y)
@@ -69,6 +71,7 @@ class MoEMLP(BaseOP):
                                                     has_bias=config.mlp_bias))
         self._router_name = router_name
 
+    @nvtx_annotate("MoE")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         logits = getattr(self, self._router_name).forward(x)
         return self.experts.forward(x, logits)
@@ -99,6 +102,7 @@ class RopeAttn(BaseOP):
         if getattr(self, "sinks", None) is not None:
             self._attn.sinks = self.sinks
 
+    @nvtx_annotate("MHA")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         qkv = self.qkv_proj.forward(x)
         o = self._attn.forward(qkv)
@@ -120,6 +124,7 @@ class DecoderLayer(BaseOP):
         if isinstance(self.mlp, GatedMLP):
             self.mlp.down_proj.defer_to_norm = True
 
+    @nvtx_annotate("Layer_{}", layer_id_field="_layer_id")
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None,
                 unreduced: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
         """``unreduced``: x is the previous layer's partial sum (see LinearRowParallel).

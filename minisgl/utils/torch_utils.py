@@ -20,13 +20,15 @@ def torch_dtype(dtype: torch.dtype):
 
 
 def nvtx_annotate(name: str, layer_id_field: str | None = None):
-    """Wrap a method in an NVTX range (for Nsight traces). ``name`` may contain ``{}``, filled
-    from ``getattr(self, layer_id_field)``."""
+    """Wrap a method in an NVTX range (for Nsight traces) when ``MINISGL_NVTX=1``. ``name`` may
+    contain ``{}``, filled from ``getattr(self, layer_id_field)``. The ranges land in eager runs
+    and in CUDA-graph captures (reference: python/minisgl/utils/torch_utils.py:23-37)."""
+    from minisgl.env import ENV
 
     def deco(fn):
         @functools.wraps(fn)
         def inner(*args, **kwargs):
-            if not torch.cuda.is_available():
+            if not ENV.NVTX or not torch.cuda.is_available():
                 return fn(*args, **kwargs)
             label = name.format(getattr(args[0], layer_id_field)) if layer_id_field else name
             torch.cuda.nvtx.range_push(label)
