@@ -300,11 +300,11 @@ void moe_route(at::Tensor logits, int64_t topk, bool renorm, bool softmax_after,
 }
 
 void moe_align(at::Tensor ids, int64_t E, int64_t bn, at::Tensor perm, at::Tensor inv, at::Tensor work,
-               at::Tensor tile_count) {
+               at::Tensor tile_count, int64_t e0) {
   check_i32(ids, "ids"); check_i32(perm, "perm"); check_i32(inv, "inv"); check_i32(work, "work");
   check_i32(tile_count, "tile_count");
   CHECK(E <= 4096, "too many experts");
-  msgl_moe_align(ids.data_ptr<int32_t>(), ids.numel(), E, bn, work.numel() / 2, perm.numel(), perm.data_ptr<int32_t>(),
+  msgl_moe_align(ids.data_ptr<int32_t>(), ids.numel(), E, e0, bn, work.numel() / 2, perm.numel(), perm.data_ptr<int32_t>(),
                  inv.data_ptr<int32_t>(), work.data_ptr(), tile_count.data_ptr<int32_t>(), stream());
 }
 
@@ -417,7 +417,8 @@ PYBIND11_MODULE(_cuda, m) {
   m.def("gemm_grouped", &gemm_grouped);
 
   m.def("moe_route", &moe_route);
-  m.def("moe_align", &moe_align);
+  m.def("moe_align", &moe_align, py::arg("ids"), py::arg("E"), py::arg("bn"), py::arg("perm"), py::arg("inv"),
+        py::arg("work"), py::arg("tile_count"), py::arg("e0") = 0);
   m.def("moe_gather", &moe_gather);
   m.def("moe_act", &moe_act);
   m.def("moe_combine", &moe_combine);

@@ -55,7 +55,8 @@ void msgl_gemm_grouped(void* out, const void* x, const void* w, const void* bias
                        cudaStream_t s);
 void msgl_moe_route(const float* logits, int T, int E, int topk, int renorm, int softmax_after, float* weights,
                     int32_t* ids, cudaStream_t s);
-void msgl_moe_align(const int32_t* ids, int pairs, int E, int bn, int max_tiles, int rows_cap, int32_t* perm,
+// experts [e0, e0 + E) are local (expert parallelism); other assignments get inv = -1
+void msgl_moe_align(const int32_t* ids, int pairs, int E, int e0, int bn, int max_tiles, int rows_cap, int32_t* perm,
                     int32_t* inv, void* work, int32_t* tile_count, cudaStream_t s);
 void msgl_moe_gather(void* xs, const void* x, const int32_t* perm, int rows, int H, int topk, cudaStream_t s);
 void msgl_moe_act(void* out, const void* y, int rows, int inter, int act, const int32_t* perm, cudaStream_t s);

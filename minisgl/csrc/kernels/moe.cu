@@ -86,7 +86,9 @@ __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int
 
 // single CTA: counts -> padded segment starts -> tile work list -> scatter of pair positions.
 // perm[row] = pair index (token * topk + k) or -1 for padding; inv[pair] = row.
-__global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__ ids, int pairs, int E, int bn,
+// Expert parallelism: only experts [e0, e0 + E) live on this rank; assignments to other experts
+// are dropped (inv = -1, no rows) and contribute nothing to the combine.
+__global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__ ids, int pairs, int E, int e0, int bn,
                                                      int max_tiles, int rows_cap, int32_t* __restrict__ perm,
                                                      int32_t* __restrict__ inv, int2* __restrict__ work,
                                                      int32_t* __restrict__ tile_count) {
@@ -99,7 +101,10 @@ __global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__
   int* tstart = sm + 3 * E; // [E]
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < pairs; i += blockDim.x) atomicAdd(&cnt[ids[i]], 1);
+  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+    const int e = ids[i] - e0;
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     int row = 0, tile = 0;
@@ -121,7 +126,11 @@ __global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__
   }
   __syncthreads();
   for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
-    const int e = ids[i];
+    const int e = ids[i] - e0;
+    if (e < 0 || e >= E) {
+      inv[i] = -1;
+      continue;
+    }
     const int pos = start[e] + atomicAdd(&cursor[e], 1);
     perm[pos] = i;
     inv[i] = pos;
@@ -178,8 +187,10 @@ __global__ void combine_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloa
   for (int c = threadIdx.x * 2; c < H; c += blockDim.x * 2) {
     float a0 = 0.f, a1 = 0.f;
     for (int k = 0; k < topk; ++k) {
+      const int row = inv[t * topk + k];
+      if (row < 0) continue;  // expert lives on another rank
       const float wk = w[t * topk + k];
-      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + (size_t)inv[t * topk + k] * H + c);
+      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + (size_t)row * H + c);
       a0 += wk * __bfloat162float(v.x);
       a1 += wk * __bfloat162float(v.y);
     }
@@ -198,9 +209,9 @@ void msgl_moe_route(const float* logits, int T, int E, int topk, int renorm, int
               weights, ids);
 }
 
-void msgl_moe_align(const int32_t* ids, int pairs, int E, int bn, int max_tiles, int rows_cap, int32_t* perm,
+void msgl_moe_align(const int32_t* ids, int pairs, int E, int e0, int bn, int max_tiles, int rows_cap, int32_t* perm,
                     int32_t* inv, void* work, int32_t* tile_count, cudaStream_t s) {
-  msgl_launch(align_kernel, dim3(1), dim3(1024), (size_t)4 * E * sizeof(int), s, 1, ids, pairs, E, bn, max_tiles,
+  msgl_launch(align_kernel, dim3(1), dim3(1024), (size_t)4 * E * sizeof(int), s, 1, ids, pairs, E, e0, bn, max_tiles,
               rows_cap, perm, inv, reinterpret_cast<int2*>(work), tile_count);
 }
 

@@ -1,8 +1,17 @@
 """Mixture-of-experts layer (reference: python/minisgl/layers/moe.py:9-59).
 
 Expert weights are packed: ``gate_up_proj [E, 2*I/tp, H]`` as ``[gate; up]`` halves and
-``down_proj [E, H, I/tp]``. Tensor parallelism shards every
-expert's intermediate dim; the sum over ranks follows the expert combine.
+``down_proj [E, H, I/tp]``. Two ways to spread them over the tensor-parallel ranks
+(``MINISGL_MOE_PARALLEL``):
+
+* ``tp`` (the reference's): every rank holds a 1/tp slice of every expert's intermediate dim;
+* ``ep`` (expert parallelism, not in the reference): rank r holds experts
+  [r E/tp, (r+1) E/tp) whole, ``[E/tp, 2I, H]``. Attention is tensor-parallel, so every rank
+  already has every token's activations: a rank runs the tokens routed to its own experts and
+  the all-reduce that follows the layer sums the ranks' contributions (the combine). Each
+  expert's GEMMs keep their full intermediate size instead of 1/tp of it.
+
+Either way the sum over ranks follows the expert combine.
 """
 
 from __future__ import annotations
@@ -16,6 +25,24 @@ from minisgl.utils import div_even
 from .base import BaseOP
 
 
+def moe_parallel_mode() -> str:
+    from minisgl.env import ENV
+
+    mode = str(ENV.MOE_PARALLEL).lower()
+    if mode not in ("tp", "ep"):
+        raise ValueError(f"MINISGL_MOE_PARALLEL must be tp or ep, got {mode!r}")
+    return mode
+
+
+def expert_range(num_experts: int) -> tuple:
+    """(first expert, number of experts) this rank holds."""
+    info = get_tp_info()
+    if info.size == 1 or moe_parallel_mode() == "tp":
+        return 0, num_experts
+    local = div_even(num_experts, info.size)
+    return info.rank * local, local
+
+
 class MoELayer(BaseOP):
     def __init__(self, num_experts: int, top_k: int, hidden_size: int, intermediate_size: int,
                  renormalize: bool = True, activation: str = "silu", has_bias: bool = False,
@@ -27,11 +54,13 @@ class MoELayer(BaseOP):
         self._act = activation
         self._num_experts = num_experts
         self._softmax_after_topk = routing == "topk_softmax"
-        inter = div_even(intermediate_size, info.size)
-        self.gate_up_proj = torch.empty(num_experts, 2 * inter, hidden_size)
-        self.down_proj = torch.empty(num_experts, hidden_size, inter)
-        self.gate_up_proj_bias = torch.empty(num_experts, 2 * inter) if has_bias else None
-        self.down_proj_bias = torch.empty(num_experts, hidden_size) if has_bias else None
+        self._e0, local = expert_range(num_experts)
+        self._ep = info.size > 1 and local < num_experts
+        inter = intermediate_size if self._ep else div_even(intermediate_size, info.size)
+        self.gate_up_proj = torch.empty(local, 2 * inter, hidden_size)
+        self.down_proj = torch.empty(local, hidden_size, inter)
+        self.gate_up_proj_bias = torch.empty(local, 2 * inter) if has_bias else None
+        self.down_proj_bias = torch.empty(local, hidden_size) if has_bias else None
         self._comm = DistributedCommunicator()
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
@@ -39,8 +68,10 @@ class MoELayer(BaseOP):
         out = be.forward(
             hidden_states, self.gate_up_proj, self.down_proj, router_logits, self._top_k,
             self._renorm, self._act, w1_bias=self.gate_up_proj_bias,
-            w2_bias=self.down_proj_bias if (self._tp == 1 or get_tp_info().rank == 0) else None,
-            softmax_after_topk=self._softmax_after_topk,
+            # TP: every rank holds a slice of each expert, so only rank 0 adds the output bias;
+            # EP: each expert's output is computed on one rank, which adds its bias
+            w2_bias=self.down_proj_bias if (self._tp == 1 or self._ep or get_tp_info().rank == 0) else None,
+            softmax_after_topk=self._softmax_after_topk, expert_offset=self._e0,
         )
         if self._tp > 1:
             out = self._comm.all_reduce(out)

@@ -61,16 +61,21 @@ def dequant_mxfp4(blocks: torch.Tensor, scales: torch.Tensor, dtype: torch.dtype
 
 def _split_gate_up_rows(w: torch.Tensor, rank: int, size: int) -> torch.Tensor:
     """``[E, 2I, ...]`` with gate / up rows interleaved -> this rank's ``[E, 2I/tp, ...]`` as
-    ``[gate; up]`` halves."""
+    ``[gate; up]`` halves (``size`` 1: whole experts)."""
     gate, up = w[:, 0::2], w[:, 1::2]
     if size > 1:
         gate, up = gate.chunk(size, dim=1)[rank], up.chunk(size, dim=1)[rank]
     return torch.cat([gate, up], dim=1).contiguous()
 
 
-def _fused_expert(key: str, t: torch.Tensor, pending: Dict[str, torch.Tensor], rank: int, size: int, dtype):
+def _fused_expert(key: str, t: torch.Tensor, pending: Dict[str, torch.Tensor], rank: int, size: int, dtype,
+                  experts: tuple | None = None):
     """Convert one gpt-oss fused-expert tensor; returns ``(name, tensor)``, ``None`` while an MXFP4
-    blocks / scales pair is incomplete, or ``False`` if ``key`` is not such a tensor."""
+    blocks / scales pair is incomplete, or ``False`` if ``key`` is not such a tensor. With
+    ``experts = (first, count)`` (expert parallelism) only those experts are kept, whole."""
+    if experts is not None and t.dim() >= 2 and ".experts." in key:
+        t = t[experts[0] : experts[0] + experts[1]]
+        rank, size = 0, 1
     for proj in ("gate_up_proj", "down_proj"):
         for part in ("_blocks", "_scales"):
             if key.endswith(f".experts.{proj}{part}"):
@@ -89,6 +94,8 @@ def _fused_expert(key: str, t: torch.Tensor, pending: Dict[str, torch.Tensor], r
     if key.endswith(".experts.down_proj") and t.dim() == 3:  # [E, I, H]
         w = t.transpose(1, 2)
         return key, (w.chunk(size, dim=-1)[rank] if size > 1 else w).contiguous()
+    if key.endswith(".experts.down_proj_bias") and t.dim() == 2:  # [E, H]: whole on every rank
+        return key, t.contiguous()
     return False
 
 
@@ -163,6 +170,14 @@ def load_weight(model_path: str, device: torch.device, config=None) -> Iterator[
     experts: Dict[str, Dict[int, torch.Tensor]] = {}
     pending: Dict[str, torch.Tensor] = {}  # gpt-oss MXFP4 blocks / scales awaiting their pair
     dtype = getattr(config, "dtype", None) or torch.bfloat16
+    ep = None  # expert parallelism: (first expert, count) held by this rank
+    if config.is_moe and info.size > 1:
+        from minisgl.layers.moe import expert_range
+
+        first, count = expert_range(config.num_experts)
+        if count < config.num_experts:
+            ep = (first, count)
+    n_local = ep[1] if ep else config.num_experts
     for path in files:
         with safetensors.safe_open(path, framework="pt", device=str(device)) as f:
             for name in f.keys():
@@ -170,14 +185,24 @@ def load_weight(model_path: str, device: torch.device, config=None) -> Iterator[
                     continue
                 raw = f.get_tensor(name)
                 key = name.removeprefix("language_model.")
-                if ".experts." in key and not _EXPERT.match(key):
-                    conv = _fused_expert(key, raw, pending, info.rank, info.size, dtype)
+                em = _EXPERT.match(key) if ".experts." in key else None
+                if ep is not None and em is not None:  # per-expert tensor under EP: keep ours, whole
+                    e = int(em.group("idx"))
+                    if not ep[0] <= e < ep[0] + ep[1]:
+                        del raw
+                        continue
+                    key = f"{em.group('pre')}.{e - ep[0]}.{em.group('name')}"
+                if ".experts." in key and em is None:
+                    conv = _fused_expert(key, raw, pending, info.rank, info.size, dtype, ep)
                     if conv is None:
                         continue
                     if conv is not False:
                         yield conv
                         continue
-                t = shard_tensor(key, raw, info.rank, info.size, config.num_kv_heads, config.head_dim)
+                if ep is not None and em is not None:
+                    t = raw
+                else:
+                    t = shard_tensor(key, raw, info.rank, info.size, config.num_kv_heads, config.head_dim)
                 del raw
                 mi = _merge_slot(key)
                 if mi is not None:
@@ -191,10 +216,10 @@ def load_weight(model_path: str, device: torch.device, config=None) -> Iterator[
                     pkey, idx = ei
                     bucket = experts.setdefault(pkey, {})
                     bucket[idx] = t
-                    if len(bucket) < config.num_experts:
+                    if len(bucket) < n_local:
                         continue
                     del experts[pkey]
-                    yield pkey, torch.stack([bucket[i] for i in range(config.num_experts)])
+                    yield pkey, torch.stack([bucket[i] for i in range(n_local)])
                 else:
                     yield key, t
     if merge or experts or pending:

@@ -42,30 +42,35 @@ def expert_act(y: torch.Tensor, activation: str) -> torch.Tensor:
 
 
 def moe_reference(x, w1, w2, gating, topk, renormalize, activation, w1_bias=None, w2_bias=None,
-                  softmax_after_topk=False):
+                  softmax_after_topk=False, expert_offset: int = 0):
+    """``w1``/``w2`` hold experts [expert_offset, expert_offset + E) (expert parallelism)."""
     w, ids = route(gating, topk, renormalize, softmax_after_topk)
     out = torch.zeros(x.shape[0], w2.shape[1], dtype=torch.float32, device=x.device)
     xf = x.float()
+    E = w1.shape[0]
     for e in torch.unique(ids).tolist():
+        le = e - expert_offset
+        if not 0 <= le < E:
+            continue
         tok, slot = torch.nonzero(ids == e, as_tuple=True)
-        y = xf[tok] @ w1[e].float().t()
+        y = xf[tok] @ w1[le].float().t()
         if w1_bias is not None:
-            y = y + w1_bias[e].float()
+            y = y + w1_bias[le].float()
         a = expert_act(y, activation)
-        z = a @ w2[e].float().t()
+        z = a @ w2[le].float().t()
         if w2_bias is not None:
-            z = z + w2_bias[e].float()
+            z = z + w2_bias[le].float()
         out.index_add_(0, tok, z * w[tok, slot, None])
     return out.to(x.dtype)
 
 
 class GroupedMoe(BaseMoeBackend):
     def forward(self, hidden_states, w1, w2, gating_output, topk, renormalize, activation="silu",
-                *, w1_bias=None, w2_bias=None, softmax_after_topk=False):
+                *, w1_bias=None, w2_bias=None, softmax_after_topk=False, expert_offset=0):
         if not hidden_states.is_cuda:
             return moe_reference(hidden_states, w1, w2, gating_output, topk, renormalize, activation,
-                                 w1_bias, w2_bias, softmax_after_topk)
+                                 w1_bias, w2_bias, softmax_after_topk, expert_offset)
         from minisgl.ops.moe import moe_forward
 
         return moe_forward(hidden_states, w1, w2, gating_output, topk, renormalize, activation,
-                           w1_bias, w2_bias, softmax_after_topk)
+                           w1_bias, w2_bias, softmax_after_topk, expert_offset)

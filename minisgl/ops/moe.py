@@ -26,7 +26,9 @@ def pick_bn(pairs: int, experts: int) -> int:
 
 
 def moe_forward(x, w1, w2, gating, topk, renormalize, activation, w1_bias=None, w2_bias=None,
-                softmax_after_topk=False):
+                softmax_after_topk=False, expert_offset: int = 0):
+    """``w1``/``w2`` hold experts [expert_offset, expert_offset + E) of the ``gating`` columns
+    (expert parallelism); assignments to other experts contribute nothing here."""
     c = _cuda()
     T, H = x.shape
     E, two_i, _ = w1.shape
@@ -44,7 +46,7 @@ def moe_forward(x, w1, w2, gating, topk, renormalize, activation, w1_bias=None, 
     inv = torch.empty(pairs, dtype=torch.int32, device=dev)
     work = torch.empty(max_tiles, 2, dtype=torch.int32, device=dev)
     count = torch.empty(1, dtype=torch.int32, device=dev)
-    c.moe_align(ids, E, bn, perm, inv, work, count)
+    c.moe_align(ids, E, bn, perm, inv, work, count, expert_offset)
     xs = torch.empty(rows, H, dtype=x.dtype, device=dev)
     c.moe_gather(xs, x.contiguous(), perm, topk)
     y1 = torch.empty(rows, two_i, dtype=x.dtype, device=dev)

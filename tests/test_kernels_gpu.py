@@ -355,3 +355,11 @@ def test_moe_forward(T, E, topk, H, I, act, renorm, after, bias):
     exp = moe_reference(x.cpu(), w1.cpu(), w2.cpu(), gate.cpu(), topk, renorm, act,
                         None if b1 is None else b1.cpu(), None if b2 is None else b2.cpu(), after)
     _close(out, exp, 3e-2, 3e-2)
+    # expert parallelism: this "rank" holds experts [E/4, E/2); assignments elsewhere drop out
+    e0, n = E // 4, E // 4
+    sub = lambda t: None if t is None else t[e0 : e0 + n].contiguous()
+    out = moe_forward(x, sub(w1), sub(w2), gate, topk, renorm, act, sub(b1), sub(b2), after, expert_offset=e0)
+    exp = moe_reference(x.cpu(), sub(w1).cpu(), sub(w2).cpu(), gate.cpu(), topk, renorm, act,
+                        None if b1 is None else sub(b1).cpu(), None if b2 is None else sub(b2).cpu(), after,
+                        expert_offset=e0)
+    _close(out, exp, 3e-2, 3e-2)

@@ -37,11 +37,16 @@ def _prompts():
             for _ in range(6)]
 
 
-@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-qwen3-moe"])
-def test_tp2_matches_tp1(tmp_path, preset, free_port):
+@pytest.mark.parametrize("preset,moe_parallel", [("tiny-qwen3", "tp"), ("tiny-qwen3-moe", "tp"),
+                                                  ("tiny-qwen3-moe", "ep"), ("tiny-gpt-oss", "tp"),
+                                                  ("tiny-gpt-oss", "ep")])
+def test_tp2_matches_tp1(tmp_path, preset, moe_parallel, free_port):
+    """TP2 (experts sliced, or whole experts per rank with MINISGL_MOE_PARALLEL=ep) gives the TP1
+    tokens; gpt-oss loads from its fused-expert checkpoint layout."""
     from minisgl.llm import LLM
 
-    path = make_checkpoint(preset, str(tmp_path / preset))
+    fmt = "fused" if preset == "tiny-gpt-oss" else "per_expert"
+    path = make_checkpoint(preset, str(tmp_path / preset), expert_format=fmt)
     prompts = _prompts()
     llm = LLM(path, dtype=torch.float32, device="cpu", max_running_req=16, distributed_port=free_port,
               max_extend_tokens=48)
@@ -54,7 +59,8 @@ def test_tp2_matches_tp1(tmp_path, preset, free_port):
     procs = []
     for r in range(2):
         env = dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE="2", MASTER_ADDR="127.0.0.1",
-                   MASTER_PORT=str(free_port + 7), TP_PROMPTS=json.dumps(prompts), PYTHONPATH=ROOT)
+                   MASTER_PORT=str(free_port + 7), TP_PROMPTS=json.dumps(prompts), PYTHONPATH=ROOT,
+                   MINISGL_MOE_PARALLEL=moe_parallel)
         procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     outs = [p.communicate(timeout=300)[0] for p in procs]
