@@ -52,6 +52,14 @@ class Req:
         self.max_device_len = self.device_len + self.output_len
         if not (0 <= self.cached_len < self.device_len <= self.max_device_len):
             raise ValueError(f"bad lengths for {self!r}")
+        # token ids live in one buffer sized for the whole request; input_ids is a view of its
+        # filled part, so appending a sampled token is an in-place write, not a concatenation
+        n = self.device_len
+        self._buf = torch.empty(self.max_device_len + 1, dtype=torch.int32)
+        self._buf[:n] = self.input_ids
+        self._np = self._buf.numpy()
+        self._len = n
+        self.input_ids = self._buf[:n]
 
     @property
     def remain_len(self) -> int:
@@ -67,8 +75,10 @@ class Req:
         self.cached_len = self.device_len
         self.device_len += 1
 
-    def append_host(self, next_token: torch.Tensor) -> None:
-        self.input_ids = torch.cat([self.input_ids, next_token])
+    def append_host(self, next_token: int) -> None:
+        self._np[self._len] = next_token
+        self._len += 1
+        self.input_ids = self._buf[: self._len]
 
     @property
     def can_decode(self) -> bool:

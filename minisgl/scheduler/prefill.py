@@ -1,7 +1,9 @@
 """FCFS prefill admission with chunking (reference: python/minisgl/scheduler/prefill.py:23-158).
 
-A request is admitted when its extend length plus its output budget fits in the KV pool (free +
-evictable) after reserving what the running decode set may still claim. A prompt that does not
+A request is admitted when its extend length plus its output budget, plus one partial page,
+fits in the KV pool (free + evictable) after reserving what the running decode set and the
+requests admitted before it in the batch may still claim (pages are allocated whole, so each
+request can hold up to page_size - 1 slots beyond its tokens). A prompt that does not
 fit the per-batch token budget becomes a ``ChunkedReq``: it is computed over several prefill
 batches, is never sampled until its last chunk, and is re-queued at the head of the list.
 """
@@ -24,7 +26,7 @@ from .utils import PendingReq
 
 
 class ChunkedReq(Req):
-    def append_host(self, next_token: torch.Tensor) -> None:
+    def append_host(self, next_token: int) -> None:
         raise RuntimeError("a chunked request is not sampled")
 
     @property
@@ -43,7 +45,7 @@ class PrefillAdder:
         if self.table_manager.available_size == 0:
             return None
         handle = self.cache_manager.match_req(p.input_ids).cuda_handle
-        need = p.input_len - handle.cached_len + p.output_len
+        need = p.input_len - handle.cached_len + p.output_len + self.cache_manager.page_size - 1
         if need + self.reserved_size > self.cache_manager.available_size:
             return None
         self.cache_manager.lock(handle)  # locking moves the match out of the evictable pool
@@ -58,7 +60,8 @@ class PrefillAdder:
         chunk = min(self.token_budget, remain)
         cls = ChunkedReq if chunk < remain else Req
         self.token_budget -= chunk
-        self.reserved_size += remain + p.output_len
+        if p.chunked_req is None:  # a continuing chunk was reserved when it was first admitted
+            self.reserved_size += remain + p.output_len + self.cache_manager.page_size - 1
         req = cls(
             input_ids=p.input_ids[: cached_len + chunk],
             table_idx=row,

@@ -133,7 +133,7 @@ class Scheduler(SchedulerIOMixin):
                 if isinstance(req, ChunkedReq):
                     continue
                 tok = tokens[i]
-                req.append_host(torch.tensor([tok], dtype=torch.int32))
+                req.append_host(tok)
                 finished = not req.can_decode
                 if not req.sampling_params.ignore_eos:
                     finished |= tok == self.eos_token_id

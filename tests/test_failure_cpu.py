@@ -70,7 +70,10 @@ def test_lost_tp_rank_raises_within_timeout(tmp_path, free_port, mode):
     assert time.time() - t0 < 170
 
 
-def test_small_kv_pool_backpressure(tmp_path, free_port):
+@pytest.mark.parametrize("page,pages", [(1, 96), (16, 8)])
+def test_small_kv_pool_backpressure(tmp_path, free_port, page, pages):
+    """Pages are allocated whole: admission reserves a partial page per request, so a tight pool
+    never runs dry mid-decode (8 pages of 16 hold about one request at a time here)."""
     from minisgl.llm import LLM
 
     path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
@@ -79,9 +82,10 @@ def test_small_kv_pool_backpressure(tmp_path, free_port):
                for _ in range(12)]
     sp = SamplingParams(max_tokens=16, ignore_eos=True)
     outs = {}
-    for name, pages in (("roomy", None), ("tight", 96)):  # 96 one-token pages: ~1.3 requests at a time
-        llm = LLM(path, dtype=torch.float32, device="cpu", max_running_req=8, page_size=1, num_page_override=pages,
-                  distributed_port=free_port + (0 if pages is None else 3), cache_type="radix")
+    for name, npages in (("roomy", None), ("tight", pages)):
+        llm = LLM(path, dtype=torch.float32, device="cpu", max_running_req=8, page_size=page,
+                  num_page_override=npages, distributed_port=free_port + (0 if npages is None else 3),
+                  cache_type="radix")
         try:
             outs[name] = [o["token_ids"] for o in llm.generate(prompts, sp)]
             llm.cache_manager.check_integrity()
