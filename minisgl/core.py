@@ -35,31 +35,35 @@ class SamplingParams:
         return (self.temperature <= 0.0 or self.top_k == 1) and self.top_p >= 1.0
 
 
-@dataclass(eq=False)
 class Req:
-    input_ids: torch.Tensor  # CPU int32, prompt + tokens sampled so far
-    table_idx: int
-    cached_len: int
-    output_len: int
-    uid: int
-    sampling_params: SamplingParams
-    cache_handle: "BaseCacheHandle"
+    """One running request. ``input_ids`` (CPU int32, prompt + tokens sampled so far) is a view
+    of a buffer sized for the whole request, so appending a sampled token is an in-place write."""
 
-    def __post_init__(self) -> None:
-        if self.input_ids.device.type != "cpu":
+    def __init__(self, input_ids: torch.Tensor, table_idx: int, cached_len: int, output_len: int,
+                 uid: int, sampling_params: SamplingParams, cache_handle: "BaseCacheHandle") -> None:
+        if input_ids.device.type != "cpu":
             raise ValueError("Req.input_ids must live on the CPU")
-        self.device_len = len(self.input_ids)
-        self.max_device_len = self.device_len + self.output_len
-        if not (0 <= self.cached_len < self.device_len <= self.max_device_len):
+        self.table_idx = table_idx
+        self.cached_len = cached_len
+        self.output_len = output_len
+        self.uid = uid
+        self.sampling_params = sampling_params
+        self.cache_handle = cache_handle
+        self.greedy = sampling_params.is_greedy
+        self.pending_prefix = 0  # matched prefix slots still to be written into the page table
+        n = len(input_ids)
+        self.device_len = n
+        self.max_device_len = n + output_len
+        if not (0 <= cached_len < n <= self.max_device_len):
             raise ValueError(f"bad lengths for {self!r}")
-        # token ids live in one buffer sized for the whole request; input_ids is a view of its
-        # filled part, so appending a sampled token is an in-place write, not a concatenation
-        n = self.device_len
         self._buf = torch.empty(self.max_device_len + 1, dtype=torch.int32)
-        self._buf[:n] = self.input_ids
+        self._buf[:n] = input_ids
         self._np = self._buf.numpy()
         self._len = n
-        self.input_ids = self._buf[:n]
+
+    @property
+    def input_ids(self) -> torch.Tensor:
+        return self._buf[: self._len]
 
     @property
     def remain_len(self) -> int:
@@ -78,7 +82,6 @@ class Req:
     def append_host(self, next_token: int) -> None:
         self._np[self._len] = next_token
         self._len += 1
-        self.input_ids = self._buf[: self._len]
 
     @property
     def can_decode(self) -> bool:

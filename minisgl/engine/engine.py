@@ -20,7 +20,7 @@ import torch.distributed as dist
 
 from minisgl.attention import create_attention_backend
 from minisgl.attention.paged import PAGED_DECODE_PAGES
-from minisgl.core import Batch, Context, Req, get_global_ctx, reset_global_ctx, set_global_ctx
+from minisgl.core import Batch, Context, Req, SamplingParams, get_global_ctx, reset_global_ctx, set_global_ctx
 from minisgl.kvcache import create_kvcache_pool
 from minisgl.layers import set_rope_device
 from minisgl.models import create_model, load_weight
@@ -126,7 +126,7 @@ class Engine:
         # ----------------------------------------------------------------- graphs
         self.dummy_req = Req(
             input_ids=torch.zeros(1, dtype=torch.int32), table_idx=self.dummy_row, cached_len=0,
-            output_len=1, uid=-1, sampling_params=None, cache_handle=None,  # type: ignore[arg-type]
+            output_len=1, uid=-1, sampling_params=SamplingParams(), cache_handle=None,  # type: ignore[arg-type]
         )
         self.dummy_req.slots = np.array([self.dummy_slot], dtype=np.int32)
         graph_bs = determine_graph_bs(config.cuda_graph_bs, config.cuda_graph_max_bs, free0,
@@ -306,28 +306,31 @@ class BatchPlan:
 
     def __init__(self, batch: Batch, pt_writes, junk_row: int):
         reqs = batch.padded_reqs
-        ext = [r.extend_len for r in reqs]
-        self.positions = np.concatenate(
-            [np.arange(r.cached_len, r.device_len, dtype=np.int32) for r in reqs]
-        ) if reqs else np.empty(0, np.int32)
-        self.tok_rows = np.repeat(np.array([r.table_idx for r in reqs], dtype=np.int32), ext)
+        n = len(reqs)
+        cached = np.fromiter((r.cached_len for r in reqs), np.int32, n)
+        self.kv_lens = np.fromiter((r.device_len for r in reqs), np.int32, n)
+        self.req_rows = np.fromiter((r.table_idx for r in reqs), np.int32, n)
+        ext = self.kv_lens - cached
         if batch.is_prefill:
-            self.input_ids = np.concatenate(
-                [r.input_ids[r.cached_len : r.device_len].numpy().astype(np.int32) for r in reqs]
-            )
-        else:
+            self.positions = np.concatenate(
+                [np.arange(c, d, dtype=np.int32) for c, d in zip(cached.tolist(), self.kv_lens.tolist())]
+            ) if n else np.empty(0, np.int32)
+            self.tok_rows = np.repeat(self.req_rows, ext)
+            self.input_ids = np.concatenate([r.input_ids[r.cached_len : r.device_len].numpy() for r in reqs])
+        else:  # one token per request
+            self.positions = cached
+            self.tok_rows = self.req_rows
             self.input_ids = np.empty(0, np.int32)
         self.pt_rows, self.pt_pos, self.pt_slots = pt_writes
         self.num_pt_writes = len(self.pt_rows)
-        self.req_rows = np.array([r.table_idx for r in reqs], dtype=np.int32)
-        self.kv_lens = np.array([r.device_len for r in reqs], dtype=np.int32)
-        self.cu_q = np.zeros(len(reqs) + 1, dtype=np.int32)
+        self.cu_q = np.zeros(n + 1, dtype=np.int32)
         np.cumsum(ext, out=self.cu_q[1:])
-        self.sample_rows = np.array(
-            [r.table_idx if r.can_decode else junk_row for r in batch.reqs], dtype=np.int32
+        self.sample_rows = np.fromiter(
+            (r.table_idx if r.max_device_len > r.device_len else junk_row for r in batch.reqs), np.int32,
+            len(batch.reqs),
         )
-        self.max_q_len = max(ext) if ext else 0
-        self.max_kv_len = int(self.kv_lens.max()) if len(reqs) else 0
+        self.max_q_len = int(ext.max()) if n else 0
+        self.max_kv_len = int(self.kv_lens.max()) if n else 0
         self.extra: Dict[str, np.ndarray] = {}  # backend-owned segments appended to the upload
 
     _ORDER = ("positions", "tok_rows", "input_ids", "pt_rows", "pt_pos", "pt_slots",

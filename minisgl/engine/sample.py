@@ -42,9 +42,9 @@ class Sampler:
     vocab_size: int
 
     def prepare(self, batch) -> BatchSamplingArgs:
-        params = [r.sampling_params for r in batch.reqs]
-        if all(p.is_greedy for p in params):
+        if all(r.greedy for r in batch.reqs):
             return BatchSamplingArgs(temperatures=None)
+        params = [r.sampling_params for r in batch.reqs]
         temps = [0.0 if p.is_greedy else max(p.temperature, 1e-6) for p in params]
         ks = [p.top_k if p.top_k >= 1 else self.vocab_size for p in params]
         ps = [min(max(p.top_p, 1e-6), 1.0) for p in params]

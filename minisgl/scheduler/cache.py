@@ -51,13 +51,19 @@ class CacheManager:
         need = 0
         rows, poss, slots = [], [], []
         for r in reqs:
-            n = getattr(r, "pending_prefix", 0)
+            n = r.pending_prefix
             if n:
                 rows.append(np.full(n, r.table_idx, dtype=np.int32))
                 poss.append(np.arange(n, dtype=np.int32))
                 slots.append(r.slots[:n])
                 r.pending_prefix = 0
-            first, last = div_ceil(r.cached_len, ps), div_ceil(r.device_len, ps)
+            c, d = r.cached_len, r.device_len
+            if d - c == 1:  # decode: a new page only when the token starts one
+                if c % ps == 0:
+                    spans.append((r, c // ps, c // ps + 1))
+                    need += 1
+                continue
+            first, last = div_ceil(c, ps), div_ceil(d, ps)
             if last > first:
                 spans.append((r, first, last))
                 need += last - first

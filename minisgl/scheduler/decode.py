@@ -13,9 +13,13 @@ class DecodeManager:
         self.running: Dict[int, Req] = {}  # uid -> req, insertion-ordered
 
     def filter_reqs(self, reqs: Iterable[Req]) -> None:
+        """Only the batch's requests changed: add those that continue, drop those that ended."""
+        running = self.running
         for r in reqs:
-            self.running.setdefault(r.uid, r)
-        self.running = {u: r for u, r in self.running.items() if r.can_decode}
+            if r.can_decode:
+                running.setdefault(r.uid, r)
+            elif running.get(r.uid) is r:
+                del running[r.uid]
 
     def remove_req(self, req: Req) -> None:
         if self.running.get(req.uid) is req:

@@ -129,14 +129,14 @@ class Scheduler(SchedulerIOMixin):
         reply: List[DetokenizeMsg] = []
         newly_finished: Set[Req] = set()
         with self.cache_manager.lazy_free_region():
-            for i, req in enumerate(batch.reqs):
+            eos = self.eos_token_id
+            for req, tok in zip(batch.reqs, tokens):
                 if isinstance(req, ChunkedReq):
                     continue
-                tok = tokens[i]
                 req.append_host(tok)
-                finished = not req.can_decode
-                if not req.sampling_params.ignore_eos:
-                    finished |= tok == self.eos_token_id
+                finished = req.device_len >= req.max_device_len
+                if tok == eos and not req.sampling_params.ignore_eos:
+                    finished = True
                 reply.append(DetokenizeMsg(uid=req.uid, next_token=tok, finished=finished))
                 if finished and req not in self.finished_reqs:
                     self.decode_manager.remove_req(req)
