@@ -77,7 +77,7 @@ class LLM(Scheduler):
     def offline_send_result(self, reply: List[DetokenizeMsg]) -> None:
         for msg in reply:
             st = self.status_map[msg.uid]
-            if not (msg.finished and msg.next_token == self.eos_token_id):
+            if not msg.eos:  # a stopping EOS is not output; with ignore_eos it is an ordinary token
                 st.output_ids.append(msg.next_token)
 
     def generate(self, prompts, sampling_params) -> List[Dict[str, object]]:

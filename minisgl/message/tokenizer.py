@@ -32,6 +32,7 @@ class DetokenizeMsg(BaseTokenizerMsg):
     uid: int
     next_token: int
     finished: bool
+    eos: bool = False  # the request stopped on this EOS token (not part of the output)
 
 
 @dataclass

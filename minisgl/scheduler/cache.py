@@ -133,6 +133,16 @@ class CacheManager:
         if finished:
             self._free(slots[new.cached_len :])
         else:
+            if prefix > old.cached_len:
+                # The pages just freed were this request's own copy of a prefix that another
+                # request cached first. The request keeps decoding, so its page-table row must
+                # point at the cached copy before its next forward, or it would read pages that
+                # are about to be handed out again (the reference keeps its own page indices
+                # here: python/minisgl/scheduler/cache.py:70-79).
+                cached = np.asarray(new.get_matched_indices()[old.cached_len : prefix], dtype=np.int32)
+                req.slots = req.slots.copy()
+                req.slots[old.cached_len : prefix] = cached
+                req.pending_prefix = max(req.pending_prefix, prefix)
             req.cache_handle = new
             self.lock(new)
 

@@ -134,10 +134,9 @@ class Scheduler(SchedulerIOMixin):
                 if isinstance(req, ChunkedReq):
                     continue
                 req.append_host(tok)
-                finished = req.device_len >= req.max_device_len
-                if tok == eos and not req.sampling_params.ignore_eos:
-                    finished = True
-                reply.append(DetokenizeMsg(uid=req.uid, next_token=tok, finished=finished))
+                stop_eos = tok == eos and not req.sampling_params.ignore_eos
+                finished = stop_eos or req.device_len >= req.max_device_len
+                reply.append(DetokenizeMsg(uid=req.uid, next_token=tok, finished=finished, eos=stop_eos))
                 if finished and req not in self.finished_reqs:
                     self.decode_manager.remove_req(req)
                     self._free_req_resources(req)

@@ -54,7 +54,7 @@ class DetokenizeManager:
         ctx_ids, full_ids = [], []
         for m in msgs:
             st = self.streams.setdefault(m.uid, _Stream())
-            if not (m.finished and m.next_token == self.eos_token_id):
+            if not m.eos:
                 st.ids.append(m.next_token)
             ctx_ids.append(st.ids[st.window : st.prefix])
             full_ids.append(st.ids[st.window :])

@@ -1,0 +1,185 @@
+"""Scheduler, cache manager and batch plan under a fake model (CPU, no GPU).
+
+The real engine runs (page table, batch plan upload, out_loc, last-token rows, greedy sampler) with
+the model replaced by a rule whose next token is a function of (last token, position):
+
+    next = (7 * token + 3 * position + 1) mod V
+
+so every request's output is known from its prompt alone, whatever the scheduler does with it:
+chunked prefill, prefix-cache hits, queueing behind a small running set or a tight KV pool, EOS.
+The fake model also checks, on every forward, that the KV slots it is about to write belong to no
+other live request (shared prefix slots are only ever read).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from minisgl.core import SamplingParams, get_global_ctx
+from minisgl.models.synthetic import make_checkpoint
+
+V = 1000
+
+
+def rule(tok: int, pos: int) -> int:
+    return (7 * tok + 3 * pos + 1) % V
+
+
+def expected(prompt, n, eos=None):
+    out, tok, pos = [], prompt[-1], len(prompt) - 1
+    for _ in range(n):
+        tok = rule(tok, pos)
+        pos += 1
+        if tok == eos:
+            break
+        out.append(tok)
+    return out
+
+
+class FakeModel:
+    """Stands in for the network. Besides producing the rule's token it keeps a mirror of the KV
+    pool (slot -> (token, position) written there) and checks that every position a request would
+    attend to maps to a slot holding exactly that request's (token, position)."""
+
+    def __init__(self, engine):
+        self.engine = engine
+        self.forwards = 0
+        self.kv = {}
+
+    def _check_kv(self, batch):
+        for r in batch.reqs:
+            ids = r.input_ids.tolist()
+            assert len(ids) == r.device_len
+            for p in range(r.cached_len, r.device_len):
+                self.kv[int(r.slots[p])] = (ids[p], p)
+        for r in batch.reqs:
+            ids = r.input_ids.tolist()
+            got = [self.kv.get(int(s)) for s in r.slots[: r.device_len]]
+            want = [(t, p) for p, t in enumerate(ids)]
+            bad = [p for p in range(r.device_len) if got[p] != want[p]]
+            assert not bad, f"req {r.uid}: positions {bad[:8]} read KV written for another token"
+
+    def forward(self):
+        ctx = get_global_ctx()
+        b = ctx.batch
+        self.forwards += 1
+        self._check_kv(b)
+        # out_loc must be the page-table slots of the extend tokens
+        want = np.concatenate([r.slots[r.cached_len : r.device_len] for r in b.padded_reqs])
+        assert b.out_loc.tolist() == want.tolist()
+        idx = b.attn_metadata.get_last_indices(b.size)
+        tok = b.input_ids[idx].long()
+        pos = b.positions[idx].long()
+        nxt = (7 * tok + 3 * pos + 1) % V
+        logits = torch.zeros(b.size, V)
+        logits[torch.arange(b.size), nxt] = 1.0
+        return logits
+
+
+@pytest.fixture(scope="module")
+def tiny_path(tmp_path_factory):
+    return make_checkpoint("tiny-qwen3", str(tmp_path_factory.mktemp("m")))
+
+
+def make_llm(path, port, **kw):
+    from minisgl.llm import LLM
+
+    kw.setdefault("max_running_req", 8)
+    llm = LLM(path, dtype=torch.float32, device="cpu", use_dummy_weight=True, distributed_port=port, **kw)
+    llm.engine.model = FakeModel(llm.engine)
+    return llm
+
+
+def prompts_with_shared_prefixes(seed, n, lo=5, hi=90):
+    g = np.random.default_rng(seed)
+    roots = [g.integers(0, V, 40).tolist() for _ in range(3)]
+    out = []
+    for i in range(n):
+        if i % 3 == 0:
+            out.append(g.integers(0, V, int(g.integers(lo, hi))).tolist())
+        else:  # a shared prefix of 8..40 tokens plus a private tail
+            root = roots[i % 3][: int(g.integers(8, 41))]
+            out.append(root + g.integers(0, V, int(g.integers(1, 30))).tolist())
+    return out
+
+
+@pytest.mark.parametrize(
+    "page,cache,budget,running,pages",
+    [
+        (1, "radix", 16384, 8, None),
+        (4, "radix", 32, 4, None),  # chunked prefill: prompts longer than the per-step budget
+        (16, "radix", 64, 3, 24),  # tight pool: requests queue for pages
+        (8, "naive", 48, 8, None),
+        (64, "radix", 16384, 16, None),
+    ],
+)
+def test_fake_model_outputs(tiny_path, free_port, page, cache, budget, running, pages):
+    llm = make_llm(tiny_path, free_port, page_size=page, cache_type=cache, max_extend_tokens=budget,
+                   max_running_req=running, num_page_override=pages)
+    try:
+        prompts = prompts_with_shared_prefixes(page, 18)
+        lens = [3 + (i * 5) % 23 for i in range(len(prompts))]
+        sps = [SamplingParams(max_tokens=n, ignore_eos=True) for n in lens]
+        for rep in range(2):  # the second pass hits the prefix cache left by the first
+            outs = llm.generate(prompts, sps)
+            for p, n, o in zip(prompts, lens, outs):
+                assert o["token_ids"] == expected(p, n), (rep, p)
+            llm.cache_manager.check_integrity()
+        cm = llm.cache_manager
+        assert cm.available_size == cm.num_pages * cm.page_size  # every page free or evictable
+        assert not llm.decode_manager.running and not llm.prefill_manager.pending_list
+    finally:
+        llm.shutdown()
+
+
+def test_eos_stops_and_is_not_returned(tiny_path, free_port):
+    llm = make_llm(tiny_path, free_port)
+    try:
+        eos = llm.eos_token_id
+        assert eos is not None and eos < V
+        # prompts whose continuation reaches EOS at a known step: solve rule(tok, pos) == eos
+        prompts, want = [], []
+        for L in (6, 11, 17):
+            pos = L - 1
+            tok = next(t for t in range(V) if rule(t, pos) == eos)
+            prompts.append([5] * (L - 1) + [tok])
+            want.append([])
+        prompts.append([1, 2, 3])
+        want.append(expected([1, 2, 3], 12, eos))
+        outs = llm.generate(prompts, SamplingParams(max_tokens=12))
+        assert [o["token_ids"] for o in outs] == want
+        ign = llm.generate(prompts[:1], SamplingParams(max_tokens=4, ignore_eos=True))
+        assert ign[0]["token_ids"] == expected(prompts[0], 4) and ign[0]["token_ids"][0] == eos
+        llm.cache_manager.check_integrity()
+    finally:
+        llm.shutdown()
+
+
+def test_max_tokens_clamped_to_context(tiny_path, free_port):
+    llm = make_llm(tiny_path, free_port, max_seq_len_override=64)
+    try:
+        p = list(range(1, 51))
+        out = llm.generate([p], SamplingParams(max_tokens=100, ignore_eos=True))[0]["token_ids"]
+        assert out == expected(p, 14)  # 64 - 50 tokens of room
+    finally:
+        llm.shutdown()
+
+
+def test_concurrent_requests_with_one_uncached_prefix(tiny_path, free_port):
+    """Requests that share a prefix nobody has cached yet are prefilled side by side, each into its
+    own pages. When the first inserts the prefix, the others' copies become redundant and go back
+    to the free list; the requests still decoding must then read the cached copy, not their freed
+    pages, which new requests are about to overwrite."""
+    llm = make_llm(tiny_path, free_port, page_size=4, max_running_req=6, num_page_override=64)
+    try:
+        g = np.random.default_rng(1)
+        root = g.integers(0, V, 32).tolist()
+        prompts = [root + g.integers(0, V, 6).tolist() for _ in range(6)]
+        prompts += [g.integers(0, V, 30).tolist() for _ in range(12)]
+        lens = [40] * 6 + [10] * 12
+        outs = llm.generate(prompts, [SamplingParams(max_tokens=n, ignore_eos=True) for n in lens])
+        for p, n, o in zip(prompts, lens, outs):
+            assert o["token_ids"] == expected(p, n)
+        llm.cache_manager.check_integrity()
+    finally:
+        llm.shutdown()
