@@ -1,7 +1,11 @@
 """Build the native extensions in-tree (no pip install): ``python -m minisgl._build``.
 
-* ``minisgl/_host*.so``  - host C++ runtime (radix tree), pybind11 only.
-* ``minisgl/_cuda*.so``  - sm_100a CUDA kernels + torch bindings.
+* ``minisgl/_host*.so``     - host C++ runtime (radix tree), pybind11 only.
+* ``minisgl/_cuda*.so``     - sm_100a CUDA kernels + torch bindings.
+* ``minisgl/_cuda_bc*.so``  - the same kernels compiled with ``-DMINISGL_BOUNDS_CHECK=1``: every
+  data-dependent index (token ids, KV slots, positions, page-table rows and entries, MoE rows) is
+  checked, a violation is recorded in the device error word and the access is skipped. Loaded
+  instead of ``_cuda`` when ``MINISGL_BOUNDS_CHECK=1``.
 
 CUDA sources are compiled with ``-gencode arch=compute_100a,code=sm_100a`` only. Kernel .cu files
 do not include torch headers (fast to compile); ``csrc/bindings.cpp`` adapts tensors to them.
@@ -55,11 +59,11 @@ def host_target() -> str:
     return os.path.join(ROOT, "_host" + EXT_SUFFIX)
 
 
-def cuda_target() -> str:
-    return os.path.join(ROOT, "_cuda" + EXT_SUFFIX)
+def cuda_target(bounds_check: bool = False) -> str:
+    return os.path.join(ROOT, ("_cuda_bc" if bounds_check else "_cuda") + EXT_SUFFIX)
 
 
-def ninja_file(debug_bounds: bool = False) -> str:
+def ninja_file() -> str:
     os.makedirs(BUILD, exist_ok=True)
     cuda = _cuda_home()
     pyinc = _py_includes()
@@ -70,22 +74,21 @@ def ninja_file(debug_bounds: bool = False) -> str:
     )
     inc = " ".join(f"-I{p}" for p in [CSRC] + pyinc)
     tinc_s = " ".join(f"-isystem {p}" for p in tinc)
-    extra = " -DMINISGL_BOUNDS_CHECK=1" if debug_bounds else ""
     lines = [
         "ninja_required_version = 1.3",
         f"cxx = g++",
         f"nvcc = {cuda}/bin/nvcc",
         f"cxxflags = -O3 -std=c++17 -fPIC -fvisibility=hidden {inc} {_abi_flag()}",
-        f"torchflags = {tinc_s} -DTORCH_EXTENSION_NAME=_cuda -DTORCH_API_INCLUDE_EXTENSION_H",
+        f"torchflags = {tinc_s} -DTORCH_API_INCLUDE_EXTENSION_H",
         f"nvccflags = -O3 -std=c++17 {' '.join(GENCODE)} -lineinfo --expt-relaxed-constexpr "
         f"-Xcompiler -fPIC -Xcompiler -fvisibility=hidden {inc} -I{cuda}/include "
-        f"-DNDEBUG{extra} -Xptxas -warn-spills",
+        f"-DNDEBUG -Xptxas -warn-spills",
         "rule cxx",
         "  command = $cxx -MMD -MF $out.d $cxxflags $extra -c $in -o $out",
         "  depfile = $out.d",
         "  deps = gcc",
         "rule nvcc",
-        "  command = $nvcc -MD -MF $out.d $nvccflags -c $in -o $out",
+        "  command = $nvcc -MD -MF $out.d $nvccflags $extra -c $in -o $out",
         "  depfile = $out.d",
         "  deps = gcc",
         "rule link",
@@ -101,23 +104,28 @@ def ninja_file(debug_bounds: bool = False) -> str:
         lines.append(f"build {o}: cxx {s}")
     lines.append(f"build {host_target()}: link {' '.join(host_objs)}")
     lines.append("  ldflags = ")
-    # cuda kernels
+    # cuda kernels: release and bounds-check variants of the same sources
     cu_srcs = sorted(glob.glob(os.path.join(CSRC, "kernels", "*.cu")))
-    cu_objs = []
-    for s in cu_srcs:
-        o = os.path.join(BUILD, "cu_" + os.path.basename(s) + ".o")
-        cu_objs.append(o)
-        lines.append(f"build {o}: nvcc {s}")
     bind = os.path.join(CSRC, "bindings.cpp")
-    bind_o = os.path.join(BUILD, "bindings.o")
-    lines.append(f"build {bind_o}: cxx {bind}")
-    lines.append(f"  extra = $torchflags -I{cuda}/include")
     libdirs = " ".join(f"-L{p} -Wl,-rpath,{p}" for p in tlib)
-    lines.append(f"build {cuda_target()}: link {' '.join(cu_objs + [bind_o])}")
-    lines.append(
-        f"  ldflags = {libdirs} -L{cuda}/lib64 -lc10 -ltorch -ltorch_cpu -ltorch_python "
-        f"-lc10_cuda -ltorch_cuda -lcudart"
-    )
+    for bc in (False, True):
+        tag = "bc_" if bc else ""
+        name = "_cuda_bc" if bc else "_cuda"
+        cu_objs = []
+        for s in cu_srcs:
+            o = os.path.join(BUILD, f"cu_{tag}" + os.path.basename(s) + ".o")
+            cu_objs.append(o)
+            lines.append(f"build {o}: nvcc {s}")
+            if bc:
+                lines.append("  extra = -DMINISGL_BOUNDS_CHECK=1")
+        bind_o = os.path.join(BUILD, f"bindings_{tag}.o" if bc else "bindings.o")
+        lines.append(f"build {bind_o}: cxx {bind}")
+        lines.append(f"  extra = $torchflags -DTORCH_EXTENSION_NAME={name} -I{cuda}/include")
+        lines.append(f"build {cuda_target(bc)}: link {' '.join(cu_objs + [bind_o])}")
+        lines.append(
+            f"  ldflags = {libdirs} -L{cuda}/lib64 -lc10 -ltorch -ltorch_cpu -ltorch_python "
+            f"-lc10_cuda -ltorch_cuda -lcudart"
+        )
     path = os.path.join(BUILD, "build.ninja")
     _write_ninja(path, "\n".join(lines) + "\n")
     return path
@@ -142,6 +150,6 @@ def build_host() -> None:
 
 
 if __name__ == "__main__":
-    which = sys.argv[1:] or None
-    build([host_target() if w == "host" else cuda_target() for w in which] if which else None,
-          verbose="-v" in sys.argv)
+    names = {"host": host_target(), "cuda": cuda_target(), "bounds": cuda_target(True)}
+    which = [w for w in sys.argv[1:] if w in names]
+    build([names[w] for w in which] or None, verbose="-v" in sys.argv)

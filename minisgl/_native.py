@@ -49,7 +49,10 @@ def cuda():
     try:
         import torch  # noqa: F401  (loads libtorch before the extension)
 
-        return _CountingModule(importlib.import_module("minisgl._cuda"))
+        from minisgl.env import ENV
+
+        name = "minisgl._cuda_bc" if ENV.BOUNDS_CHECK else "minisgl._cuda"
+        return _CountingModule(importlib.import_module(name))
     except ImportError as e:
         raise RuntimeError(
             "minisgl CUDA kernels are not built; run `python -m minisgl._build` "

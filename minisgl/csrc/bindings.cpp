@@ -128,7 +128,7 @@ void store_kv(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v_cache
   CHECK(k.stride(1) == 1 && v.stride(1) == 1, "store_kv rows must be contiguous");
   CHECK(k.stride(0) % 8 == 0 && v.stride(0) % 8 == 0, "store_kv row stride alignment");
   msgl_store_kv(k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out_loc.data_ptr<int32_t>(),
-                k.size(0), row, k.stride(0), v.stride(0), row, stream());
+                k.size(0), row, k.stride(0), v.stride(0), row, k_cache.size(0), stream());
 }
 
 void qk_norm_rope_store(at::Tensor q_out, at::Tensor qkv, at::Tensor positions, at::Tensor cos_sin,
@@ -146,7 +146,7 @@ void qk_norm_rope_store(at::Tensor q_out, at::Tensor qkv, at::Tensor positions, 
   msgl_qk_norm_rope_store(q_out.data_ptr(), qkv.data_ptr(), positions.data_ptr<int32_t>(),
                           cos_sin.data_ptr<float>(), opt_ptr(q_norm), opt_ptr(k_norm), eps,
                           k_cache.data_ptr(), v_cache.data_ptr(), out_loc.data_ptr<int32_t>(),
-                          qkv.size(0), nq, nkv, hd, nkv * hd, stream());
+                          qkv.size(0), nq, nkv, hd, nkv * hd, k_cache.size(0), cos_sin.size(0), stream());
 }
 
 // values (optional, fp32 [rows]) receives each row's maximum; vocab < 0 means all columns
@@ -191,7 +191,7 @@ void attention_prefill(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tenso
   msgl_attention_prefill(o.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                          page_table.data_ptr<int32_t>(), page_table.stride(0), rows.data_ptr<int32_t>(),
                          cu_q.data_ptr<int32_t>(), kv_lens.data_ptr<int32_t>(), rows.size(0), q.size(0),
-                         max_q_len, nq, nkv, hd, k_cache.stride(0), scale, window,
+                         max_q_len, nq, nkv, hd, k_cache.stride(0), k_cache.size(0), scale, window,
                          sinks.has_value() ? sinks->data_ptr<float>() : nullptr, stream());
 }
 
@@ -211,8 +211,8 @@ void attention_decode(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor
   if (sinks.has_value()) { check_dtype(*sinks, at::kFloat, "sinks"); CHECK(sinks->numel() == nq, "sinks size"); }
   msgl_attention_decode(o.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                         page_table.data_ptr<int32_t>(), page_table.stride(0), rows.data_ptr<int32_t>(),
-                        kv_lens.data_ptr<int32_t>(), bs, nq, nkv, hd, k_cache.stride(0), scale, window,
-                        sinks.has_value() ? sinks->data_ptr<float>() : nullptr, num_splits,
+                        kv_lens.data_ptr<int32_t>(), bs, nq, nkv, hd, k_cache.stride(0), k_cache.size(0), scale,
+                        window, sinks.has_value() ? sinks->data_ptr<float>() : nullptr, num_splits,
                         workspace.data_ptr(), stream());
 }
 
@@ -311,7 +311,8 @@ void moe_align(at::Tensor ids, int64_t E, int64_t bn, at::Tensor perm, at::Tenso
 void moe_gather(at::Tensor xs, at::Tensor x, at::Tensor perm, int64_t topk) {
   check_bf16(xs, "xs"); check_bf16(x, "x"); check_i32(perm, "perm"); check_contig(x, "x"); check_contig(xs, "xs");
   CHECK(x.size(1) % 8 == 0 && xs.size(1) == x.size(1), "gather shapes");
-  msgl_moe_gather(xs.data_ptr(), x.data_ptr(), perm.data_ptr<int32_t>(), xs.size(0), x.size(1), topk, stream());
+  msgl_moe_gather(xs.data_ptr(), x.data_ptr(), perm.data_ptr<int32_t>(), xs.size(0), x.size(1), topk, x.size(0),
+                  stream());
 }
 
 void moe_act(at::Tensor out, at::Tensor y, int64_t act, at::Tensor perm) {
@@ -324,7 +325,7 @@ void moe_combine(at::Tensor out, at::Tensor y, at::Tensor w, at::Tensor inv, int
   check_bf16(out, "out"); check_bf16(y, "y"); check_dtype(w, at::kFloat, "w"); check_i32(inv, "inv");
   CHECK(out.size(1) % 2 == 0 && y.size(1) == out.size(1), "combine shapes");
   msgl_moe_combine(out.data_ptr(), y.data_ptr(), w.data_ptr<float>(), inv.data_ptr<int32_t>(), out.size(0),
-                   out.size(1), topk, stream());
+                   out.size(1), topk, y.size(0), stream());
 }
 
 // ----- peer-memory collectives
@@ -396,7 +397,7 @@ std::tuple<int64_t, int64_t> get_error() {
 
 }  // namespace
 
-PYBIND11_MODULE(_cuda, m) {
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "minisgl sm_100a kernels";
   m.def("embedding", &embedding);
   m.def("rmsnorm", &rmsnorm);

@@ -20,11 +20,12 @@ void msgl_fused_add_rmsnorm(void* x, void* residual, const void* w, int rows, in
 void msgl_act_and_mul(void* out, const void* x, int rows, int inter, int act, cudaStream_t s);
 void msgl_store_kv(const void* k, const void* v, void* k_cache, void* v_cache,
                    const int32_t* out_loc, int n, int row_elems, int64_t k_stride, int64_t v_stride,
-                   int64_t cache_stride, cudaStream_t s);
+                   int64_t cache_stride, int64_t num_slots, cudaStream_t s);
 void msgl_qk_norm_rope_store(void* q_out, const void* qkv, const int32_t* positions,
                              const float* cos_sin, const void* q_norm, const void* k_norm,
                              float eps, void* k_cache, void* v_cache, const int32_t* out_loc,
-                             int n, int nq, int nkv, int hd, int64_t cache_stride, cudaStream_t s);
+                             int n, int nq, int nkv, int hd, int64_t cache_stride, int64_t num_slots,
+                             int max_pos, cudaStream_t s);
 // row argmax over the first `vocab` columns; out_val (optional) receives the maximum
 void msgl_argmax(int32_t* out, float* out_val, const void* logits, int rows, int vocab, int64_t stride,
                  int is_fp32, cudaStream_t s);
@@ -58,23 +59,24 @@ void msgl_moe_route(const float* logits, int T, int E, int topk, int renorm, int
 // experts [e0, e0 + E) are local (expert parallelism); other assignments get inv = -1
 void msgl_moe_align(const int32_t* ids, int pairs, int E, int e0, int bn, int max_tiles, int rows_cap, int32_t* perm,
                     int32_t* inv, void* work, int32_t* tile_count, cudaStream_t s);
-void msgl_moe_gather(void* xs, const void* x, const int32_t* perm, int rows, int H, int topk, cudaStream_t s);
+void msgl_moe_gather(void* xs, const void* x, const int32_t* perm, int rows, int H, int topk, int x_rows,
+                     cudaStream_t s);
 void msgl_moe_act(void* out, const void* y, int rows, int inter, int act, const int32_t* perm, cudaStream_t s);
 void msgl_moe_combine(void* out, const void* y, const float* w, const int32_t* inv, int T, int H, int topk,
-                      cudaStream_t s);
+                      int y_rows, cudaStream_t s);
 
 // ----- paged attention (bf16 q/kv, fp32 softmax)
 void msgl_attention_prefill(void* o, const void* q, const void* k_cache, const void* v_cache,
                             const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
                             const int32_t* cu_q, const int32_t* kv_lens, int num_reqs,
                             int total_q, int max_q_len, int nq, int nkv, int hd,
-                            int64_t cache_stride, float sm_scale, int window, const float* sinks,
-                            cudaStream_t s);
+                            int64_t cache_stride, int64_t num_slots, float sm_scale, int window,
+                            const float* sinks, cudaStream_t s);
 void msgl_attention_decode(void* o, const void* q, const void* k_cache, const void* v_cache,
                            const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
                            const int32_t* kv_lens, int bs, int nq, int nkv, int hd,
-                           int64_t cache_stride, float sm_scale, int window, const float* sinks,
-                           int num_splits, void* workspace, cudaStream_t s);
+                           int64_t cache_stride, int64_t num_slots, float sm_scale, int window,
+                           const float* sinks, int num_splits, void* workspace, cudaStream_t s);
 
 // tcgen05 ragged causal prefill attention (head_dim 128, page size 16/32/64; see attention.cu).
 // Returns 0 on success, 2 if a tensor map could not be encoded, 3 on unsupported arguments.

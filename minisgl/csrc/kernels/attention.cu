@@ -39,6 +39,7 @@ struct AttnParams {
   const int32_t* kv_lens;
   int nq, nkv, group;
   int64_t cache_stride;
+  int64_t num_slots;  // cache rows (index checks of the bounds-check build)
   float scale_log2;
   int window;
   const float* sinks;
@@ -89,8 +90,9 @@ __device__ __forceinline__ void load_kv_chunk(uint32_t sk, uint32_t sv, const At
     const int c = threadIdx.x + i * kWarps * 32;
     const int key = c / CH, part = c % CH;
     const int pos = k0 + key;
-    const bool valid = pos < kend;
-    const int64_t slot = valid ? pt[pos] : 0;
+    bool valid = pos < kend;
+    int64_t slot = valid ? pt[pos] : 0;
+    if (valid && !MSGL_IN_BOUNDS(slot >= 0 && slot < p.num_slots, kBcAttnSlot)) valid = false, slot = 0;
     const int64_t off = slot * p.cache_stride + (int64_t)kvh * HD + part * 8;
     cp_async16(sk + swz<HD>(key, part), p.k + off, valid);
     cp_async16(sv + swz<HD>(key, part), p.v + off, valid);
@@ -189,6 +191,7 @@ __global__ void __launch_bounds__(kWarps * 32) prefill_kernel(AttnParams p) {
   const int total_rows = n * G;
   if (qb * 64 >= total_rows) return;
   const int L = p.kv_lens[b], row = p.rows[b];
+  if (!MSGL_IN_BOUNDS(row >= 0 && L >= n && L <= p.pt_stride, kBcAttnRow)) return;  // CTA-uniform
   const int qpos0 = L - n;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -334,6 +337,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
   const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z;
   const int G = p.group;
   const int L = p.kv_lens[b], row = p.rows[b];
+  if (!MSGL_IN_BOUNDS(row >= 0 && L >= 0 && L <= p.pt_stride, kBcAttnRow)) return;  // CTA-uniform
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int CH = HD / 8;
   constexpr int kStageBytes = 2 * KC * HD * 2;
@@ -370,7 +374,11 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(AttnParams p) {
   for (int seg0 = kbeg; seg0 < kend; seg0 += kSlots) {
     const int seg1 = min(kend, seg0 + kSlots);
     __syncthreads();  // previous segment's readers are done with `slots`
-    for (int i = threadIdx.x; i < seg1 - seg0; i += kWarps * 32) slots[i] = pt[seg0 + i];
+    for (int i = threadIdx.x; i < seg1 - seg0; i += kWarps * 32) {
+      int sl = pt[seg0 + i];
+      if (!MSGL_IN_BOUNDS(sl >= 0 && sl < p.num_slots, kBcAttnSlot)) sl = 0;
+      slots[i] = sl;
+    }
     __syncthreads();
     const int nchunks = (seg1 - seg0 + KC - 1) / KC;
 #pragma unroll
@@ -552,7 +560,7 @@ void run_decode(const AttnParams& p, int bs, cudaStream_t s) {
 AttnParams make_params(void* o, const void* q, const void* k, const void* v, const int32_t* pt,
                        int64_t pt_stride, const int32_t* rows, const int32_t* cu_q, const int32_t* kv_lens,
                        int nq, int nkv, int64_t cache_stride, float sm_scale, int window,
-                       const float* sinks) {
+                       const float* sinks, int64_t num_slots = INT64_MAX) {
   AttnParams p;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
   p.q = reinterpret_cast<const __nv_bfloat16*>(q);
@@ -567,6 +575,7 @@ AttnParams make_params(void* o, const void* q, const void* k, const void* v, con
   p.nkv = nkv;
   p.group = nq / nkv;
   p.cache_stride = cache_stride;
+  p.num_slots = num_slots;
   p.scale_log2 = sm_scale * kLog2e;
   p.window = window;
   p.sinks = sinks;
@@ -581,11 +590,11 @@ extern "C" void msgl_attention_prefill(void* o, const void* q, const void* k_cac
                                        const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
                                        const int32_t* cu_q, const int32_t* kv_lens, int num_reqs,
                                        int total_q, int max_q_len, int nq, int nkv, int hd,
-                                       int64_t cache_stride, float sm_scale, int window,
+                                       int64_t cache_stride, int64_t num_slots, float sm_scale, int window,
                                        const float* sinks, cudaStream_t s) {
   if (num_reqs == 0 || total_q == 0) return;
   AttnParams p = make_params(o, q, k_cache, v_cache, page_table, pt_stride, rows, cu_q, kv_lens, nq,
-                             nkv, cache_stride, sm_scale, window, sinks);
+                             nkv, cache_stride, sm_scale, window, sinks, num_slots);
   if (hd == 64) run_prefill<64>(p, num_reqs, max_q_len, s);
   else run_prefill<128>(p, num_reqs, max_q_len, s);
 }
@@ -593,12 +602,12 @@ extern "C" void msgl_attention_prefill(void* o, const void* q, const void* k_cac
 extern "C" void msgl_attention_decode(void* o, const void* q, const void* k_cache, const void* v_cache,
                                       const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
                                       const int32_t* kv_lens, int bs, int nq, int nkv, int hd,
-                                      int64_t cache_stride, float sm_scale, int window,
+                                      int64_t cache_stride, int64_t num_slots, float sm_scale, int window,
                                       const float* sinks, int num_splits, void* workspace,
                                       cudaStream_t s) {
   if (bs == 0) return;
   AttnParams p = make_params(o, q, k_cache, v_cache, page_table, pt_stride, rows, nullptr, kv_lens,
-                             nq, nkv, cache_stride, sm_scale, window, sinks);
+                             nq, nkv, cache_stride, sm_scale, window, sinks, num_slots);
   p.num_splits = num_splits < 1 ? 1 : num_splits;
   p.ws = reinterpret_cast<float*>(workspace);
   if (hd == 64) run_decode<64>(p, bs, s);
@@ -640,6 +649,7 @@ struct PagedDecodeParams {
   __nv_bfloat16* o;
   const int32_t* page_table;
   int64_t pt_stride;
+  int64_t num_slots;
   const int32_t* rows;
   const int32_t* kv_lens;
   const int4* work;       // per entry two int4: {b, blk0, blk1, j}, {nchunks, slot0, -, -}
@@ -786,10 +796,13 @@ paged_decode_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
         const int lo = p.window > 0 ? max(0, L - p.window) : 0;
         const int first = max(w0.y, lo / 64), blk1 = w0.z;
         const int32_t* pt = p.page_table + (int64_t)p.rows[b] * p.pt_stride;
-        const int ngroups = min(kPdMaxGroups, max(0, blk1 - first) * gpb);
+        int ngroups = min(kPdMaxGroups, max(0, blk1 - first) * gpb);
+        if (!MSGL_IN_BOUNDS(p.rows[b] >= 0 && L >= 0 && L <= p.pt_stride, kBcAttnRow)) ngroups = 0;  // warp-uniform
         for (int gi = lane; gi < ngroups; gi += 32) {
           const int pos = first * 64 + gi * g;
-          D.slots[gi] = pos < L ? pt[pos] : 0;
+          int sl = pos < L ? pt[pos] : 0;
+          if (!MSGL_IN_BOUNDS(sl >= 0 && sl < p.num_slots, kBcAttnSlot)) sl = 0;
+          D.slots[gi] = sl;
         }
         if (lane == 0) {
           D.b = b; D.kvh = kvh; D.first = first; D.blk1 = first + ngroups / gpb; D.j = w0.w;
@@ -1101,6 +1114,7 @@ struct FmhaParams {
   __nv_bfloat16* o;
   const int32_t* page_table;
   int64_t pt_stride;
+  int64_t num_slots;
   const int32_t* rows;
   const int32_t* cu_q;
   const int32_t* kv_lens;
@@ -1153,6 +1167,7 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   if (t0 >= n) return;
   const int t1 = min(n, t0 + TT);
   const int L = p.kv_lens[b];
+  if (!MSGL_IN_BOUNDS(p.rows[b] >= 0 && L >= n && L <= p.pt_stride, kBcAttnRow)) return;  // CTA-uniform
   const int qpos0 = L - n;
   const int kend = qpos0 + t1;  // exclusive
   int kbeg = 0;
@@ -1199,6 +1214,7 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       if (g0 + lane < ngroups) {
         const int pos = blk0 * kFmKB + (g0 + lane) * g;
         slot = pos < L ? pt[pos] : 0;
+        if (!MSGL_IN_BOUNDS(slot >= 0 && slot < p.num_slots, kBcAttnSlot)) slot = 0;
       }
       const int gend = min(32, ngroups - g0);
       for (int k = 0; k < gend; ++k) {
@@ -1394,6 +1410,7 @@ extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
   p.page_table = page_table;
   p.pt_stride = pt_stride;
+  p.num_slots = num_slots;
   p.rows = rows;
   p.cu_q = cu_q;
   p.kv_lens = kv_lens;
@@ -1438,6 +1455,7 @@ extern "C" int msgl_attention_decode_paged(void* o, const void* q, int q_rows, c
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
   p.page_table = page_table;
   p.pt_stride = pt_stride;
+  p.num_slots = num_slots;
   p.rows = rows;
   p.kv_lens = kv_lens;
   p.work = reinterpret_cast<const int4*>(work);

@@ -32,6 +32,25 @@ MSGL_DEVICE void report_error(int code, int info) {
   if (atomicCAS(&minisgl_error_word, 0, code) == 0) minisgl_error_info = info;
 }
 
+// Index checks of the bounds-check build (compiled with -DMINISGL_BOUNDS_CHECK=1, loaded when
+// MINISGL_BOUNDS_CHECK=1): a failed check records kErrBounds with the site below as its info and
+// evaluates to false, and the caller skips the access instead of faulting (no trap, no device
+// assert). In the release build the macro is the constant true and the checks compile away.
+enum : int {
+  kBcEmbeddingId = 1,   // token id outside the vocabulary (unmasked embedding)
+  kBcKvSlot = 2,        // KV-cache slot outside [0, num_slots) in a cache store
+  kBcRopePos = 3,       // position outside the cos/sin table
+  kBcAttnRow = 4,       // page-table row or kv length outside the page table
+  kBcAttnSlot = 5,      // page-table entry outside [0, num_slots) in an attention read
+  kBcMoePerm = 6,       // MoE gather index outside the token rows
+  kBcMoeInv = 7,        // MoE combine index outside the expert-output rows
+};
+#if defined(MINISGL_BOUNDS_CHECK) && MINISGL_BOUNDS_CHECK
+#define MSGL_IN_BOUNDS(cond, site) ((cond) ? true : (::msgl::report_error(::msgl::kErrBounds, (site)), false))
+#else
+#define MSGL_IN_BOUNDS(cond, site) true
+#endif
+
 // ------------------------------------------------------------------------------------------
 // scalar / vector helpers
 struct alignas(16) bf16x8 {

@@ -35,6 +35,7 @@ __global__ void embedding_kernel(uint4* __restrict__ out, const uint4* __restric
   int id = ids[row] - vocab_start;
   const bool valid = id >= 0 && id < vocab_len;
   uint4* dst = out + (size_t)row * vec_per_row;
+  if (!valid && !masked) (void)MSGL_IN_BOUNDS(false, kBcEmbeddingId);
   if (masked && !valid) {
     for (int i = lane; i < vec_per_row; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
     return;
@@ -134,13 +135,15 @@ __global__ void act_and_mul_kernel(uint4* __restrict__ out, const uint4* __restr
 __global__ void store_kv_kernel(const uint4* __restrict__ k, const uint4* __restrict__ v,
                                 uint4* __restrict__ kc, uint4* __restrict__ vc,
                                 const int32_t* __restrict__ loc, int n, int vec_per_row,
-                                int64_t k_stride_v, int64_t v_stride_v, int64_t c_stride_v) {
+                                int64_t k_stride_v, int64_t v_stride_v, int64_t c_stride_v,
+                                int64_t num_slots) {
   pdl_wait();
   pdl_launch();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= n) return;
   const int64_t slot = loc[row];
+  if (!MSGL_IN_BOUNDS(slot >= 0 && slot < num_slots, kBcKvSlot)) return;
   for (int i = lane; i < vec_per_row; i += 32) {
     kc[slot * c_stride_v + i] = k[row * k_stride_v + i];
     vc[slot * c_stride_v + i] = v[row * v_stride_v + i];
@@ -161,7 +164,8 @@ __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* __restrict__ q_out,
                                           __nv_bfloat16* __restrict__ k_cache,
                                           __nv_bfloat16* __restrict__ v_cache,
                                           const int32_t* __restrict__ out_loc, int n, int nq,
-                                          int nkv, int64_t cache_stride) {
+                                          int nkv, int64_t cache_stride, int64_t num_slots,
+                                          int max_pos) {
   pdl_wait();
   pdl_launch();
   constexpr int HD = 64 * E;
@@ -170,6 +174,9 @@ __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* __restrict__ q_out,
   const int lane = threadIdx.x & 31;
   if (gw >= n * heads) return;
   const int t = gw / heads, h = gw % heads;
+  // (warp-uniform checks: one warp owns one (token, head))
+  if (h >= nq && !MSGL_IN_BOUNDS(out_loc[t] >= 0 && out_loc[t] < num_slots, kBcKvSlot)) return;
+  if (h < nq + nkv && !MSGL_IN_BOUNDS(positions[t] >= 0 && positions[t] < max_pos, kBcRopePos)) return;
   const __nv_bfloat16* src = qkv + (size_t)t * heads * HD + (size_t)h * HD;
   float a[E], b[E];
 #pragma unroll
@@ -331,20 +338,20 @@ extern "C" void msgl_act_and_mul(void* out, const void* x, int rows, int inter, 
 
 extern "C" void msgl_store_kv(const void* k, const void* v, void* k_cache, void* v_cache,
                               const int32_t* out_loc, int n, int row_elems, int64_t k_stride,
-                              int64_t v_stride, int64_t cache_stride, cudaStream_t s) {
+                              int64_t v_stride, int64_t cache_stride, int64_t num_slots, cudaStream_t s) {
   if (n == 0) return;
   const int wpb = 8;
   msgl_launch(store_kv_kernel, (n + wpb - 1) / wpb, wpb * 32, 0, s, 1, reinterpret_cast<const uint4*>(k),
               reinterpret_cast<const uint4*>(v), reinterpret_cast<uint4*>(k_cache),
               reinterpret_cast<uint4*>(v_cache), out_loc, n, row_elems / 8, k_stride / 8, v_stride / 8,
-              cache_stride / 8);
+              cache_stride / 8, num_slots);
 }
 
 extern "C" void msgl_qk_norm_rope_store(void* q_out, const void* qkv, const int32_t* positions,
                                         const float* cos_sin, const void* q_norm, const void* k_norm,
                                         float eps, void* k_cache, void* v_cache,
                                         const int32_t* out_loc, int n, int nq, int nkv, int hd,
-                                        int64_t cache_stride, cudaStream_t s) {
+                                        int64_t cache_stride, int64_t num_slots, int max_pos, cudaStream_t s) {
   if (n == 0) return;
   const int warps = n * (nq + 2 * nkv), wpb = 8;
   const dim3 grid((warps + wpb - 1) / wpb);
@@ -355,11 +362,11 @@ extern "C" void msgl_qk_norm_rope_store(void* q_out, const void* qkv, const int3
   auto kc = reinterpret_cast<__nv_bfloat16*>(k_cache);
   auto vc = reinterpret_cast<__nv_bfloat16*>(v_cache);
   if (hd == 64)
-    msgl_launch(qk_norm_rope_store_kernel<1>, grid, wpb * 32, 0, s, 1, qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride);
+    msgl_launch(qk_norm_rope_store_kernel<1>, grid, wpb * 32, 0, s, 1, qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride, num_slots, max_pos);
   else if (hd == 128)
-    msgl_launch(qk_norm_rope_store_kernel<2>, grid, wpb * 32, 0, s, 1, qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride);
+    msgl_launch(qk_norm_rope_store_kernel<2>, grid, wpb * 32, 0, s, 1, qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride, num_slots, max_pos);
   else
-    msgl_launch(qk_norm_rope_store_kernel<4>, grid, wpb * 32, 0, s, 1, qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride);
+    msgl_launch(qk_norm_rope_store_kernel<4>, grid, wpb * 32, 0, s, 1, qo, src, positions, cos_sin, qn, kn, eps, kc, vc, out_loc, n, nq, nkv, cache_stride, num_slots, max_pos);
 }
 
 extern "C" void msgl_argmax(int32_t* out, float* out_val, const void* logits, int rows, int vocab, int64_t stride,

@@ -139,14 +139,15 @@ __global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__
 
 // xs[row] = x[perm[row] / topk] (16-byte vectors), zero for padding rows
 __global__ void gather_rows_kernel(uint4* __restrict__ xs, const uint4* __restrict__ x, const int32_t* __restrict__ perm,
-                                   int rows, int vec, int topk) {
+                                   int rows, int vec, int topk, int x_rows) {
   pdl_wait();
   pdl_launch();
   const int r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
-  const int p = perm[r];
+  int p = perm[r];
   uint4* dst = xs + (size_t)r * vec;
+  if (p >= 0 && !MSGL_IN_BOUNDS(p / topk < x_rows, kBcMoePerm)) p = -1;
   if (p < 0) {
     for (int i = lane; i < vec; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
     return;
@@ -180,7 +181,8 @@ __global__ void expert_act_kernel(__nv_bfloat16* __restrict__ out, const __nv_bf
 
 // out[t, :] = sum_k w[t,k] * y[inv[t*topk+k], :]   (one CTA per token, fp32 accumulate)
 __global__ void combine_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ y,
-                               const float* __restrict__ w, const int32_t* __restrict__ inv, int H, int topk) {
+                               const float* __restrict__ w, const int32_t* __restrict__ inv, int H, int topk,
+                               int y_rows) {
   pdl_wait();
   pdl_launch();
   const int t = blockIdx.x;
@@ -189,6 +191,7 @@ __global__ void combine_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloa
     for (int k = 0; k < topk; ++k) {
       const int row = inv[t * topk + k];
       if (row < 0) continue;  // expert lives on another rank
+      if (!MSGL_IN_BOUNDS(row < y_rows, kBcMoeInv)) continue;
       const float wk = w[t * topk + k];
       const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + (size_t)row * H + c);
       a0 += wk * __bfloat162float(v.x);
@@ -215,10 +218,11 @@ void msgl_moe_align(const int32_t* ids, int pairs, int E, int e0, int bn, int ma
               rows_cap, perm, inv, reinterpret_cast<int2*>(work), tile_count);
 }
 
-void msgl_moe_gather(void* xs, const void* x, const int32_t* perm, int rows, int H, int topk, cudaStream_t s) {
+void msgl_moe_gather(void* xs, const void* x, const int32_t* perm, int rows, int H, int topk, int x_rows,
+                     cudaStream_t s) {
   if (rows == 0) return;
   msgl_launch(gather_rows_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, 1, reinterpret_cast<uint4*>(xs),
-              reinterpret_cast<const uint4*>(x), perm, rows, H / 8, topk);
+              reinterpret_cast<const uint4*>(x), perm, rows, H / 8, topk, x_rows);
 }
 
 void msgl_moe_act(void* out, const void* y, int rows, int inter, int act, const int32_t* perm, cudaStream_t s) {
@@ -230,10 +234,10 @@ void msgl_moe_act(void* out, const void* y, int rows, int inter, int act, const 
 }
 
 void msgl_moe_combine(void* out, const void* y, const float* w, const int32_t* inv, int T, int H, int topk,
-                      cudaStream_t s) {
+                      int y_rows, cudaStream_t s) {
   if (T == 0) return;
   msgl_launch(combine_kernel, dim3(T), dim3(256), 0, s, 1, reinterpret_cast<__nv_bfloat16*>(out),
-              reinterpret_cast<const __nv_bfloat16*>(y), w, inv, H, topk);
+              reinterpret_cast<const __nv_bfloat16*>(y), w, inv, H, topk, y_rows);
 }
 
 }  // extern "C"

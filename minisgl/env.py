@@ -53,8 +53,9 @@ _FLAGS = {
     "COMM_MODE": _Flag("auto", str),  # auto | nccl | fused
     "COMM_TIMEOUT_MS": _Flag(5000, int),  # bound on every device-side peer wait
     "DEBUG_CHECK_INTEGRITY": _Flag(False, _as_bool),
-    "NVTX": _Flag(False, _as_bool),
-    "MOE_PARALLEL": _Flag("tp", str),  # tp: shard every expert's intermediate dim; ep: whole experts per rank  # NVTX ranges around layers / attention / MLP / LM head / sampler
+    "NVTX": _Flag(False, _as_bool),  # NVTX ranges around layers / attention / MLP / LM head / sampler
+    "MOE_PARALLEL": _Flag("tp", str),  # tp: shard every expert's intermediate dim; ep: whole experts per rank
+    "BOUNDS_CHECK": _Flag(False, _as_bool),  # load the index-checking kernel build (_cuda_bc)
 }
 
 
