@@ -85,11 +85,35 @@ def test_server_endpoints(tmp_path, free_port, num_tokenizer):
             os.killpg(proc.pid, signal.SIGKILL)
 
 
-def test_bench_client_against_server(tmp_path, free_port):
+def test_trace_readers_and_scaling(tmp_path):
+    from minisgl.benchmark.client import read_mooncake_trace, read_qwen_trace, scale_traces
+    from minisgl.utils.hf import load_tokenizer
+
+    tok = load_tokenizer(make_checkpoint("tiny-qwen3", str(tmp_path / "m")))
+    q = tmp_path / "qwen.jsonl"
+    q.write_text("\n".join(json.dumps({"chat_id": i, "parent_chat_id": -1, "timestamp": 100.0 + 0.5 * (3 - i),
+                                         "input_length": 5 + 7 * i, "output_length": 3 + i, "type": "text",
+                                         "turn": 1, "hash_ids": [i]}) for i in range(4)) + "\n")
+    m = tmp_path / "mooncake.jsonl"
+    m.write_text("\n".join(json.dumps({"timestamp": 2000 * i, "input_length": 9 + i, "output_length": 4,
+                                         "hash_ids": []}) for i in range(3)))
+    for shared in (False, True):
+        tr = read_qwen_trace(str(q), tok, n=3, shared_text=shared)
+        assert [r.input_len for r in tr] == [5, 12, 19] and [r.output_len for r in tr] == [3, 4, 5]
+        assert [len(tok.encode(r.prompt, add_special_tokens=False)) for r in tr] == [5, 12, 19]
+    sc = scale_traces(tr, 2.0)
+    assert [r.arrival for r in sc] == [0.0, 1.0, 2.0] and [r.input_len for r in sc] == [19, 12, 5]
+    mc = read_mooncake_trace(str(m), tok)
+    assert [r.arrival for r in mc] == [0.0, 2.0, 4.0] and [r.input_len for r in mc] == [9, 10, 11]
+
+
+def test_bench_client_against_server(tmp_path, free_port, capsys):
     """The online load generator replays a small Poisson trace with shared prefixes and reports
-    TTFT / TPOT / E2E percentiles for every request."""
+    TTFT / TPOT / E2E percentiles for every request; the CLI's trace-replay and fixed-batch modes
+    run against the same server."""
     import asyncio
 
+    from minisgl.benchmark.client import main as client_main
     from minisgl.benchmark.client import run_trace, synthetic_trace
     from minisgl.utils.hf import load_tokenizer
 
@@ -108,6 +132,17 @@ def test_bench_client_against_server(tmp_path, free_port):
         stats = asyncio.run(run_trace(f"http://127.0.0.1:{port}", trace, path))
         assert stats["completed"] == 12
         assert stats["ttft_p50"] > 0 and stats["tpot_p99"] >= stats["tpot_p50"] >= 0
+        tf = tmp_path / "trace.jsonl"
+        tf.write_text("\n".join(json.dumps({"timestamp": 0.05 * i, "input_length": 20 + 3 * i, "output_length": 4})
+                                 for i in range(6)))
+        url = f"http://127.0.0.1:{port}"
+        capsys.readouterr()
+        client_main(["trace", "--url", url, "--model", path, "--file", str(tf), "--scales", "0.5,1"])
+        client_main(["batch", "--url", url, "--model", path, "--batch-size", "5", "--max-input", "60",
+                     "--min-output", "2", "--max-output", "6"])
+        rows = [json.loads(l) for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+        assert [r.get("scale") for r in rows[:2]] == [0.5, 1.0] and rows[2]["batch_size"] == 5
+        assert [r["completed"] for r in rows] == [6, 6, 5]
     finally:
         os.killpg(proc.pid, signal.SIGTERM)
         try:
