@@ -66,6 +66,12 @@ class Req:
         return self._buf[: self._len]
 
     @property
+    def host_len(self) -> int:
+        """Tokens known on the host. Under overlap scheduling ``device_len`` runs one step ahead
+        (the next batch is launched before this one's tokens are read back)."""
+        return self._len
+
+    @property
     def remain_len(self) -> int:
         return self.max_device_len - self.device_len
 

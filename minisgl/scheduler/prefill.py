@@ -60,8 +60,11 @@ class PrefillAdder:
         chunk = min(self.token_budget, remain)
         cls = ChunkedReq if chunk < remain else Req
         self.token_budget -= chunk
-        if p.chunked_req is None:  # a continuing chunk was reserved when it was first admitted
-            self.reserved_size += remain + p.output_len + self.cache_manager.page_size - 1
+        # Reserve what the request may still allocate: its unprefilled prompt, its outputs and one
+        # partial page. Every scheduling step builds a new adder whose base reservation covers only
+        # running decode requests, so a continuing chunk is reserved again here, or requests
+        # admitted behind it could take the pages its later chunks need.
+        self.reserved_size += remain + p.output_len + self.cache_manager.page_size - 1
         req = cls(
             input_ids=p.input_ids[: cached_len + chunk],
             table_idx=row,

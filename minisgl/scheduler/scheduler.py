@@ -133,9 +133,15 @@ class Scheduler(SchedulerIOMixin):
             for req, tok in zip(batch.reqs, tokens):
                 if isinstance(req, ChunkedReq):
                     continue
+                if req in self.finished_reqs:
+                    # Stopped on EOS in the previous batch, after this batch was already launched
+                    # (overlap scheduling): this token is surplus. The reference still sends it
+                    # (python/minisgl/scheduler/scheduler.py:147-164), which adds a token after
+                    # EOS to offline outputs.
+                    continue
                 req.append_host(tok)
                 stop_eos = tok == eos and not req.sampling_params.ignore_eos
-                finished = stop_eos or req.device_len >= req.max_device_len
+                finished = stop_eos or req.host_len >= req.max_device_len
                 reply.append(DetokenizeMsg(uid=req.uid, next_token=tok, finished=finished, eos=stop_eos))
                 if finished and req not in self.finished_reqs:
                     self.decode_manager.remove_req(req)

@@ -47,16 +47,20 @@ class FakeModel:
         self.kv = {}
 
     def _check_kv(self, batch):
-        for r in batch.reqs:
-            ids = r.input_ids.tolist()
-            assert len(ids) == r.device_len
+        # the tokens this forward writes come from the device input (under overlap scheduling the
+        # host copy of a decode request still lacks the token sampled by the previous step)
+        toks = batch.input_ids.tolist()
+        k = 0
+        for r in batch.padded_reqs:
             for p in range(r.cached_len, r.device_len):
-                self.kv[int(r.slots[p])] = (ids[p], p)
+                if r in batch.reqs:
+                    self.kv[int(r.slots[p])] = (toks[k], p)
+                k += 1
         for r in batch.reqs:
             ids = r.input_ids.tolist()
-            got = [self.kv.get(int(s)) for s in r.slots[: r.device_len]]
-            want = [(t, p) for p, t in enumerate(ids)]
-            bad = [p for p in range(r.device_len) if got[p] != want[p]]
+            n = min(len(ids), r.device_len)
+            got = [self.kv.get(int(s)) for s in r.slots[:n]]
+            bad = [p for p in range(n) if got[p] != (ids[p], p)]
             assert not bad, f"req {r.uid}: positions {bad[:8]} read KV written for another token"
 
     def forward(self):
@@ -177,6 +181,69 @@ def test_concurrent_requests_with_one_uncached_prefix(tiny_path, free_port):
         prompts = [root + g.integers(0, V, 6).tolist() for _ in range(6)]
         prompts += [g.integers(0, V, 30).tolist() for _ in range(12)]
         lens = [40] * 6 + [10] * 12
+        outs = llm.generate(prompts, [SamplingParams(max_tokens=n, ignore_eos=True) for n in lens])
+        for p, n, o in zip(prompts, lens, outs):
+            assert o["token_ids"] == expected(p, n)
+        llm.cache_manager.check_integrity()
+    finally:
+        llm.shutdown()
+
+
+def run_overlapped(llm):
+    """The overlap loop (schedule and launch batch N+1 before processing batch N's results), which
+    the engine uses on CUDA, driven on the CPU engine."""
+
+    def loop():
+        data = None
+        while True:
+            data = llm.overlap_loop(data)
+
+    llm.run_forever = loop
+
+
+@pytest.mark.parametrize("page", [1, 16])
+def test_overlap_loop_with_eos_stops(tiny_path, free_port, page):
+    """Under overlap scheduling a request that stops on EOS is already part of the next batch;
+    that surplus step's token must not reach the output, and the request's pages are freed once."""
+    llm = make_llm(tiny_path, free_port, page_size=page, max_running_req=6, max_extend_tokens=64)
+    run_overlapped(llm)
+    try:
+        eos = llm.eos_token_id
+        prompts, want = [], []
+        g = np.random.default_rng(3)
+        for i in range(10):
+            L = int(g.integers(4, 40))
+            if i % 2 == 0:  # reaches EOS after i // 2 + 1 generated tokens
+                prompt = g.integers(0, V, L).tolist()
+                k = i // 2 + 1
+                # choose the last prompt token so that the k-th generated token is EOS
+                for t in range(V):
+                    prompt[-1] = t
+                    seq = expected(prompt, k)
+                    if seq[-1] == eos and eos not in seq[:-1]:
+                        break
+                prompts.append(prompt)
+                want.append(expected(prompt, 20, eos))
+                assert len(want[-1]) == k - 1
+            else:
+                prompts.append(g.integers(0, V, L).tolist())
+                want.append(expected(prompts[-1], 20, eos))
+        for _ in range(2):
+            outs = llm.generate(prompts, SamplingParams(max_tokens=20))
+            assert [o["token_ids"] for o in outs] == want
+            llm.cache_manager.check_integrity()
+        cm = llm.cache_manager
+        assert cm.available_size == cm.num_pages * cm.page_size
+    finally:
+        llm.shutdown()
+
+
+def test_overlap_loop_outputs(tiny_path, free_port):
+    llm = make_llm(tiny_path, free_port, page_size=4, max_extend_tokens=32, max_running_req=4, num_page_override=40)
+    run_overlapped(llm)
+    try:
+        prompts = prompts_with_shared_prefixes(7, 14)
+        lens = [3 + (i * 5) % 23 for i in range(len(prompts))]
         outs = llm.generate(prompts, [SamplingParams(max_tokens=n, ignore_eos=True) for n in lens])
         for p, n, o in zip(prompts, lens, outs):
             assert o["token_ids"] == expected(p, n)
