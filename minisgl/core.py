@@ -51,6 +51,7 @@ class Req:
         self.cache_handle = cache_handle
         self.greedy = sampling_params.is_greedy
         self.pending_prefix = 0  # matched prefix slots still to be written into the page table
+        self.aborted = False  # resources released on abort; results of in-flight batches are dropped
         n = len(input_ids)
         self.device_len = n
         self.max_device_len = n + output_len

@@ -131,7 +131,7 @@ class Scheduler(SchedulerIOMixin):
         with self.cache_manager.lazy_free_region():
             eos = self.eos_token_id
             for req, tok in zip(batch.reqs, tokens):
-                if isinstance(req, ChunkedReq):
+                if isinstance(req, ChunkedReq) or req.aborted:
                     continue
                 if req in self.finished_reqs:
                     # Stopped on EOS in the previous batch, after this batch was already launched
@@ -170,6 +170,9 @@ class Scheduler(SchedulerIOMixin):
         elif isinstance(msg, AbortBackendMsg):
             req = self.prefill_manager.abort_req(msg.uid) or self.decode_manager.abort_req(msg.uid)
             if req is not None:
+                # a batch holding the request may still be in flight (overlap scheduling): its
+                # result for this request is dropped, so the resources are released only here
+                req.aborted = True
                 self._free_req_resources(req)
         else:
             raise NotImplementedError(f"unknown message {type(msg).__name__}")

@@ -19,4 +19,6 @@ class TableManager:
         return self._free.pop()
 
     def free(self, row: int) -> None:
+        if row in self._free:  # at most max_running_reqs entries
+            raise RuntimeError(f"page-table row {row} freed twice")
         self._free.append(row)

@@ -250,3 +250,45 @@ def test_overlap_loop_outputs(tiny_path, free_port):
         llm.cache_manager.check_integrity()
     finally:
         llm.shutdown()
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_aborts_free_everything_once(tiny_path, free_port, overlap):
+    """Requests aborted while pending, mid-chunked-prefill and mid-decode: the others still produce
+    their exact outputs, an aborted request's pages and table row are released exactly once
+    (also when a batch holding it was already in flight), and the pool ends whole."""
+    from minisgl.message import AbortBackendMsg
+
+    llm = make_llm(tiny_path, free_port, page_size=4, max_extend_tokens=24, max_running_req=4, num_page_override=60)
+    if overlap:
+        run_overlapped(llm)
+    g = np.random.default_rng(11)
+    prompts = [g.integers(0, V, int(g.integers(10, 60))).tolist() for _ in range(12)]
+    # uid -> receive call at which its abort arrives: spread so that aborts land while the
+    # request is pending, mid-chunk, just launched (prefill in flight) and decoding
+    plan = {0: 2, 1: 3, 3: 4, 5: 1, 6: 5, 7: 6, 9: 9, 11: 12}
+    orig = llm.receive_msg
+    calls = [0]
+
+    def receive(blocking=False):
+        msgs = list(orig(blocking=blocking))
+        calls[0] += 1
+        msgs += [AbortBackendMsg(uid=u) for u, c in plan.items() if c == calls[0]]
+        return msgs
+
+    llm.receive_msg = receive  # (TableManager.free raises on a row freed twice)
+    try:
+        outs = llm.generate(prompts, SamplingParams(max_tokens=15, ignore_eos=True))
+        for i, (p, o) in enumerate(zip(prompts, outs)):
+            want = expected(p, 15)
+            if i in plan:
+                assert o["token_ids"] == want[: len(o["token_ids"])]  # a prefix of the full output
+            else:
+                assert o["token_ids"] == want, i
+        llm.cache_manager.check_integrity()
+        cm = llm.cache_manager
+        assert cm.available_size == cm.num_pages * cm.page_size
+        assert llm.table_manager.available_size == 4
+        assert not llm.decode_manager.running and not llm.prefill_manager.pending_list
+    finally:
+        llm.shutdown()
