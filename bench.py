@@ -1,4 +1,5 @@
-"""Offline serving throughput: output tokens / s of ``LLM.generate`` on the BASELINE workload.
+"""Offline serving throughput: output tokens / s of ``LLM.generate`` on the headline workload
+(the reference's offline benchmark, benchmark/offline/bench.py).
 
 Model: Qwen3-14B architecture (bf16, random N(0, 0.02) weights), TP = number of GPUs.
 Workload: 256 requests, prompt lengths U[100, 1024] with uniform random token ids, output lengths
