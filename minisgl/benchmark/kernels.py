@@ -9,6 +9,10 @@ times without timing, which is the form to wrap in a profiler.
   gemm          bf16 GEMM  out[M, N] = x[M, K] @ w[N, K]^T  (--epi 0 bf16, 1 SiLU-gated, 3 fp32)
   decode-attn   paged decode attention over a longest-first work list (page size 64)
   prefill-attn  ragged causal prefill attention (requests of 100..1024 tokens; --impl tcgen05 | mma)
+  suite         every other hot kernel once at decode shapes (Qwen3-14B, --bs tokens; MoE at
+                Qwen3-30B-A3B shapes): embedding, RMSNorm, fused add+RMSNorm, QK-norm+RoPE+KV
+                store, KV store, SiLU-mul, 1-SM and 2-SM GEMMs, argmax, top-k/top-p sampling and
+                the MoE route / align / gather / grouped GEMM / activation / combine chain
 """
 
 from __future__ import annotations
@@ -151,9 +155,104 @@ def _prefill_attn(a, c) -> None:
           f"({flops / ms * 1e3 / tf:.2f} of measured)")
 
 
+def _suite(a, c) -> None:
+    """One table row per kernel: CUDA-event time (graph replay) and bytes the kernel must move.
+    Weight-streaming entries rotate over copies larger than L2; activation-sized entries are
+    latency-bound and run L2-resident, as they do inside a decode step."""
+    from minisgl import ops
+    from minisgl.layers.rotary import get_rope
+
+    torch.manual_seed(0)
+    dev, bf = "cuda", torch.bfloat16
+    T, H, nq, nkv, hd, inter, V = a.bs, 5120, 40, 8, 128, 17408, 151936
+    small = a.once  # smaller weights under a profiler (few GB on the device)
+    rows = []
+
+    def add(name, fn, nbytes):
+        if a.once:
+            fn()
+            return
+        ms = perf_cuda(fn)
+        rows.append((name, ms * 1e3, nbytes / ms / 1e6))
+
+    def rot(make, n):
+        bufs = [make() for _ in range(n)]
+        it = [0]
+
+        def nxt():
+            it[0] += 1
+            return bufs[it[0] % n]
+        return nxt
+
+    nrot = lambda nb: 1 if small else max(2, int(3e8 // nb) + 1)  # noqa: E731
+    # embedding (vocab gather)
+    Vs = 32000 if small else V
+    emb = torch.randn(Vs, H, device=dev, dtype=bf)
+    ids = torch.randint(0, Vs, (T,), device=dev, dtype=torch.int32)
+    add("embedding", lambda: ops.embedding(emb, ids), 2 * T * H * 2)
+    x = torch.randn(T, H, device=dev, dtype=bf)
+    w = torch.rand(H, device=dev, dtype=bf) + 0.5
+    res = torch.randn(T, H, device=dev, dtype=bf)
+    add("rmsnorm", lambda: ops.rmsnorm(x, w, 1e-6), 2 * T * H * 2)
+    add("fused_add_rmsnorm", lambda: ops.fused_add_rmsnorm(x, res, w, 1e-6), 4 * T * H * 2)
+    # attention input: QK-norm + RoPE + KV store, and the plain KV store
+    slots = 65536
+    kc = torch.zeros(slots, nkv, hd, device=dev, dtype=bf)
+    vc = torch.zeros_like(kc)
+    qkv = torch.randn(T, (nq + 2 * nkv) * hd, device=dev, dtype=bf)
+    pos = torch.randint(0, 4000, (T,), device=dev, dtype=torch.int32)
+    loc = torch.randperm(slots, device=dev)[:T].to(torch.int32)
+    cs = get_rope(hd, hd, 4096, 1e6).cos_sin_cache.to(dev)
+    qn = torch.rand(hd, device=dev, dtype=bf) + 0.5
+    add("qk_norm_rope_store", lambda: ops.qk_norm_rope_store(qkv, pos, cs, qn, qn, 1e-6, kc, vc, loc, nq, nkv, hd),
+        2 * qkv.numel() * 2)
+    k = torch.randn(T, nkv * hd, device=dev, dtype=bf)
+    add("store_kv", lambda: ops.store_kv(k, k, kc, vc, loc), 4 * k.numel() * 2)
+    gu = torch.randn(T, 2 * inter, device=dev, dtype=bf)
+    add("silu_and_mul", lambda: ops.silu_and_mul(gu), gu.numel() * 2 * 3 // 2)
+    # GEMMs: 1-SM (16 tokens, QKV), 2-SM gated gate_up (SiLU epilogue) and down_proj
+    for name, m, n, kk, gated in (("gemm_1sm_qkv_m16", 16, 7168, H, False),
+                                  ("gemm_2sm_gateup_silu", T, 2 * inter, H, True),
+                                  ("gemm_2sm_down", T, H, inter, False)):
+        wb = n * kk * 2
+        nw = rot(lambda: torch.randn(n, kk, device=dev, dtype=bf) * 0.02, nrot(wb))
+        xi = torch.randn(m, kk, device=dev, dtype=bf)
+        add(name, (lambda nw=nw, xi=xi, gated=gated: ops.gate_up_silu(xi, nw()) if gated else ops.linear(xi, nw())),
+            wb + xi.numel() * 2 + m * (n // 2 if gated else n) * 2)
+    # sampling over the full vocabulary (fp32 logits)
+    lg = rot(lambda: torch.randn(T, V, device=dev), 1 if small else 2)
+    add("argmax", lambda: ops.argmax(lg()), T * V * 4)
+    temp = torch.full((T,), 0.7, device=dev)
+    tk = torch.full((T,), 50, device=dev, dtype=torch.int32)
+    tp = torch.full((T,), 0.9, device=dev)
+    seed = torch.arange(T, device=dev, dtype=torch.int64)
+    step = torch.full((T,), 7, device=dev, dtype=torch.int64)
+    add("sample_topk_topp", lambda: ops.sample(lg(), temp, tk, tp, seed, step), T * V * 4)
+    # MoE decode (Qwen3-30B-A3B: hidden 2048, 128 experts of 768, top-8)
+    from minisgl.ops.moe import moe_forward
+
+    Hm, Im, E, topk = 2048, 768, 128, 8
+    w1 = torch.randn(E, 2 * Im, Hm, device=dev, dtype=bf) * 0.02
+    w2 = torch.randn(E, Hm, Im, device=dev, dtype=bf) * 0.02
+    xm = torch.randn(T, Hm, device=dev, dtype=bf)
+    gate = torch.randn(T, E, device=dev)
+    ex = min(E, T * topk)  # experts touched (upper bound)
+    add("moe_forward(route..combine)", lambda: moe_forward(xm, w1, w2, gate, topk, True, "silu"),
+        ex * 3 * Im * Hm * 2)
+    torch.cuda.synchronize()
+    if a.once:
+        print("ok", c.get_error())
+        return
+    hbm, _ = _peaks()
+    print(f"suite bs={T}: kernel, us, GB/s (of measured HBM)")
+    for name, us, gbs in rows:
+        print(f"  {name:28s} {us:8.1f} us {gbs:8.0f} GB/s ({gbs * 1e9 / hbm:.2f})")
+    print("ok", c.get_error())
+
+
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    p.add_argument("op", choices=["gemm", "decode-attn", "prefill-attn"])
+    p.add_argument("op", choices=["gemm", "decode-attn", "prefill-attn", "suite"])
     p.add_argument("--m", type=int, default=128)
     p.add_argument("--n", type=int, default=5120)
     p.add_argument("--k", type=int, default=5120)
@@ -168,7 +267,7 @@ def main(argv=None) -> None:
     from minisgl._native import cuda
 
     c = cuda()
-    {"gemm": _gemm, "decode-attn": _decode_attn, "prefill-attn": _prefill_attn}[a.op](a, c)
+    {"gemm": _gemm, "decode-attn": _decode_attn, "prefill-attn": _prefill_attn, "suite": _suite}[a.op](a, c)
 
 
 if __name__ == "__main__":
