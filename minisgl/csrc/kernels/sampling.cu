@@ -1,11 +1,16 @@
 // Temperature / top-k / top-p sampling, one CTA per row, no sort:
 //   * top-k threshold  = exact k-th largest scaled logit by 4-pass radix select on the
-//     order-preserving 32-bit key of each float;
+//     order-preserving 32-bit key of each float. Counts go to per-warp histograms, and the lanes
+//     of a warp that hit the same bin add once (match.any), so the few hot bins of the first digit
+//     (sign and exponent) do not serialise the block on one shared-memory address;
+//   * with 0 < k <= kCand the kept tokens (key >= threshold) are then compacted into shared memory
+//     in one more pass, and the max, the top-p cut and the draw run on that list;
 //   * top-p threshold  = exact nucleus cut by a mass-weighted radix select (walk bins from the
 //     top accumulating exp(z - max) until the requested probability mass is reached);
 //   * draw             = Gumbel-max: argmax over kept tokens of z - log(-log(u)), with u from a
 //     counter-based hash of (seed, step, token id) (same hash as ops/reference.py).
-// Greedy rows (temperature <= 0) take the plain argmax.
+// Greedy rows (temperature <= 0) take the plain argmax. Without top-k and top-p the draw is one
+// pass over the row.
 #include <cfloat>
 
 #include "api.h"
@@ -16,14 +21,12 @@ using namespace msgl;
 namespace {
 
 constexpr int kThreads = 1024;
+constexpr int kWarps = kThreads / 32;
+constexpr int kCand = 4096;  // shared-memory candidate list of the top-k fast path
 
 __device__ __forceinline__ uint32_t fkey(float f) {
   const uint32_t b = __float_as_uint(f);
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-__device__ __forceinline__ float unkey(uint32_t k) {
-  const uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
-  return __uint_as_float(b);
 }
 
 __device__ __forceinline__ float uniform01(uint32_t seed, uint32_t step, uint32_t idx) {
@@ -36,13 +39,20 @@ __device__ __forceinline__ float uniform01(uint32_t seed, uint32_t step, uint32_
 }
 
 struct Smem {
-  float hist_mass[256];
-  int hist_cnt[256];
+  union {
+    uint32_t cnt[kWarps][256];
+    float mass[kWarps][256];
+  } h;  // per-warp histograms
+  float cand_z[kCand];
+  int cand_i[kCand];
+  float bins_f[256];
+  uint32_t bins_u[256];
   float red_f[32];
   int red_i[32];
   uint32_t sel_prefix;
   int sel_remaining;
   float sel_above;
+  int cand_n;
 };
 
 __device__ float block_max(float v, Smem& sm) {
@@ -51,7 +61,7 @@ __device__ float block_max(float v, Smem& sm) {
   __syncthreads();
   if (lane == 0) sm.red_f[w] = v;
   __syncthreads();
-  v = lane < (int)(blockDim.x >> 5) ? sm.red_f[lane] : -FLT_MAX;
+  v = lane < kWarps ? sm.red_f[lane] : -FLT_MAX;
   return warp_max(v);
 }
 
@@ -61,7 +71,7 @@ __device__ float block_sumf(float v, Smem& sm) {
   __syncthreads();
   if (lane == 0) sm.red_f[w] = v;
   __syncthreads();
-  v = lane < (int)(blockDim.x >> 5) ? sm.red_f[lane] : 0.f;
+  v = lane < kWarps ? sm.red_f[lane] : 0.f;
   return warp_sum(v);
 }
 
@@ -77,8 +87,8 @@ __device__ int block_argmax(float v, int i, Smem& sm) {
   __syncthreads();
   if (lane == 0) { sm.red_f[w] = v; sm.red_i[w] = i; }
   __syncthreads();
-  v = lane < (int)(blockDim.x >> 5) ? sm.red_f[lane] : -FLT_MAX;
-  i = lane < (int)(blockDim.x >> 5) ? sm.red_i[lane] : 0x7fffffff;
+  v = lane < kWarps ? sm.red_f[lane] : -FLT_MAX;
+  i = lane < kWarps ? sm.red_i[lane] : 0x7fffffff;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, v, o);
@@ -88,20 +98,100 @@ __device__ int block_argmax(float v, int i, Smem& sm) {
   return i;
 }
 
-__global__ void __launch_bounds__(kThreads) sample_kernel(int32_t* __restrict__ out, const float* __restrict__ logits,
+__device__ __forceinline__ void zero_hist(Smem& sm) {
+  uint32_t* flat = &sm.h.cnt[0][0];
+  for (int j = threadIdx.x; j < kWarps * 256; j += kThreads) flat[j] = 0u;
+}
+
+// Sum the per-warp histograms into bins_u / bins_f (threads 0..255), then clear them.
+template <bool MASS>
+__device__ __forceinline__ void fold_hist(Smem& sm) {
+  __syncthreads();
+  if (threadIdx.x < 256) {
+    if constexpr (MASS) {
+      float s = 0.f;
+#pragma unroll 8
+      for (int w = 0; w < kWarps; ++w) s += sm.h.mass[w][threadIdx.x];
+      sm.bins_f[threadIdx.x] = s;
+    } else {
+      uint32_t s = 0;
+#pragma unroll 8
+      for (int w = 0; w < kWarps; ++w) s += sm.h.cnt[w][threadIdx.x];
+      sm.bins_u[threadIdx.x] = s;
+    }
+  }
+  __syncthreads();
+  zero_hist(sm);
+}
+
+// Walk bins_u / bins_f from the top (bin 255) accumulating until `target` is reached; the bin
+// where it is reached extends the prefix (bin 0 if never). Warp 0 scans, lane l owning bins
+// 255 - 8l ... 248 - 8l. Writes sel_prefix and sel_remaining (counts) or sel_above (mass).
+template <bool MASS>
+__device__ __forceinline__ void select_bin(Smem& sm, int shift, uint32_t prefix, float target_f, int target_u,
+                                           float above) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float cf[8];
+    uint32_t cu[8];
+    float sf = 0.f;
+    uint32_t su = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int b = 255 - 8 * lane - j;
+      if constexpr (MASS) { cf[j] = sm.bins_f[b]; sf += cf[j]; }
+      else { cu[j] = sm.bins_u[b]; su += cu[j]; }
+    }
+    float incf = sf;
+    uint32_t incu = su;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float tf = __shfl_up_sync(0xffffffffu, incf, o);
+      const uint32_t tu = __shfl_up_sync(0xffffffffu, incu, o);
+      if (lane >= o) { incf += tf; incu += tu; }
+    }
+    const bool reach = MASS ? (above + incf >= target_f) : (incu >= (uint32_t)target_u);
+    const unsigned hit = __ballot_sync(0xffffffffu, reach);
+    const int L = hit ? __ffs(hit) - 1 : 31;
+    if (lane == L) {
+      int j = 0;
+      if constexpr (MASS) {
+        float acc = above + (incf - sf);
+        for (; j < 7; ++j) {
+          if (acc + cf[j] >= target_f) break;
+          acc += cf[j];
+        }
+        sm.sel_above = acc;
+      } else {
+        uint32_t acc = incu - su;
+        for (; j < 7; ++j) {
+          if (acc + cu[j] >= (uint32_t)target_u) break;
+          acc += cu[j];
+        }
+        sm.sel_remaining = target_u - (int)acc;
+      }
+      sm.sel_prefix = prefix | ((uint32_t)(255 - 8 * L - j) << shift);
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict__ out, const float* __restrict__ logits,
                                                          int vocab, int64_t stride, const float* __restrict__ temperature,
                                                          const int32_t* __restrict__ top_k, const float* __restrict__ top_p,
                                                          const int64_t* __restrict__ seed, const int64_t* __restrict__ step) {
-  __shared__ Smem sm;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   pdl_wait();
   pdl_launch();
   const int r = blockIdx.x;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const float* row = logits + (size_t)r * stride;
   const float t = temperature[r];
   if (!(t > 0.f)) {
     float bv = -FLT_MAX;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+    for (int i = threadIdx.x; i < vocab; i += kThreads) {
       const float v = row[i];
       if (v > bv) { bv = v; bi = i; }
     }
@@ -110,48 +200,110 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(int32_t* __restrict__ 
     return;
   }
   const float inv_t = 1.f / t;
+  const int k = top_k[r];
+  const float p = top_p[r];
+  const uint32_t sd = (uint32_t)seed[r], st = (uint32_t)step[r];
+  zero_hist(sm);
   // ---- top-k cut (key threshold; keep key >= kcut)
   uint32_t kcut = 0;
-  const int k = top_k[r];
   if (k > 0 && k < vocab) {
     uint32_t prefix = 0, mask = 0;
     int remaining = k;
+    __syncthreads();
     for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = threadIdx.x; b < 256; b += blockDim.x) sm.hist_cnt[b] = 0;
-      __syncthreads();
-      for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-        const uint32_t key = fkey(row[i] * inv_t);
-        if ((key & mask) == prefix) atomicAdd(&sm.hist_cnt[(key >> shift) & 255], 1);
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        int acc = 0, b = 255;
-        for (; b > 0; --b) {
-          if (acc + sm.hist_cnt[b] >= remaining) break;
-          acc += sm.hist_cnt[b];
+      for (int base = 0; base < vocab; base += kThreads) {  // warp-uniform trip count (match.any)
+        const int i = base + threadIdx.x;
+        int bin = -1;
+        if (i < vocab) {
+          const uint32_t key = fkey(row[i] * inv_t);
+          if ((key & mask) == prefix) bin = (int)((key >> shift) & 255u);
         }
-        sm.sel_prefix = prefix | ((uint32_t)b << shift);
-        sm.sel_remaining = remaining - acc;
+        const unsigned m = __match_any_sync(0xffffffffu, bin);
+        if (bin >= 0 && lane == __ffs(m) - 1) atomicAdd(&sm.h.cnt[w][bin], (uint32_t)__popc(m));
       }
-      __syncthreads();
+      fold_hist<false>(sm);
+      select_bin<false>(sm, shift, prefix, 0.f, remaining, 0.f);
       prefix = sm.sel_prefix;
       remaining = sm.sel_remaining;
       mask |= 255u << shift;
     }
     kcut = prefix;
+    if (k <= kCand) {
+      // ---- compact the kept tokens into shared memory
+      if (threadIdx.x == 0) sm.cand_n = 0;
+      __syncthreads();
+      for (int base = 0; base < vocab; base += kThreads) {
+        const int i = base + threadIdx.x;
+        float z = 0.f;
+        bool keep = false;
+        if (i < vocab) {
+          z = row[i] * inv_t;
+          keep = fkey(z) >= kcut;
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        int pos0 = 0;
+        if (lane == 0 && bal) pos0 = atomicAdd(&sm.cand_n, __popc(bal));
+        pos0 = __shfl_sync(0xffffffffu, pos0, 0);
+        if (keep) {
+          const int pos = pos0 + __popc(bal & ((1u << lane) - 1u));
+          if (pos < kCand) { sm.cand_z[pos] = z; sm.cand_i[pos] = i; }
+        }
+      }
+      __syncthreads();
+      const int n = sm.cand_n;
+      if (n <= kCand) {
+        float mx = -FLT_MAX;
+        for (int j = threadIdx.x; j < n; j += kThreads) mx = fmaxf(mx, sm.cand_z[j]);
+        mx = block_max(mx, sm);
+        uint32_t pcut = kcut;
+        if (p < 1.f) {
+          float tot = 0.f;
+          for (int j = threadIdx.x; j < n; j += kThreads) tot += __expf(sm.cand_z[j] - mx);
+          tot = block_sumf(tot, sm);
+          const float target = p * tot;
+          uint32_t pre = 0, msk = 0;
+          float above = 0.f;
+          for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int j = threadIdx.x; j < n; j += kThreads) {
+              const float z = sm.cand_z[j];
+              const uint32_t key = fkey(z);
+              if ((key & msk) == pre) atomicAdd(&sm.h.mass[w][(key >> shift) & 255u], __expf(z - mx));
+            }
+            fold_hist<true>(sm);
+            select_bin<true>(sm, shift, pre, target, 0, above);
+            pre = sm.sel_prefix;
+            above = sm.sel_above;
+            msk |= 255u << shift;
+          }
+          pcut = max(pre, kcut);
+        }
+        float bv = -FLT_MAX;
+        int bi = 0x7fffffff;
+        for (int j = threadIdx.x; j < n; j += kThreads) {
+          const float z = sm.cand_z[j];
+          if (fkey(z) < pcut) continue;
+          const int i = sm.cand_i[j];
+          const float g = z - logf(-logf(uniform01(sd, st, (uint32_t)i)));
+          if (g > bv || (g == bv && i < bi)) { bv = g; bi = i; }
+        }
+        const int a = block_argmax(bv, bi, sm);
+        if (threadIdx.x == 0) out[r] = a == 0x7fffffff ? 0 : a;
+        return;
+      }
+      // more ties at the threshold than the list holds: continue over the whole row
+    }
   }
-  // ---- max of kept scaled logits and the kept mass
-  float mx = -FLT_MAX;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float z = row[i] * inv_t;
-    if (fkey(z) >= kcut) mx = fmaxf(mx, z);
-  }
-  mx = block_max(mx, sm);
+  // ---- top-p over the whole row (no top-k, or the candidate list overflowed)
   uint32_t pcut = kcut;
-  const float p = top_p[r];
   if (p < 1.f) {
+    float mx = -FLT_MAX;
+    for (int i = threadIdx.x; i < vocab; i += kThreads) {
+      const float z = row[i] * inv_t;
+      if (fkey(z) >= kcut) mx = fmaxf(mx, z);
+    }
+    mx = block_max(mx, sm);
     float tot = 0.f;
-    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+    for (int i = threadIdx.x; i < vocab; i += kThreads) {
       const float z = row[i] * inv_t;
       if (fkey(z) >= kcut) tot += __expf(z - mx);
     }
@@ -160,25 +312,13 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(int32_t* __restrict__ 
     uint32_t prefix = 0, mask = 0;
     float above = 0.f;
     for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = threadIdx.x; b < 256; b += blockDim.x) sm.hist_mass[b] = 0.f;
-      __syncthreads();
-      for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+      for (int i = threadIdx.x; i < vocab; i += kThreads) {
         const float z = row[i] * inv_t;
         const uint32_t key = fkey(z);
-        if (key >= kcut && (key & mask) == prefix) atomicAdd(&sm.hist_mass[(key >> shift) & 255], __expf(z - mx));
+        if (key >= kcut && (key & mask) == prefix) atomicAdd(&sm.h.mass[w][(key >> shift) & 255u], __expf(z - mx));
       }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        float acc = above;
-        int b = 255;
-        for (; b > 0; --b) {
-          if (acc + sm.hist_mass[b] >= target) break;
-          acc += sm.hist_mass[b];
-        }
-        sm.sel_prefix = prefix | ((uint32_t)b << shift);
-        sm.sel_above = acc;
-      }
-      __syncthreads();
+      fold_hist<true>(sm);
+      select_bin<true>(sm, shift, prefix, target, 0, above);
       prefix = sm.sel_prefix;
       above = sm.sel_above;
       mask |= 255u << shift;
@@ -186,10 +326,9 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(int32_t* __restrict__ 
     pcut = max(prefix, kcut);
   }
   // ---- Gumbel-max draw among kept tokens
-  const uint32_t sd = (uint32_t)seed[r], st = (uint32_t)step[r];
   float bv = -FLT_MAX;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+  for (int i = threadIdx.x; i < vocab; i += kThreads) {
     const float z = row[i] * inv_t;
     if (fkey(z) < pcut) continue;
     const float u = uniform01(sd, st, (uint32_t)i);
@@ -206,8 +345,13 @@ extern "C" void msgl_sample(int32_t* out, const float* logits, int rows, int voc
                             const float* temperature, const int32_t* top_k, const float* top_p,
                             const int64_t* seed, const int64_t* step, cudaStream_t s) {
   if (rows == 0) return;
-  msgl_launch(sample_kernel, dim3(rows), dim3(kThreads), 0, s, 1, out, logits, vocab, stride, temperature, top_k,
-              top_p, seed, step);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
+    attr_set = true;
+  }
+  msgl_launch(sample_kernel, dim3(rows), dim3(kThreads), sizeof(Smem), s, 1, out, logits, vocab, stride, temperature,
+              top_k, top_p, seed, step);
 }
 
 MSGL_ERROR_ACCESSOR(msgl_err_sampling)

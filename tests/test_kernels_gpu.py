@@ -294,6 +294,46 @@ def test_sampling_matches_reference():
             assert logits[i, a[i]].cpu() / max(float(temp[i]), 1e-6) >= kth
 
 
+@pytest.mark.parametrize("case", ["topk_fast", "topk_full", "topp_only", "temp_only", "tie_overflow"])
+def test_sampling_paths(case):
+    """Each path of the sampling kernel on a full-size vocabulary: top-k <= 4096 (shared-memory
+    candidate list), larger top-k (whole-row passes), top-p alone, temperature alone, and a row of
+    ties at the top-k threshold that overflows the candidate list. Every draw must lie in the kept
+    set (top-k by the float threshold, then the top-p nucleus up to float rounding at its edge);
+    draws agree with the fp32/fp64 reference and are deterministic."""
+    from minisgl import ops
+
+    B, V = 24, 151936
+    g = torch.Generator(device="cpu").manual_seed(7)
+    logits = torch.randn(B, V, generator=g) * 2
+    k, p = {"topk_fast": (40, 0.9), "topk_full": (6000, 0.95), "topp_only": (V, 0.8), "temp_only": (V, 1.0),
+            "tie_overflow": (10, 1.0)}[case]
+    if case == "tie_overflow":
+        logits[:, :5000] = 3.0  # 5000 tokens tie at the 10th-largest value
+        logits[:, 5000:] = torch.randn(B, V - 5000, generator=g).clamp(max=2.5)
+    temp = torch.full((B,), 0.8)
+    topk = torch.full((B,), k, dtype=torch.int32)
+    topp = torch.full((B,), p)
+    seed = torch.arange(B, dtype=torch.int64) * 13 + 5
+    step = torch.arange(B, dtype=torch.int64) + 40
+    args = [x.to(DEV) for x in (temp, topk, topp, seed, step)]
+    a = ops.sample(logits.to(DEV), *args).cpu()
+    a2 = ops.sample(logits.to(DEV), *args).cpu()
+    assert torch.equal(a, a2)
+    b = ref.sample(logits, temp, topk, topp, seed, step)
+    assert (a == b).float().mean() >= 0.9, (a, b)
+    for i in range(B):
+        z = logits[i] / 0.8
+        keep = torch.ones(V, dtype=torch.bool)
+        if 0 < k < V:
+            keep &= z >= torch.topk(z, k).values[-1]
+        assert keep[a[i]], (i, int(a[i]))
+        if p < 1.0:
+            pr = torch.softmax(z.double().masked_fill(~keep, float("-inf")), -1)
+            above = pr[pr > pr[a[i]]].sum()  # mass strictly above the drawn token
+            assert above < p + 1e-4, (i, float(above))
+
+
 def test_store_kv():
     from minisgl import ops
 
