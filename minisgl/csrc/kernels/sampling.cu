@@ -38,6 +38,51 @@ __device__ __forceinline__ float uniform01(uint32_t seed, uint32_t step, uint32_
   return ((float)(x >> 8) + 0.5f) * (1.0f / 16777216.0f);
 }
 
+// Visit every element of a row as f(index, value, valid), in the same order on every lane of a warp
+// (f may use warp-collective operations; valid is false on padding lanes). Four float4 loads per
+// thread are in flight before any is used: with one scalar load per thread at a time the passes
+// were bound by L2 latency, not bandwidth.
+template <typename F>
+__device__ __forceinline__ void for_row(const float* __restrict__ row, int vocab, F&& f) {
+  constexpr int U = 4;
+  const bool vec = (vocab % 4 == 0) && ((reinterpret_cast<uintptr_t>(row) & 15u) == 0);
+  if (vec) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const int n4 = vocab / 4;
+    for (int base = 0; base < n4; base += kThreads * U) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = base + u * kThreads + (int)threadIdx.x;
+        v[u] = j < n4 ? __ldg(r4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = base + u * kThreads + (int)threadIdx.x;
+        const bool ok = j < n4;
+        f(4 * j, v[u].x, ok);
+        f(4 * j + 1, v[u].y, ok);
+        f(4 * j + 2, v[u].z, ok);
+        f(4 * j + 3, v[u].w, ok);
+      }
+    }
+  } else {
+    for (int base = 0; base < vocab; base += kThreads * U) {
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + u * kThreads + (int)threadIdx.x;
+        v[u] = i < vocab ? __ldg(row + i) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + u * kThreads + (int)threadIdx.x;
+        f(i, v[u], i < vocab);
+      }
+    }
+  }
+}
+
 struct Smem {
   union {
     uint32_t cnt[kWarps][256];
@@ -191,10 +236,9 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict
   if (!(t > 0.f)) {
     float bv = -FLT_MAX;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < vocab; i += kThreads) {
-      const float v = row[i];
-      if (v > bv) { bv = v; bi = i; }
-    }
+    for_row(row, vocab, [&](int i, float v, bool ok) {
+      if (ok && (v > bv || (v == bv && i < bi))) { bv = v; bi = i; }
+    });
     const int a = block_argmax(bv, bi, sm);
     if (threadIdx.x == 0) out[r] = a == 0x7fffffff ? 0 : a;
     return;
@@ -211,16 +255,17 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict
     int remaining = k;
     __syncthreads();
     for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int base = 0; base < vocab; base += kThreads) {  // warp-uniform trip count (match.any)
-        const int i = base + threadIdx.x;
+      for_row(row, vocab, [&](int, float v, bool ok) {
         int bin = -1;
-        if (i < vocab) {
-          const uint32_t key = fkey(row[i] * inv_t);
+        if (ok) {
+          const uint32_t key = fkey(v * inv_t);
           if ((key & mask) == prefix) bin = (int)((key >> shift) & 255u);
         }
-        const unsigned m = __match_any_sync(0xffffffffu, bin);
-        if (bin >= 0 && lane == __ffs(m) - 1) atomicAdd(&sm.h.cnt[w][bin], (uint32_t)__popc(m));
-      }
+        if (__any_sync(0xffffffffu, bin >= 0)) {  // later digits: most warps hold no matching key
+          const unsigned m = __match_any_sync(0xffffffffu, bin);
+          if (bin >= 0 && lane == __ffs(m) - 1) atomicAdd(&sm.h.cnt[w][bin], (uint32_t)__popc(m));
+        }
+      });
       fold_hist<false>(sm);
       select_bin<false>(sm, shift, prefix, 0.f, remaining, 0.f);
       prefix = sm.sel_prefix;
@@ -232,23 +277,20 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict
       // ---- compact the kept tokens into shared memory
       if (threadIdx.x == 0) sm.cand_n = 0;
       __syncthreads();
-      for (int base = 0; base < vocab; base += kThreads) {
-        const int i = base + threadIdx.x;
-        float z = 0.f;
-        bool keep = false;
-        if (i < vocab) {
-          z = row[i] * inv_t;
-          keep = fkey(z) >= kcut;
-        }
+      for_row(row, vocab, [&](int i, float v, bool ok) {
+        const float z = v * inv_t;
+        const bool keep = ok && fkey(z) >= kcut;
         const unsigned bal = __ballot_sync(0xffffffffu, keep);
-        int pos0 = 0;
-        if (lane == 0 && bal) pos0 = atomicAdd(&sm.cand_n, __popc(bal));
-        pos0 = __shfl_sync(0xffffffffu, pos0, 0);
-        if (keep) {
-          const int pos = pos0 + __popc(bal & ((1u << lane) - 1u));
-          if (pos < kCand) { sm.cand_z[pos] = z; sm.cand_i[pos] = i; }
+        if (bal) {  // warp-uniform
+          int pos0 = 0;
+          if (lane == 0) pos0 = atomicAdd(&sm.cand_n, __popc(bal));
+          pos0 = __shfl_sync(0xffffffffu, pos0, 0);
+          if (keep) {
+            const int pos = pos0 + __popc(bal & ((1u << lane) - 1u));
+            if (pos < kCand) { sm.cand_z[pos] = z; sm.cand_i[pos] = i; }
+          }
         }
-      }
+      });
       __syncthreads();
       const int n = sm.cand_n;
       if (n <= kCand) {
@@ -297,26 +339,26 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict
   uint32_t pcut = kcut;
   if (p < 1.f) {
     float mx = -FLT_MAX;
-    for (int i = threadIdx.x; i < vocab; i += kThreads) {
-      const float z = row[i] * inv_t;
-      if (fkey(z) >= kcut) mx = fmaxf(mx, z);
-    }
+    for_row(row, vocab, [&](int, float v, bool ok) {
+      const float z = v * inv_t;
+      if (ok && fkey(z) >= kcut) mx = fmaxf(mx, z);
+    });
     mx = block_max(mx, sm);
     float tot = 0.f;
-    for (int i = threadIdx.x; i < vocab; i += kThreads) {
-      const float z = row[i] * inv_t;
-      if (fkey(z) >= kcut) tot += __expf(z - mx);
-    }
+    for_row(row, vocab, [&](int, float v, bool ok) {
+      const float z = v * inv_t;
+      if (ok && fkey(z) >= kcut) tot += __expf(z - mx);
+    });
     tot = block_sumf(tot, sm);
     const float target = p * tot;
     uint32_t prefix = 0, mask = 0;
     float above = 0.f;
     for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int i = threadIdx.x; i < vocab; i += kThreads) {
-        const float z = row[i] * inv_t;
+      for_row(row, vocab, [&](int, float v, bool ok) {
+        const float z = v * inv_t;
         const uint32_t key = fkey(z);
-        if (key >= kcut && (key & mask) == prefix) atomicAdd(&sm.h.mass[w][(key >> shift) & 255u], __expf(z - mx));
-      }
+        if (ok && key >= kcut && (key & mask) == prefix) atomicAdd(&sm.h.mass[w][(key >> shift) & 255u], __expf(z - mx));
+      });
       fold_hist<true>(sm);
       select_bin<true>(sm, shift, prefix, target, 0, above);
       prefix = sm.sel_prefix;
@@ -328,13 +370,12 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict
   // ---- Gumbel-max draw among kept tokens
   float bv = -FLT_MAX;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < vocab; i += kThreads) {
-    const float z = row[i] * inv_t;
-    if (fkey(z) < pcut) continue;
-    const float u = uniform01(sd, st, (uint32_t)i);
-    const float g = z - logf(-logf(u));
-    if (g > bv) { bv = g; bi = i; }
-  }
+  for_row(row, vocab, [&](int i, float v, bool ok) {
+    const float z = v * inv_t;
+    if (!ok || fkey(z) < pcut) return;
+    const float g = z - logf(-logf(uniform01(sd, st, (uint32_t)i)));
+    if (g > bv || (g == bv && i < bi)) { bv = g; bi = i; }
+  });
   const int a = block_argmax(bv, bi, sm);
   if (threadIdx.x == 0) out[r] = a == 0x7fffffff ? 0 : a;
 }
