@@ -149,3 +149,36 @@ def test_bench_client_against_server(tmp_path, free_port, capsys):
             proc.wait(timeout=20)
         except subprocess.TimeoutExpired:
             os.killpg(proc.pid, signal.SIGKILL)
+
+
+def test_server_tp2_matches_tp1(tmp_path, free_port):
+    """Two scheduler ranks behind one server (rank 0 receives, publishes the requests to rank 1 and
+    broadcasts the message count over gloo every step): the same greedy completions as one rank."""
+    import requests
+
+    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
+    prompts = ["hello world", "the quick brown fox", "a"]
+    texts = {}
+    for i, tp in enumerate((1, 2)):
+        port = free_port + 20 * i
+        proc = subprocess.Popen(
+            [sys.executable, "-m", "minisgl", "--model", path, "--device", "cpu", "--port", str(port), "--dtype",
+             "float32", "--tp", str(tp), "--max-running-requests", "8"],
+            cwd=ROOT, env=dict(os.environ, PYTHONPATH=ROOT), stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+            text=True, start_new_session=True)
+        try:
+            _wait_ready(port, proc)
+            out = []
+            for p in prompts:
+                r = requests.post(f"http://127.0.0.1:{port}/v1/completions", json={
+                    "model": "m", "prompt": p, "max_tokens": 8, "temperature": 0.0, "ignore_eos": True},
+                    timeout=60).json()
+                out.append(r["choices"][0]["text"])
+            texts[tp] = out
+        finally:
+            os.killpg(proc.pid, signal.SIGTERM)
+            try:
+                proc.wait(timeout=20)
+            except subprocess.TimeoutExpired:
+                os.killpg(proc.pid, signal.SIGKILL)
+    assert texts[2] == texts[1] and all(texts[1])
