@@ -165,16 +165,34 @@ void argmax(at::Tensor out, at::Tensor logits, c10::optional<at::Tensor> values,
   msgl_argmax(out.data_ptr<int32_t>(), vp, logits.data_ptr(), logits.size(0), v, logits.stride(0), f32, stream());
 }
 
+// col_ids: optional [rows, vocab] int32 token id per column; id_offset: token id of column 0
+// otherwise; values: optional fp32 [rows] winning score (see msgl_sample)
 void sample(at::Tensor out, at::Tensor logits, at::Tensor temperature, at::Tensor top_k, at::Tensor top_p,
-            at::Tensor seed, at::Tensor step) {
+            at::Tensor seed, at::Tensor step, c10::optional<at::Tensor> col_ids, int64_t id_offset,
+            c10::optional<at::Tensor> values) {
   check_i32(out, "out"); check_cuda(logits, "logits");
   at::Tensor lf = logits.scalar_type() == at::kFloat ? logits : logits.to(at::kFloat);
   CHECK(lf.stride(-1) == 1, "logits rows must be contiguous");
   check_dtype(temperature, at::kFloat, "temperature"); check_dtype(top_p, at::kFloat, "top_p");
   check_dtype(top_k, at::kInt, "top_k"); check_dtype(seed, at::kLong, "seed"); check_dtype(step, at::kLong, "step");
-  msgl_sample(out.data_ptr<int32_t>(), lf.data_ptr<float>(), lf.size(0), lf.size(1), lf.stride(0),
+  const int64_t rows = lf.size(0), vocab = lf.size(1);
+  CHECK(out.numel() >= rows && temperature.numel() >= rows && top_k.numel() >= rows && top_p.numel() >= rows &&
+            seed.numel() >= rows && step.numel() >= rows, "sampling parameters shorter than the batch");
+  const int32_t* ids = nullptr;
+  if (col_ids.has_value()) {
+    check_i32(*col_ids, "col_ids"); check_contig(*col_ids, "col_ids");
+    CHECK(col_ids->size(0) == rows && col_ids->size(1) == vocab, "col_ids must be [rows, vocab]");
+    ids = col_ids->data_ptr<int32_t>();
+  }
+  float* vals = nullptr;
+  if (values.has_value()) {
+    check_cuda(*values, "values"); check_dtype(*values, at::kFloat, "values");
+    CHECK(values->numel() >= rows, "values too short");
+    vals = values->data_ptr<float>();
+  }
+  msgl_sample(out.data_ptr<int32_t>(), lf.data_ptr<float>(), rows, vocab, lf.stride(0),
               temperature.data_ptr<float>(), top_k.data_ptr<int32_t>(), top_p.data_ptr<float>(),
-              seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(), stream());
+              seed.data_ptr<int64_t>(), step.data_ptr<int64_t>(), ids, (int)id_offset, vals, stream());
 }
 
 void attention_prefill(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor page_table,
@@ -411,7 +429,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope_store", &qk_norm_rope_store);
   m.def("argmax", &argmax, py::arg("out"), py::arg("logits"), py::arg("values") = py::none(),
         py::arg("vocab") = -1);
-  m.def("sample", &sample);
+  m.def("sample", &sample, py::arg("out"), py::arg("logits"), py::arg("temperature"), py::arg("top_k"),
+        py::arg("top_p"), py::arg("seed"), py::arg("step"), py::arg("col_ids") = py::none(),
+        py::arg("id_offset") = 0, py::arg("values") = py::none());
   m.def("attention_prefill", &attention_prefill);
   m.def("attention_decode", &attention_decode);
   m.def("get_error", &get_error);

@@ -29,9 +29,13 @@ void msgl_qk_norm_rope_store(void* q_out, const void* qkv, const int32_t* positi
 // row argmax over the first `vocab` columns; out_val (optional) receives the maximum
 void msgl_argmax(int32_t* out, float* out_val, const void* logits, int rows, int vocab, int64_t stride,
                  int is_fp32, cudaStream_t s);
+// col_ids (optional, [rows, vocab] int32): token id of each column (candidate lists); otherwise
+// column i is token id_offset + i. out_val (optional): the winning Gumbel score per row (the max
+// logit on greedy rows), for combining vocabulary shards.
 void msgl_sample(int32_t* out, const float* logits, int rows, int vocab, int64_t stride,
                  const float* temperature, const int32_t* top_k, const float* top_p,
-                 const int64_t* seed, const int64_t* step, cudaStream_t s);
+                 const int64_t* seed, const int64_t* step, const int32_t* col_ids, int id_offset,
+                 float* out_val, cudaStream_t s);
 
 // ----- GEMM: out[M,N] = epi(x[M,K] @ w[N,K]^T + bias)
 //   epi 0: bf16 out; 1: silu(g)*u on 64-row interleaved gate/up (out has N/2 cols);

@@ -120,8 +120,8 @@ __device__ float block_sumf(float v, Smem& sm) {
   return warp_sum(v);
 }
 
-// argmax of val with lowest-index ties across the block
-__device__ int block_argmax(float v, int i, Smem& sm) {
+// argmax of val with lowest-index ties across the block (*vout: the maximum)
+__device__ int block_argmax(float v, int i, Smem& sm, float* vout) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, v, o);
@@ -140,6 +140,7 @@ __device__ int block_argmax(float v, int i, Smem& sm) {
     const int oi = __shfl_xor_sync(0xffffffffu, i, o);
     if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
   }
+  *vout = v;
   return i;
 }
 
@@ -221,10 +222,16 @@ __device__ __forceinline__ void select_bin(Smem& sm, int shift, uint32_t prefix,
   __syncthreads();
 }
 
+// Column i of row r is token col_ids[r][i] when col_ids is given (a candidate list, ascending ids),
+// else token id_offset + i (a vocabulary shard). The token id keys the Gumbel noise and is what
+// out[r] receives; out_val[r] (optional) receives the winning Gumbel score (the maximum logit on
+// greedy rows), which is what shards compare to combine their draws.
 __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict__ out, const float* __restrict__ logits,
                                                          int vocab, int64_t stride, const float* __restrict__ temperature,
                                                          const int32_t* __restrict__ top_k, const float* __restrict__ top_p,
-                                                         const int64_t* __restrict__ seed, const int64_t* __restrict__ step) {
+                                                         const int64_t* __restrict__ seed, const int64_t* __restrict__ step,
+                                                         const int32_t* __restrict__ col_ids, int id_offset,
+                                                         float* __restrict__ out_val) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   pdl_wait();
@@ -232,6 +239,14 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict
   const int r = blockIdx.x;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const float* row = logits + (size_t)r * stride;
+  const int32_t* ids = col_ids != nullptr ? col_ids + (size_t)r * vocab : nullptr;
+  auto token = [&](int i) -> int { return ids != nullptr ? ids[i] : id_offset + i; };
+  auto emit = [&](int a, float v) {
+    if (threadIdx.x == 0) {
+      out[r] = token(a == 0x7fffffff ? 0 : a);
+      if (out_val != nullptr) out_val[r] = a == 0x7fffffff ? -FLT_MAX : v;
+    }
+  };
   const float t = temperature[r];
   if (!(t > 0.f)) {
     float bv = -FLT_MAX;
@@ -239,8 +254,9 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict
     for_row(row, vocab, [&](int i, float v, bool ok) {
       if (ok && (v > bv || (v == bv && i < bi))) { bv = v; bi = i; }
     });
-    const int a = block_argmax(bv, bi, sm);
-    if (threadIdx.x == 0) out[r] = a == 0x7fffffff ? 0 : a;
+    float mv;
+    const int a = block_argmax(bv, bi, sm, &mv);
+    emit(a, mv);
     return;
   }
   const float inv_t = 1.f / t;
@@ -325,11 +341,12 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict
           const float z = sm.cand_z[j];
           if (fkey(z) < pcut) continue;
           const int i = sm.cand_i[j];
-          const float g = z - logf(-logf(uniform01(sd, st, (uint32_t)i)));
+          const float g = z - logf(-logf(uniform01(sd, st, (uint32_t)token(i))));
           if (g > bv || (g == bv && i < bi)) { bv = g; bi = i; }
         }
-        const int a = block_argmax(bv, bi, sm);
-        if (threadIdx.x == 0) out[r] = a == 0x7fffffff ? 0 : a;
+        float mv;
+        const int a = block_argmax(bv, bi, sm, &mv);
+        emit(a, mv);
         return;
       }
       // more ties at the threshold than the list holds: continue over the whole row
@@ -373,18 +390,20 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(int32_t* __restrict
   for_row(row, vocab, [&](int i, float v, bool ok) {
     const float z = v * inv_t;
     if (!ok || fkey(z) < pcut) return;
-    const float g = z - logf(-logf(uniform01(sd, st, (uint32_t)i)));
+    const float g = z - logf(-logf(uniform01(sd, st, (uint32_t)token(i))));
     if (g > bv || (g == bv && i < bi)) { bv = g; bi = i; }
   });
-  const int a = block_argmax(bv, bi, sm);
-  if (threadIdx.x == 0) out[r] = a == 0x7fffffff ? 0 : a;
+  float mv;
+  const int a = block_argmax(bv, bi, sm, &mv);
+  emit(a, mv);
 }
 
 }  // namespace
 
 extern "C" void msgl_sample(int32_t* out, const float* logits, int rows, int vocab, int64_t stride,
                             const float* temperature, const int32_t* top_k, const float* top_p,
-                            const int64_t* seed, const int64_t* step, cudaStream_t s) {
+                            const int64_t* seed, const int64_t* step, const int32_t* col_ids, int id_offset,
+                            float* out_val, cudaStream_t s) {
   if (rows == 0) return;
   static bool attr_set = false;
   if (!attr_set) {
@@ -392,7 +411,7 @@ extern "C" void msgl_sample(int32_t* out, const float* logits, int rows, int voc
     attr_set = true;
   }
   msgl_launch(sample_kernel, dim3(rows), dim3(kThreads), sizeof(Smem), s, 1, out, logits, vocab, stride, temperature,
-              top_k, top_p, seed, step);
+              top_k, top_p, seed, step, col_ids, id_offset, out_val);
 }
 
 MSGL_ERROR_ACCESSOR(msgl_err_sampling)

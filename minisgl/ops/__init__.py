@@ -107,12 +107,17 @@ def argmax(logits, vocab: int | None = None, with_values: bool = False):
     return (out, vals) if with_values else out
 
 
-def sample(logits, temperature, top_k, top_p, seed, step):
+def sample(logits, temperature, top_k, top_p, seed, step, col_ids=None, id_offset: int = 0,
+           with_values: bool = False):
+    """Temperature / top-k / top-p draw per row. Column j is token ``col_ids[row, j]`` (a
+    candidate list sorted by id) or ``id_offset + j`` (a vocabulary shard); token ids are returned.
+    ``with_values`` also returns each row's winning score, for combining shards."""
     if not _on_gpu(logits):
-        return ref.sample(logits, temperature, top_k, top_p, seed, step)
+        return ref.sample(logits, temperature, top_k, top_p, seed, step, col_ids, id_offset, with_values)
     out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
-    _cuda().sample(out, logits, temperature, top_k, top_p, seed, step)
-    return out
+    vals = torch.empty(logits.shape[0], dtype=torch.float32, device=logits.device) if with_values else None
+    _cuda().sample(out, logits, temperature, top_k, top_p, seed, step, col_ids, id_offset, vals)
+    return (out, vals) if with_values else out
 
 
 __all__ = [

@@ -181,10 +181,12 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
     return torch.argmax(logits.float(), dim=-1).to(torch.int32)
 
 
-def _uniform_from_counter(seed: torch.Tensor, step: torch.Tensor, vocab: int) -> torch.Tensor:
-    """Counter-based uniforms in (0,1) keyed by (seed, step, vocab id); same hash as the kernel."""
+def _uniform_from_counter(seed: torch.Tensor, step: torch.Tensor, vocab: int,
+                          ids: torch.Tensor | None = None) -> torch.Tensor:
+    """Counter-based uniforms in (0,1) keyed by (seed, step, token id); same hash as the kernel.
+    Token ids are ``ids`` ([rows, vocab]) when given, else 0..vocab-1."""
     M = 0xFFFFFFFF
-    idx = torch.arange(vocab, dtype=torch.int64)[None, :]
+    idx = torch.arange(vocab, dtype=torch.int64)[None, :] if ids is None else ids.long()
     x = (seed.long()[:, None] * 0x9E3779B1 + step.long()[:, None] * 0x85EBCA77 + idx * 0xC2B2AE3D) & M
     for _ in range(2):  # murmur3 finalizer rounds
         x ^= x >> 16
@@ -202,18 +204,32 @@ def sample(
     top_p: torch.Tensor,
     seed: torch.Tensor,
     step: torch.Tensor,
-) -> torch.Tensor:
+    col_ids: torch.Tensor | None = None,
+    id_offset: int = 0,
+    with_values: bool = False,
+):
     """Temperature / top-k / top-p sampling by the Gumbel-max trick with counter-based noise:
     keep tokens inside the top-k and the top-p nucleus of softmax(logits / T), then return
-    argmax(logits / T - log(-log(u))). Rows with temperature <= 0 are greedy."""
+    argmax(logits / T - log(-log(u))). Rows with temperature <= 0 are greedy.
+
+    Column j of a row is token ``col_ids[row, j]`` (a candidate list in ascending id order) or
+    ``id_offset + j`` (a vocabulary shard); the noise is keyed by the token id and the token id is
+    returned. ``with_values`` also returns the winning score (the maximum logit on greedy rows)."""
     lf = logits.float()
     bs, V = lf.shape
-    out = torch.empty(bs, dtype=torch.int32, device=logits.device)
-    u = _uniform_from_counter(seed.cpu(), step.cpu(), V).to(lf.device)
+    pos = torch.empty(bs, dtype=torch.int64)
+    vals = torch.empty(bs, dtype=torch.float32)
+    ids = col_ids.cpu() if col_ids is not None else None
+    u = _uniform_from_counter(seed.cpu(), step.cpu(), V,
+                              None if ids is None and id_offset == 0 else
+                              (ids if ids is not None else torch.arange(V)[None, :] + id_offset)).to(lf.device)
+    if u.shape[0] == 1 and bs > 1:
+        u = u.expand(bs, V)
     for i in range(bs):
         t = float(temperature[i])
         if t <= 0:
-            out[i] = int(torch.argmax(lf[i]))
+            pos[i] = int(torch.argmax(lf[i]))
+            vals[i] = float(lf[i, pos[i]])
             continue
         z = lf[i] / t
         k = int(top_k[i])
@@ -231,8 +247,14 @@ def sample(
             keep &= probs >= thr
         g = z.double() - torch.log(-torch.log(u[i]))
         g = g.masked_fill(~keep, float("-inf"))
-        out[i] = int(torch.argmax(g))
-    return out
+        pos[i] = int(torch.argmax(g))
+        vals[i] = float(g[pos[i]])
+    if ids is not None:
+        out = ids.gather(1, pos.view(bs, 1)).view(bs).to(torch.int32)
+    else:
+        out = (pos + id_offset).to(torch.int32)
+    out = out.to(logits.device)
+    return (out, vals.to(logits.device)) if with_values else out
 
 
 def rope_cos_sin(max_pos: int, rotary_dim: int, inv_freq: torch.Tensor) -> torch.Tensor:

@@ -334,6 +334,49 @@ def test_sampling_paths(case):
             assert above < p + 1e-4, (i, float(above))
 
 
+@pytest.mark.parametrize("tp", [2, 8])
+def test_sampling_shards_reproduce_unsharded_draws(tp):
+    """What vocabulary-parallel sampling does on each rank, emulated on one GPU: (1) temperature-only
+    and greedy rows drawn per shard (token ids offset, winning scores returned) and combined by best
+    score equal the unsharded draw; (2) top-k rows sampled over gathered per-shard candidate lists
+    (sorted by token id, passed as column ids) equal the unsharded draw."""
+    from minisgl import ops
+
+    B, V = 32, 151936
+    g = torch.Generator(device="cpu").manual_seed(11)
+    logits = (torch.randn(B, V, generator=g) * 2).to(DEV)
+    seed = (torch.arange(B, dtype=torch.int64) * 7 + 3).to(DEV)
+    step = (torch.arange(B, dtype=torch.int64) + 17).to(DEV)
+    width = (V + tp - 1) // tp
+    shards = [(r * width, min(V, (r + 1) * width)) for r in range(tp)]
+    # (1) temperature only, every other row greedy
+    temp = torch.tensor([0.0 if i % 2 else 0.9 for i in range(B)], device=DEV)
+    k = torch.full((B,), V, dtype=torch.int32, device=DEV)
+    p = torch.ones(B, device=DEV)
+    want = ops.sample(logits, temp, k, p, seed, step)
+    ids, vals = zip(*[ops.sample(logits[:, lo:hi].contiguous(), temp, k, p, seed, step, id_offset=lo,
+                                 with_values=True) for lo, hi in shards])
+    best = torch.stack(vals).argmax(0)
+    got = torch.stack(ids).gather(0, best.view(1, B)).view(B)
+    assert torch.equal(got.cpu(), want.cpu())
+    # (2) top-k 40 (every third row also top-p 0.9) from per-shard candidate lists
+    temp = torch.full((B,), 0.8, device=DEV)
+    k = torch.full((B,), 40, dtype=torch.int32, device=DEV)
+    p = torch.tensor([0.9 if i % 3 == 0 else 1.0 for i in range(B)], device=DEV)
+    want = ops.sample(logits, temp, k, p, seed, step).cpu()
+    cv, ci = [], []
+    for lo, hi in shards:
+        v, i = torch.topk(logits[:, lo:hi], 56, dim=1)
+        cv.append(v)
+        ci.append(i.to(torch.int32) + lo)
+    cid, order = torch.sort(torch.cat(ci, 1), dim=1)
+    cval = torch.cat(cv, 1).gather(1, order).contiguous()
+    got = ops.sample(cval, temp, k, p, seed, step, col_ids=cid.contiguous()).cpu()
+    exact = p.cpu() >= 1.0
+    assert torch.equal(got[exact], want[exact])
+    assert (got == want).float().mean() >= 0.9
+
+
 def test_store_kv():
     from minisgl import ops
 

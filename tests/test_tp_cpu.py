@@ -67,3 +67,62 @@ def test_tp2_matches_tp1(tmp_path, preset, moe_parallel, free_port):
     assert all(p.returncode == 0 for p in procs), outs
     line = [l for l in outs[0].splitlines() if l.startswith("RESULT ")][0]
     assert json.loads(line[len("RESULT "):]) == ref
+
+
+SAMPLING_WORKER = r"""
+import json, os, sys
+sys.path.insert(0, {root!r})
+import torch
+from minisgl.core import SamplingParams
+from minisgl.llm import LLM
+prompts = json.loads(os.environ["TP_PROMPTS"])
+specs = json.loads(os.environ["TP_SPECS"])
+llm = LLM({path!r}, dtype=torch.float32, device="cpu", max_running_req=16)
+res = []
+for spec in specs:
+    sps = [SamplingParams(max_tokens=10, ignore_eos=True, **s) for s in spec]
+    res.append([o["token_ids"] for o in llm.generate(prompts, sps)])
+if int(os.environ["RANK"]) == 0:
+    print("RESULT " + json.dumps(res), flush=True)
+llm.shutdown()
+"""
+
+
+def test_tp2_sampling_matches_tp1(tmp_path, free_port):
+    """Sampled decoding under vocabulary parallelism draws the TP1 tokens in each combine mode:
+    temperature only (per-shard draws, score/id pairs exchanged), top-k (+ top-p) (per-shard
+    candidate lists), greedy rows mixed with top-k rows, and top-p alone (full logits gathered)."""
+    from minisgl.llm import LLM
+
+    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
+    prompts = _prompts()
+    n = len(prompts)
+    specs = [
+        [dict(temperature=0.8)] * n,
+        [dict(temperature=0.9, top_k=20, top_p=0.9)] * n,
+        [dict(temperature=0.0) if i % 2 else dict(temperature=1.1, top_k=5) for i in range(n)],
+        [dict(temperature=0.7, top_p=0.8)] * n,
+    ]
+    llm = LLM(path, dtype=torch.float32, device="cpu", max_running_req=16, distributed_port=free_port)
+    try:
+        ref = []
+        for spec in specs:
+            sps = [SamplingParams(max_tokens=10, ignore_eos=True, **s) for s in spec]
+            ref.append([o["token_ids"] for o in llm.generate(prompts, sps)])
+    finally:
+        llm.shutdown()
+    script = tmp_path / "worker.py"
+    script.write_text(SAMPLING_WORKER.format(root=ROOT, path=path))
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE="2", MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(free_port + 9), TP_PROMPTS=json.dumps(prompts), TP_SPECS=json.dumps(specs),
+                   PYTHONPATH=ROOT)
+        procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    outs = [p.communicate(timeout=300)[0] for p in procs]
+    assert all(p.returncode == 0 for p in procs), outs
+    line = [l for l in outs[0].splitlines() if l.startswith("RESULT ")][0]
+    got = json.loads(line[len("RESULT "):])
+    for mode, a, b in zip(("temperature", "topk", "greedy+topk", "full"), got, ref):
+        assert a == b, mode
