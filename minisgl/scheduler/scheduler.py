@@ -160,8 +160,12 @@ class Scheduler(SchedulerIOMixin):
             raise KeyboardInterrupt
         elif isinstance(msg, UserMsg):
             n, cap = len(msg.input_ids), self.engine.max_seq_len
-            if cap - n <= 0:
-                logger.warning_rank0(f"request {msg.uid} dropped: input length {n} >= {cap}")
+            reason = ("empty prompt" if n == 0 else f"input length {n} >= {cap}" if n >= cap else
+                      "max_tokens < 1" if msg.sampling_params.max_tokens < 1 else None)
+            if reason is not None:
+                # finish it at once with no output, so that its client is answered
+                logger.warning_rank0(f"request {msg.uid} rejected: {reason}")
+                self.send_result([DetokenizeMsg(uid=msg.uid, next_token=0, finished=True, eos=True)])
                 return
             if msg.sampling_params.max_tokens > cap - n:
                 msg.sampling_params.max_tokens = cap - n

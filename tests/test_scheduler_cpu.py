@@ -292,3 +292,18 @@ def test_aborts_free_everything_once(tiny_path, free_port, overlap):
         assert not llm.decode_manager.running and not llm.prefill_manager.pending_list
     finally:
         llm.shutdown()
+
+
+def test_rejected_requests_finish_empty(tiny_path, free_port):
+    """An empty prompt, a prompt at the context limit and max_tokens = 0 are answered at once with
+    no tokens (instead of being dropped, which left their clients waiting); the rest run."""
+    llm = make_llm(tiny_path, free_port, max_seq_len_override=64)
+    try:
+        prompts = [[], list(range(1, 65)), [5, 6, 7], [8, 9]]
+        sps = [SamplingParams(max_tokens=4, ignore_eos=True)] * 2 + [
+            SamplingParams(max_tokens=0, ignore_eos=True), SamplingParams(max_tokens=4, ignore_eos=True)]
+        outs = [o["token_ids"] for o in llm.generate(prompts, sps)]
+        assert outs == [[], [], [], expected([8, 9], 4)]
+        llm.cache_manager.check_integrity()
+    finally:
+        llm.shutdown()
