@@ -21,6 +21,7 @@ import torch.distributed as dist
 from minisgl.attention import create_attention_backend
 from minisgl.attention.paged import PAGED_DECODE_PAGES
 from minisgl.core import Batch, Context, Req, SamplingParams, get_global_ctx, reset_global_ctx, set_global_ctx
+from minisgl.env import ENV
 from minisgl.kvcache import create_kvcache_pool
 from minisgl.layers import set_rope_device
 from minisgl.models import create_model, load_weight
@@ -161,13 +162,11 @@ class Engine:
     def _init_peer_comm(self, config: EngineConfig) -> None:
         if not self.is_cuda or config.tp_info.size == 1:
             return
-        mode = config.comm if config.comm != "auto" else os.environ.get("MINISGL_COMM_MODE", "auto")
+        mode = config.comm if config.comm != "auto" else ENV.COMM_MODE
         if mode == "nccl":
             return
         if mode in ("auto", "peer", "fused"):
             from minisgl.parallel.peer import enable_peer_comm
-
-            from minisgl.env import ENV
 
             # all-reduce messages are [tokens, hidden]; the LM-head gather is [bs, vocab/tp] fp32
             max_bytes = max(config.max_forward_len * self.model_config.hidden_size * self.dtype.itemsize,

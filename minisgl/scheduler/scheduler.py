@@ -151,6 +151,8 @@ class Scheduler(SchedulerIOMixin):
                     self.cache_manager.cache_req(req, finished=False)
         self.finished_reqs = newly_finished
         self.send_result(reply)
+        if ENV.DEBUG_CHECK_INTEGRITY:
+            self.cache_manager.prefix_cache.check_integrity()
 
     def _process_one_msg(self, msg: BaseBackendMsg) -> None:
         if isinstance(msg, BatchBackendMsg):
