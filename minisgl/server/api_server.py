@@ -81,6 +81,7 @@ class ModelList(BaseModel):
 class _Pending:
     replies: List[UserReply] = field(default_factory=list)
     event: asyncio.Event = field(default_factory=asyncio.Event)
+    prompt_tokens: int = 0  # reported by the tokenizer worker
 
 
 @dataclass
@@ -120,6 +121,9 @@ class FrontendManager:
                 p.event.clear()
                 batch, p.replies = p.replies, []
                 for r in batch:
+                    if r.num_input_tokens and not r.finished and not r.incremental_output:
+                        p.prompt_tokens = r.num_input_tokens  # prompt length, not output
+                        continue
                     yield r
                     if r.finished:
                         return
@@ -216,6 +220,7 @@ async def _completion(req: OpenAICompletionRequest, request: Request, chat: bool
     else:
         return {"error": "either 'messages' or 'prompt' is required"}
     uid = st.new_user()
+    pend = st.pending[uid]
     await st.send_one(TokenizeMsg(uid=uid, text=text, sampling_params=req.sampling()))
     if req.stream:
         return StreamingResponse(st.guard(st.stream_chat(uid, req.model, chat), request, uid),
@@ -228,7 +233,8 @@ async def _completion(req: OpenAICompletionRequest, request: Request, chat: bool
               if chat else {"index": 0, "text": content, "finish_reason": "stop"})
     return {"id": f"{'chat' if chat else ''}cmpl-{uid}", "object": "chat.completion" if chat else "text_completion",
             "created": int(time.time()), "model": req.model, "choices": [choice],
-            "usage": {"prompt_tokens": 0, "completion_tokens": n, "total_tokens": n}}
+            "usage": {"prompt_tokens": pend.prompt_tokens, "completion_tokens": n,
+                      "total_tokens": pend.prompt_tokens + n}}
 
 
 @app.post("/v1/chat/completions")

@@ -71,6 +71,10 @@ def tokenize_worker(*, tokenizer_path: str, addr: str, create: bool, backend_add
                 to_backend.put(_one_or_batch(
                     [UserMsg(uid=m.uid, input_ids=t, sampling_params=m.sampling_params) for m, t in zip(toks, ids)],
                     BatchBackendMsg))
+                # the prompt length, for the response's usage (a reply without text)
+                to_frontend.put(_one_or_batch(
+                    [UserReply(uid=m.uid, incremental_output="", finished=False, num_input_tokens=max(1, len(t)))
+                     for m, t in zip(toks, ids)], BatchFrontendMsg))
             if aborts:
                 to_backend.put(_one_or_batch([AbortBackendMsg(uid=m.uid) for m in aborts], BatchBackendMsg))
             logger.debug(f"handled {len(detoks)} detok / {len(toks)} tok / {len(aborts)} abort")

@@ -50,6 +50,8 @@ def test_server_endpoints(tmp_path, free_port, num_tokenizer):
             "model": "m", "messages": [{"role": "user", "content": "hello"}], "max_tokens": 6,
             "temperature": 0.0, "ignore_eos": True}, timeout=60).json()
         assert r["object"] == "chat.completion" and r["usage"]["completion_tokens"] >= 1
+        assert r["usage"]["prompt_tokens"] > 1
+        assert r["usage"]["total_tokens"] == r["usage"]["prompt_tokens"] + r["usage"]["completion_tokens"]
         text = r["choices"][0]["message"]["content"]
         # streaming returns the same greedy text in pieces
         chunks = []
