@@ -1,0 +1,133 @@
+"""Tensor-parallel collective micro-benchmark, one process per GPU:
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m minisgl.benchmark.comm [--hidden 5120]
+
+For each token count it times, on decode-sized activations [T, hidden] bf16:
+
+* ``nvls``  - the fused NVLS all-reduce + residual add + RMSNorm kernel (one launch);
+* ``peer``  - the IPC peer-memory all-reduce followed by the fused add + RMSNorm kernel;
+* ``nccl``  - NCCL all-reduce (torch.distributed) followed by the same norm kernel (the baseline).
+
+Each variant runs 20 times inside one CUDA graph, replayed 10 times; the CUDA-event time per call
+is the MAX over ranks. The roofline is the slower of the bytes each GPU must send over NVLink
+(its T x hidden x 2 partial) at the measured 770 GB/s per direction and the norm's HBM traffic at
+the measured copy bandwidth; rank 0 prints one JSON line per token count with each variant's time
+and its fraction of that roofline.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+NVLINK_BPS = 770e9  # measured peer copy, per direction per GPU
+
+
+def _hbm_bps() -> float:
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    try:
+        with open(os.path.join(root, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]) * 1e9
+    except (OSError, KeyError, ValueError):
+        return 6.65e12
+
+
+def _time(fn, stream, calls: int = 20, reps: int = 10) -> float:
+    """Milliseconds per call: ``calls`` calls captured in one graph, replayed ``reps`` times."""
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(calls):
+            fn()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        g.replay()
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(reps):
+            g.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / (calls * reps)
+    del g
+    return ms
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser("minisgl.benchmark.comm")
+    ap.add_argument("--hidden", type=int, default=5120)
+    ap.add_argument("--tokens", default="1,8,16,64,128,256,512")
+    a = ap.parse_args(argv)
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+    cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=60))
+    from minisgl import ops
+    from minisgl.parallel.comm import TorchDistributedImpl
+    from minisgl.parallel.nvls import NvlsNormComm
+    from minisgl.parallel.peer import PeerCommImpl
+
+    H, eps = a.hidden, 1e-6
+    tokens = [int(t) for t in a.tokens.split(",")]
+    cap = max(tokens) * H * 2
+    nccl = TorchDistributedImpl()
+    peer = PeerCommImpl(cpu, dev, cap, nccl)
+    try:
+        nvls = NvlsNormComm(dist.group.WORLD, cpu, dev, cap)
+    except RuntimeError as e:
+        nvls = None
+        if rank == 0:
+            print(json.dumps({"nvls": f"unavailable: {e}"}), flush=True)
+    s = torch.cuda.Stream()
+    w = (torch.rand(H, device=dev) + 0.5).to(torch.bfloat16)
+    hbm = _hbm_bps()
+    for T in tokens:
+        x = torch.randn(T, H, device=dev, dtype=torch.bfloat16)
+        res = torch.randn(T, H, device=dev, dtype=torch.bfloat16)
+        times = {}
+        if nvls is not None:
+            times["nvls"] = _time(lambda: nvls.all_reduce_add_rmsnorm(x, res, w, eps), s)
+
+        ybuf = x.clone()
+
+        def unfused(impl):
+            # NCCL reduces in place and the norm then overwrites the sum with normalised rows, so
+            # repeated calls stay bounded; the peer all-reduce returns a new tensor
+            def run():
+                y = impl.all_reduce(ybuf)
+                ops.fused_add_rmsnorm(y, res, w, eps)
+            return run
+
+        times["peer"] = _time(unfused(peer), s)
+        times["nccl"] = _time(unfused(nccl), s)
+        t = torch.tensor([times[k] for k in sorted(times)], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=cpu)
+        times = {k: float(v) for k, v in zip(sorted(times), t)}
+        nbytes = T * H * 2
+        roof_ms = max(nbytes / NVLINK_BPS, 4 * nbytes / hbm) * 1e3  # norm: x, residual in/out, out
+        if rank == 0:
+            row = {"world": world, "tokens": T, "hidden": H, "roofline_us": round(roof_ms * 1e3, 2)}
+            for k, v in times.items():
+                row[f"{k}_us"] = round(v * 1e3, 2)
+                row[f"{k}_frac"] = round(roof_ms / v, 3)
+            print(json.dumps(row), flush=True)
+    torch.cuda.synchronize()
+    dist.barrier(group=cpu)
+    if nvls is not None:
+        nvls.close()
+    peer.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
