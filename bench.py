@@ -23,7 +23,10 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
-MODELS = {"qwen3-14b": "qwen3-14b", "qwen3-0.6b": "qwen3-0.6b", "qwen3-32b": "qwen3-32b"}
+# gpt-oss-120b (MoE, bf16 experts: ~240 GB of weights) needs TP >= 2; with MINISGL_MOE_PARALLEL=ep
+# each rank holds whole experts
+MODELS = {"qwen3-14b": "qwen3-14b", "qwen3-0.6b": "qwen3-0.6b", "qwen3-32b": "qwen3-32b",
+          "gpt-oss-120b": "gpt-oss-120b"}
 CONFIG = dict(max_running_req=256, cuda_graph_max_bs=256, page_size=64, max_seq_len_override=4096,
               max_extend_tokens=16384)
 
