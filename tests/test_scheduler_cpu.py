@@ -44,6 +44,7 @@ class FakeModel:
     def __init__(self, engine):
         self.engine = engine
         self.forwards = 0
+        self.prefill_tokens = 0  # prompt tokens actually computed (prefix-cache hits excluded)
         self.kv = {}
 
     def _check_kv(self, batch):
@@ -67,6 +68,8 @@ class FakeModel:
         ctx = get_global_ctx()
         b = ctx.batch
         self.forwards += 1
+        if b.is_prefill:
+            self.prefill_tokens += sum(r.device_len - r.cached_len for r in b.reqs)
         self._check_kv(b)
         # out_loc must be the page-table slots of the extend tokens
         want = np.concatenate([r.slots[r.cached_len : r.device_len] for r in b.padded_reqs])
@@ -124,11 +127,25 @@ def test_fake_model_outputs(tiny_path, free_port, page, cache, budget, running, 
         prompts = prompts_with_shared_prefixes(page, 18)
         lens = [3 + (i * 5) % 23 for i in range(len(prompts))]
         sps = [SamplingParams(max_tokens=n, ignore_eos=True) for n in lens]
+        computed = []
         for rep in range(2):  # the second pass hits the prefix cache left by the first
+            fm = llm.engine.model
+            before = fm.prefill_tokens
             outs = llm.generate(prompts, sps)
             for p, n, o in zip(prompts, lens, outs):
                 assert o["token_ids"] == expected(p, n), (rep, p)
             llm.cache_manager.check_integrity()
+            computed.append(fm.prefill_tokens - before)
+        total = sum(len(p) for p in prompts)
+        assert computed[0] <= total
+        if cache == "naive":
+            assert computed == [total, total]
+        elif pages is None:
+            # the first pass left every prompt cached (evictable, nothing evicted): the second pass
+            # reuses each prompt's whole pages short of its last token and computes the rest
+            assert computed[1] == sum(len(p) - (len(p) - 1) // page * page for p in prompts), computed
+        else:
+            assert computed[1] <= computed[0]
         cm = llm.cache_manager
         assert cm.available_size == cm.num_pages * cm.page_size  # every page free or evictable
         assert not llm.decode_manager.running and not llm.prefill_manager.pending_list
