@@ -53,15 +53,53 @@ class OpenAICompletionRequest(BaseModel):
     top_p: float = 1.0
     n: int = 1
     stream: bool = False
-    stop: List[str] = []
+    stop: List[str] | str | None = None  # one string or several; output ends before the first match
     presence_penalty: float = 0.0
     frequency_penalty: float = 0.0
     ignore_eos: bool = False
     seed: int | None = None
 
+    def stop_list(self) -> List[str]:
+        return [self.stop] if isinstance(self.stop, str) else list(self.stop or [])
+
     def sampling(self) -> SamplingParams:
         return SamplingParams(temperature=self.temperature, top_k=self.top_k, top_p=self.top_p,
                               ignore_eos=self.ignore_eos, max_tokens=self.max_tokens, seed=self.seed)
+
+
+class StopMatcher:
+    """Cuts a streamed completion at the first occurrence of any stop string (OpenAI ``stop``).
+
+    ``feed`` returns the text that is safe to send: it holds back a tail that could still grow
+    into a stop string across chunk boundaries. After a match ``done`` is set and the text before
+    the stop string is the last output; ``flush`` releases the held tail at the end of a request.
+    (The reference accepts ``stop`` and ignores it.)"""
+
+    def __init__(self, stops: List[str]):
+        self.stops = [x for x in stops if x]
+        self.buf = ""
+        self.done = False
+
+    def feed(self, piece: str) -> str:
+        if not self.stops:
+            return piece
+        self.buf += piece
+        hits = [i for i in (self.buf.find(x) for x in self.stops) if i >= 0]
+        if hits:
+            out, self.buf, self.done = self.buf[: min(hits)], "", True
+            return out
+        hold = 0
+        for x in self.stops:
+            for k in range(min(len(x) - 1, len(self.buf)), hold, -1):
+                if self.buf.endswith(x[:k]):
+                    hold = k
+                    break
+        out, self.buf = self.buf[: len(self.buf) - hold], self.buf[len(self.buf) - hold:]
+        return out
+
+    def flush(self) -> str:
+        out, self.buf = self.buf, ""
+        return out
 
 
 class ModelCard(BaseModel):
@@ -153,19 +191,30 @@ class FrontendManager:
             yield f"data: {r.incremental_output}\n".encode()
         yield b"data: [DONE]\n"
 
-    async def stream_chat(self, uid: int, model: str, chat: bool) -> AsyncIterator[bytes]:
+    async def stream_chat(self, uid: int, model: str, chat: bool, stop: List[str] = ()) -> AsyncIterator[bytes]:
         first = True
         obj = "chat.completion.chunk" if chat else "text_completion"
-        async for r in self.replies(uid):
+        matcher = StopMatcher(list(stop))
+
+        def chunk(text: str) -> bytes:
             if chat:
                 delta = {"role": "assistant"} if first else {}
-                if r.incremental_output:
-                    delta["content"] = r.incremental_output
+                if text:
+                    delta["content"] = text
                 choice = {"delta": delta, "index": 0, "finish_reason": None}
             else:
-                choice = {"text": r.incremental_output, "index": 0, "finish_reason": None}
+                choice = {"text": text, "index": 0, "finish_reason": None}
+            return f"data: {json.dumps({'id': f'cmpl-{uid}', 'object': obj, 'model': model, 'choices': [choice]})}\n\n".encode()
+
+        async for r in self.replies(uid):
+            text = matcher.feed(r.incremental_output)
+            if r.finished:
+                text += matcher.flush()
+            yield chunk(text)
             first = False
-            yield f"data: {json.dumps({'id': f'cmpl-{uid}', 'object': obj, 'model': model, 'choices': [choice]})}\n\n".encode()
+            if matcher.done:  # stop string reached: the scheduler can drop the request
+                await self.abort_user(uid)
+                break
         end = {"delta": {}, "index": 0, "finish_reason": "stop"} if chat else {"text": "", "index": 0, "finish_reason": "stop"}
         yield f"data: {json.dumps({'id': f'cmpl-{uid}', 'object': obj, 'model': model, 'choices': [end]})}\n\n".encode()
         yield b"data: [DONE]\n\n"
@@ -223,12 +272,18 @@ async def _completion(req: OpenAICompletionRequest, request: Request, chat: bool
     pend = st.pending[uid]
     await st.send_one(TokenizeMsg(uid=uid, text=text, sampling_params=req.sampling()))
     if req.stream:
-        return StreamingResponse(st.guard(st.stream_chat(uid, req.model, chat), request, uid),
+        return StreamingResponse(st.guard(st.stream_chat(uid, req.model, chat, req.stop_list()), request, uid),
                                  media_type="text/event-stream")
     content, n = "", 0
+    matcher = StopMatcher(req.stop_list())
     async for r in st.replies(uid):
-        content += r.incremental_output
+        content += matcher.feed(r.incremental_output)
         n += 1
+        if r.finished:
+            content += matcher.flush()
+        if matcher.done:
+            await st.abort_user(uid)
+            break
     choice = ({"index": 0, "message": {"role": "assistant", "content": content}, "finish_reason": "stop"}
               if chat else {"index": 0, "text": content, "finish_reason": "stop"})
     return {"id": f"{'chat' if chat else ''}cmpl-{uid}", "object": "chat.completion" if chat else "text_completion",

@@ -184,3 +184,44 @@ def test_server_tp2_matches_tp1(tmp_path, free_port):
             except subprocess.TimeoutExpired:
                 os.killpg(proc.pid, signal.SIGKILL)
     assert texts[2] == texts[1] and all(texts[1])
+
+
+def test_stop_strings(tmp_path, free_port):
+    """OpenAI ``stop``: the completion ends before the first occurrence of a stop string, in the
+    plain and the streamed response alike (the stream holds back text that could still grow into
+    a stop string across chunks), and the request is released in the scheduler."""
+    import requests
+
+    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
+    port = free_port
+    proc = subprocess.Popen(
+        [sys.executable, "-m", "minisgl", "--model", path, "--device", "cpu", "--port", str(port), "--dtype",
+         "float32", "--max-running-requests", "8"],
+        cwd=ROOT, env=dict(os.environ, PYTHONPATH=ROOT), stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+        text=True, start_new_session=True)
+    try:
+        _wait_ready(port, proc)
+        url = f"http://127.0.0.1:{port}/v1/completions"
+        body = {"model": "m", "prompt": "hello world", "max_tokens": 12, "temperature": 0.0, "ignore_eos": True}
+        full = requests.post(url, json=body, timeout=60).json()["choices"][0]["text"]
+        assert len(full) >= 6, full
+        stop = full[3:6]
+        want = full[: full.find(stop)]
+        got = requests.post(url, json=dict(body, stop=stop), timeout=60).json()["choices"][0]["text"]
+        assert got == want
+        pieces = []
+        with requests.post(url, json=dict(body, stop=[stop, "\u0000never"], stream=True), stream=True,
+                           timeout=60) as s:
+            for line in s.iter_lines():
+                if line.startswith(b"data: ") and line != b"data: [DONE]":
+                    pieces.append(json.loads(line[6:])["choices"][0]["text"])
+        assert "".join(pieces) == want
+        # the server keeps serving after the early stops
+        again = requests.post(url, json=body, timeout=60).json()["choices"][0]["text"]
+        assert again == full
+    finally:
+        os.killpg(proc.pid, signal.SIGTERM)
+        try:
+            proc.wait(timeout=20)
+        except subprocess.TimeoutExpired:
+            os.killpg(proc.pid, signal.SIGKILL)
