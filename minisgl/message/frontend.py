@@ -31,6 +31,7 @@ class UserReply(BaseFrontendMsg):
     finished: bool
     num_output_tokens: int = 0
     num_input_tokens: int = 0
+    finish_reason: str = ""  # on the final reply: "stop" (EOS) or "length" (max_tokens / context)
 
 
 _TABLE = {c.__name__: c for c in (BatchFrontendMsg, UserReply)}

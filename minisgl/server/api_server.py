@@ -206,16 +206,18 @@ class FrontendManager:
                 choice = {"text": text, "index": 0, "finish_reason": None}
             return f"data: {json.dumps({'id': f'cmpl-{uid}', 'object': obj, 'model': model, 'choices': [choice]})}\n\n".encode()
 
+        reason = "stop"
         async for r in self.replies(uid):
             text = matcher.feed(r.incremental_output)
             if r.finished:
                 text += matcher.flush()
+                reason = r.finish_reason or "stop"
             yield chunk(text)
             first = False
             if matcher.done:  # stop string reached: the scheduler can drop the request
                 await self.abort_user(uid)
                 break
-        end = {"delta": {}, "index": 0, "finish_reason": "stop"} if chat else {"text": "", "index": 0, "finish_reason": "stop"}
+        end = {"delta": {}, "index": 0, "finish_reason": reason} if chat else {"text": "", "index": 0, "finish_reason": reason}
         yield f"data: {json.dumps({'id': f'cmpl-{uid}', 'object': obj, 'model': model, 'choices': [end]})}\n\n".encode()
         yield b"data: [DONE]\n\n"
 
@@ -274,18 +276,19 @@ async def _completion(req: OpenAICompletionRequest, request: Request, chat: bool
     if req.stream:
         return StreamingResponse(st.guard(st.stream_chat(uid, req.model, chat, req.stop_list()), request, uid),
                                  media_type="text/event-stream")
-    content, n = "", 0
+    content, n, reason = "", 0, "stop"
     matcher = StopMatcher(req.stop_list())
     async for r in st.replies(uid):
         content += matcher.feed(r.incremental_output)
         n += 1
         if r.finished:
             content += matcher.flush()
+            reason = r.finish_reason or "stop"
         if matcher.done:
             await st.abort_user(uid)
             break
-    choice = ({"index": 0, "message": {"role": "assistant", "content": content}, "finish_reason": "stop"}
-              if chat else {"index": 0, "text": content, "finish_reason": "stop"})
+    choice = ({"index": 0, "message": {"role": "assistant", "content": content}, "finish_reason": reason}
+              if chat else {"index": 0, "text": content, "finish_reason": reason})
     return {"id": f"{'chat' if chat else ''}cmpl-{uid}", "object": "chat.completion" if chat else "text_completion",
             "created": int(time.time()), "model": req.model, "choices": [choice],
             "usage": {"prompt_tokens": pend.prompt_tokens, "completion_tokens": n,

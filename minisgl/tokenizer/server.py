@@ -64,7 +64,9 @@ def tokenize_worker(*, tokenizer_path: str, addr: str, create: bool, backend_add
             if detoks:
                 texts = detok.detokenize(detoks)
                 to_frontend.put(_one_or_batch(
-                    [UserReply(uid=m.uid, incremental_output=t, finished=m.finished) for m, t in zip(detoks, texts)],
+                    [UserReply(uid=m.uid, incremental_output=t, finished=m.finished,
+                               finish_reason=("stop" if m.eos else "length") if m.finished else "")
+                     for m, t in zip(detoks, texts)],
                     BatchFrontendMsg))
             if toks:
                 ids = tok.tokenize(toks)

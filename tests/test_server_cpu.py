@@ -62,7 +62,7 @@ def test_server_endpoints(tmp_path, free_port, num_tokenizer):
                 if line.startswith(b"data: ") and line != b"data: [DONE]":
                     chunks.append(json.loads(line[6:]))
         assert chunks[0]["choices"][0]["delta"]["role"] == "assistant"
-        assert chunks[-1]["choices"][0]["finish_reason"] == "stop"
+        assert chunks[-1]["choices"][0]["finish_reason"] == "length"  # ended by max_tokens
         assert "".join(c["choices"][0]["delta"].get("content", "") for c in chunks) == text
         r = requests.post(f"{base}/v1/completions", json={"model": "m", "prompt": "abc", "max_tokens": 4,
                                                           "temperature": 0.0, "ignore_eos": True}, timeout=60).json()
@@ -203,12 +203,14 @@ def test_stop_strings(tmp_path, free_port):
         _wait_ready(port, proc)
         url = f"http://127.0.0.1:{port}/v1/completions"
         body = {"model": "m", "prompt": "hello world", "max_tokens": 12, "temperature": 0.0, "ignore_eos": True}
-        full = requests.post(url, json=body, timeout=60).json()["choices"][0]["text"]
+        r0 = requests.post(url, json=body, timeout=60).json()["choices"][0]
+        full = r0["text"]
+        assert r0["finish_reason"] == "length"  # max_tokens reached (EOS ignored)
         assert len(full) >= 6, full
         stop = full[3:6]
         want = full[: full.find(stop)]
-        got = requests.post(url, json=dict(body, stop=stop), timeout=60).json()["choices"][0]["text"]
-        assert got == want
+        r1 = requests.post(url, json=dict(body, stop=stop), timeout=60).json()["choices"][0]
+        assert r1["text"] == want and r1["finish_reason"] == "stop"
         pieces = []
         with requests.post(url, json=dict(body, stop=[stop, "\u0000never"], stream=True), stream=True,
                            timeout=60) as s:
