@@ -227,3 +227,17 @@ def test_stop_strings(tmp_path, free_port):
             proc.wait(timeout=20)
         except subprocess.TimeoutExpired:
             os.killpg(proc.pid, signal.SIGKILL)
+
+
+def test_interactive_shell(tmp_path):
+    """``python -m minisgl.shell``: answers each line (the chat history is kept), handles /reset and
+    unknown commands, and /exit shuts the backend processes down."""
+    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
+    env = dict(os.environ, PYTHONPATH=ROOT, MINISGL_SHELL_MAX_TOKENS="4", MINISGL_SHELL_TEMPERATURE="0")
+    proc = subprocess.run(
+        [sys.executable, "-m", "minisgl.shell", "--model", path, "--device", "cpu", "--dtype", "float32"],
+        cwd=ROOT, env=env, input="hello\n/reset\n/foo\nhi again\n/exit\n", capture_output=True, text=True,
+        timeout=240)
+    out = proc.stdout + proc.stderr
+    assert proc.returncode == 0, out[-3000:]
+    assert "unknown command /foo" in out and "Exiting shell..." in out, out[-3000:]
