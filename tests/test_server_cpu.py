@@ -221,6 +221,10 @@ def test_stop_strings(tmp_path, free_port):
         # the server keeps serving after the early stops
         again = requests.post(url, json=body, timeout=60).json()["choices"][0]["text"]
         assert again == full
+        # seeded sampling is reproducible across requests (the noise is keyed by seed, step, token)
+        sb = dict(body, temperature=1.0, top_k=50, seed=7)
+        a, b = (requests.post(url, json=sb, timeout=60).json()["choices"][0]["text"] for _ in range(2))
+        assert a == b
     finally:
         os.killpg(proc.pid, signal.SIGTERM)
         try:
