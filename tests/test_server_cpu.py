@@ -245,3 +245,16 @@ def test_interactive_shell(tmp_path):
     out = proc.stdout + proc.stderr
     assert proc.returncode == 0, out[-3000:]
     assert "unknown command /foo" in out and "Exiting shell..." in out, out[-3000:]
+
+
+def test_online_benchmark_launcher(tmp_path, free_port):
+    """``python -m minisgl.benchmark.online`` starts the server, replays Poisson load and reports
+    latency statistics per rate, then stops the server."""
+    from minisgl.benchmark.online import main
+
+    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
+    rows = main(["--model", path, "--port", str(free_port), "--num-requests", "6", "--rates", "20,40",
+                 "--in-median", "30", "--out-median", "4", "--prefix-len", "20", "--startup-timeout", "180",
+                 "--", "--device", "cpu", "--dtype", "float32", "--max-running-requests", "8"])
+    assert [r["rate"] for r in rows] == [20.0, 40.0]
+    assert all(r["completed"] == 6 and r["ttft_p50"] > 0 for r in rows)
