@@ -126,3 +126,31 @@ def test_tp2_sampling_matches_tp1(tmp_path, free_port):
     got = json.loads(line[len("RESULT "):])
     for mode, a, b in zip(("temperature", "topk", "greedy+topk", "full"), got, ref):
         assert a == b, mode
+
+
+def test_tp4_replicates_kv_heads(tmp_path, free_port):
+    """Four ranks for a model with two KV heads: each rank keeps a replica of the KV head its
+    query heads use (the reference's rule when tp > kv heads) and the tokens equal TP1."""
+    from minisgl.llm import LLM
+
+    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
+    assert json.load(open(os.path.join(path, "config.json")))["num_key_value_heads"] < 4
+    prompts = _prompts()
+    llm = LLM(path, dtype=torch.float32, device="cpu", max_running_req=16, distributed_port=free_port,
+              max_extend_tokens=48)
+    try:
+        ref = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=12, ignore_eos=True))]
+    finally:
+        llm.shutdown()
+    script = tmp_path / "worker.py"
+    script.write_text(WORKER.format(root=ROOT, path=path))
+    procs = []
+    for r in range(4):
+        env = dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE="4", MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(free_port + 13), TP_PROMPTS=json.dumps(prompts), PYTHONPATH=ROOT)
+        procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    outs = [p.communicate(timeout=300)[0] for p in procs]
+    assert all(p.returncode == 0 for p in procs), outs
+    line = [l for l in outs[0].splitlines() if l.startswith("RESULT ")][0]
+    assert json.loads(line[len("RESULT "):]) == ref
