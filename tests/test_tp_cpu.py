@@ -128,12 +128,15 @@ def test_tp2_sampling_matches_tp1(tmp_path, free_port):
         assert a == b, mode
 
 
-def test_tp4_replicates_kv_heads(tmp_path, free_port):
-    """Four ranks for a model with two KV heads: each rank keeps a replica of the KV head its
-    query heads use (the reference's rule when tp > kv heads) and the tokens equal TP1."""
+@pytest.mark.parametrize("preset,moe_parallel", [("tiny-qwen3", "tp"), ("tiny-gpt-oss", "ep")])
+def test_tp4_replicates_kv_heads(tmp_path, free_port, preset, moe_parallel):
+    """Four ranks for models with two KV heads: each rank keeps a replica of the KV head its
+    query heads use (the reference's rule when tp > kv heads), with k/v biases and attention sinks
+    for gpt-oss and two whole experts per rank under expert parallelism; tokens equal TP1."""
     from minisgl.llm import LLM
 
-    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"))
+    fmt = "fused" if preset == "tiny-gpt-oss" else "per_expert"
+    path = make_checkpoint(preset, str(tmp_path / "m"), expert_format=fmt)
     assert json.load(open(os.path.join(path, "config.json")))["num_key_value_heads"] < 4
     prompts = _prompts()
     llm = LLM(path, dtype=torch.float32, device="cpu", max_running_req=16, distributed_port=free_port,
@@ -147,7 +150,8 @@ def test_tp4_replicates_kv_heads(tmp_path, free_port):
     procs = []
     for r in range(4):
         env = dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE="4", MASTER_ADDR="127.0.0.1",
-                   MASTER_PORT=str(free_port + 13), TP_PROMPTS=json.dumps(prompts), PYTHONPATH=ROOT)
+                   MASTER_PORT=str(free_port + 13), TP_PROMPTS=json.dumps(prompts), PYTHONPATH=ROOT,
+                   MINISGL_MOE_PARALLEL=moe_parallel)
         procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     outs = [p.communicate(timeout=300)[0] for p in procs]
