@@ -1,6 +1,9 @@
 """CPU oracle: the engine's reference path vs Hugging Face transformers on identical random
 weights (greedy tokens must match exactly), for each supported dense/MoE family."""
 
+import json
+import os
+
 import pytest
 import torch
 
@@ -125,3 +128,43 @@ def test_gpt_oss_mxfp4_checkpoint_loads_like_dequantized(tmp_path, tp):
             assert loaded[f].keys() == ref.keys(), f
             for k in ref:
                 assert torch.equal(loaded[f][k], ref[k]), (f, k, rank)
+
+
+def test_mistral3_layout_loads_like_the_text_model(tmp_path, free_port):
+    """A Mistral3 (vision-language) checkpoint: the text model's config nested under
+    ``text_config``, its weights under ``language_model.``, plus vision weights that are skipped.
+    It must load and generate exactly like the same weights in the plain text-model layout."""
+    import shutil
+
+    import safetensors.torch as st
+
+    from minisgl.llm import LLM
+
+    src = make_checkpoint("tiny-llama", str(tmp_path / "llama"))
+    dst = tmp_path / "mistral3"
+    shutil.copytree(src, dst)
+    cfg = json.load(open(os.path.join(src, "config.json")))
+    text = {k: v for k, v in cfg.items() if k not in ("architectures", "rope_scaling")}
+    text["model_type"] = "mistral"
+    json.dump({"architectures": ["Mistral3ForConditionalGeneration"], "model_type": "mistral3",
+               "text_config": text, "torch_dtype": cfg.get("torch_dtype", "float32")},
+              open(dst / "config.json", "w"))
+    plain = dict(cfg, architectures=["MistralForCausalLM"], model_type="mistral")
+    plain.pop("rope_scaling", None)
+    json.dump(plain, open(os.path.join(src, "config.json"), "w"))
+    for f in os.listdir(dst):
+        if f.endswith(".safetensors"):
+            tensors = st.load_file(str(dst / f))
+            out = {f"language_model.{k}": v for k, v in tensors.items()}
+            out["vision_tower.patch_conv.weight"] = torch.zeros(4, 3, 2, 2)
+            out["multi_modal_projector.linear_1.weight"] = torch.zeros(4, 4)
+            st.save_file(out, str(dst / f))
+    prompts = [[1, 2, 3, 4, 5], [9, 8, 7]]
+    outs = []
+    for i, p in enumerate((src, str(dst))):
+        llm = LLM(p, dtype=torch.float32, device="cpu", max_running_req=4, distributed_port=free_port + 3 * i)
+        try:
+            outs.append([o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=6, ignore_eos=True))])
+        finally:
+            llm.shutdown()
+    assert outs[0] == outs[1]
