@@ -21,6 +21,10 @@ if TYPE_CHECKING:
     from minisgl.moe import BaseMoeBackend
 
 
+# max_tokens of a request without a limit of its own: the scheduler clamps it to the context left
+UNBOUNDED_MAX_TOKENS = 1 << 30
+
+
 @dataclass
 class SamplingParams:
     temperature: float = 0.0

@@ -16,7 +16,7 @@ from typing import List, NamedTuple, Set, Tuple
 
 import torch
 
-from minisgl.core import Batch, Req
+from minisgl.core import UNBOUNDED_MAX_TOKENS, Batch, Req
 from minisgl.env import ENV
 from minisgl.message import (
     AbortBackendMsg,
@@ -170,8 +170,9 @@ class Scheduler(SchedulerIOMixin):
                 self.send_result([DetokenizeMsg(uid=msg.uid, next_token=0, finished=True, eos=True)])
                 return
             if msg.sampling_params.max_tokens > cap - n:
+                if msg.sampling_params.max_tokens < UNBOUNDED_MAX_TOKENS:
+                    logger.warning_rank0(f"request {msg.uid}: max_tokens clamped to {cap - n}")
                 msg.sampling_params.max_tokens = cap - n
-                logger.warning_rank0(f"request {msg.uid}: max_tokens clamped to {cap - n}")
             self.prefill_manager.add_one_req(msg)
         elif isinstance(msg, AbortBackendMsg):
             req = self.prefill_manager.abort_req(msg.uid) or self.decode_manager.abort_req(msg.uid)

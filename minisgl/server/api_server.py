@@ -21,7 +21,7 @@ from fastapi import FastAPI, Request
 from fastapi.responses import StreamingResponse
 from pydantic import BaseModel, Field
 
-from minisgl.core import SamplingParams
+from minisgl.core import UNBOUNDED_MAX_TOKENS, SamplingParams
 from minisgl.env import ENV
 from minisgl.message import AbortMsg, BaseFrontendMsg, BaseTokenizerMsg, BatchFrontendMsg, TokenizeMsg, UserReply
 from minisgl.utils import init_logger
@@ -47,7 +47,7 @@ class OpenAICompletionRequest(BaseModel):
     model: str = ""
     prompt: str | None = None
     messages: List[Message] | None = None
-    max_tokens: int = 16
+    max_tokens: int | None = 16  # null: up to the context limit
     temperature: float = 1.0
     top_k: int = -1
     top_p: float = 1.0
@@ -63,8 +63,10 @@ class OpenAICompletionRequest(BaseModel):
         return [self.stop] if isinstance(self.stop, str) else list(self.stop or [])
 
     def sampling(self) -> SamplingParams:
+        # the scheduler clamps max_tokens to what the context leaves after the prompt
+        max_tokens = UNBOUNDED_MAX_TOKENS if self.max_tokens is None else self.max_tokens
         return SamplingParams(temperature=self.temperature, top_k=self.top_k, top_p=self.top_p,
-                              ignore_eos=self.ignore_eos, max_tokens=self.max_tokens, seed=self.seed)
+                              ignore_eos=self.ignore_eos, max_tokens=max_tokens, seed=self.seed)
 
 
 class StopMatcher:

@@ -211,6 +211,9 @@ def test_stop_strings(tmp_path, free_port):
         want = full[: full.find(stop)]
         r1 = requests.post(url, json=dict(body, stop=stop), timeout=60).json()["choices"][0]
         assert r1["text"] == want and r1["finish_reason"] == "stop"
+        # max_tokens null means "up to the context limit"; the stop string ends it here
+        r2 = requests.post(url, json=dict(body, stop=stop, max_tokens=None), timeout=60).json()["choices"][0]
+        assert r2["text"] == want
         pieces = []
         with requests.post(url, json=dict(body, stop=[stop, "\u0000never"], stream=True), stream=True,
                            timeout=60) as s:
