@@ -272,29 +272,43 @@ async def _completion(req: OpenAICompletionRequest, request: Request, chat: bool
         text = [m.model_dump() for m in req.messages]
     else:
         return {"error": "either 'messages' or 'prompt' is required"}
-    uid = st.new_user()
-    pend = st.pending[uid]
-    await st.send_one(TokenizeMsg(uid=uid, text=text, sampling_params=req.sampling()))
+    n_choices = max(1, req.n)
+    if req.stream and n_choices > 1:
+        return {"error": "stream with n > 1 is not supported"}
+    uids = [st.new_user() for _ in range(n_choices)]
+    pend = st.pending[uids[0]]
+    for i, u in enumerate(uids):
+        sp = req.sampling()
+        if sp.seed is not None:
+            sp.seed += i  # n choices from one seed: distinct, reproducible draws
+        await st.send_one(TokenizeMsg(uid=u, text=text, sampling_params=sp))
     if req.stream:
+        uid = uids[0]
         return StreamingResponse(st.guard(st.stream_chat(uid, req.model, chat, req.stop_list()), request, uid),
                                  media_type="text/event-stream")
-    content, n, reason = "", 0, "stop"
-    matcher = StopMatcher(req.stop_list())
-    async for r in st.replies(uid):
-        content += matcher.feed(r.incremental_output)
-        n += 1
-        if r.finished:
-            content += matcher.flush()
-            reason = r.finish_reason or "stop"
-        if matcher.done:
-            await st.abort_user(uid)
-            break
-    choice = ({"index": 0, "message": {"role": "assistant", "content": content}, "finish_reason": reason}
-              if chat else {"index": 0, "text": content, "finish_reason": reason})
-    return {"id": f"{'chat' if chat else ''}cmpl-{uid}", "object": "chat.completion" if chat else "text_completion",
-            "created": int(time.time()), "model": req.model, "choices": [choice],
-            "usage": {"prompt_tokens": pend.prompt_tokens, "completion_tokens": n,
-                      "total_tokens": pend.prompt_tokens + n}}
+
+    async def collect(uid: int, index: int):
+        content, n, reason = "", 0, "stop"
+        matcher = StopMatcher(req.stop_list())
+        async for r in st.replies(uid):
+            content += matcher.feed(r.incremental_output)
+            n += 1
+            if r.finished:
+                content += matcher.flush()
+                reason = r.finish_reason or "stop"
+            if matcher.done:
+                await st.abort_user(uid)
+                break
+        choice = ({"index": index, "message": {"role": "assistant", "content": content}, "finish_reason": reason}
+                  if chat else {"index": index, "text": content, "finish_reason": reason})
+        return choice, n
+
+    results = await asyncio.gather(*[collect(u, i) for i, u in enumerate(uids)])
+    n_out = sum(k for _, k in results)
+    return {"id": f"{'chat' if chat else ''}cmpl-{uids[0]}", "object": "chat.completion" if chat else "text_completion",
+            "created": int(time.time()), "model": req.model, "choices": [c for c, _ in results],
+            "usage": {"prompt_tokens": pend.prompt_tokens, "completion_tokens": n_out,
+                      "total_tokens": pend.prompt_tokens + n_out}}
 
 
 @app.post("/v1/chat/completions")

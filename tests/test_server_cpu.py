@@ -228,6 +228,12 @@ def test_stop_strings(tmp_path, free_port):
         sb = dict(body, temperature=1.0, top_k=50, seed=7)
         a, b = (requests.post(url, json=sb, timeout=60).json()["choices"][0]["text"] for _ in range(2))
         assert a == b
+        # n choices: choice i uses seed + i, so choice 0 repeats the single-choice draw
+        rn = requests.post(url, json=dict(sb, n=3), timeout=60).json()
+        assert [c["index"] for c in rn["choices"]] == [0, 1, 2] and rn["choices"][0]["text"] == a
+        assert rn["usage"]["completion_tokens"] == 3 * 12
+        one = requests.post(url, json=dict(sb, seed=8), timeout=60).json()["choices"][0]["text"]
+        assert rn["choices"][1]["text"] == one
     finally:
         os.killpg(proc.pid, signal.SIGTERM)
         try:
