@@ -130,6 +130,40 @@ for it, T in enumerate([1, 7, 128, 256, 129, 800, 3, 256, 1, 400, 2, 64]):
     torch.cuda.synchronize()
     torch.testing.assert_close(res.float(), exp_res.float(), atol=3e-2, rtol=2e-2)
     torch.testing.assert_close(out.float(), exp_out.float(), atol=3e-2, rtol=2e-2)
+# CUDA-graph replays: the per-CTA epochs keep advancing across replays of one captured sequence
+# (LL and reduce forms alternating); a different rank lags before each replay
+Ts = [4, 300, 8, 300]
+xs, res0, exp = [], [], []
+for i, T in enumerate(Ts):
+    gp = torch.Generator(device="cpu").manual_seed(1000 + 10 * i + rank)
+    xs.append(torch.randn(T, H, generator=gp).to(dev, torch.bfloat16))
+    gr = torch.Generator(device="cpu").manual_seed(2000 + i)
+    res0.append(torch.randn(T, H, generator=gr).to(dev, torch.bfloat16))
+    parts = [torch.empty_like(xs[i]) for _ in range(world)]
+    dist.all_gather(parts, xs[i])
+    r32 = (torch.stack([p.float() for p in parts]).sum(0) + res0[i].float()).to(torch.bfloat16).float()
+    exp.append((r32 * torch.rsqrt(r32.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(torch.bfloat16))
+res = [r.clone() for r in res0]
+outs = [None] * len(Ts)
+side = torch.cuda.Stream()
+with torch.cuda.stream(side):
+    for i in range(len(Ts)):
+        res[i].copy_(res0[i])
+        impl.all_reduce_add_rmsnorm(xs[i], res[i], w, eps)
+torch.cuda.synchronize()
+graph = torch.cuda.CUDAGraph()
+with torch.cuda.graph(graph, stream=side):
+    for i in range(len(Ts)):
+        res[i].copy_(res0[i])
+        outs[i], _ = impl.all_reduce_add_rmsnorm(xs[i], res[i], w, eps)
+for rep in range(6):
+    if rank == rep % world:
+        torch.cuda._sleep(3_000_000)
+    graph.replay()
+    torch.cuda.synchronize()
+    for i in range(len(Ts)):
+        torch.testing.assert_close(outs[i].float(), exp[i].float(), atol=3e-2, rtol=2e-2)
+del graph
 assert cuda().get_error()[0] == 0
 dist.barrier(group=cpu)
 impl.close()
