@@ -58,6 +58,7 @@ class OpenAICompletionRequest(BaseModel):
     frequency_penalty: float = 0.0
     ignore_eos: bool = False
     seed: int | None = None
+    stream_options: Dict[str, bool] | None = None  # {"include_usage": true}: a final usage chunk
 
     def stop_list(self) -> List[str]:
         return [self.stop] if isinstance(self.stop, str) else list(self.stop or [])
@@ -193,8 +194,11 @@ class FrontendManager:
             yield f"data: {r.incremental_output}\n".encode()
         yield b"data: [DONE]\n"
 
-    async def stream_chat(self, uid: int, model: str, chat: bool, stop: List[str] = ()) -> AsyncIterator[bytes]:
+    async def stream_chat(self, uid: int, model: str, chat: bool, stop: List[str] = (),
+                          include_usage: bool = False) -> AsyncIterator[bytes]:
         first = True
+        pend = self.pending.get(uid)
+        n_out = 0
         obj = "chat.completion.chunk" if chat else "text_completion"
         matcher = StopMatcher(list(stop))
 
@@ -210,6 +214,7 @@ class FrontendManager:
 
         reason = "stop"
         async for r in self.replies(uid):
+            n_out += 1
             text = matcher.feed(r.incremental_output)
             if r.finished:
                 text += matcher.flush()
@@ -221,6 +226,10 @@ class FrontendManager:
                 break
         end = {"delta": {}, "index": 0, "finish_reason": reason} if chat else {"text": "", "index": 0, "finish_reason": reason}
         yield f"data: {json.dumps({'id': f'cmpl-{uid}', 'object': obj, 'model': model, 'choices': [end]})}\n\n".encode()
+        if include_usage:  # OpenAI stream_options.include_usage: one last chunk with no choices
+            p_tok = pend.prompt_tokens if pend is not None else 0
+            usage = {"prompt_tokens": p_tok, "completion_tokens": n_out, "total_tokens": p_tok + n_out}
+            yield f"data: {json.dumps({'id': f'cmpl-{uid}', 'object': obj, 'model': model, 'choices': [], 'usage': usage})}\n\n".encode()
         yield b"data: [DONE]\n\n"
 
     def shutdown(self) -> None:
@@ -284,7 +293,8 @@ async def _completion(req: OpenAICompletionRequest, request: Request, chat: bool
         await st.send_one(TokenizeMsg(uid=u, text=text, sampling_params=sp))
     if req.stream:
         uid = uids[0]
-        return StreamingResponse(st.guard(st.stream_chat(uid, req.model, chat, req.stop_list()), request, uid),
+        usage = bool((req.stream_options or {}).get("include_usage"))
+        return StreamingResponse(st.guard(st.stream_chat(uid, req.model, chat, req.stop_list(), usage), request, uid),
                                  media_type="text/event-stream")
 
     async def collect(uid: int, index: int):

@@ -221,6 +221,15 @@ def test_stop_strings(tmp_path, free_port):
                 if line.startswith(b"data: ") and line != b"data: [DONE]":
                     pieces.append(json.loads(line[6:])["choices"][0]["text"])
         assert "".join(pieces) == want
+        # stream_options.include_usage: a last chunk with the usage and no choices
+        last = None
+        with requests.post(url, json=dict(body, stream=True, stream_options={"include_usage": True}), stream=True,
+                           timeout=60) as s:
+            for line in s.iter_lines():
+                if line.startswith(b"data: ") and line != b"data: [DONE]":
+                    last = json.loads(line[6:])
+        assert last["choices"] == [] and last["usage"]["completion_tokens"] == 12
+        assert last["usage"]["prompt_tokens"] > 1
         # the server keeps serving after the early stops
         again = requests.post(url, json=body, timeout=60).json()["choices"][0]["text"]
         assert again == full
