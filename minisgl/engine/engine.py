@@ -66,6 +66,11 @@ class Engine:
             # python/minisgl/engine/engine.py, _adjust_config).
             logger.warning_rank0(f"page size {config.page_size} overridden to 64 (CUDA decode needs 16, 32 or 64)")
             object.__setattr__(config, "page_size", 64)
+        if self.is_cuda and config.dtype == torch.float16:
+            # the sm_100a kernels are written for bf16 activations and weights (same width, wider
+            # range); float16 requests, including "auto" on float16/float32 checkpoints, run in bf16
+            logger.warning_rank0("dtype float16 served as bfloat16 on CUDA")
+            object.__setattr__(config, "dtype", torch.bfloat16)
         torch.manual_seed(config.seed)
         if self.is_cuda:
             torch.cuda.set_device(self.device)
