@@ -63,14 +63,17 @@ class RequestResult:
 
 
 def generate_prompt(tokenizer, n_tokens: int, rng: random.Random) -> str:
-    """A text that encodes to ``n_tokens`` tokens (no special tokens)."""
+    """A text that encodes to ``n_tokens`` tokens (no special tokens): random words, encoded once
+    per batch of words (not once per word), cut to ``n_tokens`` ids and decoded."""
     words: List[str] = []
-    while True:
-        words.append("".join(rng.choice("abcdefghijklmnopqrstuvwxyz") for _ in range(rng.randint(2, 8))))
-        if len(tokenizer.encode(" ".join(words), add_special_tokens=False)) >= n_tokens:
-            break
-    ids = tokenizer.encode(" ".join(words), add_special_tokens=False)[:n_tokens]
-    return tokenizer.decode(ids)
+    ids: List[int] = []
+    want = max(1, n_tokens)
+    while len(ids) < n_tokens:
+        words += ["".join(rng.choice("abcdefghijklmnopqrstuvwxyz") for _ in range(rng.randint(2, 8)))
+                  for _ in range(want)]
+        ids = tokenizer.encode(" ".join(words), add_special_tokens=False)
+        want = max(8, n_tokens - len(ids))
+    return tokenizer.decode(ids[:n_tokens])
 
 
 def synthetic_trace(tokenizer, n: int, rate: float, *, in_median: float = 1200, in_sigma: float = 1.0,
