@@ -143,7 +143,7 @@ class Scheduler(SchedulerIOMixin):
                 stop_eos = tok == eos and not req.sampling_params.ignore_eos
                 finished = stop_eos or req.host_len >= req.max_device_len
                 reply.append(DetokenizeMsg(uid=req.uid, next_token=tok, finished=finished, eos=stop_eos))
-                if finished and req not in self.finished_reqs:
+                if finished:
                     self.decode_manager.remove_req(req)
                     self._free_req_resources(req)
                     newly_finished.add(req)
