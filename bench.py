@@ -112,8 +112,13 @@ def run(args, impl: str):
             print(json.dumps({"impl": "reference", "unavailable":
                               "the reference's offline LLM API is single-GPU only (tp_info fixed to (0, 1))"}))
             return
+        ref_root = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref_root, "minisgl")):
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference is not installed in baseline/_ref (pip install --target baseline/_ref)"}))
+            return
         sys.path[:] = [p for p in sys.path if os.path.abspath(p or ".") != ROOT]
-        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        sys.path.insert(0, ref_root)
         for m in [m for m in sys.modules if m == "minisgl" or m.startswith("minisgl.")]:
             del sys.modules[m]
         os.chdir(tempfile.gettempdir())
