@@ -35,9 +35,22 @@ from .base import BaseLLMModel
 from .config import ModelConfig
 
 
+def padded_intermediate(inter: int, tp: int) -> int:
+    """Intermediate size with each rank's share rounded up to a whole gate/up interleave block.
+    The loader fills the extra gate/up rows and down_proj columns with zeros, which contribute
+    nothing (act(0) * 0 = 0), so models whose share is not a multiple of the block still load."""
+    from minisgl.ops.reference import GATE_UP_BLOCK
+    from minisgl.utils import div_even
+
+    local = div_even(inter, tp)
+    return -(-local // GATE_UP_BLOCK) * GATE_UP_BLOCK * tp
+
+
 class GatedMLP(BaseOP):
     def __init__(self, config: ModelConfig, intermediate_size: int | None = None):
-        inter = intermediate_size or config.intermediate_size
+        from minisgl.parallel import get_tp_info
+
+        inter = padded_intermediate(intermediate_size or config.intermediate_size, get_tp_info().size)
         self.gate_up_proj = LinearColParallelMerged(config.hidden_size, [inter, inter], has_bias=False)
         if config.hidden_act not in ("silu", "gelu", "gelu_pytorch_tanh"):
             raise ValueError(f"unsupported activation {config.hidden_act}")

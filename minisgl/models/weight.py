@@ -27,7 +27,7 @@ from typing import Dict, Iterator, Tuple
 
 import torch
 
-from minisgl.ops.reference import interleave_gate_up
+from minisgl.ops.reference import GATE_UP_BLOCK, interleave_gate_up
 from minisgl.parallel import get_tp_info
 from minisgl.utils import div_ceil
 
@@ -131,11 +131,23 @@ def _merge_slot(key: str):
     return None
 
 
+def _pad_to_block(t: torch.Tensor, dim: int) -> torch.Tensor:
+    """Zero-pad a dense MLP shard along ``dim`` to a whole number of gate/up interleave blocks
+    (the layer sizes come from ``padded_intermediate``)."""
+    n = t.shape[dim]
+    pad = -n % GATE_UP_BLOCK
+    if pad == 0:
+        return t
+    shape = list(t.shape)
+    shape[dim] = pad
+    return torch.cat([t, t.new_zeros(shape)], dim=dim)
+
+
 def _finish_merge(key: str, parts: Dict[str, torch.Tensor]) -> torch.Tensor:
     if "gate_up_proj" in key and ".experts." in key:  # experts keep [gate; up] halves
         return torch.cat([parts["gate"], parts["up"]], dim=0)
     if "gate_up_proj" in key:
-        g, u = parts["gate"], parts["up"]
+        g, u = _pad_to_block(parts["gate"], 0), _pad_to_block(parts["up"], 0)
         if g.dim() == 1:  # bias
             return interleave_gate_up(g[:, None], u[:, None])[:, 0]
         return interleave_gate_up(g, u)
@@ -203,6 +215,8 @@ def load_weight(model_path: str, device: torch.device, config=None) -> Iterator[
                     t = raw
                 else:
                     t = shard_tensor(key, raw, info.rank, info.size, config.num_kv_heads, config.head_dim)
+                    if key.endswith(".down_proj.weight") and ".experts." not in key:
+                        t = _pad_to_block(t, t.dim() - 1)  # dense MLP: match the padded gate/up rows
                 del raw
                 mi = _merge_slot(key)
                 if mi is not None:

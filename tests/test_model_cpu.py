@@ -39,7 +39,8 @@ def _hf_greedy(path, prompts, n_new):
     return outs
 
 
-@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-llama", "tiny-qwen2", "tiny-qwen3-moe", "tiny-gpt-oss"])
+@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-llama", "tiny-qwen2", "tiny-qwen3-moe", "tiny-gpt-oss",
+                                    "tiny-qwen3-odd"])
 def test_greedy_matches_hf(tmp_path, preset, free_port):
     """gpt-oss: checkpoint in its own fused-expert layout (what transformers loads); covers biased
     attention with sinks, alternating sliding-window layers, YaRN RoPE, top-k-then-softmax routing

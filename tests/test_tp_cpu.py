@@ -37,7 +37,7 @@ def _prompts():
             for _ in range(6)]
 
 
-@pytest.mark.parametrize("preset,moe_parallel", [("tiny-qwen3", "tp"), ("tiny-qwen3-moe", "tp"),
+@pytest.mark.parametrize("preset,moe_parallel", [("tiny-qwen3", "tp"), ("tiny-qwen3-odd", "tp"), ("tiny-qwen3-moe", "tp"),
                                                   ("tiny-qwen3-moe", "ep"), ("tiny-gpt-oss", "tp"),
                                                   ("tiny-gpt-oss", "ep")])
 def test_tp2_matches_tp1(tmp_path, preset, moe_parallel, free_port):
