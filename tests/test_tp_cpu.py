@@ -128,7 +128,7 @@ def test_tp2_sampling_matches_tp1(tmp_path, free_port):
         assert a == b, mode
 
 
-@pytest.mark.parametrize("preset,moe_parallel", [("tiny-qwen3", "tp"), ("tiny-gpt-oss", "ep")])
+@pytest.mark.parametrize("preset,moe_parallel", [("tiny-qwen3", "tp"), ("tiny-qwen2", "tp"), ("tiny-gpt-oss", "ep")])
 def test_tp4_replicates_kv_heads(tmp_path, free_port, preset, moe_parallel):
     """Four ranks for models with two KV heads: each rank keeps a replica of the KV head its
     query heads use (the reference's rule when tp > kv heads), with k/v biases and attention sinks
