@@ -20,11 +20,12 @@ PRESETS: Dict[str, dict] = {
         num_attention_heads=4, num_key_value_heads=2, head_dim=64, intermediate_size=512,
         vocab_size=1024, rope_theta=1e6, tie_word_embeddings=True, max_position_embeddings=4096,
     ),
-    # an intermediate size whose per-rank share is not a whole gate/up interleave block
+    # an intermediate size whose per-rank share is not a whole gate/up interleave block, and a
+    # vocabulary that does not split evenly over ranks
     "tiny-qwen3-odd": dict(
         architectures=["Qwen3ForCausalLM"], model_type="qwen3", num_hidden_layers=2, hidden_size=256,
         num_attention_heads=4, num_key_value_heads=2, head_dim=64, intermediate_size=320,
-        vocab_size=1024, rope_theta=1e6, tie_word_embeddings=True, max_position_embeddings=4096,
+        vocab_size=1001, rope_theta=1e6, tie_word_embeddings=True, max_position_embeddings=4096,
     ),
     "tiny-llama": dict(
         architectures=["LlamaForCausalLM"], model_type="llama", num_hidden_layers=2, hidden_size=256,

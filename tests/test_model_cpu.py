@@ -11,7 +11,7 @@ from minisgl.core import SamplingParams
 from minisgl.models.synthetic import make_checkpoint
 
 
-def _prompts(n=8, vocab=1024, seed=0, shared_prefix=16):
+def _prompts(n=8, vocab=1000, seed=0, shared_prefix=16):
     g = torch.Generator().manual_seed(seed)
     prefix = torch.randint(0, vocab, (shared_prefix,), generator=g).tolist()
     out = []

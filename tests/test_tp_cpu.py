@@ -33,7 +33,7 @@ llm.shutdown()
 
 def _prompts():
     g = torch.Generator().manual_seed(3)
-    return [torch.randint(0, 1024, (int(torch.randint(8, 40, (1,), generator=g)),), generator=g).tolist()
+    return [torch.randint(0, 1000, (int(torch.randint(8, 40, (1,), generator=g)),), generator=g).tolist()
             for _ in range(6)]
 
 
