@@ -20,7 +20,7 @@ import torch.distributed as dist
 
 from minisgl.attention import create_attention_backend
 from minisgl.attention.paged import PAGED_DECODE_PAGES
-from minisgl.core import Batch, Context, Req, SamplingParams, get_global_ctx, reset_global_ctx, set_global_ctx
+from minisgl.core import Batch, Context, Req, SamplingParams, reset_global_ctx, set_global_ctx
 from minisgl.env import ENV
 from minisgl.kvcache import create_kvcache_pool
 from minisgl.layers import set_rope_device
