@@ -6,7 +6,9 @@ Workload: 256 requests, prompt lengths U[100, 1024] with uniform random token id
 U[100, 1024], greedy, EOS ignored. One *step* = one ``generate`` over the whole workload.
 
 ``python bench.py --gpus N --steps K --warmup W [--impl ours|reference] [--model qwen3-14b]``
-For N > 1 run under ``torchrun --nproc-per-node N``; rank 0 prints one JSON line.
+For N > 1 run under ``torchrun --nproc-per-node N``; rank 0 prints one JSON line. The reference arm
+(``--impl reference``) runs the unmodified reference installed in ``baseline/_ref``: its ``LLM`` at
+N = 1 and, per torchrun rank, its own offline-mode ``Scheduler`` at N > 1.
 """
 
 from __future__ import annotations
@@ -108,10 +110,6 @@ def run(args, impl: str):
     total_out = sum(outs)
 
     if impl == "reference":
-        if world > 1:
-            print(json.dumps({"impl": "reference", "unavailable":
-                              "the reference's offline LLM API is single-GPU only (tp_info fixed to (0, 1))"}))
-            return
         ref_root = os.path.join(ROOT, "baseline", "_ref")
         if not os.path.isdir(os.path.join(ref_root, "minisgl")):
             print(json.dumps({"impl": "reference", "unavailable":
@@ -126,13 +124,36 @@ def run(args, impl: str):
         from minisgl.llm import LLM
 
         assert "baseline" in (getattr(sys.modules["minisgl.llm"], "__file__", "") or ""), "reference not isolated"
-        llm = LLM(path, dtype=torch.bfloat16, use_dummy_weight=True, **CONFIG)
+        if world == 1:
+            llm = LLM(path, dtype=torch.bfloat16, use_dummy_weight=True, **CONFIG)
+        else:
+            # The reference's LLM constructor fixes tp_info to (0, 1) (python/minisgl/llm/llm.py:
+            # 29-36); everything else about offline mode works per rank (its scheduler I/O picks the
+            # offline receive/send methods for every rank, python/minisgl/scheduler/io.py:30-33).
+            # So each torchrun rank builds the reference's own Scheduler with its rank's tp_info and
+            # runs the stock LLM.generate loop; the engine, pynccl, cuBLAS and FlashInfer paths are
+            # the reference's, unmodified.
+            from minisgl.distributed import DistributedInfo
+            from minisgl.scheduler import Scheduler, SchedulerConfig
+
+            # the reference's engine rendezvouses on its own tcp://127.0.0.1:2333 store, hosted by
+            # rank 0; under torchrun that variable would make every rank a client of the agent's
+            # store instead, and nobody would host 2333
+            os.environ.pop("TORCHELASTIC_USE_AGENT_STORE", None)
+
+            class RankLLM(LLM):
+                def __init__(self, model_path, dtype, **kwargs):
+                    Scheduler.__init__(self, SchedulerConfig(model_path=model_path, dtype=dtype, offline_mode=True,
+                                                             tp_info=DistributedInfo(rank, world), **kwargs))
+                    self.pending_requests, self.status_map, self.counter = [], {}, 0  # its LLM.__init__ state
+
+            llm = RankLLM(path, torch.bfloat16, use_dummy_weight=True, **CONFIG)
         with torch.no_grad():  # the reference's dummy init is N(0, 1); rescale to N(0, 0.02)
             for k, v in llm.engine.model.state_dict().items():
                 if v.is_floating_point() and "norm" not in k:
                     v.mul_(0.02)
         dev = torch.device(f"cuda:{local}")
-        cpu_group = None
+        cpu_group = llm.tp_cpu_group if world > 1 else None
     else:
         sys.path.insert(0, ROOT)
         from minisgl.core import SamplingParams
@@ -179,8 +200,7 @@ def run(args, impl: str):
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=cpu_group)
         dev_ms, wall_ms = float(t[0]), float(t[1])
     if rank != 0:
-        if impl != "reference":
-            llm.shutdown()
+        close(llm, impl, world)
         return
     line = {
         "metric": "offline output tok/s Qwen3-14B @TP1/2/4/8 B200" if args.model == "qwen3-14b"
@@ -213,7 +233,15 @@ def run(args, impl: str):
         line["e2e"] = {"value": round(total_out / (wall_ms / 1000), 2), "unit": "tok/s",
                        "h2d_bytes_per_step": None, "d2h_bytes_per_step": None}
     print(json.dumps(line), flush=True)
-    llm.shutdown() if impl != "reference" else None
+    close(llm, impl, world)
+
+
+def close(llm, impl: str, world: int) -> None:
+    if impl != "reference":
+        llm.shutdown()
+    elif world > 1:
+        # CUDA graphs that hold NCCL calls go before the process group (the reference's own order)
+        llm.engine.shutdown()
 
 
 def main():

@@ -68,10 +68,6 @@ def ninja_file() -> str:
     cuda = _cuda_home()
     pyinc = _py_includes()
     tinc, tlib = _torch_paths()
-    cutlass = os.path.join(
-        os.path.dirname(os.path.dirname(os.path.abspath(__import__("pybind11").__file__))),
-        "flashinfer", "data", "cutlass", "include",
-    )
     inc = " ".join(f"-I{p}" for p in [CSRC] + pyinc)
     tinc_s = " ".join(f"-isystem {p}" for p in tinc)
     lines = [

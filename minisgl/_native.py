@@ -26,7 +26,8 @@ class _CountingModule:
     """Forwards attribute access to the extension and counts kernel-launching calls."""
 
     _NON_LAUNCH = {"get_error", "num_sms", "gemm_splits", "peer_flag_bytes", "peer_alloc", "peer_free",
-                   "ipc_handle", "ipc_open", "ipc_close", "peer_grid", "nvls_grid", "nvls_flag_bytes"}
+                   "ipc_handle", "ipc_open", "ipc_close", "peer_grid", "nvls_grid", "nvls_flag_bytes",
+                   "nvls_state_words", "nvls_ticket_offset"}
 
     def __init__(self, mod):
         self._mod = mod

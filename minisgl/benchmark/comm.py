@@ -6,13 +6,20 @@ For each token count it times, on decode-sized activations [T, hidden] bf16:
 
 * ``nvls``  - the fused NVLS all-reduce + residual add + RMSNorm kernel (one launch);
 * ``peer``  - the IPC peer-memory all-reduce followed by the fused add + RMSNorm kernel;
-* ``nccl``  - NCCL all-reduce (torch.distributed) followed by the same norm kernel (the baseline).
+* ``nccl``  - NCCL all-reduce (torch.distributed) followed by the same norm kernel (the baseline);
+* ``gemm_nvls`` - the row-parallel GEMM ``[T, K] x [hidden, K]^T`` (``--k``, default the Qwen3-14B
+  o_proj shard 5120 / N) fused with the collective: the GEMM writes the NVLS staging region and
+  signals arrival, then reduce-scatter + residual + RMSNorm + all-gather (the engine's decode path);
+* ``gemm_nccl`` - the same GEMM, then NCCL all-reduce and the norm kernel (the reference's shape of
+  the step: cuBLAS GEMM, NCCL all-reduce, fused_add_rmsnorm).
 
 Each variant runs 20 times inside one CUDA graph, replayed 10 times; the CUDA-event time per call
-is the MAX over ranks. The roofline is the slower of the bytes each GPU must send over NVLink
-(its T x hidden x 2 partial) at the measured 770 GB/s per direction and the norm's HBM traffic at
-the measured copy bandwidth; rank 0 prints one JSON line per token count with each variant's time
-and its fraction of that roofline.
+is the MAX over ranks. Rooflines: for the collective alone, the slower of the bytes each GPU must
+move over NVLink (reduce-scatter in + all-gather out: 2 x T x hidden x 2 x (N-1)/N) at the measured
+770 GB/s per direction and the norm's HBM traffic at the measured copy bandwidth; for the GEMM
+variants, the slower of that and the GEMM's own bound (FLOPs at the measured bf16 peak, weight bytes
+at HBM bandwidth). Rank 0 prints one JSON line per token count with each variant's time and its
+fraction of its roofline.
 """
 
 from __future__ import annotations
@@ -28,13 +35,15 @@ import torch.distributed as dist
 NVLINK_BPS = 770e9  # measured peer copy, per direction per GPU
 
 
-def _hbm_bps() -> float:
+def _peaks() -> tuple:
+    """(HBM bytes/s, bf16 FLOP/s burst) measured on this pool, or the fallback figures."""
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     try:
         with open(os.path.join(root, "MEASURED_PEAKS.json")) as f:
-            return float(json.load(f)["hbm_gbs"]) * 1e9
+            d = json.load(f)
+        return float(d["hbm_gbs"]) * 1e9, float(d["bf16_tflops"]) * 1e12
     except (OSError, KeyError, ValueError):
-        return 6.65e12
+        return 6.65e12, 1.59e15
 
 
 def _time(fn, stream, calls: int = 20, reps: int = 10) -> float:
@@ -65,6 +74,7 @@ def main(argv=None) -> None:
     ap = argparse.ArgumentParser("minisgl.benchmark.comm")
     ap.add_argument("--hidden", type=int, default=5120)
     ap.add_argument("--tokens", default="1,8,16,64,128,256,512")
+    ap.add_argument("--k", type=int, default=0, help="GEMM input features per rank (0: 5120 / N)")
     a = ap.parse_args(argv)
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -90,7 +100,9 @@ def main(argv=None) -> None:
             print(json.dumps({"nvls": f"unavailable: {e}"}), flush=True)
     s = torch.cuda.Stream()
     w = (torch.rand(H, device=dev) + 0.5).to(torch.bfloat16)
-    hbm = _hbm_bps()
+    hbm, flops = _peaks()
+    K = a.k or 5120 // world
+    wt = (torch.randn(H, K, device=dev) * 0.02).to(torch.bfloat16)
     for T in tokens:
         x = torch.randn(T, H, device=dev, dtype=torch.bfloat16)
         res = torch.randn(T, H, device=dev, dtype=torch.bfloat16)
@@ -110,16 +122,35 @@ def main(argv=None) -> None:
 
         times["peer"] = _time(unfused(peer), s)
         times["nccl"] = _time(unfused(nccl), s)
+        xin = (torch.randn(T, K, device=dev) * 0.5).to(torch.bfloat16)
+        if nvls is not None:
+            def gemm_nvls():
+                y = nvls.linear_into_staging(xin, wt, None)
+                if y is None:  # LL-sized batch: plain GEMM, then the LL collective
+                    y = ops.linear(xin, wt)
+                nvls.all_reduce_add_rmsnorm(y, res, w, eps)
+
+            times["gemm_nvls"] = _time(gemm_nvls, s)
+
+        def gemm_nccl():
+            y = nccl.all_reduce(ops.linear(xin, wt))
+            ops.fused_add_rmsnorm(y, res, w, eps)
+
+        times["gemm_nccl"] = _time(gemm_nccl, s)
         t = torch.tensor([times[k] for k in sorted(times)], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=cpu)
         times = {k: float(v) for k, v in zip(sorted(times), t)}
         nbytes = T * H * 2
-        roof_ms = max(nbytes / NVLINK_BPS, 4 * nbytes / hbm) * 1e3  # norm: x, residual in/out, out
+        link = 2 * nbytes * (world - 1) / world  # reduce-scatter in + all-gather out, per GPU
+        roof_ms = max(link / NVLINK_BPS, 4 * nbytes / hbm) * 1e3  # norm: x, residual in/out, out
+        gemm_ms = max(2 * T * K * H / flops, K * H * 2 / hbm) * 1e3
         if rank == 0:
-            row = {"world": world, "tokens": T, "hidden": H, "roofline_us": round(roof_ms * 1e3, 2)}
+            row = {"world": world, "tokens": T, "hidden": H, "k": K, "roofline_us": round(roof_ms * 1e3, 2),
+                   "gemm_roofline_us": round(max(roof_ms, gemm_ms) * 1e3, 2)}
             for k, v in times.items():
+                r = max(roof_ms, gemm_ms) if k.startswith("gemm") else roof_ms
                 row[f"{k}_us"] = round(v * 1e3, 2)
-                row[f"{k}_frac"] = round(roof_ms / v, 3)
+                row[f"{k}_frac"] = round(r / v, 3)
             print(json.dumps(row), flush=True)
     torch.cuda.synchronize()
     dist.barrier(group=cpu)

@@ -66,7 +66,11 @@ def main(argv=None) -> list:
     from minisgl.utils.hf import load_tokenizer
 
     cmd = [sys.executable, "-m", "minisgl", "--model", a.model, "--tp", str(a.tp), "--port", str(a.port)] + extra
-    proc = subprocess.Popen(cmd, start_new_session=True)
+    from minisgl.utils.proc import die_with_parent
+
+    # its own process group (killed as a group below), and killed by the kernel if this launcher dies
+    # first (a timeout or a signal skips the finally clause)
+    proc = subprocess.Popen(cmd, start_new_session=True, preexec_fn=die_with_parent)
     rows = []
     try:
         wait_ready(a.port, proc, a.startup_timeout)

@@ -113,6 +113,27 @@ void gemm(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tensor> 
   gemm_ex(out, x, w, bias, epi, -1, -1);
 }
 
+// bf16 GEMM into this rank's NVLS staging region (out), signalling arrival on the multicast counter
+// at `arrive_mc` through the local ticket at `arrive_ticket` (fused row-parallel collective)
+void gemm_signal(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, int64_t arrive_ticket,
+                 int64_t arrive_mc) {
+  check_bf16(x, "x"); check_bf16(w, "w"); check_bf16(out, "out");
+  check_contig(x, "x"); check_contig(w, "w"); check_contig(out, "out");
+  CHECK(w.dim() == 2, "gemm_signal takes a row-major [N, K] weight");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  CHECK(w.size(1) == K, "gemm K mismatch: x ", x.sizes(), " w ", w.sizes());
+  CHECK(K % 8 == 0 && N % 8 == 0, "gemm needs K and N multiples of 8");
+  CHECK(out.size(0) == M && out.size(1) == N, "gemm out shape");
+  CHECK(arrive_ticket != 0 && arrive_mc != 0, "gemm_signal needs the arrival ticket and counter");
+  if (bias.has_value()) { check_bf16(*bias, "bias"); CHECK(bias->numel() == N, "bias size"); }
+  CHECK(M > 0, "gemm_signal needs at least one row (every rank must arrive)");
+  const int64_t wsb = msgl_gemm_workspace_bytes(M, N, K, 0);
+  at::Tensor& ws = gemm_workspace(x.device(), wsb);
+  msgl_gemm_ex3(out.data_ptr(), x.data_ptr(), w.data_ptr(), 0, opt_ptr(bias), M, N, K, out.stride(0), 0, -1, -1,
+                ws.data_ptr(), ws.numel(), reinterpret_cast<uint32_t*>(arrive_ticket),
+                reinterpret_cast<void*>(arrive_mc), stream());
+}
+
 void act_and_mul(at::Tensor out, at::Tensor x, int64_t act) {
   check_bf16(out, "out"); check_bf16(x, "x"); check_contig(out, "out"); check_contig(x, "x");
   const int inter = x.size(1) / 2;
@@ -393,18 +414,50 @@ void peer_collective(int64_t mode, at::Tensor out, at::Tensor in, std::vector<in
 // rank's and the multicast address of the same allocation).
 void nvls_allreduce_rmsnorm(int64_t uc, int64_t mc, int64_t rank, int64_t world, at::Tensor x, at::Tensor residual, at::Tensor w,
                             at::Tensor out, double eps, int64_t cap_bytes, at::Tensor state, int64_t timeout_ns,
-                            bool first) {
+                            bool first, int64_t mode) {
   check_bf16(x, "x"); check_bf16(residual, "residual"); check_bf16(w, "w"); check_bf16(out, "out");
   check_contig(x, "x"); check_contig(residual, "residual"); check_contig(out, "out"); check_contig(w, "w");
   check_cuda(state, "state"); check_dtype(state, at::kInt, "state");
-  CHECK(state.numel() >= 2 * msgl_nvls_grid(), "nvls state tensor too small");
+  CHECK(state.numel() >= msgl_nvls_state_words(), "nvls state tensor too small");
   const int64_t H = x.size(-1), T = x.numel() / H;
   CHECK(residual.numel() == x.numel() && out.numel() == x.numel() && w.numel() == H, "nvls norm shapes");
   const int rc = msgl_nvls_allreduce_rmsnorm(reinterpret_cast<void*>(uc), reinterpret_cast<void*>(mc), rank, world,
                                              x.data_ptr(), residual.data_ptr(), w.data_ptr(), out.data_ptr(), T, H,
                                              eps, cap_bytes, reinterpret_cast<uint32_t*>(state.data_ptr()),
-                                             timeout_ns, first ? 1 : 0, stream());
+                                             timeout_ns, first ? 1 : 0, (int)mode, stream());
   CHECK(rc == 0, "nvls all-reduce rejected its arguments (code ", rc, ")");
+}
+
+void plan_apply(at::Tensor page_table, at::Tensor pt_rows, at::Tensor pt_pos, at::Tensor pt_slots, at::Tensor tok_rows,
+                at::Tensor positions, at::Tensor out_loc) {
+  for (auto* t : {&page_table, &pt_rows, &pt_pos, &pt_slots, &tok_rows, &positions, &out_loc}) {
+    check_cuda(*t, "plan tensor"); check_dtype(*t, at::kInt, "plan tensor"); check_contig(*t, "plan tensor");
+  }
+  CHECK(page_table.dim() == 2, "page table must be 2-D");
+  CHECK(pt_rows.numel() == pt_pos.numel() && pt_rows.numel() == pt_slots.numel(), "page-table write lists");
+  CHECK(tok_rows.numel() == positions.numel() && out_loc.numel() == positions.numel(), "token lists");
+  msgl_plan_apply(page_table.data_ptr<int32_t>(), page_table.stride(0), page_table.size(0), pt_rows.data_ptr<int32_t>(),
+                  pt_pos.data_ptr<int32_t>(), pt_slots.data_ptr<int32_t>(), (int)pt_rows.numel(),
+                  tok_rows.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), (int)positions.numel(),
+                  out_loc.data_ptr<int32_t>(), stream());
+}
+
+void gather_i32(at::Tensor dst, at::Tensor src, at::Tensor idx) {
+  for (auto* t : {&dst, &src, &idx}) {
+    check_cuda(*t, "gather tensor"); check_dtype(*t, at::kInt, "gather tensor"); check_contig(*t, "gather tensor");
+  }
+  CHECK(dst.numel() == idx.numel(), "gather sizes");
+  msgl_gather_i32(dst.data_ptr<int32_t>(), src.data_ptr<int32_t>(), src.numel(), idx.data_ptr<int32_t>(),
+                  (int)idx.numel(), stream());
+}
+
+void scatter_i32(at::Tensor dst, at::Tensor idx, at::Tensor src) {
+  for (auto* t : {&dst, &src, &idx}) {
+    check_cuda(*t, "scatter tensor"); check_dtype(*t, at::kInt, "scatter tensor"); check_contig(*t, "scatter tensor");
+  }
+  CHECK(src.numel() == idx.numel(), "scatter sizes");
+  msgl_scatter_i32(dst.data_ptr<int32_t>(), dst.numel(), idx.data_ptr<int32_t>(), src.data_ptr<int32_t>(),
+                   (int)idx.numel(), stream());
 }
 
 std::tuple<int64_t, int64_t> get_error() {
@@ -453,6 +506,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_collective", &peer_collective);
   m.def("nvls_grid", []() { return msgl_nvls_grid(); });
   m.def("nvls_flag_bytes", []() { return msgl_nvls_flag_bytes(); });
+  m.def("nvls_state_words", []() { return msgl_nvls_state_words(); });
+  m.def("nvls_ticket_offset", []() { return msgl_nvls_ticket_offset(); });
+  m.def("gemm_signal", &gemm_signal);
+  m.def("plan_apply", &plan_apply);
+  m.def("gather_i32", &gather_i32);
+  m.def("scatter_i32", &scatter_i32);
   m.def("nvls_allreduce_rmsnorm", &nvls_allreduce_rmsnorm);
   m.def("num_sms", []() { return msgl_num_sms(); });
   m.def("gemm_splits", [](int64_t M, int64_t N, int64_t K) { return msgl_gemm_pick_splits(M, N, K); });

@@ -53,6 +53,11 @@ void msgl_gemm_ex(void* out, const void* x, const void* w, const void* bias, int
 void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M, int N,
                    int K, int ldo, int epi, int splits, int wide, void* workspace, int64_t ws_bytes,
                    cudaStream_t s);
+// msgl_gemm_ex2 whose output is this rank's NVLS staging region: the launch's last CTA adds 1 to the
+// multicast arrival counter `arrive_mc` (local ticket `arrive_ticket`), for the fused collective.
+void msgl_gemm_ex3(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M, int N,
+                   int K, int ldo, int epi, int force_splits, int force_wide, void* workspace, int64_t ws_cap,
+                   uint32_t* arrive_ticket, void* arrive_mc, cudaStream_t s);
 
 // ----- routed experts (MoE)
 void msgl_gemm_grouped(void* out, const void* x, const void* w, const void* bias, int rows_cap, int N, int K,
@@ -102,20 +107,35 @@ int msgl_attention_decode_paged(void* o, const void* q, int q_rows, const void* 
 // ----- allocation-free decode attention (no counterpart in the reference; see attention.cu):
 // split-KV scratch comes from a fixed 8 MiB file-scope device array instead of a workspace
 // argument. Returns 0 on success, 1 if the problem needs more scratch than that, 2 if the
-// per-device set-up failed, 3 on bad arguments, 4 if the launch failed. Calls that overlap on the
+// per-device set-up failed, 3 on bad arguments, 4 if a launch failed. `num_slots` bounds the
+// page-table entries in the bounds-check build. Calls that overlap on the
 // GPU race on the shared scratch; the first call on a device must precede any stream capture.
 int msgl_attention_decode_noalloc(void* o, const void* q, const void* k_cache, const void* v_cache,
                                   const int32_t* page_table, int64_t pt_stride, const int32_t* rows,
                                   const int32_t* kv_lens, int bs, int nq, int nkv, int hd,
-                                  int64_t cache_stride, float sm_scale, int window, const float* sinks,
-                                  int num_splits, cudaStream_t s);
+                                  int64_t cache_stride, int64_t num_slots, float sm_scale, int window,
+                                  const float* sinks, int num_splits, cudaStream_t s);
 
 // ----- NVLS (multicast) all-reduce fused with residual add + RMSNorm (see comm.cu)
+// ----- batch metadata (plan.cu): page-table writes + out_loc gather in one launch; int32 gather /
+// scatter through an index list
+void msgl_plan_apply(int32_t* page_table, int64_t pt_stride, int64_t pt_rows_total, const int32_t* pt_rows,
+                     const int32_t* pt_pos, const int32_t* pt_slots, int n_writes, const int32_t* tok_rows,
+                     const int32_t* positions, int n_tok, int32_t* out_loc, cudaStream_t s);
+void msgl_gather_i32(int32_t* dst, const int32_t* src, int64_t src_len, const int32_t* idx, int n, cudaStream_t s);
+void msgl_scatter_i32(int32_t* dst, int64_t dst_len, const int32_t* idx, const int32_t* src, int n, cudaStream_t s);
+
+// mode 0: LL (small messages; out written), 1: RS with x copied into staging, 2: RS with x already
+// in staging, 3: RS with staging written and arrival signalled by msgl_gemm_ex3. RS writes the
+// normalised rows into the buffer's gather region and only this rank's rows (i % world == rank) of
+// the residual. Returns 0, 3 on bad arguments, 4 if the launch failed.
 int msgl_nvls_grid();
 int msgl_nvls_flag_bytes();
+int msgl_nvls_state_words();
+int64_t msgl_nvls_ticket_offset();
 int msgl_nvls_allreduce_rmsnorm(void* uc, void* mc, int rank, int world, const void* x, void* residual, const void* w,
                                 void* out, int T, int H, float eps, int64_t cap_bytes, uint32_t* state,
-                                int64_t timeout_ns, int first, cudaStream_t s);
+                                int64_t timeout_ns, int first, int mode, cudaStream_t s);
 
 // ----- peer-memory collectives (CUDA IPC over NVLink)
 int msgl_peer_flag_bytes();

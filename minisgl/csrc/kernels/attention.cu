@@ -533,28 +533,23 @@ int decode_smem() {
 
 template <int HD>
 void run_prefill(const AttnParams& p, int num_reqs, int max_q_len, cudaStream_t s) {
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill_smem<HD>());
-    set = true;
-  }
+  msgl_set_smem<prefill_kernel<HD>>(prefill_smem<HD>());
   const dim3 grid((max_q_len * p.group + 63) / 64, num_reqs, p.nkv);
   msgl_launch(prefill_kernel<HD>, grid, dim3(kWarps * 32), prefill_smem<HD>(), s, 1, p);
 }
 
+// Returns the first CUDA error of the attribute call or the launches (cudaSuccess if all went out).
 template <int HD>
-void run_decode(const AttnParams& p, int bs, cudaStream_t s) {
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem<HD>());
-    set = true;
-  }
+cudaError_t run_decode(const AttnParams& p, int bs, cudaStream_t s) {
+  cudaError_t e = msgl_set_smem<decode_kernel<HD>>(decode_smem<HD>());
+  if (e != cudaSuccess) return e;
   const dim3 grid(p.nkv, bs, p.num_splits);
-  msgl_launch(decode_kernel<HD>, grid, dim3(kWarps * 32), decode_smem<HD>(), s, 1, p);
-  if (p.num_splits > 1) {
+  e = msgl_launch(decode_kernel<HD>, grid, dim3(kWarps * 32), decode_smem<HD>(), s, 1, p);
+  if (e == cudaSuccess && p.num_splits > 1) {
     const int warps = bs * p.nq;
-    msgl_launch(decode_combine_kernel<HD>, dim3((warps + 7) / 8), dim3(256), 0, s, 1, p, bs);
+    e = msgl_launch(decode_combine_kernel<HD>, dim3((warps + 7) / 8), dim3(256), 0, s, 1, p, bs);
   }
+  return e;
 }
 
 AttnParams make_params(void* o, const void* q, const void* k, const void* v, const int32_t* pt,
@@ -1064,11 +1059,7 @@ template <int HD>
 int run_paged_decode(const PagedDecodeParams& p, const void* q, int q_rows, const void* k, const void* v,
                      int64_t num_slots, int64_t cache_stride, cudaStream_t s) {
   using C = PdCfg<HD>;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(paged_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    set = true;
-  }
+  msgl_set_smem<paged_decode_kernel<HD>>(C::kSmem);
   CUtensorMap tk, tv, tq;
   const cuuint64_t kdims[3] = {(cuuint64_t)HD, (cuuint64_t)p.nkv, (cuuint64_t)num_slots};
   const cuuint64_t kstr[2] = {(cuuint64_t)HD * 2, (cuuint64_t)cache_stride * 2};
@@ -1422,11 +1413,7 @@ extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total
   p.page = page;
   p.scale_log2 = sm_scale * kLog2e;
   p.window = window;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(fmha_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FmSmem::kBytes);
-    set = true;
-  }
+  msgl_set_smem<fmha_prefill_kernel>(FmSmem::kBytes);
   CUtensorMap tq, tk, tv;
   const cuuint64_t qdims[3] = {(cuuint64_t)hd, (cuuint64_t)nq, (cuuint64_t)total_q};
   const cuuint64_t qstr[2] = {(cuuint64_t)hd * 2, (cuuint64_t)nq * hd * 2};
@@ -1495,7 +1482,11 @@ extern "C" int msgl_attention_decode_paged(void* o, const void* q, int q_rows, c
 //   * The problem must fit: bs * nq * num_splits * (hd + 2) * 4 bytes <= kNoAllocScratchBytes when
 //     num_splits > 1 (a single split uses no scratch). Larger requests are rejected before any launch.
 //   * Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
-// Returns 0 on success, otherwise one of kNoAlloc* below (nothing is launched on error).
+//   * `num_slots` is the number of KV-cache slots; the bounds-check build checks every page-table
+//     entry the kernels read against it (the release build does not read it).
+// Returns 0 on success, otherwise one of kNoAlloc* below. kNoAllocTooLarge, kNoAllocSetupFailed and
+// kNoAllocBadArgs launch nothing; kNoAllocLaunch means a launch failed (the CUDA error of that launch,
+// not an older sticky one, decides it).
 // =================================================================================================
 #include <mutex>
 
@@ -1527,8 +1518,9 @@ void* noalloc_scratch_for_current_device() {
 extern "C" __attribute__((visibility("default"))) int msgl_attention_decode_noalloc(
     void* o, const void* q, const void* k_cache, const void* v_cache, const int32_t* page_table, int64_t pt_stride,
     const int32_t* rows, const int32_t* kv_lens, int bs, int nq, int nkv, int hd, int64_t cache_stride,
-    float sm_scale, int window, const float* sinks, int num_splits, cudaStream_t s) {
-  if (bs < 0 || nkv <= 0 || nq % nkv != 0 || nq / nkv > 16 || (hd != 64 && hd != 128)) return kNoAllocBadArgs;
+    int64_t num_slots, float sm_scale, int window, const float* sinks, int num_splits, cudaStream_t s) {
+  if (bs < 0 || nkv <= 0 || nq % nkv != 0 || nq / nkv > 16 || (hd != 64 && hd != 128) || num_slots <= 0)
+    return kNoAllocBadArgs;
   if (bs == 0) return kNoAllocOk;
   const int splits = num_splits < 1 ? 1 : num_splits;
   const size_t need = splits > 1 ? (size_t)bs * nq * splits * (hd + 2) * 4 : 0;
@@ -1536,10 +1528,9 @@ extern "C" __attribute__((visibility("default"))) int msgl_attention_decode_noal
   void* scratch = noalloc_scratch_for_current_device();
   if (scratch == nullptr) return kNoAllocSetupFailed;
   AttnParams p = make_params(o, q, k_cache, v_cache, page_table, pt_stride, rows, nullptr, kv_lens, nq, nkv,
-                             cache_stride, sm_scale, window, sinks);
+                             cache_stride, sm_scale, window, sinks, num_slots);
   p.num_splits = splits;
   p.ws = reinterpret_cast<float*>(scratch);
-  if (hd == 64) run_decode<64>(p, bs, s);
-  else run_decode<128>(p, bs, s);
-  return cudaPeekAtLastError() == cudaSuccess ? kNoAllocOk : kNoAllocLaunch;
+  const cudaError_t e = hd == 64 ? run_decode<64>(p, bs, s) : run_decode<128>(p, bs, s);
+  return e == cudaSuccess ? kNoAllocOk : kNoAllocLaunch;
 }

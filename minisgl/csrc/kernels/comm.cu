@@ -33,11 +33,6 @@ struct PeerBufs {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // Publish epoch to all ranks for block b, then wait for every rank's epoch. Returns false on timeout.
 __device__ bool block_barrier(const PeerBufs& bufs, int rank, int world, int b, uint32_t epoch,
@@ -210,55 +205,74 @@ void msgl_peer_collective(void* const* bases, int rank, int world, int mode, voi
 }  // extern "C"
 
 
+
+
 // =================================================================================================
-// NVLink SHARP (NVLS) all-reduce fused with residual add + RMSNorm for decode-sized activations.
-// Every rank's symmetric buffer is bound to one NVLink multicast object; a multimem store or
-// reduction on the multicast address reaches the same offset on every GPU through the switch.
-// Buffer: [flags: kNvlsGrid x 128 B | data parity 0 | data parity 1], cap bytes per parity.
-// CTA b owns rows b, b + kNvlsGrid, ... of the [T, H] activation on every rank; a per-CTA call
-// counter in device memory (CUDA-graph replays stay in lockstep) gives the parity and the epoch.
+// NVLink SHARP (NVLS) all-reduce fused with residual add + RMSNorm (the collective that follows
+// every row-parallel GEMM of a tensor-parallel decoder, and the vocab-parallel embedding).
 //
-// Small messages (world x T x H x 4 <= 2 MiB), "LL" form, no barrier: every rank stores its rows
-// with multimem.st as 8-byte {bf16x2 data, epoch} words into its own slot on every GPU; a reader
-// spins on its local copy until every word carries the epoch (an aligned 8-byte store lands
-// whole), so data and synchronisation arrive together in one one-way NVLink trip.
-// Larger messages, "reduce" form: stage the rows locally, one barrier per CTA (multimem.red of a
-// per-CTA counter on every GPU, bounded spin on the local copy), then multimem.ld_reduce returns
-// the sum over all ranks (fp32 accumulation in the switch).
-// Both then add the residual, store the new residual (bf16) and the RMS-normalised row (bf16).
-// Parity reuse is safe: a CTA writes parity p again only in the call after next, which it starts
-// after seeing every peer's data of the next call, which each peer sends after finishing its reads
-// of parity p.
-// Virtual aliases: staging stores (unicast address) and switch reads (multicast address) meet in
-// the owning GPU's L2 after the sys-scope release, so no proxy fence is issued per access.
+// Every rank's symmetric buffer is bound to one NVLink multicast object: a multimem store or
+// reduction on the multicast address reaches the same offset on every GPU through the switch, and
+// multimem.ld_reduce returns the sum of all GPUs' copies (fp32 accumulation in the switch).
+// Buffer: [flags: kNvlsGrid x 128 B | LL parity 0 | LL parity 1 | staging | gather], `cap` bytes
+// per data region. Per-CTA state words in device memory advance inside the kernel, so CUDA-graph
+// replays stay in lockstep across ranks.
+//
+// Small messages (world x T x H x 4 bytes below a limit): "LL" form, no barrier. Every rank stores
+// its rows with multimem.st as 8-byte {bf16x2 data, epoch} words into its own slot on every GPU; a
+// reader spins on its local copy until every word carries the epoch (an aligned 8-byte store lands
+// whole), so data and synchronisation arrive together in one NVLink trip. Each rank then sums all
+// slots for every row itself. Parity reuse is safe: a CTA writes parity p again only in the call
+// after next, which it starts after seeing every peer's data of the next call, which each peer
+// sends after finishing its reads of parity p.
+//
+// Larger messages: reduce-scatter + norm + all-gather ("RS" form), the shape of the fused
+// row-parallel path:
+//   1. the rank's partial sum [T, H] lands in its staging region: written there by the producing
+//      GEMM's epilogue (mode 3: that GEMM's last CTA also signals arrival), by the previous kernel
+//      (mode 2), or copied in here (mode 1); arrival = one multimem.red on counter 1 per rank;
+//   2. once every rank arrived, rank r owns rows i with i % world == r: it reads their sum with
+//      multimem.ld_reduce, adds its residual rows, normalises, keeps the new residual rows (the
+//      residual stream stays sharded by row between the fused norms, which are its only readers),
+//      and multimem-stores the normalised rows into the gather region of every GPU;
+//   3. arrival on counter 2 after those stores; CTA 0 waits for every rank's, so the kernel ends
+//      only when the gather region (the returned activations) holds every row on this GPU.
+// Each GPU sends/receives T x H x 2 bytes per phase instead of every rank reducing every row
+// (world x the switch traffic). Staging and gather need no parity: a rank writes its staging for
+// call c+1 only after call c's second barrier (every rank done reading it), and every rank's
+// gather stores of call c+1 follow the first barrier of c+1, which follows every rank's reads of
+// call c's gathered rows (by the GEMM that consumes them, earlier in its stream).
+// All waits are bounded by %globaltimer: on expiry the kernel records kErrPeerTimeout and returns.
 namespace {
 
 constexpr int kNvlsGrid = 128;
 constexpr int kNvlsThreads = 256;
-constexpr int kNvlsFlagStride = 128;  // one flag per 128-byte line: the per-CTA atomics never share a line
+constexpr int kNvlsFlagStride = 128;  // one counter per 128-byte line
 constexpr int kNvlsFlagBytes = kNvlsGrid * kNvlsFlagStride;
 constexpr int kNvlsMaxVec = 8;  // 16-byte vectors per thread per row: H <= 8 * 8 * 256 = 16384
+constexpr int kNvlsStateWords = 4 * kNvlsGrid + 64;  // per CTA {LL calls, RS calls, -, -} + 2 tickets
+constexpr int kTicket1 = 4 * kNvlsGrid;             // local arrival tickets, 128 bytes apart
+constexpr int kTicket2 = 4 * kNvlsGrid + 32;
+
+enum NvlsMode : int { kModeLL = 0, kModeStage = 1, kModePrestaged = 2, kModeGemmArrived = 3 };
 
 struct NvlsParams {
   uint8_t* uc;        // this rank's symmetric buffer
   uint8_t* mc;        // multicast address of the same buffer
   int rank, world;
-  const uint4* x;     // [T, H] partial (bf16)
-  uint4* residual;    // [T, H] bf16, updated in place (residual += sum)
+  const uint4* x;     // [T, H] partial (bf16); unused in modes 2 and 3 (already in staging)
+  uint4* residual;    // [T, H] bf16, updated in place (residual += sum); RS: this rank's rows only
   const uint4* w;     // [H] bf16 norm weight
-  uint4* out;         // [T, H] bf16 normalised
+  uint4* out;         // [T, H] bf16 normalised (LL); RS writes the gather region instead
   int T, H;
   float eps;
   int64_t cap;
-  uint32_t* state;    // [kNvlsGrid][2] per CTA: calls (parity, LL epoch), reduce-form calls (barrier target)
+  uint32_t* state;    // kNvlsStateWords
   uint64_t timeout_ns;
   int first;          // 1: residual is not read (it becomes the sum)
-  int ll;             // 1: LL form (see above), 0: reduce form
+  int mode;
 };
 
-__device__ __forceinline__ void mm_red_release_add(uint8_t* mc_addr, uint32_t v) {
-  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc_addr), "r"(v) : "memory");
-}
 __device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const uint8_t* mc_addr) {
   uint4 r;
   asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
@@ -266,6 +280,11 @@ __device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const uint8_t* mc_addr) {
                : "l"(mc_addr)
                : "memory");
   return r;
+}
+__device__ __forceinline__ void mm_st_bf16x8(uint8_t* mc_addr, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
 }
 __device__ __forceinline__ void mm_st_b64(uint8_t* mc_addr, uint64_t v) {
   asm volatile("multimem.st.relaxed.sys.global.b64 [%0], %1;" ::"l"(mc_addr), "l"(v) : "memory");
@@ -280,6 +299,20 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
 }
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
+}
+
+// spin (one thread) until the counter reaches `target` (wrap-safe); false on timeout
+__device__ __forceinline__ bool wait_counter(const uint8_t* counter, uint32_t target, uint64_t timeout_ns, int site) {
+  const uint32_t* c = reinterpret_cast<const uint32_t*>(counter);
+  if ((int)(ld_acquire_sys(c) - target) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while ((int)(ld_acquire_sys(c) - target) < 0) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      report_error(kErrPeerTimeout, site);
+      return false;
+    }
+  }
+  return true;
 }
 
 // LL form: sum over every rank's slot of one 8-element group (4 words {bf16x2, epoch}); spins on
@@ -309,7 +342,7 @@ __device__ __forceinline__ bool ll_gather8(const uint8_t* base, int64_t slot_byt
       f[2 * j + 1] += bf16_hi(d[j]);
     }
   }
-  // the all-reduce result is bf16, as with the reduce form
+  // the all-reduce result is bf16, as with ld_reduce
 #pragma unroll
   for (int j = 0; j < 8; j += 2) {
     const uint32_t q = pack_bf16(f[j], f[j + 1]);
@@ -319,23 +352,64 @@ __device__ __forceinline__ bool ll_gather8(const uint8_t* base, int64_t slot_byt
   return true;
 }
 
+// Sum (already in vals) + residual -> residual (bf16); RMS-normalise the stored residual; returns
+// the normalised 16-byte vectors in vals. Block-wide: every thread calls it for the same row.
+__device__ __forceinline__ void add_residual_norm(const NvlsParams& p, int row, float (&vals)[kNvlsMaxVec][8],
+                                                  float* s_red) {
+  const int tid = threadIdx.x, nv = p.H / 8;
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNvlsMaxVec; ++k) {
+    const int v = tid + k * kNvlsThreads;
+    if (v < nv) {
+      const int64_t idx = (int64_t)row * nv + v;
+      if (!p.first) {
+        float r[8];
+        unpack8(p.residual[idx], r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vals[k][j] += r[j];
+      }
+      const uint4 packed = pack8(vals[k]);
+      p.residual[idx] = packed;
+      unpack8(packed, vals[k]);  // normalise the stored (bf16) residual
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += vals[k][j] * vals[k][j];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNvlsThreads / 32; ++i) tot += s_red[i];
+  __syncthreads();  // s_red reuse by the next row
+  const float rstd = rsqrtf(tot / (float)p.H + p.eps);
+#pragma unroll
+  for (int k = 0; k < kNvlsMaxVec; ++k) {
+    const int v = tid + k * kNvlsThreads;
+    if (v < nv) {
+      float wf[8];
+      unpack8(p.w[v], wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) vals[k][j] = vals[k][j] * rstd * wf[j];
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParams p) {
   const int b = blockIdx.x, tid = threadIdx.x;
-  pdl_wait();
-  pdl_launch();
-  __shared__ uint32_t s_calls, s_rcalls;
-  __shared__ float s_red[kNvlsThreads / 32];
-  if (tid == 0) {
-    s_calls = p.state[2 * b] + 1;
-    s_rcalls = p.state[2 * b + 1] + (p.ll ? 0 : 1);
-  }
-  __syncthreads();
-  const uint32_t calls = s_calls, rcalls = s_rcalls;
-  const size_t off = kNvlsFlagBytes + (size_t)(calls & 1) * p.cap;
   const int nv = p.H / 8;
-  const int64_t slot_bytes = (int64_t)p.T * p.H * 4;  // LL: 8 bytes per bf16 pair
-  bool ok = true;
-  if (p.ll) {
+  __shared__ float s_red[kNvlsThreads / 32];
+  __shared__ uint32_t s_calls;
+  pdl_launch();
+  if (p.mode == kModeLL) {
+    pdl_wait();
+    if (tid == 0) s_calls = p.state[4 * b] + 1;
+    __syncthreads();
+    const uint32_t calls = s_calls;
+    const size_t off = kNvlsFlagBytes + (size_t)(calls & 1) * p.cap;
+    const int64_t slot_bytes = (int64_t)p.T * p.H * 4;  // 8 bytes per bf16 pair
     // 1. send: my rows into my slot on every GPU, each bf16 pair tagged with the epoch
     uint8_t* my_slot = p.mc + off + p.rank * slot_bytes;
     const uint64_t tag = (uint64_t)calls << 32;
@@ -348,81 +422,84 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParam
         mm_st_b64(dst + 16, tag | u.z);
         mm_st_b64(dst + 24, tag | u.w);
       }
-  } else {
-    // 1. stage this CTA's rows, 2. barrier across ranks for them
-    uint4* mine = reinterpret_cast<uint4*>(p.uc + off);
-    for (int row = b; row < p.T; row += kNvlsGrid)
-      for (int v = tid; v < nv; v += kNvlsThreads) mine[(int64_t)row * nv + v] = p.x[(int64_t)row * nv + v];
-    __syncthreads();
-    if (tid == 0) {
-      mm_red_release_add(p.mc + b * kNvlsFlagStride, 1u);
-      const uint32_t* flag = reinterpret_cast<const uint32_t*>(p.uc + b * kNvlsFlagStride);
-      const uint32_t target = rcalls * (uint32_t)p.world;  // flags count reduce-form calls only
-      const uint64_t t0 = globaltimer_ns();
-      while ((int)(ld_acquire_sys(flag) - target) < 0) {
-        if (globaltimer_ns() - t0 > p.timeout_ns) {
-          report_error(kErrPeerTimeout, 1000 + b);
-          ok = false;
-          break;
-        }
-      }
-    }
-    ok = __syncthreads_and(ok) != 0;
-  }
-  // 3. sum over ranks, add residual, normalise
-  if (ok) {
-    const uint8_t* mdata = p.mc + off;
+    // 2. every rank's slot, summed, + residual, normalised
     const uint8_t* ldata = p.uc + off;
     for (int row = b; row < p.T; row += kNvlsGrid) {
       float vals[kNvlsMaxVec][8];
-      float ss = 0.f;
       bool good = true;
 #pragma unroll
       for (int k = 0; k < kNvlsMaxVec; ++k) {
         const int v = tid + k * kNvlsThreads;
-        if (v < nv) {
-          const int64_t idx = (int64_t)row * nv + v;
-          if (p.ll) good &= ll_gather8(ldata, slot_bytes, p.world, idx * 32, calls, p.timeout_ns, vals[k]);
-          else unpack8(mm_ld_reduce_bf16x8(mdata + idx * 16), vals[k]);
-          if (!p.first) {
-            float r[8];
-            unpack8(p.residual[idx], r);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) vals[k][j] += r[j];
-          }
-          const uint4 packed = pack8(vals[k]);
-          p.residual[idx] = packed;
-          unpack8(packed, vals[k]);  // normalise the stored (bf16) residual
-#pragma unroll
-          for (int j = 0; j < 8; ++j) ss += vals[k][j] * vals[k][j];
-        }
+        if (v < nv) good &= ll_gather8(ldata, slot_bytes, p.world, ((int64_t)row * nv + v) * 32, calls,
+                                       p.timeout_ns, vals[k]);
       }
       if (!good) report_error(kErrPeerTimeout, 2000 + b);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if ((tid & 31) == 0) s_red[tid >> 5] = ss;
-      __syncthreads();
-      float tot = 0.f;
-#pragma unroll
-      for (int i = 0; i < kNvlsThreads / 32; ++i) tot += s_red[i];
-      const float rstd = rsqrtf(tot / (float)p.H + p.eps);
+      add_residual_norm(p, row, vals, s_red);
 #pragma unroll
       for (int k = 0; k < kNvlsMaxVec; ++k) {
         const int v = tid + k * kNvlsThreads;
-        if (v < nv) {
-          float wf[8];
-          unpack8(p.w[v], wf);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) vals[k][j] = vals[k][j] * rstd * wf[j];
-          p.out[(int64_t)row * nv + v] = pack8(vals[k]);
-        }
+        if (v < nv) p.out[(int64_t)row * nv + v] = pack8(vals[k]);
       }
-      __syncthreads();  // s_red reuse
+    }
+    if (tid == 0) p.state[4 * b] = calls;
+    return;
+  }
+
+  // ---------------------------------------------------------------------------- RS form
+  // Wait for the producer in every mode: the per-CTA call counters (and tickets) were last written
+  // by the previous call of this kernel, which completed before the producer did (every kernel of
+  // the chain waits for its predecessor before it ends), but not necessarily before this grid
+  // started (programmatic launch lets several grids of the chain be resident at once). In mode 3
+  // the producer GEMM already published its tiles to every rank before finishing.
+  pdl_wait();
+  if (tid == 0) s_calls = p.state[4 * b + 1] + 1;
+  __syncthreads();
+  const uint32_t rs = s_calls;
+  const uint32_t target = rs * (uint32_t)p.world;  // each rank adds 1 per call to each counter
+  uint8_t* stage_uc = p.uc + kNvlsFlagBytes + 2 * p.cap;
+  const uint8_t* stage_mc = p.mc + kNvlsFlagBytes + 2 * p.cap;
+  uint8_t* gather_mc = p.mc + kNvlsFlagBytes + 3 * p.cap;
+  uint8_t* cnt1_mc = p.mc;
+  uint8_t* cnt2_mc = p.mc + kNvlsFlagStride;
+  if (p.mode != kModeGemmArrived) {
+    // stage (or just publish) this rank's partial sum
+    if (p.mode == kModeStage) {
+      const int64_t n16 = (int64_t)p.T * nv;
+      uint4* dst = reinterpret_cast<uint4*>(stage_uc);
+      for (int64_t i = (int64_t)b * kNvlsThreads + tid; i < n16; i += (int64_t)kNvlsGrid * kNvlsThreads)
+        dst[i] = p.x[i];
+    }
+    __syncthreads();
+    if (tid == 0) rank_arrive(p.state + kTicket1, kNvlsGrid, cnt1_mc);
+  }
+  // 1. every rank's partial is staged
+  bool ok = true;
+  if (tid == 0) ok = wait_counter(p.uc, target, p.timeout_ns, 3000 + b);
+  ok = __syncthreads_and(ok) != 0;
+  if (ok) {
+    // 2. reduce-scatter by row, residual + norm, all-gather of the normalised rows
+    for (int i = b * p.world + p.rank; i < p.T; i += kNvlsGrid * p.world) {
+      float vals[kNvlsMaxVec][8];
+#pragma unroll
+      for (int k = 0; k < kNvlsMaxVec; ++k) {
+        const int v = tid + k * kNvlsThreads;
+        if (v < nv) unpack8(mm_ld_reduce_bf16x8(stage_mc + ((int64_t)i * nv + v) * 16), vals[k]);
+      }
+      add_residual_norm(p, i, vals, s_red);
+#pragma unroll
+      for (int k = 0; k < kNvlsMaxVec; ++k) {
+        const int v = tid + k * kNvlsThreads;
+        if (v < nv) mm_st_bf16x8(gather_mc + ((int64_t)i * nv + v) * 16, pack8(vals[k]));
+      }
     }
   }
+  // 3. this CTA's gather stores are issued; the rank's last CTA publishes them
+  __syncthreads();
   if (tid == 0) {
-    p.state[2 * b] = calls;
-    p.state[2 * b + 1] = rcalls;
+    rank_arrive(p.state + kTicket2, kNvlsGrid, cnt2_mc);
+    if (b == 0 && wait_counter(p.uc + kNvlsFlagStride, target, p.timeout_ns, 4000))
+      fence_proxy_async_global();  // gathered rows are read next by TMA loads
+    p.state[4 * b + 1] = rs;
   }
 }
 
@@ -430,21 +507,20 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParam
 
 extern "C" int msgl_nvls_grid() { return kNvlsGrid; }
 extern "C" int msgl_nvls_flag_bytes() { return kNvlsFlagBytes; }
+extern "C" int msgl_nvls_state_words() { return kNvlsStateWords; }
+extern "C" int64_t msgl_nvls_ticket_offset() { return (int64_t)kTicket1 * 4; }
 
 extern "C" int msgl_nvls_allreduce_rmsnorm(void* uc, void* mc, int rank, int world, const void* x, void* residual,
                                            const void* w, void* out, int T, int H, float eps, int64_t cap_bytes,
-                                           uint32_t* state, int64_t timeout_ns, int first, cudaStream_t s) {
+                                           uint32_t* state, int64_t timeout_ns, int first, int mode, cudaStream_t s) {
   if (H % 8 != 0 || H > 8 * kNvlsMaxVec * kNvlsThreads || (int64_t)T * H * 2 > cap_bytes) return 3;
+  if (mode < kModeLL || mode > kModeGemmArrived || world < 1 || rank < 0 || rank >= world) return 3;
+  if (mode == kModeLL && (int64_t)world * T * H * 4 > cap_bytes) return 3;
   NvlsParams p;
   p.uc = reinterpret_cast<uint8_t*>(uc);
   p.mc = reinterpret_cast<uint8_t*>(mc);
   p.rank = rank;
   p.world = world;
-  // LL while every rank's tagged copy is small (its 8-byte multicast stores cost more per byte than
-  // ld_reduce, but it needs no barrier); MINISGL_NVLS_LL_BYTES overrides the limit
-  static const int64_t ll_limit = getenv("MINISGL_NVLS_LL_BYTES") ? atoll(getenv("MINISGL_NVLS_LL_BYTES")) : (2 << 20);
-  const int64_t ll_bytes = (int64_t)world * T * H * 4;
-  p.ll = (ll_bytes <= cap_bytes && ll_bytes <= ll_limit) ? 1 : 0;
   p.x = reinterpret_cast<const uint4*>(x);
   p.residual = reinterpret_cast<uint4*>(residual);
   p.w = reinterpret_cast<const uint4*>(w);
@@ -456,8 +532,8 @@ extern "C" int msgl_nvls_allreduce_rmsnorm(void* uc, void* mc, int rank, int wor
   p.state = state;
   p.timeout_ns = (uint64_t)timeout_ns;
   p.first = first;
-  msgl_launch(nvls_ar_rmsnorm_kernel, dim3(kNvlsGrid), dim3(kNvlsThreads), 0, s, 1, p);
-  return 0;
+  p.mode = mode;
+  return msgl_launch(nvls_ar_rmsnorm_kernel, dim3(kNvlsGrid), dim3(kNvlsThreads), 0, s, 1, p) == cudaSuccess ? 0 : 4;
 }
 
 MSGL_ERROR_ACCESSOR(msgl_err_comm)

@@ -9,6 +9,8 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <atomic>
+#include <mutex>
 #include <utility>
 
 #define MSGL_DEVICE __device__ __forceinline__
@@ -402,6 +404,36 @@ MSGL_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory");
 MSGL_DEVICE void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ------------------------------------------------------------------------------------------
+// cross-GPU signalling (NVLink / NVSwitch peer and multicast memory)
+MSGL_DEVICE uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// atomic add on the same offset of every GPU bound to the multicast object (release, system scope)
+MSGL_DEVICE void mm_red_release_add(void* mc_addr, uint32_t v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc_addr), "r"(v) : "memory");
+}
+// orders this thread's async-proxy (TMA) global writes, completed by bulk_wait, with its later
+// generic-proxy operations
+MSGL_DEVICE void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Rank-wide arrival on a multicast counter, one call per CTA (one thread, after a CTA barrier that
+// follows the CTA's writes): CTAs take tickets from a local counter; the last of `ctas` resets it
+// for the next use and adds 1 to the counter on every GPU with release semantics at system scope,
+// so a rank that sees the counter reach its target also sees every write of every CTA of every
+// arrived rank (the fences make the ticket chain cumulative, as in a threadfence reduction).
+MSGL_DEVICE void rank_arrive(uint32_t* ticket, uint32_t ctas, void* counter_mc) {
+  __threadfence();
+  const uint32_t old = atomicAdd(ticket, 1u);
+  if (old == ctas - 1) {
+    atomicExch(ticket, 0u);
+    __threadfence_system();
+    mm_red_release_add(counter_mc, 1u);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // named barriers among a subset of warps
 MSGL_DEVICE void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -453,6 +485,25 @@ inline cudaError_t msgl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, 
   cfg.attrs = attr;
   cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for one kernel, done once per (kernel, device):
+// the attribute belongs to the device's context, so a process that launches on several GPUs sets it
+// on each. Thread-safe; returns the CUDA error of the attribute call (cudaSuccess once it is set).
+template <auto Kernel>
+inline cudaError_t msgl_set_smem(int bytes) {
+  static std::mutex mu;
+  static std::atomic<uint64_t> done{0};  // bit d: set on device d (devices 0..63)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  std::lock_guard<std::mutex> g(mu);
+  if (bit != 0 && (done.load(std::memory_order_relaxed) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(reinterpret_cast<const void*>(Kernel), cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
 }
 
 #define MSGL_ERROR_ACCESSOR(fn)                                                   \

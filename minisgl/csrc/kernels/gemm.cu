@@ -88,7 +88,18 @@ struct Params {
   int64_t bias_stride;    // per-expert bias stride (grouped)
   int M, n_out, kblocks;
   int n_tiles, m_tiles, splits;  // splits > 1: grid (splits, tiles), cluster (splits, 1, 1)
+  // fused collective: when set, the output is this rank's staging region of the NVLS buffer and
+  // the launch's last CTA to finish adds 1 to the multicast arrival counter (see comm.cu)
+  uint32_t* arrive_ticket;
+  void* arrive_mc;
 };
+
+// End of a GEMM CTA whose output feeds the NVLS reduce-scatter: every epilogue thread that issued
+// TMA stores has waited for them (bulk_wait) and fenced the async proxy; after the CTA barrier that
+// precedes this call, one thread takes the CTA's arrival ticket.
+__device__ __forceinline__ void gemm_arrive(uint32_t* ticket, void* mc) {
+  if (mc != nullptr && threadIdx.x == 0) rank_arrive(ticket, gridDim.x * gridDim.y * gridDim.z, mc);
+}
 
 __device__ __forceinline__ float act_silu(float g) { return g / (1.f + __expf(-g)); }
 __device__ __forceinline__ float act_gelu(float g) {
@@ -468,10 +479,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
       cluster_sync();  // every push into and out of this CTA's smem has landed
     }
   }
-  if (warp >= 2 && lane == 0) bulk_wait<0>();
+  if (warp >= 2 && lane == 0) {
+    bulk_wait<0>();
+    if (p.arrive_mc != nullptr) fence_proxy_async_global();
+  }
 
   tc_fence_before();
   __syncthreads();
+  gemm_arrive(p.arrive_ticket, p.arrive_mc);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
@@ -521,7 +536,10 @@ struct Params2 {
   const __nv_bfloat16* bias;
   int M, n_out, kblocks;
   int n_tiles, m_tiles, splits;  // n_tiles counts pair tiles (256 weight rows, 512 if gated)
+  uint32_t* arrive_ticket;       // as in Params
+  void* arrive_mc;
 };
+
 
 template <int BN, int EPI>
 __device__ __forceinline__ void store_item2(const float (&v)[32], const float (&g2)[32], const Params2& p, int nt,
@@ -780,9 +798,13 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
       }
     }
   }
-  if (warp >= 2 && lane == 0) bulk_wait<0>();
+  if (warp >= 2 && lane == 0) {
+    bulk_wait<0>();
+    if (p.arrive_mc != nullptr) fence_proxy_async_global();
+  }
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its pair / cluster peers may still address its smem / TMEM
+  gemm_arrive(p.arrive_ticket, p.arrive_mc);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_2sm(tmem_base, C::kTmemCols);
@@ -945,11 +967,7 @@ template <int BN, int EPI>
 static void launch2(Params2 p, const void* x, const void* w, void* out, int N, int K, int ldo, size_t ws_cap,
                     cudaStream_t s) {
   using C = Cfg2<BN, EPI>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemm2_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    attr_set = true;
-  }
+  msgl_set_smem<gemm2_kernel<BN, EPI>>(C::kSmem);
   const CUtensorMap mw = make_map(w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, BK, C::kRowsA, true);
   const CUtensorMap mx = make_map(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, K, K, BK, C::kTok, true);
   const CUtensorMap mo = EPI == kF32
@@ -1011,11 +1029,7 @@ static int best_splits(int tiles, int kblocks, int cap) {
 template <int BN, int EPI, bool WIDE>
 static void launch(const Params& p, const void* x, const void* w, void* out, int N, int K, int ldo, cudaStream_t s) {
   using C = Cfg<BN, EPI, WIDE>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemm_kernel<BN, EPI, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    attr_set = true;
-  }
+  msgl_set_smem<gemm_kernel<BN, EPI, WIDE>>(C::kSmem);
   const CUtensorMap mw = p.w_blocked ? make_map_blocked(w, N, K, C::kRowsA)
                                      : make_map(w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, BK, C::kRowsA, true);
   const CUtensorMap mx = make_map(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, K, K, BK, BN, true);
@@ -1076,10 +1090,13 @@ static void launch_2sm_bn(int bn, Params2 p, const void* x, const void* w, void*
 }
 
 static void launch_2sm(const void* x, const void* w, const void* bias, void* out, int M, int N, int K, int ldo,
-                       int epi, int force_splits, void* ws, size_t ws_cap, cudaStream_t s) {
+                       int epi, int force_splits, void* ws, size_t ws_cap, uint32_t* arrive_ticket,
+                       void* arrive_mc, cudaStream_t s) {
   const bool act = is_act(epi);
   Params2 p;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.arrive_ticket = arrive_ticket;
+  p.arrive_mc = arrive_mc;
   p.M = M;
   p.n_out = act ? N / 2 : N;
   p.kblocks = (K + BK - 1) / BK;
@@ -1128,10 +1145,19 @@ extern "C" void msgl_gemm_ex(void* out, const void* x, const void* w, const void
 extern "C" void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M,
                               int N, int K, int ldo, int epi, int force_splits, int force_wide, void* workspace,
                               int64_t ws_cap, cudaStream_t s) {
+  msgl_gemm_ex3(out, x, w, w_blocked, bias, M, N, K, ldo, epi, force_splits, force_wide, workspace, ws_cap, nullptr,
+                nullptr, s);
+}
+
+extern "C" void msgl_gemm_ex3(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M,
+                              int N, int K, int ldo, int epi, int force_splits, int force_wide, void* workspace,
+                              int64_t ws_cap, uint32_t* arrive_ticket, void* arrive_mc, cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
   Plan pl = make_plan(M, N, K, epi, force_splits, force_wide);
   Params p;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.arrive_ticket = arrive_ticket;
+  p.arrive_mc = arrive_mc;
   p.grp_count = nullptr;
   p.grp_work = nullptr;
   p.bias_stride = 0;
@@ -1143,7 +1169,8 @@ extern "C" void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blo
   p.kblocks = (K + BK - 1) / BK;
   p.splits = pl.splits;
   if (use_2sm(M, N, K, epi, force_wide, w_blocked)) {
-    launch_2sm(x, w, bias, out, M, N, K, ldo, epi, force_splits, workspace, (size_t)ws_cap, s);
+    launch_2sm(x, w, bias, out, M, N, K, ldo, epi, force_splits, workspace, (size_t)ws_cap, arrive_ticket, arrive_mc,
+               s);
     return;
   }
   const bool wide = pl.wide;
@@ -1166,11 +1193,7 @@ template <int BN>
 static void launch_grouped(const Params& p, const void* x, const void* w, void* out, int E, int N, int K, int ldo,
                            cudaStream_t s) {
   using C = Cfg<BN, kBf16, false>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemm_kernel<BN, kBf16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    attr_set = true;
-  }
+  msgl_set_smem<gemm_kernel<BN, kBf16, false>>(C::kSmem);
   const CUtensorMap mw = make_map_experts(w, E, N, K, C::kRowsA);
   const CUtensorMap mx = make_map(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, K, K, BK, BN, true);
   const CUtensorMap mo = make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, C::kChunk, false);
@@ -1188,6 +1211,8 @@ extern "C" void msgl_gemm_grouped(void* out, const void* x, const void* w, const
   if (rows_cap <= 0 || N <= 0 || max_tiles <= 0) return;
   Params p;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.arrive_ticket = nullptr;
+  p.arrive_mc = nullptr;
   p.bias_stride = N;
   p.w_blocked = 0;
   p.grp_count = tile_count;

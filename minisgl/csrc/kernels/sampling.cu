@@ -405,11 +405,7 @@ extern "C" void msgl_sample(int32_t* out, const float* logits, int rows, int voc
                             const int64_t* seed, const int64_t* step, const int32_t* col_ids, int id_offset,
                             float* out_val, cudaStream_t s) {
   if (rows == 0) return;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
-    attr_set = true;
-  }
+  msgl_set_smem<sample_kernel>((int)sizeof(Smem));
   msgl_launch(sample_kernel, dim3(rows), dim3(kThreads), sizeof(Smem), s, 1, out, logits, vocab, stride, temperature,
               top_k, top_p, seed, step, col_ids, id_offset, out_val);
 }

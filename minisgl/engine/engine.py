@@ -2,7 +2,8 @@
 (reference: python/minisgl/engine/engine.py:29-233).
 
 Batch metadata reaches the device as ONE packed int32 upload (``BatchPlan``, built on the host by
-the scheduler); the page-table scatter and the ``out_loc`` gather are then done on the device.
+the scheduler); one kernel then applies its page-table writes and gathers ``out_loc``
+(``csrc/kernels/plan.cu``).
 Decode input ids come from ``last_tokens`` (one int32 per page-table row, written by the sampler),
 so a decode step never waits for the host.
 """
@@ -18,6 +19,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
+from minisgl._native import cuda as _cuda
 from minisgl.attention import create_attention_backend
 from minisgl.attention.paged import PAGED_DECODE_PAGES
 from minisgl.core import Batch, Context, Req, SamplingParams, reset_global_ctx, set_global_ctx
@@ -252,10 +254,16 @@ class Engine:
         else:
             dev_buf = host
         dev = {k: dev_buf[s:e] for k, (s, e) in views.items()}
-        if plan.num_pt_writes:
-            self.page_table[dev["pt_rows"].long(), dev["pt_pos"].long()] = dev["pt_slots"]
         batch.positions = dev["positions"]
-        batch.out_loc = self.page_table[dev["tok_rows"].long(), dev["positions"].long()]
+        if self.is_cuda:
+            # one launch: page-table writes, then out_loc = page_table[tok_rows, positions]
+            batch.out_loc = torch.empty(dev["positions"].numel(), dtype=torch.int32, device=self.device)
+            _cuda().plan_apply(self.page_table, dev["pt_rows"], dev["pt_pos"], dev["pt_slots"], dev["tok_rows"],
+                               dev["positions"], batch.out_loc)
+        else:
+            if plan.num_pt_writes:
+                self.page_table[dev["pt_rows"].long(), dev["pt_pos"].long()] = dev["pt_slots"]
+            batch.out_loc = self.page_table[dev["tok_rows"].long(), dev["positions"].long()]
         meta = {"dev": dev, "max_q_len": plan.max_q_len, "max_kv_len": plan.max_kv_len}
         self.attn_backend.prepare_metadata(batch, meta)
         return dev
@@ -263,6 +271,9 @@ class Engine:
     def forward_batch(self, batch: Batch, args: BatchSamplingArgs, dev: dict) -> ForwardOutput:
         if batch.is_prefill:
             batch.input_ids = dev["input_ids"]
+        elif self.is_cuda:
+            batch.input_ids = torch.empty(dev["req_rows"].numel(), dtype=torch.int32, device=self.device)
+            _cuda().gather_i32(batch.input_ids, self.last_tokens, dev["req_rows"])
         else:
             batch.input_ids = self.last_tokens[dev["req_rows"].long()]
         with self.ctx.forward_batch(batch):
@@ -278,7 +289,10 @@ class Engine:
         else:
             next_tokens = self.sampler.sample(logits[: batch.size], args)
         next_tokens = next_tokens.to(torch.int32)
-        self.last_tokens[dev["sample_rows"].long()] = next_tokens
+        if self.is_cuda:
+            _cuda().scatter_i32(self.last_tokens, dev["sample_rows"], next_tokens.contiguous())
+        else:
+            self.last_tokens[dev["sample_rows"].long()] = next_tokens
         if self.is_cuda:
             cpu = torch.empty(next_tokens.shape, dtype=torch.int32, pin_memory=True)
             cpu.copy_(next_tokens, non_blocking=True)

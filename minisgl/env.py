@@ -56,6 +56,8 @@ _FLAGS = {
     "NVTX": _Flag(False, _as_bool),  # NVTX ranges around layers / attention / MLP / LM head / sampler
     "MOE_PARALLEL": _Flag("tp", str),  # tp: shard every expert's intermediate dim; ep: whole experts per rank
     "BOUNDS_CHECK": _Flag(False, _as_bool),  # load the index-checking kernel build (_cuda_bc)
+    "NVLS_LL_BYTES": _Flag(2 << 20, parse_mem_bytes),  # largest world x T x H x 4 sent in the LL form
+    "NVLS_GEMM_FUSION": _Flag(True, _as_bool),  # row-parallel GEMMs write the NVLS staging region
 }
 
 

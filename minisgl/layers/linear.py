@@ -69,11 +69,18 @@ class LinearRowParallel(_Linear):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         bias = self.bias if (self.bias is not None and self._bias_scale) else None
-        y = ops.linear(x, self.weight, bias)
         self.deferred = False
+        fused = DistributedCommunicator.norm_impl if (self._tp > 1 and self._reduce and self.defer_to_norm) else None
+        if fused is not None and x.is_cuda:
+            # GEMM fused with the collective: the output tiles land in this rank's NVLS staging
+            # region and the GEMM signals the other ranks itself (None: batch too small or too large)
+            y = fused.linear_into_staging(x, self.weight, bias)
+            if y is not None:
+                self.deferred = True
+                return y
+        y = ops.linear(x, self.weight, bias)
         if self._tp > 1 and self._reduce:
-            fused = DistributedCommunicator.norm_impl
-            if self.defer_to_norm and fused is not None and fused.fits(y):
+            if fused is not None and fused.fits(y):
                 self.deferred = True
             else:
                 y = self._comm.all_reduce(y)

@@ -63,6 +63,11 @@ class MoELayer(BaseOP):
         self.down_proj_bias = torch.empty(local, hidden_size) if has_bias else None
         self._comm = DistributedCommunicator()
 
+    # set by the model when the next norm can take the unreduced per-rank sum (fused all-reduce +
+    # RMSNorm); `deferred` tells whether the last forward left it unreduced
+    defer_to_norm = False
+    deferred = False
+
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         be = get_global_ctx().moe_backend
         out = be.forward(
@@ -73,6 +78,11 @@ class MoELayer(BaseOP):
             w2_bias=self.down_proj_bias if (self._tp == 1 or self._ep or get_tp_info().rank == 0) else None,
             softmax_after_topk=self._softmax_after_topk, expert_offset=self._e0,
         )
+        self.deferred = False
         if self._tp > 1:
-            out = self._comm.all_reduce(out)
+            fused = DistributedCommunicator.norm_impl
+            if self.defer_to_norm and fused is not None and fused.fits(out):
+                self.deferred = True
+            else:
+                out = self._comm.all_reduce(out)
         return out

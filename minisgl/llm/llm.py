@@ -1,15 +1,21 @@
 """Offline API: ``LLM(model_path, **config).generate(prompts, sampling_params)``
-(reference: python/minisgl/llm/llm.py:28-98).
+(reference: python/minisgl/llm/llm.py:28-98; the constructor and ``generate`` signatures and the
+``[{"text", "token_ids"}]`` result are that file's public surface).
 
-Runs an in-process scheduler in offline mode. Under ``torchrun`` (``WORLD_SIZE > 1``) every rank
-constructs the same ``LLM`` with the same prompts and the ranks form one tensor-parallel group.
+``LLM`` is a scheduler in offline mode: instead of a ZeroMQ socket its input is a queue of the
+prompts handed to ``generate``, released in slices of about one prefill chunk's worth of prompt
+tokens whenever the scheduler polls, and its output is a per-request token list. The scheduler loop
+ends (``RequestAllFinished``) when it would block with nothing queued. Under ``torchrun``
+(``WORLD_SIZE > 1``) every rank constructs the same ``LLM``, gets the same prompts and runs the same
+schedule; the ranks form one tensor-parallel group.
 """
 
 from __future__ import annotations
 
+import collections
+import dataclasses
 import os
-from dataclasses import dataclass
-from typing import Dict, List, Tuple
+from typing import Deque, Dict, List, Sequence, Tuple
 
 import torch
 
@@ -20,35 +26,27 @@ from minisgl.scheduler import Scheduler, SchedulerConfig
 
 
 class RequestAllFinished(Exception):
-    pass
+    """Raised by the offline input when the scheduler waits for work and none is queued."""
 
 
-@dataclass
-class RequestStatus:
-    uid: int
-    input_ids: List[int]
-    output_ids: List[int]
-
-
-def _tp_from_env() -> Tuple[DistributedInfo, bool]:
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    if ws > 1:
-        return DistributedInfo(int(os.environ["RANK"]), ws), True
-    return DistributedInfo(0, 1), False
+def _rank_from_env() -> Tuple[DistributedInfo, bool]:
+    """(tp_info, launched by torchrun) from the launcher's environment."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world <= 1:
+        return DistributedInfo(0, 1), False
+    return DistributedInfo(int(os.environ["RANK"]), world), True
 
 
 class LLM(Scheduler):
     def __init__(self, model_path: str, dtype: torch.dtype = torch.bfloat16, **kwargs):
-        info, external = _tp_from_env()
+        info, external = _rank_from_env()
         kwargs.setdefault("tp_info", info)
         kwargs.setdefault("external_process_group", external)
-        config = SchedulerConfig(model_path=model_path, dtype=dtype, offline_mode=True, **kwargs)
-        super().__init__(config)
-        self.pending_requests: List[Tuple[List[int] | str, SamplingParams]] = []
-        self.status_map: Dict[int, RequestStatus] = {}
-        self.counter = 0
+        super().__init__(SchedulerConfig(model_path=model_path, dtype=dtype, offline_mode=True, **kwargs))
+        self._queue: Deque[Tuple[int, object, SamplingParams]] = collections.deque()
+        self._outputs: Dict[int, List[int]] = {}
 
-    def _tokenize_one(self, prompt) -> torch.Tensor:
+    def _as_ids(self, prompt) -> torch.Tensor:
         if isinstance(prompt, str):
             return torch.tensor(self.tokenizer.encode(prompt), dtype=torch.int32)
         if isinstance(prompt, torch.Tensor):
@@ -56,43 +54,36 @@ class LLM(Scheduler):
         return torch.tensor(prompt, dtype=torch.int32)
 
     def offline_receive_msg(self, blocking: bool = False) -> List[BaseBackendMsg]:
-        if blocking and not self.pending_requests:
-            raise RequestAllFinished()
-        out: List[BaseBackendMsg] = []
-        total = 0
-        taken = 0
-        for prompt, sp in self.pending_requests:
-            if total >= self.prefill_budget:
-                break
-            ids = self._tokenize_one(prompt)
-            total += len(ids)
-            uid = self.counter + taken
-            taken += 1
-            out.append(UserMsg(uid=uid, input_ids=ids, sampling_params=SamplingParams(**vars(sp))))
-            self.status_map[uid] = RequestStatus(uid, ids.tolist(), [])
-        self.counter += taken
-        self.pending_requests = self.pending_requests[taken:]
-        return out
+        if not self._queue:
+            if blocking:
+                raise RequestAllFinished()
+            return []
+        msgs: List[BaseBackendMsg] = []
+        tokens = 0
+        while self._queue and tokens < self.prefill_budget:
+            uid, prompt, sp = self._queue.popleft()
+            ids = self._as_ids(prompt)
+            tokens += int(ids.numel())
+            # the scheduler may clamp max_tokens; the caller's object stays untouched
+            msgs.append(UserMsg(uid=uid, input_ids=ids, sampling_params=dataclasses.replace(sp)))
+        return msgs
 
     def offline_send_result(self, reply: List[DetokenizeMsg]) -> None:
         for msg in reply:
-            st = self.status_map[msg.uid]
             if not msg.eos:  # a stopping EOS is not output; with ignore_eos it is an ordinary token
-                st.output_ids.append(msg.next_token)
+                self._outputs[msg.uid].append(msg.next_token)
 
-    def generate(self, prompts, sampling_params) -> List[Dict[str, object]]:
-        self.pending_requests = []
-        self.status_map = {}
-        self.counter = 0
+    def generate(self, prompts: Sequence, sampling_params: SamplingParams | Sequence[SamplingParams]
+                 ) -> List[Dict[str, object]]:
         if isinstance(sampling_params, SamplingParams):
             sampling_params = [sampling_params] * len(prompts)
-        self.pending_requests = list(zip(prompts, sampling_params))
+        if len(sampling_params) != len(prompts):
+            raise ValueError(f"{len(prompts)} prompts but {len(sampling_params)} sampling params")
+        self._queue = collections.deque((uid, p, sp) for uid, (p, sp) in enumerate(zip(prompts, sampling_params)))
+        self._outputs = {uid: [] for uid in range(len(prompts))}
         try:
             self.run_forever()
         except RequestAllFinished:
             pass
-        results = []
-        for i in range(len(prompts)):
-            st = self.status_map[i]
-            results.append({"text": self.tokenizer.decode(st.output_ids), "token_ids": st.output_ids})
-        return results
+        return [{"text": self.tokenizer.decode(ids), "token_ids": ids}
+                for ids in (self._outputs[uid] for uid in range(len(prompts)))]

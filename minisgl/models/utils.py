@@ -89,7 +89,9 @@ class MoEMLP(BaseOP):
         logits = getattr(self, self._router_name).forward(x)
         return self.experts.forward(x, logits)
 
-    output_unreduced = False
+    @property
+    def output_unreduced(self) -> bool:
+        return self.experts.deferred
 
 
 class RopeAttn(BaseOP):
@@ -133,9 +135,13 @@ class DecoderLayer(BaseOP):
         self.post_attention_layernorm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
         self._layer_id = layer_id
         # at TP > 1 the row-parallel outputs are reduced by the norms that follow them (fused)
+        # (every reduction whose result feeds a norm is deferred to it, so with the NVLS row-sharded
+        # form the residual stream is only ever read by the fused norms)
         self.self_attn.o_proj.defer_to_norm = True
         if isinstance(self.mlp, GatedMLP):
             self.mlp.down_proj.defer_to_norm = True
+        else:
+            self.mlp.experts.defer_to_norm = True
 
     @nvtx_annotate("Layer_{}", layer_id_field="_layer_id")
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None,

@@ -1,4 +1,11 @@
-"""Scheduler configuration (reference: python/minisgl/scheduler/config.py:14-41)."""
+"""Scheduler configuration (reference: python/minisgl/scheduler/config.py:14-41).
+
+The public fields and their defaults are the reference's: ``max_extend_tokens`` (the prefill chunk
+size), ``cache_type`` (``radix`` | ``naive``) and ``offline_mode``. Every ZeroMQ endpoint of one
+server is an IPC socket under /tmp named after its channel and the process that built the config,
+so two servers on one machine never share a socket and every child process (which receives a copy
+of the config) derives the same names.
+"""
 
 from __future__ import annotations
 
@@ -7,9 +14,9 @@ from dataclasses import dataclass, field
 
 from minisgl.engine.config import EngineConfig
 
-
-def _pid_suffix() -> str:
-    return f".pid={os.getpid()}"
+# channel -> socket number: scheduler input, detokenizer input, rank-0 -> rank-N fan-out,
+# frontend input, tokenizer input (the last two are used by the server, minisgl/server/args.py)
+IPC_CHANNELS = {"backend": 0, "detokenizer": 1, "broadcast": 2, "frontend": 3, "tokenizer": 4}
 
 
 @dataclass(frozen=True)
@@ -17,24 +24,31 @@ class SchedulerConfig(EngineConfig):
     max_extend_tokens: int = 8192
     cache_type: str = "radix"
     offline_mode: bool = False
-    _unique_suffix: str = field(default_factory=_pid_suffix)
+    ipc_owner: int = field(default_factory=os.getpid)
+
+    def ipc_addr(self, channel: str) -> str:
+        return f"ipc:///tmp/minisgl_{IPC_CHANNELS[channel]}.pid={self.ipc_owner}"
 
     @property
     def zmq_backend_addr(self) -> str:
-        return "ipc:///tmp/minisgl_0" + self._unique_suffix
+        return self.ipc_addr("backend")
 
     @property
     def zmq_detokenizer_addr(self) -> str:
-        return "ipc:///tmp/minisgl_1" + self._unique_suffix
+        return self.ipc_addr("detokenizer")
 
     @property
     def zmq_scheduler_broadcast_addr(self) -> str:
-        return "ipc:///tmp/minisgl_2" + self._unique_suffix
+        return self.ipc_addr("broadcast")
 
     @property
     def max_forward_len(self) -> int:
+        # the longest forward is one full prefill chunk
         return self.max_extend_tokens
 
     @property
-    def backend_create_detokenizer_link(self) -> bool:
+    def scheduler_binds_detokenizer(self) -> bool:
+        """Whether rank 0's scheduler creates (binds) the detokenizer socket. Offline and
+        single-tokenizer setups have it bind; the server with separate tokenizer workers has the
+        detokenizer bind instead."""
         return True

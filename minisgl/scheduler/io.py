@@ -36,7 +36,7 @@ class SchedulerIOMixin:
             )
             self._send_into_tokenizer = ZmqPushQueue(
                 config.zmq_detokenizer_addr,
-                create=config.backend_create_detokenizer_link,
+                create=config.scheduler_binds_detokenizer,
                 encoder=BaseTokenizerMsg.encoder,
             )
             self._queues += [self._recv_from_tokenizer, self._send_into_tokenizer]

@@ -22,7 +22,6 @@ from minisgl.kvcache import BaseCacheHandle
 from .cache import CacheManager
 from .decode import DecodeManager
 from .table import TableManager
-from .utils import PendingReq
 
 
 class ChunkedReq(Req):
@@ -34,6 +33,22 @@ class ChunkedReq(Req):
         return False
 
 
+class Waiting:
+    """A request in the prefill queue: its prompt, its output budget and, after its first chunk
+    ran, the ``ChunkedReq`` that carries its page-table row, slots and cache handle to the next
+    chunk."""
+
+    __slots__ = ("uid", "input_ids", "sampling_params", "prompt_len", "budget", "chunk")
+
+    def __init__(self, uid: int, input_ids: torch.Tensor, sampling_params) -> None:
+        self.uid = uid
+        self.input_ids = input_ids
+        self.sampling_params = sampling_params
+        self.prompt_len = int(input_ids.shape[0])
+        self.budget = int(sampling_params.max_tokens)
+        self.chunk: ChunkedReq | None = None
+
+
 @dataclass
 class PrefillAdder:
     token_budget: int
@@ -41,11 +56,11 @@ class PrefillAdder:
     cache_manager: CacheManager
     table_manager: TableManager
 
-    def _admit(self, p: PendingReq) -> Tuple[BaseCacheHandle, int, np.ndarray] | None:
+    def _admit(self, p: Waiting) -> Tuple[BaseCacheHandle, int, np.ndarray] | None:
         if self.table_manager.available_size == 0:
             return None
         handle = self.cache_manager.match_req(p.input_ids).cuda_handle
-        need = p.input_len - handle.cached_len + p.output_len + self.cache_manager.page_size - 1
+        need = p.prompt_len - handle.cached_len + p.budget + self.cache_manager.page_size - 1
         if need + self.reserved_size > self.cache_manager.available_size:
             return None
         self.cache_manager.lock(handle)  # locking moves the match out of the evictable pool
@@ -55,8 +70,8 @@ class PrefillAdder:
         row = self.table_manager.allocate()
         return handle, row, np.asarray(handle.get_matched_indices(), dtype=np.int32)
 
-    def _make(self, p: PendingReq, handle, row: int, cached_len: int, slots: np.ndarray) -> Req:
-        remain = p.input_len - cached_len
+    def _make(self, p: Waiting, handle, row: int, cached_len: int, slots: np.ndarray) -> Req:
+        remain = p.prompt_len - cached_len
         chunk = min(self.token_budget, remain)
         cls = ChunkedReq if chunk < remain else Req
         self.token_budget -= chunk
@@ -64,25 +79,25 @@ class PrefillAdder:
         # partial page. Every scheduling step builds a new adder whose base reservation covers only
         # running decode requests, so a continuing chunk is reserved again here, or requests
         # admitted behind it could take the pages its later chunks need.
-        self.reserved_size += remain + p.output_len + self.cache_manager.page_size - 1
+        self.reserved_size += remain + p.budget + self.cache_manager.page_size - 1
         req = cls(
             input_ids=p.input_ids[: cached_len + chunk],
             table_idx=row,
             cached_len=cached_len,
-            output_len=p.output_len,
+            output_len=p.budget,
             uid=p.uid,
             sampling_params=p.sampling_params,
             cache_handle=handle,
         )
         req.slots = slots
         # a fresh admission with a cache hit must publish the matched slots to its page-table row
-        req.pending_prefix = cached_len if p.chunked_req is None else 0
+        req.pending_prefix = cached_len if p.chunk is None else 0
         return req
 
-    def try_add_one(self, p: PendingReq) -> Req | None:
+    def try_add_one(self, p: Waiting) -> Req | None:
         if self.token_budget <= 0:
             return None
-        if (c := p.chunked_req) is not None:
+        if (c := p.chunk) is not None:
             return self._make(p, c.cache_handle, c.table_idx, c.cached_len, c.slots)
         got = self._admit(p)
         if got is None:
@@ -96,10 +111,10 @@ class PrefillManager:
     cache_manager: CacheManager
     table_manager: TableManager
     decode_manager: DecodeManager
-    pending_list: List[PendingReq] = field(default_factory=list)
+    pending_list: List[Waiting] = field(default_factory=list)
 
     def add_one_req(self, msg) -> None:
-        self.pending_list.append(PendingReq(msg.uid, msg.input_ids, msg.sampling_params))
+        self.pending_list.append(Waiting(msg.uid, msg.input_ids, msg.sampling_params))
 
     def schedule_next_batch(self, prefill_budget: int) -> Batch | None:
         if not self.pending_list:
@@ -111,13 +126,13 @@ class PrefillManager:
             table_manager=self.table_manager,
         )
         reqs: List[Req] = []
-        chunked: List[PendingReq] = []
+        chunked: List[Waiting] = []
         for p in self.pending_list:
             r = adder.try_add_one(p)
             if r is None:
                 break
-            p.chunked_req = r if isinstance(r, ChunkedReq) else None
-            if p.chunked_req is not None:
+            p.chunk = r if isinstance(r, ChunkedReq) else None
+            if p.chunk is not None:
                 chunked.append(p)
             reqs.append(r)
         if not reqs:
@@ -129,7 +144,7 @@ class PrefillManager:
         for i, p in enumerate(self.pending_list):
             if p.uid == uid:
                 self.pending_list.pop(i)
-                return p.chunked_req
+                return p.chunk
         return None
 
     @property

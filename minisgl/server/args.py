@@ -31,18 +31,18 @@ class ServerArgs(SchedulerConfig):
 
     @property
     def zmq_frontend_addr(self) -> str:
-        return "ipc:///tmp/minisgl_3" + self._unique_suffix
+        return self.ipc_addr("frontend")
 
     @property
     def zmq_tokenizer_addr(self) -> str:
-        return self.zmq_detokenizer_addr if self.share_tokenizer else "ipc:///tmp/minisgl_4" + self._unique_suffix
+        return self.zmq_detokenizer_addr if self.share_tokenizer else self.ipc_addr("tokenizer")
 
     @property
     def tokenizer_create_addr(self) -> bool:
         return self.share_tokenizer
 
     @property
-    def backend_create_detokenizer_link(self) -> bool:
+    def scheduler_binds_detokenizer(self) -> bool:
         return not self.share_tokenizer
 
     @property

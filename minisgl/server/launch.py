@@ -17,6 +17,9 @@ def _run_scheduler(args, ack_queue) -> None:
     import torch
 
     from minisgl.scheduler import Scheduler
+    from minisgl.utils.proc import die_with_parent
+
+    die_with_parent()  # a rank never outlives the server process that spawned it
 
     with torch.inference_mode():
         sched = Scheduler(args)

@@ -41,6 +41,9 @@ def tokenize_worker(*, tokenizer_path: str, addr: str, create: bool, backend_add
                     ack_queue=None) -> None:
     from minisgl.utils.hf import load_tokenizer
     from minisgl.utils.mp import ZmqPullQueue, ZmqPushQueue
+    from minisgl.utils.proc import die_with_parent
+
+    die_with_parent()  # the worker never outlives the server process that spawned it
 
     from .detokenize import DetokenizeManager
     from .tokenize import TokenizeManager

@@ -96,6 +96,7 @@ torch.cuda.set_device(rank)
 dev = torch.device("cuda", rank)
 dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
 cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=60))
+from minisgl import ops
 from minisgl._native import cuda
 from minisgl.parallel.nvls import NvlsNormComm
 try:
@@ -108,61 +109,109 @@ except RuntimeError as e:
 H, eps = 5120, 1e-6
 g = torch.Generator(device="cpu").manual_seed(1234)
 w = (torch.rand(H, generator=g) + 0.5).to(dev, torch.bfloat16)
-# T x world x H x 4 <= 2 MiB uses the LL form (T <= 51 at 2 ranks), larger T the reduce form; alternate them
+
+
+def expected(x, res0):
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x)
+    s = torch.stack([p.float() for p in parts]).sum(0)
+    if res0 is not None:
+        s = s + res0.float()
+    r = s.to(torch.bfloat16)
+    r32 = r.float()
+    return r, (r32 * torch.rsqrt(r32.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(torch.bfloat16)
+
+
+def check(T, res, out, exp_res, exp_out):
+    # the RS form keeps only this rank's residual rows (i % world == rank); LL keeps them all
+    rows = torch.arange(T, device=dev)
+    mine = rows if impl.is_ll(T, H) else rows[rows % world == rank]
+    torch.testing.assert_close(res[mine].float(), exp_res[mine].float(), atol=3e-2, rtol=2e-2)
+    torch.testing.assert_close(out.float(), exp_out.float(), atol=3e-2, rtol=2e-2)
+
+
+# LL for T x world x H x 4 <= 2 MiB (T <= 51 at 2 ranks, 12 at 8), RS above; alternate them
 for it, T in enumerate([1, 7, 128, 256, 129, 800, 3, 256, 1, 400, 2, 64]):
     gp = torch.Generator(device="cpu").manual_seed(100 * it + rank)
     x = torch.randn(T, H, generator=gp).to(dev, torch.bfloat16)
     gr = torch.Generator(device="cpu").manual_seed(100 * it + 77)
     first = it % 4 == 0
     res0 = None if first else torch.randn(T, H, generator=gr).to(dev, torch.bfloat16)
-    parts = [torch.empty_like(x) for _ in range(world)]
-    dist.all_gather(parts, x)
-    s = torch.stack([p.float() for p in parts]).sum(0)
-    if res0 is not None:
-        s = s + res0.float()
-    exp_res = s.to(torch.bfloat16)
-    r32 = exp_res.float()
-    exp_out = (r32 * torch.rsqrt(r32.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(torch.bfloat16)
+    exp_res, exp_out = expected(x, res0)
     if it == 2 and rank == 0:
         torch.cuda._sleep(5_000_000)  # a lagging rank
     res = None if first else res0.clone()
     out, res = impl.all_reduce_add_rmsnorm(x, res, w, eps)
     torch.cuda.synchronize()
-    torch.testing.assert_close(res.float(), exp_res.float(), atol=3e-2, rtol=2e-2)
-    torch.testing.assert_close(out.float(), exp_out.float(), atol=3e-2, rtol=2e-2)
-# CUDA-graph replays: the per-CTA epochs keep advancing across replays of one captured sequence
-# (LL and reduce forms alternating); a different rank lags before each replay
-Ts = [4, 300, 8, 300]
+    check(T, res, out, exp_res, exp_out)
+
+# GEMM fused with the collective: the row-parallel GEMM writes this rank's staging region and
+# signals arrival itself; the partial sums are the same GEMM's output through the plain path
+for it, (T, K) in enumerate([(64, 640), (256, 2560), (200, 640), (96, 4352), (256, 5120)]):
+    gp = torch.Generator(device="cpu").manual_seed(500 + 10 * it + rank)
+    xin = (torch.randn(T, K, generator=gp) * 0.5).to(dev, torch.bfloat16)
+    wt = (torch.randn(H, K, generator=gp) * 0.02).to(dev, torch.bfloat16)
+    gr = torch.Generator(device="cpu").manual_seed(900 + it)
+    res0 = torch.randn(T, H, generator=gr).to(dev, torch.bfloat16)
+    partial = ops.linear(xin, wt)
+    exp_res, exp_out = expected(partial, res0)
+    if it == 1 and rank == world - 1:
+        torch.cuda._sleep(5_000_000)
+    y = impl.linear_into_staging(xin, wt, None)
+    assert y is not None and not impl.is_ll(T, H)
+    res = res0.clone()
+    out, res = impl.all_reduce_add_rmsnorm(y, res, w, eps)
+    torch.cuda.synchronize()
+    check(T, res, out, exp_res, exp_out)
+
+# CUDA-graph replays: the per-CTA call counters keep advancing across replays of one captured
+# sequence (LL, RS and GEMM-fused RS calls interleaved); a different rank lags before each replay.
+# An RS call's output is a view of the gather region, overwritten by the next RS call, so each
+# result is copied out right after its call (as the GEMM that consumes it would read it).
+Ts = [4, 300, 8, 300, 128]
 xs, res0, exp = [], [], []
 for i, T in enumerate(Ts):
     gp = torch.Generator(device="cpu").manual_seed(1000 + 10 * i + rank)
-    xs.append(torch.randn(T, H, generator=gp).to(dev, torch.bfloat16))
+    if i == 4:  # GEMM-fused call: K = 640, the input is [T, K]
+        xin = (torch.randn(T, 640, generator=gp) * 0.5).to(dev, torch.bfloat16)
+        wt = (torch.randn(H, 640, generator=gp) * 0.02).to(dev, torch.bfloat16)
+        xs.append((xin, wt))
+        part = ops.linear(xin, wt)
+    else:
+        xs.append(torch.randn(T, H, generator=gp).to(dev, torch.bfloat16))
+        part = xs[i]
     gr = torch.Generator(device="cpu").manual_seed(2000 + i)
     res0.append(torch.randn(T, H, generator=gr).to(dev, torch.bfloat16))
-    parts = [torch.empty_like(xs[i]) for _ in range(world)]
-    dist.all_gather(parts, xs[i])
-    r32 = (torch.stack([p.float() for p in parts]).sum(0) + res0[i].float()).to(torch.bfloat16).float()
-    exp.append((r32 * torch.rsqrt(r32.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(torch.bfloat16))
+    exp.append(expected(part, res0[i])[1])
 res = [r.clone() for r in res0]
-outs = [None] * len(Ts)
-side = torch.cuda.Stream()
-with torch.cuda.stream(side):
+saved = [torch.empty(T, H, dtype=torch.bfloat16, device=dev) for T in Ts]
+
+
+def sequence():
     for i in range(len(Ts)):
         res[i].copy_(res0[i])
-        impl.all_reduce_add_rmsnorm(xs[i], res[i], w, eps)
+        if i == 4:
+            y = impl.linear_into_staging(xs[i][0], xs[i][1], None)
+        else:
+            y = xs[i]
+        out, _ = impl.all_reduce_add_rmsnorm(y, res[i], w, eps)
+        saved[i].copy_(out)
+
+
+side = torch.cuda.Stream()
+with torch.cuda.stream(side):
+    sequence()
 torch.cuda.synchronize()
 graph = torch.cuda.CUDAGraph()
 with torch.cuda.graph(graph, stream=side):
-    for i in range(len(Ts)):
-        res[i].copy_(res0[i])
-        outs[i], _ = impl.all_reduce_add_rmsnorm(xs[i], res[i], w, eps)
+    sequence()
 for rep in range(6):
     if rank == rep % world:
         torch.cuda._sleep(3_000_000)
     graph.replay()
     torch.cuda.synchronize()
     for i in range(len(Ts)):
-        torch.testing.assert_close(outs[i].float(), exp[i].float(), atol=3e-2, rtol=2e-2)
+        torch.testing.assert_close(saved[i].float(), exp[i].float(), atol=3e-2, rtol=2e-2)
 del graph
 assert cuda().get_error()[0] == 0
 dist.barrier(group=cpu)

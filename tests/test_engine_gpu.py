@@ -1,5 +1,16 @@
-"""End-to-end engine on the GPU: the bf16 sm_100a path against the fp32 CPU oracle, and
-CUDA-graph / overlap scheduling against plain eager execution."""
+"""End-to-end engine on the GPU against the fp32 CPU oracle (the same engine on ``device="cpu"``,
+reference ops in float32), plus CUDA-graph / overlap scheduling against plain eager execution and
+tensor parallelism on 2 and 4 GPUs.
+
+Logits are compared directly: the engine's sampler is tapped so every row it samples from is
+recorded per request. Greedy decoding is checked with teacher forcing: each token the GPU picks at
+step j must be the oracle's argmax after the prompt plus the GPU's first j tokens, or within the bf16
+logit error of it (a near-tie, where bf16 and fp32 may legitimately choose differently)."""
+
+import json
+import os
+import subprocess
+import sys
 
 import pytest
 import torch
@@ -8,6 +19,11 @@ from minisgl.core import SamplingParams
 from minisgl.models.synthetic import make_checkpoint
 
 pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PRESETS = ["tiny-qwen3", "tiny-llama", "tiny-qwen2", "tiny-qwen3-moe", "tiny-gpt-oss"]
+# bf16 end to end (weights, activations, KV cache) vs fp32 on these 2-layer models: logits differ by
+# well under this (absolute; logits are O(1)); a choice within it of the oracle's best is a near-tie
+LOGIT_TOL = 0.06
 
 
 def _prompts(n, vocab, seed=0, lo=16, hi=64):
@@ -16,34 +32,108 @@ def _prompts(n, vocab, seed=0, lo=16, hi=64):
             for _ in range(n)]
 
 
-def _run(path, prompts, sp, port, **kw):
+class _Tap:
+    """Records, per request uid, every logits row the engine's sampler receives."""
+
+    def __init__(self, llm):
+        eng = llm.engine
+        self.rows = {}
+        fwd, sample = eng.forward_batch, eng.sampler.sample
+        cur = []
+
+        def forward_batch(batch, args, dev):
+            cur[:] = [r.uid for r in batch.reqs]
+            return fwd(batch, args, dev)
+
+        def tapped(logits, args):
+            for i, uid in enumerate(cur):
+                self.rows.setdefault(uid, []).append(logits[i].float().cpu())
+            return sample(logits, args)
+
+        eng.forward_batch = forward_batch
+        eng.sampler.sample = tapped
+
+
+def _run(path, prompts, sp, port, tap=False, **kw):
     from minisgl.llm import LLM
 
     llm = LLM(path, distributed_port=port, **kw)
+    t = _Tap(llm) if tap else None
     try:
         out = [o["token_ids"] for o in llm.generate(prompts, sp)]
         llm.cache_manager.check_integrity()
-        from minisgl._native import cuda
-
         if llm.engine.is_cuda:
+            from minisgl._native import cuda
+
             code, info = cuda().get_error()
             assert code == 0, (code, info)
     finally:
         llm.shutdown()
-    return out
+    return (out, t.rows) if tap else out
 
 
-@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-llama", "tiny-qwen2", "tiny-qwen3-moe"])
-def test_gpu_first_tokens_match_oracle(tmp_path, preset, free_port):
+def _oracle_logits(path, prompts, port):
+    """fp32 CPU logits after each prompt (one row per prompt)."""
+    _, rows = _run(path, prompts, SamplingParams(max_tokens=1, ignore_eos=True), port, tap=True,
+                   dtype=torch.float32, device="cpu", max_running_req=64)
+    return [rows[i][0] for i in range(len(prompts))]
+
+
+def _check_against_oracle(path, prompts, outs, port, tol=LOGIT_TOL):
+    """Teacher-forced check of greedy sequences `outs` (one per prompt) on the fp32 oracle."""
+    forced, where = [], []
+    for i, (p, o) in enumerate(zip(prompts, outs)):
+        for j in range(len(o)):
+            forced.append(p + o[:j])
+            where.append((i, j))
+    rows = _oracle_logits(path, forced, port)
+    worst, exact = 0.0, 0
+    for (i, j), row in zip(where, rows):
+        tok = outs[i][j]
+        gap = float(row.max() - row[tok])
+        worst = max(worst, gap)
+        exact += int(gap == 0.0)
+        assert gap <= tol, f"prompt {i} step {j}: token {tok} is {gap:.4f} below the oracle's best"
+    return worst, exact / len(where)
+
+
+@pytest.mark.parametrize("preset", PRESETS)
+def test_gpu_prefill_logits_match_oracle(tmp_path, preset, free_port):
+    """Full-vocabulary logits after the prompt: bf16 GPU vs fp32 CPU, and the greedy first token
+    wherever the oracle's top two are further apart than the tolerance."""
     if not torch.cuda.is_available():
         pytest.skip("no GPU")
     path = make_checkpoint(preset, str(tmp_path / preset), dtype=torch.bfloat16)
     prompts = _prompts(16, 1024)
     sp = SamplingParams(max_tokens=1, ignore_eos=True)
-    gpu = _run(path, prompts, sp, free_port, dtype=torch.bfloat16, max_running_req=32, num_page_override=4096)
-    cpu = _run(path, prompts, sp, free_port + 1, dtype=torch.float32, device="cpu", max_running_req=32)
-    agree = sum(a == b for a, b in zip(gpu, cpu)) / len(gpu)
-    assert agree >= 0.8, (gpu, cpu)
+    _, gpu = _run(path, prompts, sp, free_port, tap=True, dtype=torch.bfloat16, max_running_req=32,
+                  num_page_override=4096)
+    cpu = _oracle_logits(path, prompts, free_port + 1)
+    for i in range(len(prompts)):
+        g, c = gpu[i][0], cpu[i]
+        assert g.shape == c.shape
+        err = float((g - c).abs().max())
+        cos = float(torch.nn.functional.cosine_similarity(g, c, dim=0))
+        assert err <= LOGIT_TOL and cos >= 0.999, (preset, i, err, cos)
+        top2 = torch.topk(c, 2).values
+        if float(top2[0] - top2[1]) > 2 * LOGIT_TOL:
+            assert int(g.argmax()) == int(c.argmax()), (preset, i)
+
+
+@pytest.mark.parametrize("preset", PRESETS)
+def test_gpu_decode_tracks_oracle(tmp_path, preset, free_port):
+    """16 greedy tokens per prompt through CUDA graphs and overlap scheduling, every step checked
+    against the oracle with teacher forcing."""
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    path = make_checkpoint(preset, str(tmp_path / preset), dtype=torch.bfloat16)
+    prompts = _prompts(12, 1024, seed=5)
+    sp = SamplingParams(max_tokens=16, ignore_eos=True)
+    outs = _run(path, prompts, sp, free_port, dtype=torch.bfloat16, max_running_req=32, num_page_override=4096,
+                cuda_graph_max_bs=16)
+    assert all(len(o) == 16 for o in outs)
+    worst, exact = _check_against_oracle(path, prompts, outs, free_port + 1)
+    assert exact >= 0.9, (worst, exact)  # near-ties are rare; most steps pick the oracle's exact argmax
 
 
 def test_graphs_and_overlap_are_consistent(tmp_path, free_port, monkeypatch):
@@ -62,3 +152,60 @@ def test_graphs_and_overlap_are_consistent(tmp_path, free_port, monkeypatch):
     # chunked prefill + radix cache hits on a repeated workload keep the same greedy tokens
     c = _run(path, prompts + prompts[:4], sp, free_port + 2, cuda_graph_max_bs=8, max_extend_tokens=64, **kw)
     assert c[:24] == a and c[24:] == a[:4]
+
+
+TP_WORKER = r"""
+import json, os, sys
+sys.path.insert(0, {root!r})
+import torch
+from minisgl.core import SamplingParams
+from minisgl.llm import LLM
+prompts = json.loads(os.environ["TP_PROMPTS"])
+llm = LLM({path!r}, dtype=torch.bfloat16, max_running_req=32, num_page_override=4096, cuda_graph_max_bs=16,
+          comm=os.environ["TP_COMM"], distributed_timeout=120)
+out = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=16, ignore_eos=True))]
+llm.cache_manager.check_integrity()
+from minisgl._native import cuda
+assert cuda().get_error()[0] == 0
+if int(os.environ["RANK"]) == 0:
+    print("RESULT " + json.dumps(out), flush=True)
+llm.shutdown()
+"""
+
+
+@pytest.mark.multigpu
+@pytest.mark.parametrize("comm", ["auto", "nccl"])
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_engine_tracks_oracle(tmp_path, free_port, world, comm):
+    """TP2 / TP4 on real GPUs (one process per GPU, launched like torchrun), with the fused NVLS /
+    peer collectives (`auto`) and with NCCL: every greedy step matches the fp32 oracle (teacher
+    forced), and most sequences equal the TP1 GPU run exactly. Exact equality with TP1 is not
+    required everywhere: TP ranks round their partial sums to bf16 before the reduction, so a
+    near-tie may resolve differently."""
+    n = torch.cuda.device_count() if torch.cuda.is_available() else 0
+    if n < world:
+        pytest.skip(f"needs {world} GPUs")
+    path = make_checkpoint("tiny-qwen3", str(tmp_path / "m"), dtype=torch.bfloat16)
+    prompts = _prompts(12, 1024, seed=7)
+    tp1 = _run(path, prompts, SamplingParams(max_tokens=16, ignore_eos=True), free_port, dtype=torch.bfloat16,
+               max_running_req=32, num_page_override=4096, cuda_graph_max_bs=16)
+    script = tmp_path / "worker.py"
+    script.write_text(TP_WORKER.format(root=ROOT, path=path))
+    procs = []
+    for r in range(world):
+        env = dict(os.environ, RANK=str(r), LOCAL_RANK=str(r), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(free_port + 11), TP_PROMPTS=json.dumps(prompts), TP_COMM=comm, PYTHONPATH=ROOT)
+        procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    try:
+        outs = [p.communicate(timeout=600)[0] for p in procs]
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+    assert all(p.returncode == 0 for p in procs), outs
+    line = [l for l in outs[0].splitlines() if l.startswith("RESULT ")][0]
+    tpn = json.loads(line[len("RESULT "):])
+    _check_against_oracle(path, prompts, tpn, free_port + 2)
+    same = sum(a == b for a, b in zip(tpn, tp1))
+    assert same >= len(prompts) // 2, (same, tpn, tp1)

@@ -205,10 +205,21 @@ def _paged_pages_setup(lens_kv, nq, nkv, hd, page, seed=0):
 def test_attention_decode_paged(hd, nq, nkv, page, window, sinks, num_ctas):
     """Persistent paged decode (work list, TMA page loads, last-arriver combine) against the fp32
     reference; few CTAs force multi-chunk requests; run twice to check the counters return to zero."""
+    _paged_decode_case(hd, nq, nkv, page, window, sinks, num_ctas, [1, 5, 64, 65, 300, 1000, 777, 4000, 129])
+
+
+@pytest.mark.parametrize("page", [16, 64])
+@pytest.mark.parametrize("num_ctas", [148, 2])
+def test_attention_decode_paged_short_window(page, num_ctas):
+    """gpt-oss-style decode: head_dim 64, 2 query heads per kv head, a 16-token sliding window and
+    sinks, on requests around the window length (every kv length from 1 to 48)."""
+    _paged_decode_case(64, 4, 2, page, 16, True, num_ctas, list(range(1, 49)))
+
+
+def _paged_decode_case(hd, nq, nkv, page, window, sinks, num_ctas, lens_kv):
     from minisgl.attention.paged import decode_work_list
     import numpy as np
 
-    lens_kv = [1, 5, 64, 65, 300, 1000, 777, 4000, 129]
     B = len(lens_kv)
     q, kc, vc, pt, rows, cu, kvl = _paged_pages_setup(lens_kv, nq, nkv, hd, page)
     sk = torch.randn(nq, device=DEV) if sinks else None
@@ -446,3 +457,40 @@ def test_moe_forward(T, E, topk, H, I, act, renorm, after, bias):
                         None if b1 is None else sub(b1).cpu(), None if b2 is None else sub(b2).cpu(), after,
                         expert_offset=e0)
     _close(out, exp, 3e-2, 3e-2)
+
+
+@pytest.mark.parametrize("n_tok,n_writes", [(1, 1), (256, 256), (5000, 5064), (16384, 16384)])
+def test_plan_apply_gather_scatter(n_tok, n_writes):
+    """Batch metadata kernel: page-table writes then the out_loc gather (which must see them), and
+    the int32 gather / scatter of decode input ids and sampled tokens, against torch indexing."""
+    g = torch.Generator(device="cpu").manual_seed(n_tok)
+    rows, cols = 300, 4096
+    pt = torch.randint(0, 1 << 20, (rows, cols), generator=g, dtype=torch.int32)
+    # distinct (row, pos) write targets; the tokens read some of them and some untouched entries
+    flat = torch.randperm(rows * cols, generator=g)[:n_writes]
+    pt_rows, pt_pos = (flat // cols).to(torch.int32), (flat % cols).to(torch.int32)
+    pt_slots = torch.randint(0, 1 << 20, (n_writes,), generator=g, dtype=torch.int32)
+    pick = torch.randint(0, rows * cols, (n_tok,), generator=g)
+    pick[: n_tok // 2] = flat[torch.randint(0, n_writes, (n_tok // 2,), generator=g)]
+    tok_rows, positions = (pick // cols).to(torch.int32), (pick % cols).to(torch.int32)
+    exp_pt = pt.clone()
+    exp_pt[pt_rows.long(), pt_pos.long()] = pt_slots
+    exp_loc = exp_pt[tok_rows.long(), positions.long()]
+    dpt = pt.to(DEV)
+    out_loc = torch.empty(n_tok, dtype=torch.int32, device=DEV)
+    _c().plan_apply(dpt, pt_rows.to(DEV), pt_pos.to(DEV), pt_slots.to(DEV), tok_rows.to(DEV), positions.to(DEV),
+                    out_loc)
+    assert torch.equal(dpt.cpu(), exp_pt)
+    assert torch.equal(out_loc.cpu(), exp_loc)
+    src = torch.randint(-1000, 1000, (rows + 2,), generator=g, dtype=torch.int32)
+    idx = torch.randint(0, rows + 2, (n_tok,), generator=g, dtype=torch.int32)
+    dst = torch.empty(n_tok, dtype=torch.int32, device=DEV)
+    _c().gather_i32(dst, src.to(DEV), idx.to(DEV))
+    assert torch.equal(dst.cpu(), src[idx.long()])
+    uniq = torch.randperm(rows + 2, generator=g)[: min(n_tok, rows + 2)].to(torch.int32)
+    vals = torch.randint(-1000, 1000, (uniq.numel(),), generator=g, dtype=torch.int32)
+    sc = src.to(DEV)
+    _c().scatter_i32(sc, uniq.to(DEV), vals.to(DEV))
+    exp = src.clone()
+    exp[uniq.long()] = vals
+    assert torch.equal(sc.cpu(), exp)

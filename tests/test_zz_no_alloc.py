@@ -8,29 +8,26 @@ rejected without launching anything. This file is collected last on purpose.
 """
 
 import ctypes
-import glob
 import math
-import os
 
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 SCRATCH_BYTES = 8 << 20
 
 
 def _lib():
     from minisgl._native import cuda
 
-    cuda()  # loads torch's libraries and the extension into the process first
-    so = glob.glob(os.path.join(ROOT, "minisgl", "_cuda*.so"))
-    assert so, "CUDA extension not built"
-    lib = ctypes.CDLL(so[0])
+    mod = cuda()  # loads torch's libraries and the release extension into the process first
+    # the exact shared object behind the module the other assertions read (not the bounds-check
+    # build, whose scratch array and device error word are separate copies)
+    lib = ctypes.CDLL(mod.__file__)
     fn = lib.msgl_attention_decode_noalloc
     P, I, L = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
-    fn.argtypes = [P, P, P, P, P, L, P, P, I, I, I, I, L, ctypes.c_float, I, P, I, P]
+    fn.argtypes = [P, P, P, P, P, L, P, P, I, I, I, I, L, L, ctypes.c_float, I, P, I, P]
     fn.restype = ctypes.c_int
     return fn
 
@@ -55,7 +52,7 @@ def _setup(bs, nq, nkv, hd, seed=0):
 def _call(fn, o, q, kc, vc, pt, rows, kvl, splits, sinks=None):
     bs, nq, hd = q.shape
     return fn(o.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), pt.data_ptr(), pt.stride(0),
-              rows.data_ptr(), kvl.data_ptr(), bs, nq, kc.shape[1], hd, kc.stride(0),
+              rows.data_ptr(), kvl.data_ptr(), bs, nq, kc.shape[1], hd, kc.stride(0), kc.shape[0],
               1.0 / math.sqrt(hd), -1, None if sinks is None else sinks.data_ptr(), splits,
               torch.cuda.current_stream().cuda_stream)
 
@@ -72,11 +69,17 @@ def test_noalloc_matches_workspace_entry_point(splits):
     ws = torch.empty(24 * 40 * splits * 130 * 4, dtype=torch.uint8, device="cuda")
     expect = torch.empty_like(q)
     cuda().attention_decode(expect, q, kc, vc, pt, rows, kvl, 1.0 / math.sqrt(128), -1, sinks, splits, ws)
+    from minisgl.ops import reference as ref
+
+    cu = torch.arange(q.shape[0] + 1, dtype=torch.int32)
+    fp32 = ref.paged_attention(q.cpu(), kc.cpu(), vc.cpu(), pt.cpu(), rows.cpu(), cu, kvl.cpu(),
+                               1.0 / math.sqrt(128), -1, sinks.cpu())
     for _ in range(2):  # the shared scratch keeps the previous call's contents
         out = torch.full_like(q, float("nan"))
         assert _call(fn, out, q, kc, vc, pt, rows, kvl, splits, sinks) == 0
         torch.cuda.synchronize()
         torch.testing.assert_close(out.float().cpu(), expect.float().cpu(), atol=2e-2, rtol=2e-2)
+        torch.testing.assert_close(out.float().cpu(), fp32.float(), atol=2e-2, rtol=2e-2)
     assert cuda().get_error()[0] == 0
 
 
