@@ -70,11 +70,42 @@ def _time(fn, stream, calls: int = 20, reps: int = 10) -> float:
     return ms
 
 
+def _trace(nvls, x, xin, wt, res, w, eps, rank: int, T: int) -> None:
+    """Phase spans (us) of one RS call, from the kernel's %globaltimer stamps: start (after the
+    producer wait) -> staged/arrived -> first barrier passed -> rows reduced, normalised and
+    gathered -> second arrival -> second barrier (CTA 0). Medians over the CTAs that own rows."""
+    import statistics
+
+    tr = torch.zeros(128 * 8, dtype=torch.int64, device=x.device)
+    out = {}
+    for name in ("stage", "gemm"):
+        for _ in range(3):
+            if name == "gemm":
+                y = nvls.linear_into_staging(xin, wt, None)
+                nvls.all_reduce_add_rmsnorm(y, res, w, eps, trace=tr)
+            else:
+                nvls.all_reduce_add_rmsnorm(x, res, w, eps, trace=tr)
+        torch.cuda.synchronize()
+        grid = min(128, -(-(-(-T // nvls.world)) // 2))  # the RS launch: two rows in flight per CTA
+        t = tr.view(128, 8)[:grid].cpu()
+        t0 = int(t[:, 0].min())
+        active = list(range(grid))
+        span = lambda i, j: statistics.median(float(t[b, j] - t[b, i]) / 1e3 for b in active)
+        out[name] = {"start_spread": round(float(t[:, 0].max() - t0) / 1e3, 2), "arrive1": round(span(0, 1), 2),
+                     "wait1": round(span(1, 2), 2), "rows": round(span(2, 3), 2), "arrive2": round(span(3, 4), 2),
+                     "wait2_cta0": round(float(t[0, 5] - t[0, 4]) / 1e3, 2),
+                     "total_cta0": round(float(t[0, 5] - t0) / 1e3, 2)}
+    if rank == 0:
+        print(json.dumps({"trace_tokens": T, **out}), flush=True)
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser("minisgl.benchmark.comm")
     ap.add_argument("--hidden", type=int, default=5120)
     ap.add_argument("--tokens", default="1,8,16,64,128,256,512")
     ap.add_argument("--k", type=int, default=0, help="GEMM input features per rank (0: 5120 / N)")
+    ap.add_argument("--trace", action="store_true",
+                    help="also print per-phase %%globaltimer spans of the reduce-scatter form (rank 0)")
     a = ap.parse_args(argv)
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -152,6 +183,8 @@ def main(argv=None) -> None:
                 row[f"{k}_us"] = round(v * 1e3, 2)
                 row[f"{k}_frac"] = round(r / v, 3)
             print(json.dumps(row), flush=True)
+        if a.trace and nvls is not None and not nvls.is_ll(T, H):
+            _trace(nvls, x, xin, wt, res, w, eps, rank, T)
     torch.cuda.synchronize()
     dist.barrier(group=cpu)
     if nvls is not None:

@@ -7,6 +7,7 @@ in ``MEASURED_PEAKS.json`` (fallback: 6.65 TB/s and 1.59 PFLOP/s). ``--once`` ru
 times without timing, which is the form to wrap in a profiler.
 
   gemm          bf16 GEMM  out[M, N] = x[M, K] @ w[N, K]^T  (--epi 0 bf16, 1 SiLU-gated, 3 fp32)
+  gemm-sweep    Qwen3-14B decode GEMMs per TP degree: automatic plan vs every forced tiling vs cuBLAS
   decode-attn   paged decode attention over a longest-first work list (page size 64)
   prefill-attn  ragged causal prefill attention (requests of 100..1024 tokens; --impl tcgen05 | mma)
   suite         every other hot kernel once at decode shapes (Qwen3-14B, --bs tokens; MoE at
@@ -250,9 +251,64 @@ def _suite(a, c) -> None:
     print("ok", c.get_error())
 
 
+def _gemm_sweep(a, c) -> None:
+    """Decode GEMMs of Qwen3-14B at each TP degree's per-rank shapes: the automatic plan, every
+    forced tiling (split count x 1-SM 128/256-row or 2-SM tiles) and cuBLAS (torch.matmul) on the
+    same shape. One JSON line per (tp, shape, tokens): times in us, best forced variant, cuBLAS."""
+    hbm, _ = _peaks()
+    H, I, nq, nkv, hd = 5120, 17408, 40, 8, 128
+    for tp in [int(t) for t in a.tps.split(",")]:
+        kv = max(1, nkv // tp)
+        shapes = {"qkv": ((nq // tp + 2 * kv) * hd, H, 0), "o": (H, nq * hd // tp, 0),
+                  "gate_up": (2 * I // tp, H, 1), "down": (H, I // tp, 0)}
+        for name, (N, K, epi) in shapes.items():
+            nw = max(2, int(3e8 // (N * K * 2)) + 1)
+            ws = [torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02 for _ in range(nw)]
+            wts = [w.t() for w in ws]
+            for M in [int(m) for m in a.ms.split(",")]:
+                x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+                out = torch.empty(M, N // 2 if epi == 1 else N, device="cuda", dtype=torch.bfloat16)
+                it = [0]
+
+                def ours(splits, wide):
+                    def run():
+                        c.gemm_ex(out, x, ws[it[0] % nw], None, epi, splits, wide)
+                        it[0] += 1
+                    return perf_cuda(run) * 1e3
+
+                def cublas():
+                    def run():
+                        torch.matmul(x, wts[it[0] % nw])
+                        it[0] += 1
+                    return perf_cuda(run) * 1e3
+
+                ours(-1, -1)  # warm the clocks and caches on this shape before timing anything
+                row = {"tp": tp, "shape": name, "M": M, "N": N, "K": K}
+                best = (1e9, None)
+                for wide in ([1, 2] if epi == 1 else [0, 1, 2]):
+                    for splits in (1, 2, 3, 4):  # the tilings the GPU tests cover
+                        if wide == 2 and splits > 3:
+                            continue
+                        try:
+                            t = ours(splits, wide)
+                        except RuntimeError:
+                            continue
+                        if t < best[0]:
+                            best = (t, f"wide{wide}/s{splits}")
+                row["auto_us"] = round(ours(-1, -1), 2)
+                row["best_us"], row["best"] = round(best[0], 2), best[1]
+                row["cublas_us"] = round(cublas(), 2) if epi == 0 else None
+                row["auto_hbm_frac"] = round(N * K * 2 / (row["auto_us"] * 1e-6) / hbm, 3)
+                print(json.dumps(row), flush=True)
+            del ws, wts
+    print("ok", c.get_error())
+
+
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    p.add_argument("op", choices=["gemm", "decode-attn", "prefill-attn", "suite"])
+    p.add_argument("op", choices=["gemm", "gemm-sweep", "decode-attn", "prefill-attn", "suite"])
+    p.add_argument("--tps", default="1,2,4,8", help="gemm-sweep: TP degrees")
+    p.add_argument("--ms", default="16,64,128,256", help="gemm-sweep: token counts")
     p.add_argument("--m", type=int, default=128)
     p.add_argument("--n", type=int, default=5120)
     p.add_argument("--k", type=int, default=5120)
@@ -267,7 +323,8 @@ def main(argv=None) -> None:
     from minisgl._native import cuda
 
     c = cuda()
-    {"gemm": _gemm, "decode-attn": _decode_attn, "prefill-attn": _prefill_attn, "suite": _suite}[a.op](a, c)
+    {"gemm": _gemm, "gemm-sweep": _gemm_sweep, "decode-attn": _decode_attn, "prefill-attn": _prefill_attn,
+     "suite": _suite}[a.op](a, c)
 
 
 if __name__ == "__main__":

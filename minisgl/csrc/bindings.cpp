@@ -113,6 +113,30 @@ void gemm(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tensor> 
   gemm_ex(out, x, w, bias, epi, -1, -1);
 }
 
+// Greedy pick fused into the LM-head GEMM: ids[t] = id_offset + argmax_r (x[t] . w[r]) over the first
+// n_valid rows of w (and the max into vals when given), without writing the logits.
+void lm_head_argmax(at::Tensor ids, c10::optional<at::Tensor> vals, at::Tensor x, at::Tensor w,
+                    c10::optional<at::Tensor> bias, int64_t n_valid, int64_t id_offset) {
+  check_bf16(x, "x"); check_bf16(w, "w"); check_contig(x, "x"); check_contig(w, "w");
+  check_cuda(ids, "ids"); check_dtype(ids, at::kInt, "ids");
+  CHECK(w.dim() == 2 && x.dim() == 2 && w.size(1) == x.size(1), "lm head shapes: x ", x.sizes(), " w ", w.sizes());
+  const int64_t M = x.size(0), K = x.size(1);
+  CHECK(n_valid > 0 && n_valid <= w.size(0), "n_valid out of range");
+  CHECK(K % 8 == 0, "K must be a multiple of 8");
+  CHECK(ids.numel() == M, "ids size");
+  if (vals.has_value()) { check_cuda(*vals, "vals"); check_dtype(*vals, at::kFloat, "vals"); CHECK(vals->numel() == M, "vals size"); }
+  if (bias.has_value()) { check_bf16(*bias, "bias"); CHECK(bias->numel() >= n_valid, "bias size"); }
+  if (M == 0) return;
+  const int64_t n_blk = (n_valid + 31) / 32;
+  at::Tensor part = at::empty({n_blk, M, 2}, x.options().dtype(at::kFloat));
+  const int64_t wsb = msgl_gemm_workspace_bytes(M, n_valid, K, 0);
+  at::Tensor& ws = gemm_workspace(x.device(), wsb);
+  msgl_gemm_argmax(part.data_ptr(), x.data_ptr(), w.data_ptr(), opt_ptr(bias), M, n_valid, K, ws.data_ptr(),
+                   ws.numel(), stream());
+  msgl_argmax_partials(ids.data_ptr<int32_t>(), vals.has_value() ? vals->data_ptr<float>() : nullptr,
+                       part.data_ptr(), n_blk, M, id_offset, stream());
+}
+
 // bf16 GEMM into this rank's NVLS staging region (out), signalling arrival on the multicast counter
 // at `arrive_mc` through the local ticket at `arrive_ticket` (fused row-parallel collective)
 void gemm_signal(at::Tensor out, at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, int64_t arrive_ticket,
@@ -313,21 +337,26 @@ void attention_decode_paged(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::
 }
 
 // ----- routed experts
+// epi 0: out [rows, N]; 1 / 2 / 4 (SiLU / GELU / gpt-oss SwiGLU): w's rows gate/up interleaved in
+// 128-row blocks, out the activated [rows, N / 2]
 void gemm_grouped(at::Tensor out, at::Tensor xs, at::Tensor w, c10::optional<at::Tensor> bias, at::Tensor tile_count,
-                  at::Tensor work, int64_t bn) {
+                  at::Tensor work, int64_t bn, int64_t epi) {
   check_bf16(out, "out"); check_bf16(xs, "xs"); check_bf16(w, "w");
   check_contig(xs, "xs"); check_contig(w, "w"); check_contig(out, "out");
   check_i32(tile_count, "tile_count"); check_i32(work, "work");
   CHECK(w.dim() == 3, "expert weights must be [E, N, K]");
+  CHECK(epi == 0 || epi == 1 || epi == 2 || epi == 4, "grouped gemm epilogue must be 0, 1, 2 or 4");
   const int64_t E = w.size(0), N = w.size(1), K = w.size(2);
-  CHECK(xs.size(1) == K && out.size(1) == N && out.size(0) == xs.size(0), "grouped gemm shapes");
+  const int64_t n_out = epi == 0 ? N : N / 2;
+  if (epi != 0) CHECK(N % 256 == 0, "gated grouped gemm needs 2I to be a multiple of 256");
+  CHECK(xs.size(1) == K && out.size(1) == n_out && out.size(0) == xs.size(0), "grouped gemm shapes");
   CHECK(K % 8 == 0 && N % 8 == 0, "grouped gemm needs K, N multiples of 8");
   CHECK(bn == 16 || bn == 32 || bn == 64 || bn == 128, "bn must be 16/32/64/128");
   CHECK(xs.size(0) % bn == 0, "row capacity must be a multiple of bn");
   if (bias.has_value()) { check_bf16(*bias, "bias"); CHECK(bias->numel() == E * N, "bias must be [E, N]"); }
   const int max_tiles = work.numel() / 2;
   msgl_gemm_grouped(out.data_ptr(), xs.data_ptr(), w.data_ptr(), opt_ptr(bias), xs.size(0), N, K, out.stride(0), E,
-                    tile_count.data_ptr<int32_t>(), work.data_ptr(), max_tiles, bn, stream());
+                    tile_count.data_ptr<int32_t>(), work.data_ptr(), max_tiles, bn, (int)epi, stream());
 }
 
 void moe_route(at::Tensor logits, int64_t topk, bool renorm, bool softmax_after, at::Tensor weights, at::Tensor ids) {
@@ -414,17 +443,23 @@ void peer_collective(int64_t mode, at::Tensor out, at::Tensor in, std::vector<in
 // rank's and the multicast address of the same allocation).
 void nvls_allreduce_rmsnorm(int64_t uc, int64_t mc, int64_t rank, int64_t world, at::Tensor x, at::Tensor residual, at::Tensor w,
                             at::Tensor out, double eps, int64_t cap_bytes, at::Tensor state, int64_t timeout_ns,
-                            bool first, int64_t mode) {
+                            bool first, int64_t mode, c10::optional<at::Tensor> trace) {
   check_bf16(x, "x"); check_bf16(residual, "residual"); check_bf16(w, "w"); check_bf16(out, "out");
   check_contig(x, "x"); check_contig(residual, "residual"); check_contig(out, "out"); check_contig(w, "w");
   check_cuda(state, "state"); check_dtype(state, at::kInt, "state");
   CHECK(state.numel() >= msgl_nvls_state_words(), "nvls state tensor too small");
+  if (trace.has_value()) {
+    check_cuda(*trace, "trace"); check_dtype(*trace, at::kLong, "trace");
+    CHECK(trace->numel() >= 8 * msgl_nvls_grid(), "nvls trace tensor too small");
+  }
   const int64_t H = x.size(-1), T = x.numel() / H;
   CHECK(residual.numel() == x.numel() && out.numel() == x.numel() && w.numel() == H, "nvls norm shapes");
   const int rc = msgl_nvls_allreduce_rmsnorm(reinterpret_cast<void*>(uc), reinterpret_cast<void*>(mc), rank, world,
                                              x.data_ptr(), residual.data_ptr(), w.data_ptr(), out.data_ptr(), T, H,
                                              eps, cap_bytes, reinterpret_cast<uint32_t*>(state.data_ptr()),
-                                             timeout_ns, first ? 1 : 0, (int)mode, stream());
+                                             timeout_ns, first ? 1 : 0, (int)mode,
+                                             trace.has_value() ? reinterpret_cast<uint64_t*>(trace->data_ptr()) : nullptr,
+                                             stream());
   CHECK(rc == 0, "nvls all-reduce rejected its arguments (code ", rc, ")");
 }
 
@@ -509,6 +544,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvls_state_words", []() { return msgl_nvls_state_words(); });
   m.def("nvls_ticket_offset", []() { return msgl_nvls_ticket_offset(); });
   m.def("gemm_signal", &gemm_signal);
+  m.def("lm_head_argmax", &lm_head_argmax);
   m.def("plan_apply", &plan_apply);
   m.def("gather_i32", &gather_i32);
   m.def("scatter_i32", &scatter_i32);

@@ -58,10 +58,19 @@ void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blocked, const
 void msgl_gemm_ex3(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M, int N,
                    int K, int ldo, int epi, int force_splits, int force_wide, void* workspace, int64_t ws_cap,
                    uint32_t* arrive_ticket, void* arrive_mc, cudaStream_t s);
+// LM-head greedy pick fused into the GEMM (out = x @ w^T is never written): part is
+// [ceil(N / 32)][M] float2 {largest value, its row}; msgl_argmax_partials reduces it per token to the
+// row (+ id_offset) and optionally its value. Ties resolve to the lowest row.
+void msgl_gemm_argmax(void* part, const void* x, const void* w, const void* bias, int M, int N, int K,
+                      void* workspace, int64_t ws_cap, cudaStream_t s);
+void msgl_argmax_partials(int32_t* out, float* out_val, const void* part, int n_blk, int M, int id_offset,
+                          cudaStream_t s);
 
 // ----- routed experts (MoE)
+// epi 0: plain bf16 output; 1 / 2 / 4 (SiLU / GELU / gpt-oss SwiGLU): w rows gate/up interleaved in
+// 128-row blocks and the activated [rows, N / 2] written by the epilogue
 void msgl_gemm_grouped(void* out, const void* x, const void* w, const void* bias, int rows_cap, int N, int K,
-                       int ldo, int E, const int* tile_count, const void* work, int max_tiles, int bn,
+                       int ldo, int E, const int* tile_count, const void* work, int max_tiles, int bn, int epi,
                        cudaStream_t s);
 void msgl_moe_route(const float* logits, int T, int E, int topk, int renorm, int softmax_after, float* weights,
                     int32_t* ids, cudaStream_t s);
@@ -128,14 +137,15 @@ void msgl_scatter_i32(int32_t* dst, int64_t dst_len, const int32_t* idx, const i
 // mode 0: LL (small messages; out written), 1: RS with x copied into staging, 2: RS with x already
 // in staging, 3: RS with staging written and arrival signalled by msgl_gemm_ex3. RS writes the
 // normalised rows into the buffer's gather region and only this rank's rows (i % world == rank) of
-// the residual. Returns 0, 3 on bad arguments, 4 if the launch failed.
+// the residual. `trace` (optional, [128][8] uint64) receives %globaltimer stamps of the RS phases per
+// CTA. Returns 0, 3 on bad arguments, 4 if the launch failed.
 int msgl_nvls_grid();
 int msgl_nvls_flag_bytes();
 int msgl_nvls_state_words();
 int64_t msgl_nvls_ticket_offset();
 int msgl_nvls_allreduce_rmsnorm(void* uc, void* mc, int rank, int world, const void* x, void* residual, const void* w,
                                 void* out, int T, int H, float eps, int64_t cap_bytes, uint32_t* state,
-                                int64_t timeout_ns, int first, int mode, cudaStream_t s);
+                                int64_t timeout_ns, int first, int mode, uint64_t* trace, cudaStream_t s);
 
 // ----- peer-memory collectives (CUDA IPC over NVLink)
 int msgl_peer_flag_bytes();

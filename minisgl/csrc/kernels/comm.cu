@@ -11,6 +11,7 @@
 // two-shot form (reduce-scatter then all-gather through peer memory) moves 2(n-1)/n of the data
 // per rank for large ones; all-gather copies every peer's slice. Waits never exceed a time limit: on expiry the kernel
 // records kErrPeerTimeout and returns, leaving the context usable. No multicast is used.
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 
@@ -250,9 +251,12 @@ constexpr int kNvlsThreads = 256;
 constexpr int kNvlsFlagStride = 128;  // one counter per 128-byte line
 constexpr int kNvlsFlagBytes = kNvlsGrid * kNvlsFlagStride;
 constexpr int kNvlsMaxVec = 8;  // 16-byte vectors per thread per row: H <= 8 * 8 * 256 = 16384
-constexpr int kNvlsStateWords = 4 * kNvlsGrid + 64;  // per CTA {LL calls, RS calls, -, -} + 2 tickets
-constexpr int kTicket1 = 4 * kNvlsGrid;             // local arrival tickets, 128 bytes apart
-constexpr int kTicket2 = 4 * kNvlsGrid + 32;
+// state words: LL call count per CTA [0, kNvlsGrid); the RS call count; two local arrival tickets
+// (each on its own 128-byte line)
+constexpr int kStateRS = 4 * kNvlsGrid;
+constexpr int kTicket1 = 4 * kNvlsGrid + 32;
+constexpr int kTicket2 = 4 * kNvlsGrid + 64;
+constexpr int kNvlsStateWords = 4 * kNvlsGrid + 96;
 
 enum NvlsMode : int { kModeLL = 0, kModeStage = 1, kModePrestaged = 2, kModeGemmArrived = 3 };
 
@@ -271,6 +275,7 @@ struct NvlsParams {
   uint64_t timeout_ns;
   int first;          // 1: residual is not read (it becomes the sum)
   int mode;
+  uint64_t* trace;    // optional [kNvlsGrid][8] %globaltimer stamps of the RS phases (profiling)
 };
 
 __device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const uint8_t* mc_addr) {
@@ -397,6 +402,56 @@ __device__ __forceinline__ void add_residual_norm(const NvlsParams& p, int row, 
   }
 }
 
+// RS rows: groups of kRsGroup threads per row, kRsGroups per CTA; H <= kRsMaxVec x 8 x kRsGroup
+constexpr int kRsGroup = 128;
+constexpr int kRsGroups = kNvlsThreads / kRsGroup;
+constexpr int kRsMaxVec = 8;
+
+// add_residual_norm for one 128-thread group (rank-local rows of the RS form): the sum of squares
+// goes through the group's own slice of s_red and named barrier 1 + g.
+__device__ __forceinline__ void group_residual_norm(const NvlsParams& p, int row, int g, int gt,
+                                                    float (&vals)[kRsMaxVec][8], float* s_red) {
+  const int nv = p.H / 8;
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kRsMaxVec; ++k) {
+    const int v = gt + k * kRsGroup;
+    if (v < nv) {
+      const int64_t idx = (int64_t)row * nv + v;
+      if (!p.first) {
+        float r[8];
+        unpack8(p.residual[idx], r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vals[k][j] += r[j];
+      }
+      const uint4 packed = pack8(vals[k]);
+      p.residual[idx] = packed;
+      unpack8(packed, vals[k]);  // normalise the stored (bf16) residual
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += vals[k][j] * vals[k][j];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((gt & 31) == 0) s_red[gt >> 5] = ss;
+  named_bar_sync(1 + g, kRsGroup);
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRsGroup / 32; ++i) tot += s_red[i];
+  named_bar_sync(1 + g, kRsGroup);  // s_red reuse by the group's next row
+  const float rstd = rsqrtf(tot / (float)p.H + p.eps);
+#pragma unroll
+  for (int k = 0; k < kRsMaxVec; ++k) {
+    const int v = gt + k * kRsGroup;
+    if (v < nv) {
+      float wf[8];
+      unpack8(p.w[v], wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) vals[k][j] = vals[k][j] * rstd * wf[j];
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParams p) {
   const int b = blockIdx.x, tid = threadIdx.x;
   const int nv = p.H / 8;
@@ -405,7 +460,7 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParam
   pdl_launch();
   if (p.mode == kModeLL) {
     pdl_wait();
-    if (tid == 0) s_calls = p.state[4 * b] + 1;
+    if (tid == 0) s_calls = p.state[b] + 1;
     __syncthreads();
     const uint32_t calls = s_calls;
     const size_t off = kNvlsFlagBytes + (size_t)(calls & 1) * p.cap;
@@ -441,7 +496,7 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParam
         if (v < nv) p.out[(int64_t)row * nv + v] = pack8(vals[k]);
       }
     }
-    if (tid == 0) p.state[4 * b] = calls;
+    if (tid == 0) p.state[b] = calls;
     return;
   }
 
@@ -452,7 +507,9 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParam
   // started (programmatic launch lets several grids of the chain be resident at once). In mode 3
   // the producer GEMM already published its tiles to every rank before finishing.
   pdl_wait();
-  if (tid == 0) s_calls = p.state[4 * b + 1] + 1;
+  uint64_t* tr = (p.trace != nullptr && tid == 0) ? p.trace + b * 8 : nullptr;
+  if (tr) tr[0] = globaltimer_ns();
+  if (tid == 0) s_calls = p.state[kStateRS] + 1;
   __syncthreads();
   const uint32_t rs = s_calls;
   const uint32_t target = rs * (uint32_t)p.world;  // each rank adds 1 per call to each counter
@@ -466,29 +523,36 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParam
     if (p.mode == kModeStage) {
       const int64_t n16 = (int64_t)p.T * nv;
       uint4* dst = reinterpret_cast<uint4*>(stage_uc);
-      for (int64_t i = (int64_t)b * kNvlsThreads + tid; i < n16; i += (int64_t)kNvlsGrid * kNvlsThreads)
+      for (int64_t i = (int64_t)b * kNvlsThreads + tid; i < n16; i += (int64_t)gridDim.x * kNvlsThreads)
         dst[i] = p.x[i];
     }
     __syncthreads();
-    if (tid == 0) rank_arrive(p.state + kTicket1, kNvlsGrid, cnt1_mc);
+    if (tid == 0) rank_arrive(p.state + kTicket1, gridDim.x, cnt1_mc);
   }
+  if (tr) tr[1] = globaltimer_ns();
   // 1. every rank's partial is staged
   bool ok = true;
   if (tid == 0) ok = wait_counter(p.uc, target, p.timeout_ns, 3000 + b);
   ok = __syncthreads_and(ok) != 0;
+  if (tr) tr[2] = globaltimer_ns();
   if (ok) {
-    // 2. reduce-scatter by row, residual + norm, all-gather of the normalised rows
-    for (int i = b * p.world + p.rank; i < p.T; i += kNvlsGrid * p.world) {
-      float vals[kNvlsMaxVec][8];
+    // 2. reduce-scatter by row, residual + norm, all-gather of the normalised rows. Each CTA is two
+    // 128-thread groups working on different rows (reductions through a group-local named barrier),
+    // so twice as many rows are in flight as CTAs: the phase costs about one multimem round trip.
+    const int g = tid / kRsGroup, gt = tid % kRsGroup;
+    for (int j = b * kRsGroups + g;; j += gridDim.x * kRsGroups) {
+      const int i = j * p.world + p.rank;
+      if (i >= p.T) break;
+      float vals[kRsMaxVec][8];
 #pragma unroll
-      for (int k = 0; k < kNvlsMaxVec; ++k) {
-        const int v = tid + k * kNvlsThreads;
+      for (int k = 0; k < kRsMaxVec; ++k) {
+        const int v = gt + k * kRsGroup;
         if (v < nv) unpack8(mm_ld_reduce_bf16x8(stage_mc + ((int64_t)i * nv + v) * 16), vals[k]);
       }
-      add_residual_norm(p, i, vals, s_red);
+      group_residual_norm(p, i, g, gt, vals, s_red + g * (kRsGroup / 32));
 #pragma unroll
-      for (int k = 0; k < kNvlsMaxVec; ++k) {
-        const int v = tid + k * kNvlsThreads;
+      for (int k = 0; k < kRsMaxVec; ++k) {
+        const int v = gt + k * kRsGroup;
         if (v < nv) mm_st_bf16x8(gather_mc + ((int64_t)i * nv + v) * 16, pack8(vals[k]));
       }
     }
@@ -496,10 +560,17 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_ar_rmsnorm_kernel(NvlsParam
   // 3. this CTA's gather stores are issued; the rank's last CTA publishes them
   __syncthreads();
   if (tid == 0) {
-    rank_arrive(p.state + kTicket2, kNvlsGrid, cnt2_mc);
-    if (b == 0 && wait_counter(p.uc + kNvlsFlagStride, target, p.timeout_ns, 4000))
-      fence_proxy_async_global();  // gathered rows are read next by TMA loads
-    p.state[4 * b + 1] = rs;
+    if (tr) tr[3] = globaltimer_ns();
+    rank_arrive(p.state + kTicket2, gridDim.x, cnt2_mc);
+    if (tr) tr[4] = globaltimer_ns();
+    if (b == 0) {
+      if (wait_counter(p.uc + kNvlsFlagStride, target, p.timeout_ns, 4000))
+        fence_proxy_async_global();  // gathered rows are read next by TMA loads
+      // every CTA of this call read the count before its arrival, and the second barrier passed
+      // only after all of them arrived
+      p.state[kStateRS] = rs;
+    }
+    if (tr) tr[5] = globaltimer_ns();
   }
 }
 
@@ -512,10 +583,12 @@ extern "C" int64_t msgl_nvls_ticket_offset() { return (int64_t)kTicket1 * 4; }
 
 extern "C" int msgl_nvls_allreduce_rmsnorm(void* uc, void* mc, int rank, int world, const void* x, void* residual,
                                            const void* w, void* out, int T, int H, float eps, int64_t cap_bytes,
-                                           uint32_t* state, int64_t timeout_ns, int first, int mode, cudaStream_t s) {
+                                           uint32_t* state, int64_t timeout_ns, int first, int mode, uint64_t* trace,
+                                           cudaStream_t s) {
   if (H % 8 != 0 || H > 8 * kNvlsMaxVec * kNvlsThreads || (int64_t)T * H * 2 > cap_bytes) return 3;
   if (mode < kModeLL || mode > kModeGemmArrived || world < 1 || rank < 0 || rank >= world) return 3;
   if (mode == kModeLL && (int64_t)world * T * H * 4 > cap_bytes) return 3;
+  if (mode != kModeLL && H > kRsMaxVec * 8 * kRsGroup) return 3;
   NvlsParams p;
   p.uc = reinterpret_cast<uint8_t*>(uc);
   p.mc = reinterpret_cast<uint8_t*>(mc);
@@ -533,7 +606,12 @@ extern "C" int msgl_nvls_allreduce_rmsnorm(void* uc, void* mc, int rank, int wor
   p.timeout_ns = (uint64_t)timeout_ns;
   p.first = first;
   p.mode = mode;
-  return msgl_launch(nvls_ar_rmsnorm_kernel, dim3(kNvlsGrid), dim3(kNvlsThreads), 0, s, 1, p) == cudaSuccess ? 0 : 4;
+  p.trace = trace;
+  // RS: one 128-thread group per row of this rank's share (rows i % world == rank), two per CTA
+  const int rows_local = (T + world - 1) / world;
+  const int grid = mode == kModeLL ? kNvlsGrid
+                                   : std::max(1, std::min(kNvlsGrid, (rows_local + kRsGroups - 1) / kRsGroups));
+  return msgl_launch(nvls_ar_rmsnorm_kernel, dim3(grid), dim3(kNvlsThreads), 0, s, 1, p) == cudaSuccess ? 0 : 4;
 }
 
 MSGL_ERROR_ACCESSOR(msgl_err_comm)

@@ -428,7 +428,7 @@ MSGL_DEVICE void rank_arrive(uint32_t* ticket, uint32_t ctas, void* counter_mc) 
   const uint32_t old = atomicAdd(ticket, 1u);
   if (old == ctas - 1) {
     atomicExch(ticket, 0u);
-    __threadfence_system();
+    __threadfence();  // acquire side of the ticket chain; the red's release covers system scope
     mm_red_release_add(counter_mc, 1u);
   }
 }

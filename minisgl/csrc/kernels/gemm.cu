@@ -39,7 +39,10 @@ constexpr int BK = 64;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + kEpiWarps * 32;
 
-enum Epi : int { kBf16 = 0, kSilu = 1, kGelu = 2, kF32 = 3 };
+// kSwiglu: gpt-oss's clamped SwiGLU, min(g, 7) * sigmoid(1.702 min(g, 7)) * (clamp(u, -7, 7) + 1)
+// kArgmax: no output tile; per (32 weight rows, token) the largest value and its row (the LM head's
+// greedy pick, see argmax_item)
+enum Epi : int { kBf16 = 0, kSilu = 1, kGelu = 2, kF32 = 3, kSwiglu = 4, kArgmax = 5 };
 
 constexpr int pow2ceil(int x) {
   int p = 32;
@@ -49,7 +52,7 @@ constexpr int pow2ceil(int x) {
 
 template <int BN, int EPI, bool WIDE>
 struct Cfg {
-  static constexpr bool kAct = EPI == kSilu || EPI == kGelu;
+  static constexpr bool kAct = EPI == kSilu || EPI == kGelu || EPI == kSwiglu;
   static constexpr bool kTwo = kAct || WIDE;           // two 128-row MMA halves per tile
   static constexpr int kRowsA = kTwo ? 256 : 128;
   static constexpr int kOutPerTile = kAct ? 128 : kRowsA;
@@ -59,7 +62,7 @@ struct Cfg {
   static constexpr int kA = kRowsA * BK * 2;
   static constexpr int kB = BN * BK * 2;
   static constexpr int kStage = kA + kB;
-  static constexpr int kOutElem = EPI == kF32 ? 4 : 2;
+  static constexpr int kOutElem = (EPI == kF32 || EPI == kArgmax) ? 4 : 2;
   static constexpr int kChunk = BN >= 32 ? 32 : 16;
   static constexpr int kStageOut = kChunk * 32 * kOutElem;
   static constexpr int kEpiSmem = kEpiWarps * kStageOut;
@@ -92,6 +95,7 @@ struct Params {
   // the launch's last CTA to finish adds 1 to the multicast arrival counter (see comm.cu)
   uint32_t* arrive_ticket;
   void* arrive_mc;
+  float2* argmax_out;  // kArgmax: [ceil(n_out / 32)][M] of {max, row as int bits}
 };
 
 // End of a GEMM CTA whose output feeds the NVLS reduce-scatter: every epilogue thread that issued
@@ -104,6 +108,16 @@ __device__ __forceinline__ void gemm_arrive(uint32_t* ticket, void* mc) {
 __device__ __forceinline__ float act_silu(float g) { return g / (1.f + __expf(-g)); }
 __device__ __forceinline__ float act_gelu(float g) {
   return 0.5f * g * (1.f + tanhf(0.7978845608028654f * (g + 0.044715f * g * g * g)));
+}
+template <int EPI>
+__device__ __forceinline__ float gated_act(float g, float up) {
+  if constexpr (EPI == kSwiglu) {
+    g = fminf(g, 7.f);
+    up = fminf(fmaxf(up, -7.f), 7.f);
+    return g / (1.f + __expf(-1.702f * g)) * (up + 1.f);
+  } else {
+    return (EPI == kSilu ? act_silu(g) : act_gelu(g)) * up;
+  }
 }
 
 // tile -> (weight tile, token tile): groups of 8 weight tiles sweep all token tiles so one wave's
@@ -178,6 +192,33 @@ __device__ __forceinline__ void xchg_add(const float* blk, int lane, float (&v)[
   }
 }
 
+// kArgmax epilogue of one item: lane l holds o[j] = row (ocol0 + l) for tokens token0 + j, j < W.
+// The 32 x W values go through the warp's staging smem transposed (XOR swizzle: both the row-wise
+// writes and the token-wise reads touch 32 different banks); lane t then scans token t's 32 rows
+// in order (strict > keeps the lowest row among equal values) and writes {max, row} to block
+// ocol0 / 32 of argmax_out. Rows >= n_out do not take part.
+template <int W>
+__device__ __forceinline__ void argmax_item(const float (&o)[32], int ocol0, int n_out, int M, int token0, int lane,
+                                            uint8_t* stage_out, float2* argmax_out) {
+  float* s = reinterpret_cast<float*>(stage_out);
+  __syncwarp();
+  const bool row_ok = ocol0 + lane < n_out;
+#pragma unroll
+  for (int j = 0; j < W; ++j) s[j * 32 + (lane ^ j)] = row_ok ? o[j] : -INFINITY;
+  __syncwarp();
+  if (lane < W && token0 + lane < M) {
+    float best = -INFINITY;
+    int bi = 0;
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      const float x = s[lane * 32 + (c ^ lane)];
+      if (x > best) { best = x; bi = c; }
+    }
+    argmax_out[(int64_t)(ocol0 >> 5) * M + token0 + lane] = make_float2(best, __int_as_float(ocol0 + bi));
+  }
+  __syncwarp();
+}
+
 // bias + activation for one (part, 32-token chunk) item of a warp's 32 accumulator rows, staged
 // in smem as [W tokens][32 cols] and written with a TMA store (rows >= M / cols >= n_out clipped)
 template <int BN, int EPI, bool WIDE>
@@ -199,10 +240,14 @@ __device__ __forceinline__ void store_item(const float (&v)[32], const float (&g
   for (int j = 0; j < W; ++j) {
     if constexpr (C::kAct) {
       const float g = v[j] + bias_a, up = g2[j] + bias_b;
-      o[j] = (EPI == kSilu ? act_silu(g) : act_gelu(g)) * up;
+      o[j] = gated_act<EPI>(g, up);
     } else {
       o[j] = v[j] + bias_a;
     }
+  }
+  if constexpr (EPI == kArgmax) {
+    argmax_item<W>(o, ocol0, p.n_out, p.M, row0 + c * W, lane, stage_out, p.argmax_out);
+    return;
   }
   if (lane == 0) bulk_wait_read<0>();
   __syncwarp();
@@ -506,7 +551,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 // =================================================================================================
 template <int BN, int EPI>
 struct Cfg2 {
-  static constexpr bool kAct = EPI == kSilu || EPI == kGelu;
+  static constexpr bool kAct = EPI == kSilu || EPI == kGelu || EPI == kSwiglu;
   static constexpr int kRowsA = kAct ? 256 : 128;  // weight rows loaded per CTA
   static constexpr int kTok = BN / 2;               // token rows loaded per CTA
   static constexpr int kAccCols = (kAct ? 2 : 1) * BN;
@@ -515,7 +560,7 @@ struct Cfg2 {
   static constexpr int kA = kRowsA * BK * 2;
   static constexpr int kB = kTok * BK * 2;
   static constexpr int kStage = kA + kB;
-  static constexpr int kOutElem = EPI == kF32 ? 4 : 2;
+  static constexpr int kOutElem = (EPI == kF32 || EPI == kArgmax) ? 4 : 2;
   static constexpr int kStageOut = 32 * 32 * kOutElem;
   static constexpr int kEpiSmem = kEpiWarps * kStageOut;
   static constexpr int kStages = std::min(8, (220 * 1024 - kEpiSmem) / kStage);
@@ -538,6 +583,7 @@ struct Params2 {
   int n_tiles, m_tiles, splits;  // n_tiles counts pair tiles (256 weight rows, 512 if gated)
   uint32_t* arrive_ticket;       // as in Params
   void* arrive_mc;
+  float2* argmax_out;            // as in Params
 };
 
 
@@ -563,10 +609,14 @@ __device__ __forceinline__ void store_item2(const float (&v)[32], const float (&
   for (int j = 0; j < 32; ++j) {
     if constexpr (C::kAct) {
       const float g = v[j] + bias_a, up = g2[j] + bias_b;
-      o[j] = (EPI == kSilu ? act_silu(g) : act_gelu(g)) * up;
+      o[j] = gated_act<EPI>(g, up);
     } else {
       o[j] = v[j] + bias_a;
     }
+  }
+  if constexpr (EPI == kArgmax) {
+    argmax_item<32>(o, ocol0, p.n_out, p.M, row0 + c * 32, lane, stage_out, p.argmax_out);
+    return;
   }
   if (lane == 0) bulk_wait_read<0>();
   __syncwarp();
@@ -898,7 +948,7 @@ static int num_sms_cached() {
   return n;
 }
 
-static bool is_act(int epi) { return epi == kSilu || epi == kGelu; }
+static bool is_act(int epi) { return epi == kSilu || epi == kGelu || epi == kSwiglu; }
 
 struct Plan {
   int bn;
@@ -912,11 +962,20 @@ struct Plan {
 // tiles with BN = round-up(M) <= 256 tokens; gated outputs use 256-row tiles (128 gate + 128 up)
 // with BN <= 256 for decode and 128 for prefill. Split-K (a cluster of 2 or 4 CTAs per tile,
 // reduced through DSMEM) only pays off for long K with few tiles.
+// Gated outputs of a small weight matrix (a tensor-parallel shard's gate_up: few 256-row tiles):
+// 128-token tiles on one SM, so split-K can spread the weights over every SM (decode-shape sweep on
+// B200: 2.2x faster at TP8, 1.8x at TP4 than one 256-token 2-SM tile per 512 rows).
+static bool small_gated(int M, int N, int epi) {
+  return is_act(epi) && (N / 256) * ((M + 127) / 128) <= num_sms_cached() / 2;
+}
+
 static Plan make_plan(int M, int N, int K, int epi, int force_splits, int force_wide) {
   Plan pl;
   const bool act = is_act(epi);
   if (M <= 256) pl.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
   else pl.bn = act ? 128 : 256;
+  const bool gated_split = force_wide < 0 && small_gated(M, N, epi);
+  if (gated_split) pl.bn = std::min(pl.bn, 128);
   pl.wide = act || force_wide == 1;
   pl.rows_a = pl.wide ? 256 : 128;
   pl.tiles = ((N + pl.rows_a - 1) / pl.rows_a) * ((M + pl.bn - 1) / pl.bn);
@@ -926,7 +985,9 @@ static Plan make_plan(int M, int N, int K, int epi, int force_splits, int force_
   const bool can_split = !(pl.rows_a == 256 && pl.bn > 128);
   int splits = 1;
   if (force_splits > 0) splits = force_splits;
-  else if (!act && M <= 128 && pl.tiles <= sms / 2 && kblocks >= 16) {
+  else if (gated_split && kblocks >= 16) {
+    splits = std::max(1, std::min(std::min(sms / pl.tiles, kblocks / 8), 4));
+  } else if (!act && M <= 128 && pl.tiles <= sms / 2 && kblocks >= 16) {
     // weight-streaming regime: use as many K-splits as keep every SM busy in one wave
     splits = std::max(1, std::min(sms / pl.tiles, kblocks / 8));
   } else if (!act && pl.tiles <= sms / 2 && kblocks >= 48) {
@@ -1073,6 +1134,7 @@ static bool use_2sm(int M, int N, int K, int epi, int force_wide, int w_blocked)
   if (force_wide >= 0) return false;
   if (const char* e = getenv("MINISGL_GEMM_2SM"))
     if (e[0] == '0') return false;
+  if (small_gated(M, N, epi)) return false;
   return M > 64 && K >= 4096;
 }
 
@@ -1091,12 +1153,13 @@ static void launch_2sm_bn(int bn, Params2 p, const void* x, const void* w, void*
 
 static void launch_2sm(const void* x, const void* w, const void* bias, void* out, int M, int N, int K, int ldo,
                        int epi, int force_splits, void* ws, size_t ws_cap, uint32_t* arrive_ticket,
-                       void* arrive_mc, cudaStream_t s) {
+                       void* arrive_mc, float2* argmax_out, cudaStream_t s) {
   const bool act = is_act(epi);
   Params2 p;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   p.arrive_ticket = arrive_ticket;
   p.arrive_mc = arrive_mc;
+  p.argmax_out = argmax_out;
   p.M = M;
   p.n_out = act ? N / 2 : N;
   p.kblocks = (K + BK - 1) / BK;
@@ -1118,6 +1181,7 @@ static void launch_2sm(const void* x, const void* w, const void* bias, void* out
     case kBf16: launch_2sm_bn<kBf16>(bn, p, x, w, out, N, K, ldo, ws_cap, s); break;
     case kF32: launch_2sm_bn<kF32>(bn, p, x, w, out, N, K, ldo, ws_cap, s); break;
     case kSilu: launch_2sm_bn<kSilu>(bn, p, x, w, out, N, K, ldo, ws_cap, s); break;
+    case kArgmax: launch_2sm_bn<kArgmax>(bn, p, x, w, out, N, K, ldo, ws_cap, s); break;
     default: launch_2sm_bn<kGelu>(bn, p, x, w, out, N, K, ldo, ws_cap, s); break;
   }
 }
@@ -1127,6 +1191,10 @@ static void launch_2sm(const void* x, const void* w, const void* bias, void* out
 
 using namespace msgl;
 using namespace msgl::gemm;
+
+static void gemm_run(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M, int N, int K,
+                     int ldo, int epi, int force_splits, int force_wide, void* workspace, int64_t ws_cap,
+                     uint32_t* arrive_ticket, void* arrive_mc, float2* argmax_out, cudaStream_t s);
 
 extern "C" int msgl_gemm_pick_splits(int M, int N, int K) { return make_plan(M, N, K, kBf16, -1, -1).splits; }
 
@@ -1152,12 +1220,29 @@ extern "C" void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blo
 extern "C" void msgl_gemm_ex3(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M,
                               int N, int K, int ldo, int epi, int force_splits, int force_wide, void* workspace,
                               int64_t ws_cap, uint32_t* arrive_ticket, void* arrive_mc, cudaStream_t s) {
+  gemm_run(out, x, w, w_blocked, bias, M, N, K, ldo, epi, force_splits, force_wide, workspace, ws_cap, arrive_ticket,
+           arrive_mc, nullptr, s);
+}
+
+// LM-head greedy pick fused into the GEMM: no logits are written; for every token and every block
+// of 32 weight rows (vocab ids) the largest logit and its row go to part[block][token] (float2
+// {value, row as int bits}); msgl_argmax_partials then reduces the blocks.
+extern "C" void msgl_gemm_argmax(void* part, const void* x, const void* w, const void* bias, int M, int N, int K,
+                                 void* workspace, int64_t ws_cap, cudaStream_t s) {
+  gemm_run(part, x, w, 0, bias, M, N, K, N, kArgmax, -1, -1, workspace, ws_cap, nullptr, nullptr,
+           reinterpret_cast<float2*>(part), s);
+}
+
+static void gemm_run(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M, int N, int K,
+                     int ldo, int epi, int force_splits, int force_wide, void* workspace, int64_t ws_cap,
+                     uint32_t* arrive_ticket, void* arrive_mc, float2* argmax_out, cudaStream_t s) {
   if (M <= 0 || N <= 0) return;
   Plan pl = make_plan(M, N, K, epi, force_splits, force_wide);
   Params p;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   p.arrive_ticket = arrive_ticket;
   p.arrive_mc = arrive_mc;
+  p.argmax_out = argmax_out;
   p.grp_count = nullptr;
   p.grp_work = nullptr;
   p.bias_stride = 0;
@@ -1170,13 +1255,15 @@ extern "C" void msgl_gemm_ex3(void* out, const void* x, const void* w, int w_blo
   p.splits = pl.splits;
   if (use_2sm(M, N, K, epi, force_wide, w_blocked)) {
     launch_2sm(x, w, bias, out, M, N, K, ldo, epi, force_splits, workspace, (size_t)ws_cap, arrive_ticket, arrive_mc,
-               s);
+               argmax_out, s);
     return;
   }
   const bool wide = pl.wide;
   switch (epi) {
     case kBf16: wide ? dispatch_bn<kBf16, true>(pl.bn, p, x, w, out, N, K, ldo, s)
                      : dispatch_bn<kBf16, false>(pl.bn, p, x, w, out, N, K, ldo, s); break;
+    case kArgmax: wide ? dispatch_bn<kArgmax, true>(pl.bn, p, x, w, out, N, K, ldo, s)
+                       : dispatch_bn<kArgmax, false>(pl.bn, p, x, w, out, N, K, ldo, s); break;
     case kSilu: dispatch_bn<kSilu, true>(pl.bn, p, x, w, out, N, K, ldo, s); break;
     case kGelu: dispatch_bn<kGelu, true>(pl.bn, p, x, w, out, N, K, ldo, s); break;
     default: wide ? dispatch_bn<kF32, true>(pl.bn, p, x, w, out, N, K, ldo, s)
@@ -1189,46 +1276,106 @@ extern "C" void msgl_gemm(void* out, const void* x, const void* w, const void* b
   msgl_gemm_ex(out, x, w, bias, M, N, K, ldo, epi, splits, -1, workspace, s);
 }
 
-template <int BN>
+template <int BN, int EPI>
 static void launch_grouped(const Params& p, const void* x, const void* w, void* out, int E, int N, int K, int ldo,
                            cudaStream_t s) {
-  using C = Cfg<BN, kBf16, false>;
-  msgl_set_smem<gemm_kernel<BN, kBf16, false>>(C::kSmem);
+  constexpr bool kGated = EPI != kBf16;
+  using C = Cfg<BN, EPI, kGated>;
+  msgl_set_smem<gemm_kernel<BN, EPI, kGated>>(C::kSmem);
   const CUtensorMap mw = make_map_experts(w, E, N, K, C::kRowsA);
   const CUtensorMap mx = make_map(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, K, K, BK, BN, true);
   const CUtensorMap mo = make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, C::kChunk, false);
   const int units = p.n_tiles * p.m_tiles;
-  msgl_launch(gemm_kernel<BN, kBf16, false>, dim3(std::min(units, num_sms_cached())), dim3(kThreads), C::kSmem, s,
+  msgl_launch(gemm_kernel<BN, EPI, kGated>, dim3(std::min(units, num_sms_cached())), dim3(kThreads), C::kSmem, s,
               1, mw, mx, mo, p);
+}
+
+template <int EPI>
+static void launch_grouped_bn(int bn, const Params& p, const void* x, const void* w, void* out, int E, int N, int K,
+                              int ldo, cudaStream_t s) {
+  switch (bn) {
+    case 16: launch_grouped<16, EPI>(p, x, w, out, E, N, K, ldo, s); break;
+    case 32: launch_grouped<32, EPI>(p, x, w, out, E, N, K, ldo, s); break;
+    case 64: launch_grouped<64, EPI>(p, x, w, out, E, N, K, ldo, s); break;
+    default: launch_grouped<128, EPI>(p, x, w, out, E, N, K, ldo, s); break;
+  }
 }
 
 // Grouped GEMM for routed experts: for every token tile t < *tile_count (device), rows
 // [work[t].y, work[t].y + bn) of x (permuted activations, [rows_cap, K]) times expert work[t].x of
 // w ([E, N, K]) -> the same rows of out ([rows_cap, N], row stride ldo), plus bias[e] if given.
+// epi 1 / 2 / 4 (SiLU / GELU / gpt-oss SwiGLU): w's rows are gate / up interleaved in 128-row
+// blocks (N % 256 == 0) and out is the activated [rows_cap, N / 2], computed in the epilogue.
 extern "C" void msgl_gemm_grouped(void* out, const void* x, const void* w, const void* bias, int rows_cap, int N,
                                   int K, int ldo, int E, const int* tile_count, const void* work, int max_tiles,
-                                  int bn, cudaStream_t s) {
+                                  int bn, int epi, cudaStream_t s) {
   if (rows_cap <= 0 || N <= 0 || max_tiles <= 0) return;
+  const bool gated = epi != kBf16;
   Params p;
   p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   p.arrive_ticket = nullptr;
   p.arrive_mc = nullptr;
+  p.argmax_out = nullptr;
   p.bias_stride = N;
   p.w_blocked = 0;
   p.grp_count = tile_count;
   p.grp_work = reinterpret_cast<const int2*>(work);
   p.M = rows_cap;
-  p.n_out = N;
-  p.n_tiles = (N + 127) / 128;
+  p.n_out = gated ? N / 2 : N;
+  p.n_tiles = gated ? N / 256 : (N + 127) / 128;
   p.m_tiles = max_tiles;
   p.kblocks = (K + BK - 1) / BK;
   p.splits = 1;
-  switch (bn) {
-    case 16: launch_grouped<16>(p, x, w, out, E, N, K, ldo, s); break;
-    case 32: launch_grouped<32>(p, x, w, out, E, N, K, ldo, s); break;
-    case 64: launch_grouped<64>(p, x, w, out, E, N, K, ldo, s); break;
-    default: launch_grouped<128>(p, x, w, out, E, N, K, ldo, s); break;
+  switch (epi) {
+    case kSilu: launch_grouped_bn<kSilu>(bn, p, x, w, out, E, N, K, ldo, s); break;
+    case kGelu: launch_grouped_bn<kGelu>(bn, p, x, w, out, E, N, K, ldo, s); break;
+    case kSwiglu: launch_grouped_bn<kSwiglu>(bn, p, x, w, out, E, N, K, ldo, s); break;
+    default: launch_grouped_bn<kBf16>(bn, p, x, w, out, E, N, K, ldo, s); break;
   }
+}
+
+namespace {
+
+// One CTA per token: the best of its blocks' {value, row} partials; equal values resolve to the
+// lowest row, as torch.argmax does. Rows are offset by `id_offset` (a vocabulary shard's first id).
+__global__ void argmax_partials_kernel(int32_t* __restrict__ out, float* __restrict__ out_val,
+                                       const float2* __restrict__ part, int n_blk, int M, int id_offset) {
+  pdl_wait();
+  pdl_launch();
+  const int t = blockIdx.x;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int b = threadIdx.x; b < n_blk; b += blockDim.x) {
+    const float2 v = part[(int64_t)b * M + t];
+    const int r = __float_as_int(v.y);
+    if (v.x > best || (v.x == best && r < bi)) { best = v.x; bi = r; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) { sv[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < nw; ++w)
+      if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
+    out[t] = bi + id_offset;
+    if (out_val != nullptr) out_val[t] = best;
+  }
+}
+
+}  // namespace
+
+extern "C" void msgl_argmax_partials(int32_t* out, float* out_val, const void* part, int n_blk, int M, int id_offset,
+                                     cudaStream_t s) {
+  if (M <= 0) return;
+  msgl_launch(argmax_partials_kernel, dim3(M), dim3(256), 0, s, 1, out, out_val, reinterpret_cast<const float2*>(part),
+              n_blk, M, id_offset);
 }
 
 extern "C" int msgl_num_sms() { return num_sms_cached(); }

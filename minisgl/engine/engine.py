@@ -131,6 +131,11 @@ class Engine:
             lm_head.return_local = True
             self._lm_shard = (lm_head.vocab_shard, config.tp_info.size, DistributedCommunicator())
 
+        # The decode graphs end at the final norm and the LM head runs after them, so a greedy batch
+        # can take its argmax inside the LM-head GEMM (no logits written) and a sampled one gets logits.
+        self._split_lm_head = self.is_cuda and hasattr(self.model, "forward_hidden")
+        self._fused_greedy = self._split_lm_head and bool(ENV.FUSED_LM_HEAD)
+
         # ----------------------------------------------------------------- graphs
         self.dummy_req = Req(
             input_ids=torch.zeros(1, dtype=torch.int32), table_idx=self.dummy_row, cached_len=0,
@@ -276,14 +281,27 @@ class Engine:
             _cuda().gather_i32(batch.input_ids, self.last_tokens, dev["req_rows"])
         else:
             batch.input_ids = self.last_tokens[dev["req_rows"].long()]
+        fused_greedy = self._fused_greedy and args.temperatures is None
         with self.ctx.forward_batch(batch):
             if self.graph_runner.can_use_cuda_graph(batch):
-                logits = self.graph_runner.replay(batch)
+                out = self.graph_runner.replay(batch)
             else:
-                logits = self.model.forward()
+                out = self.model.forward_hidden() if self._split_lm_head else self.model.forward()
+            if fused_greedy:
+                ids, vals = self.model.lm_head.greedy(out[: batch.size] if batch.is_decode else out)
+            elif self._split_lm_head:
+                logits = self.model.lm_head.forward(out)
+            else:
+                logits = out
         for req in batch.reqs:
             req.complete_one()
-        if self._lm_shard is not None:
+        if fused_greedy:
+            if self._lm_shard is not None:  # every rank's (best logit, id) pair per row -> the best
+                shard, tp, comm = self._lm_shard
+                next_tokens = self.sampler.combine_pairs(vals, ids, batch.size, tp, comm)
+            else:
+                next_tokens = ids
+        elif self._lm_shard is not None:
             shard, tp, comm = self._lm_shard
             next_tokens = self.sampler.sample_sharded(logits[: batch.size], args, shard, tp, comm)
         else:

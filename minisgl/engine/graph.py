@@ -1,9 +1,10 @@
 """Decode CUDA graphs (reference: python/minisgl/engine/graph.py:20-171).
 
 One graph per padded batch size in ``[1, 2, 4, 8, 16, ..., max]`` sharing one memory pool.
-Static buffers hold input ids, positions and out_loc; each graph keeps its own output (fp32 logits,
-this rank's vocab shard at TP > 1). Batches are padded with a dummy
-request whose page-table row points at a dummy KV slot.
+Static buffers hold input ids, positions and out_loc; each graph keeps its own output: the final
+normalised hidden states (the engine runs the LM head after the graph, as a greedy argmax fused into
+the LM-head GEMM or as logits for sampling). Batches are padded with a dummy request whose
+page-table row points at a dummy KV slot.
 """
 
 from __future__ import annotations
@@ -42,7 +43,7 @@ class GraphRunner:
         self.dummy_req = dummy_req
         self.graph_map: Dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_launches: Dict[int, int] = {}
-        self.outputs: Dict[int, torch.Tensor] = {}  # each graph's own logits tensor (no copy-out)
+        self.outputs: Dict[int, torch.Tensor] = {}  # each graph's own output tensor (no copy-out)
         if self.max_graph_bs and engine.device.type == "cuda":
             self._capture()
         else:
@@ -71,11 +72,12 @@ class GraphRunner:
             g = torch.cuda.CUDAGraph()
             from .counters import COUNTERS
 
+            fwd = eng.model.forward_hidden if eng._split_lm_head else eng.model.forward
             with ctx.forward_batch(batch):
-                eng.model.forward()  # warm up outside the capture
+                fwd()  # warm up outside the capture
                 before = COUNTERS.launches
                 with torch.cuda.graph(g, pool=pool, stream=eng.stream):
-                    self.outputs[bs] = eng.model.forward()
+                    self.outputs[bs] = fwd()
                 self.graph_launches[bs] = COUNTERS.launches - before
             pool = pool or g.pool()
             self.graph_map[bs] = g

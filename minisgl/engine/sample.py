@@ -123,6 +123,11 @@ class Sampler:
         full = comm.all_gather(local.contiguous()).view(tp, rows, width).permute(1, 0, 2).reshape(rows, tp * width)
         return self.sample(full[:, : self.vocab_size], args)
 
+    @nvtx_annotate("Sampler")
+    def combine_pairs(self, val: torch.Tensor, ids: torch.Tensor, rows: int, tp: int, comm) -> torch.Tensor:
+        """Greedy picks made per vocabulary shard (in the LM-head GEMM) -> the batch's tokens."""
+        return self._combine_pairs(val, ids, rows, tp, comm)
+
     @staticmethod
     def _combine_pairs(val: torch.Tensor, ids: torch.Tensor, rows: int, tp: int, comm) -> torch.Tensor:
         """Each rank's (score, token id) per row -> the token of the best score; ranks hold

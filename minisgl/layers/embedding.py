@@ -87,6 +87,17 @@ class ParallelLMHead(VocabParallelEmbedding):
         return self._vocab_range
 
     @nvtx_annotate("LMHead")
+    def greedy(self, x: torch.Tensor):
+        """Greedy pick of this rank's vocabulary shard without writing the logits: the argmax is
+        taken inside the LM-head GEMM's epilogue. Returns (global token id int32, its logit fp32)
+        per row; at TP > 1 the sampler combines the ranks' pairs."""
+        batch = get_global_ctx().batch
+        if batch.is_prefill:
+            x = x.index_select(0, batch.attn_metadata.get_last_indices(batch.size))
+        start, valid = self._vocab_range
+        return ops.lm_head_argmax(x, self.lm_weight, self.bias, valid, start)
+
+    @nvtx_annotate("LMHead")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         batch = get_global_ctx().batch
         if batch.is_prefill:

@@ -67,6 +67,19 @@ class MoELayer(BaseOP):
     # RMSNorm); `deferred` tells whether the last forward left it unreduced
     defer_to_norm = False
     deferred = False
+    _interleaved = False  # gate_up_proj in the gated grouped-GEMM layout (CUDA)
+
+    def load_state_dict(self, state_dict, *, prefix: str = "", _internal: bool = False) -> None:
+        super().load_state_dict(state_dict, prefix=prefix, _internal=_internal)
+        if self.gate_up_proj.is_cuda:
+            # gate / up rows interleaved in 128-row blocks (intermediate size padded to a whole
+            # block) so the first grouped GEMM applies the activation in its epilogue; the public
+            # tensors then hold the GPU layout
+            from minisgl.ops.moe import interleave_experts
+
+            self.gate_up_proj, self.down_proj, self.gate_up_proj_bias = interleave_experts(
+                self.gate_up_proj, self.down_proj, self.gate_up_proj_bias)
+            self._interleaved = True
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         be = get_global_ctx().moe_backend
@@ -77,6 +90,7 @@ class MoELayer(BaseOP):
             # EP: each expert's output is computed on one rank, which adds its bias
             w2_bias=self.down_proj_bias if (self._tp == 1 or self._ep or get_tp_info().rank == 0) else None,
             softmax_after_topk=self._softmax_after_topk, expert_offset=self._e0,
+            w1_interleaved=self._interleaved,
         )
         self.deferred = False
         if self._tp > 1:

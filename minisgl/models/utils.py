@@ -86,7 +86,9 @@ class MoEMLP(BaseOP):
 
     @nvtx_annotate("MoE")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        logits = getattr(self, self._router_name).forward(x)
+        router = getattr(self, self._router_name)
+        # fp32 router logits: expert choice compares logits that bf16 rounding would tie
+        logits = ops.linear_f32(x, router.weight, router.bias)
         return self.experts.forward(x, logits)
 
     @property
@@ -188,6 +190,9 @@ class DecoderForCausalLM(BaseLLMModel):
                                       tie_word_embeddings=config.tie_word_embeddings,
                                       tied_embedding=tied)
 
+    def forward_hidden(self) -> torch.Tensor:
+        """The final normalised hidden states (the LM head's input)."""
+        return self.model.forward(get_global_ctx().batch.input_ids)
+
     def forward(self) -> torch.Tensor:
-        h = self.model.forward(get_global_ctx().batch.input_ids)
-        return self.lm_head.forward(h)
+        return self.lm_head.forward(self.forward_hidden())

@@ -66,11 +66,11 @@ def moe_reference(x, w1, w2, gating, topk, renormalize, activation, w1_bias=None
 
 class GroupedMoe(BaseMoeBackend):
     def forward(self, hidden_states, w1, w2, gating_output, topk, renormalize, activation="silu",
-                *, w1_bias=None, w2_bias=None, softmax_after_topk=False, expert_offset=0):
+                *, w1_bias=None, w2_bias=None, softmax_after_topk=False, expert_offset=0, w1_interleaved=False):
         if not hidden_states.is_cuda:
             return moe_reference(hidden_states, w1, w2, gating_output, topk, renormalize, activation,
                                  w1_bias, w2_bias, softmax_after_topk, expert_offset)
         from minisgl.ops.moe import moe_forward
 
         return moe_forward(hidden_states, w1, w2, gating_output, topk, renormalize, activation,
-                           w1_bias, w2_bias, softmax_after_topk, expert_offset)
+                           w1_bias, w2_bias, softmax_after_topk, expert_offset, w1_interleaved)

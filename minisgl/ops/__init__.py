@@ -51,6 +51,30 @@ def linear(x, w, bias=None):
     return out
 
 
+def linear_f32(x, w, bias=None):
+    """``x @ w^T (+ bias)`` with fp32 output (the MoE router: expert selection compares logits
+    that bf16 rounding would often tie)."""
+    if not _on_gpu(x):
+        return ref.linear(x.float(), w.float(), None if bias is None else bias.float())
+    out = torch.empty(x.shape[0], w.shape[0], dtype=torch.float32, device=x.device)
+    _cuda().gemm(out, x, w, bias, 3)
+    return out
+
+
+def lm_head_argmax(x, w, bias, n_valid: int, id_offset: int = 0):
+    """(id_offset + argmax over the first ``n_valid`` rows of ``x @ w^T (+ bias)``, its value) per
+    row of ``x``; on the GPU the argmax runs in the GEMM epilogue and no logits are written. Ties
+    resolve to the lowest id."""
+    if not _on_gpu(x):
+        logits = ref.linear(x, w[:n_valid], None if bias is None else bias[:n_valid]).float()
+        vals, idx = logits.max(dim=-1)
+        return idx.to(torch.int32) + id_offset, vals
+    ids = torch.empty(x.shape[0], dtype=torch.int32, device=x.device)
+    vals = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    _cuda().lm_head_argmax(ids, vals, x.contiguous(), w, bias, n_valid, id_offset)
+    return ids, vals
+
+
 def gate_up_silu(x, w, act: str = "silu"):
     if not _on_gpu(x):
         return ref.gate_up_silu(x, w, act)
@@ -128,6 +152,8 @@ __all__ = [
     "rmsnorm",
     "fused_add_rmsnorm",
     "linear",
+    "linear_f32",
+    "lm_head_argmax",
     "gate_up_silu",
     "silu_and_mul",
     "gelu_and_mul",

@@ -72,7 +72,9 @@ class NvlsNormComm:
     # ------------------------------------------------------------------ shapes and regions
     def fits(self, x: torch.Tensor) -> bool:
         h = x.shape[-1]
-        return x.dtype == torch.bfloat16 and x.numel() * 2 <= self.cap and h % 8 == 0 and h <= 16384
+        if not (x.dtype == torch.bfloat16 and x.numel() * 2 <= self.cap and h % 8 == 0 and h <= 16384):
+            return False
+        return self.is_ll(x.numel() // h, h) or h <= 8192  # the RS form takes hidden sizes up to 8192
 
     def is_ll(self, tokens: int, hidden: int) -> bool:
         b = self.world * tokens * hidden * 4
@@ -95,7 +97,7 @@ class NvlsNormComm:
         rank. Returns the staging view (pass it to ``all_reduce_add_rmsnorm``), or None when this
         batch uses the LL form or does not fit (the caller then runs the plain GEMM)."""
         tokens, hidden = x.shape[0], weight.shape[0]
-        if (not self.gemm_fusion or tokens == 0 or weight.dim() != 2 or hidden % 8 != 0 or hidden > 16384
+        if (not self.gemm_fusion or tokens == 0 or weight.dim() != 2 or hidden % 8 != 0 or hidden > 8192
                 or tokens * hidden * 2 > self.cap or self.is_ll(tokens, hidden)):
             return None
         y = self.staging(tokens, hidden)
@@ -104,7 +106,7 @@ class NvlsNormComm:
         return y
 
     def all_reduce_add_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor,
-                               eps: float):
+                               eps: float, trace: torch.Tensor | None = None):
         """(sum_ranks(x) + residual) -> (rmsnorm of it, it); residual is updated in place (RS form:
         this rank's rows only)."""
         x = x.contiguous()
@@ -119,7 +121,7 @@ class NvlsNormComm:
             mode = MODE_GEMM_ARRIVED if self._staged_by_gemm == x.data_ptr() else MODE_STAGE
         self._staged_by_gemm = None
         _cuda().nvls_allreduce_rmsnorm(self.uc, self.mc, self.rank, self.world, x, residual, weight, out, eps,
-                                       self.cap, self.state, self.timeout_ns, first, mode)
+                                       self.cap, self.state, self.timeout_ns, first, mode, trace)
         return out, residual
 
     def close(self) -> None:

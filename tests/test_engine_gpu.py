@@ -26,6 +26,28 @@ PRESETS = ["tiny-qwen3", "tiny-llama", "tiny-qwen2", "tiny-qwen3-moe", "tiny-gpt
 LOGIT_TOL = 0.06
 
 
+MOE_PRESETS = ("tiny-qwen3-moe", "tiny-gpt-oss")
+
+
+def _checkpoint(tmp_path, preset):
+    """bf16 synthetic checkpoint. The routers of these random MoE models give logits within a few
+    hundredths of each other; at such a near-tie bf16 and fp32 legitimately pick different experts,
+    which changes a token's hidden state by far more than the bf16 error (and, through the KV cache,
+    the next few steps). Scaling the router weights makes the expert choice well separated, so the
+    comparison measures the kernels rather than tie-breaking."""
+    path = make_checkpoint(preset, str(tmp_path / preset), dtype=torch.bfloat16)
+    if preset in MOE_PRESETS:
+        from safetensors.torch import load_file, save_file
+
+        f = os.path.join(path, "model.safetensors")
+        sd = load_file(f)
+        for k in list(sd):
+            if k.endswith(("mlp.gate.weight", "mlp.router.weight", "mlp.router.bias")):
+                sd[k] = (sd[k].float() * 40.0).to(sd[k].dtype)
+        save_file(sd, f)
+    return path
+
+
 def _prompts(n, vocab, seed=0, lo=16, hi=64):
     g = torch.Generator().manual_seed(seed)
     return [torch.randint(0, vocab, (int(torch.randint(lo, hi + 1, (1,), generator=g)),), generator=g).tolist()
@@ -55,9 +77,16 @@ class _Tap:
 
 
 def _run(path, prompts, sp, port, tap=False, **kw):
+    from minisgl.env import ENV
     from minisgl.llm import LLM
 
-    llm = LLM(path, distributed_port=port, **kw)
+    fused = ENV.FUSED_LM_HEAD
+    if tap:  # the tap reads the logits the sampler receives; the fused greedy LM head writes none
+        ENV.FUSED_LM_HEAD = False
+    try:
+        llm = LLM(path, distributed_port=port, **kw)
+    finally:
+        ENV.FUSED_LM_HEAD = fused
     t = _Tap(llm) if tap else None
     try:
         out = [o["token_ids"] for o in llm.generate(prompts, sp)]
@@ -79,8 +108,11 @@ def _oracle_logits(path, prompts, port):
     return [rows[i][0] for i in range(len(prompts))]
 
 
-def _check_against_oracle(path, prompts, outs, port, tol=LOGIT_TOL):
-    """Teacher-forced check of greedy sequences `outs` (one per prompt) on the fp32 oracle."""
+def _check_against_oracle(path, prompts, outs, port, tol=LOGIT_TOL, gpu_rows=None):
+    """Teacher-forced check of greedy sequences `outs` (one per prompt) on the fp32 oracle: every
+    chosen token within `tol` of the oracle's best logit and, when the GPU's own logits rows are given
+    (`gpu_rows[prompt][step]`), every row within `tol` of the oracle's row. Returns the largest gap
+    and the fraction of steps that chose the oracle's exact argmax."""
     forced, where = [], []
     for i, (p, o) in enumerate(zip(prompts, outs)):
         for j in range(len(o)):
@@ -94,6 +126,9 @@ def _check_against_oracle(path, prompts, outs, port, tol=LOGIT_TOL):
         worst = max(worst, gap)
         exact += int(gap == 0.0)
         assert gap <= tol, f"prompt {i} step {j}: token {tok} is {gap:.4f} below the oracle's best"
+        if gpu_rows is not None:
+            err = float((gpu_rows[i][j] - row).abs().max())
+            assert err <= tol, f"prompt {i} step {j}: logits differ from the oracle by {err:.4f}"
     return worst, exact / len(where)
 
 
@@ -103,7 +138,7 @@ def test_gpu_prefill_logits_match_oracle(tmp_path, preset, free_port):
     wherever the oracle's top two are further apart than the tolerance."""
     if not torch.cuda.is_available():
         pytest.skip("no GPU")
-    path = make_checkpoint(preset, str(tmp_path / preset), dtype=torch.bfloat16)
+    path = _checkpoint(tmp_path, preset)
     prompts = _prompts(16, 1024)
     sp = SamplingParams(max_tokens=1, ignore_eos=True)
     _, gpu = _run(path, prompts, sp, free_port, tap=True, dtype=torch.bfloat16, max_running_req=32,
@@ -122,18 +157,35 @@ def test_gpu_prefill_logits_match_oracle(tmp_path, preset, free_port):
 
 @pytest.mark.parametrize("preset", PRESETS)
 def test_gpu_decode_tracks_oracle(tmp_path, preset, free_port):
-    """16 greedy tokens per prompt through CUDA graphs and overlap scheduling, every step checked
-    against the oracle with teacher forcing."""
+    """16 greedy tokens per prompt through CUDA graphs and overlap scheduling, every step's logits
+    and choice checked against the oracle with teacher forcing."""
     if not torch.cuda.is_available():
         pytest.skip("no GPU")
-    path = make_checkpoint(preset, str(tmp_path / preset), dtype=torch.bfloat16)
+    path = _checkpoint(tmp_path, preset)
     prompts = _prompts(12, 1024, seed=5)
     sp = SamplingParams(max_tokens=16, ignore_eos=True)
-    outs = _run(path, prompts, sp, free_port, dtype=torch.bfloat16, max_running_req=32, num_page_override=4096,
-                cuda_graph_max_bs=16)
+    outs, rows = _run(path, prompts, sp, free_port, tap=True, dtype=torch.bfloat16, max_running_req=32,
+                      num_page_override=4096, cuda_graph_max_bs=16)
     assert all(len(o) == 16 for o in outs)
-    worst, exact = _check_against_oracle(path, prompts, outs, free_port + 1)
+    worst, exact = _check_against_oracle(path, prompts, outs, free_port + 1, gpu_rows=rows)
     assert exact >= 0.9, (worst, exact)  # near-ties are rare; most steps pick the oracle's exact argmax
+
+
+@pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-gpt-oss"])
+def test_fused_greedy_lm_head_tracks_oracle(tmp_path, preset, free_port):
+    """Greedy decoding with the argmax taken inside the LM-head GEMM (the default; no logits are
+    written): every step's token checked against the fp32 oracle with teacher forcing."""
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from minisgl.env import ENV
+
+    assert ENV.FUSED_LM_HEAD
+    path = _checkpoint(tmp_path, preset)
+    prompts = _prompts(12, 1024, seed=9)
+    outs = _run(path, prompts, SamplingParams(max_tokens=16, ignore_eos=True), free_port, dtype=torch.bfloat16,
+                max_running_req=32, num_page_override=4096, cuda_graph_max_bs=16)
+    worst, exact = _check_against_oracle(path, prompts, outs, free_port + 1)
+    assert exact >= 0.9, (worst, exact)
 
 
 def test_graphs_and_overlap_are_consistent(tmp_path, free_port, monkeypatch):

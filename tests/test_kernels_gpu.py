@@ -449,6 +449,12 @@ def test_moe_forward(T, E, topk, H, I, act, renorm, after, bias):
     exp = moe_reference(x.cpu(), w1.cpu(), w2.cpu(), gate.cpu(), topk, renorm, act,
                         None if b1 is None else b1.cpu(), None if b2 is None else b2.cpu(), after)
     _close(out, exp, 3e-2, 3e-2)
+    # the activation in the first grouped GEMM's epilogue (gate/up interleaved, I padded to 128)
+    from minisgl.ops.moe import interleave_experts
+
+    w1i, w2i, b1i = interleave_experts(w1, w2, b1)
+    out = moe_forward(x, w1i, w2i, gate, topk, renorm, act, b1i, b2, after, w1_interleaved=True)
+    _close(out, exp, 3e-2, 3e-2)
     # expert parallelism: this "rank" holds experts [E/4, E/2); assignments elsewhere drop out
     e0, n = E // 4, E // 4
     sub = lambda t: None if t is None else t[e0 : e0 + n].contiguous()
@@ -494,3 +500,29 @@ def test_plan_apply_gather_scatter(n_tok, n_writes):
     exp = src.clone()
     exp[uniq.long()] = vals
     assert torch.equal(sc.cpu(), exp)
+
+
+@pytest.mark.parametrize("M", [1, 7, 64, 130, 256])
+@pytest.mark.parametrize("N,n_valid,K", [(1024, 1001, 256), (18992, 18992, 5120), (151936, 151936, 1024)])
+def test_lm_head_argmax(M, N, n_valid, K):
+    """Greedy pick fused into the LM-head GEMM (no logits written) against the argmax of the fp32
+    logits over the first n_valid rows: the same id wherever the best logit leads the second by more
+    than the GEMM's bf16-input rounding, and a maximum within that rounding of the true one."""
+    g = torch.Generator(device="cpu").manual_seed(M + N)
+    x = torch.randn(M, K, generator=g).to(DEV, torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) / math.sqrt(K)).to(DEV, torch.bfloat16)
+    w[n_valid:] = 10.0  # padding rows must never win
+    bias = (torch.randn(N, generator=g) * 0.1).to(DEV, torch.bfloat16) if N == 1024 else None
+    ids = torch.empty(M, dtype=torch.int32, device=DEV)
+    vals = torch.empty(M, dtype=torch.float32, device=DEV)
+    _c().lm_head_argmax(ids, vals, x, w, bias, n_valid, 5)
+    logits = x.float() @ w[:n_valid].float().t()
+    if bias is not None:
+        logits += bias[:n_valid].float()
+    top2 = torch.topk(logits, 2, dim=1).values
+    exp = logits.argmax(dim=1).to(torch.int32) + 5
+    clear = (top2[:, 0] - top2[:, 1]) > 1e-3
+    assert torch.equal(ids[clear].cpu(), exp[clear].cpu())
+    got = logits.gather(1, (ids.long() - 5).clamp(0, n_valid - 1)[:, None])[:, 0]
+    torch.testing.assert_close(got.cpu(), top2[:, 0].cpu(), atol=1e-3, rtol=1e-4)
+    torch.testing.assert_close(vals.cpu(), top2[:, 0].cpu(), atol=1e-3, rtol=1e-4)
