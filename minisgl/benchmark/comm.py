@@ -130,6 +130,10 @@ def main(argv=None) -> None:
         if rank == 0:
             print(json.dumps({"nvls": f"unavailable: {e}"}), flush=True)
     s = torch.cuda.Stream()
+    from .perf import ClockSampler
+
+    clocks = ClockSampler(local)
+    clocks.start()
     w = (torch.rand(H, device=dev) + 0.5).to(torch.bfloat16)
     hbm, flops = _peaks()
     K = a.k or 5120 // world
@@ -186,6 +190,11 @@ def main(argv=None) -> None:
         if a.trace and nvls is not None and not nvls.is_ll(T, H):
             _trace(nvls, x, xin, wt, res, w, eps, rank, T)
     torch.cuda.synchronize()
+    c = clocks.stop()
+    clk = [None] * world
+    dist.all_gather_object(clk, c, group=cpu)
+    if rank == 0:
+        print(json.dumps({"clocks": clk}), flush=True)
     dist.barrier(group=cpu)
     if nvls is not None:
         nvls.close()

@@ -285,16 +285,20 @@ def _gemm_sweep(a, c) -> None:
                 ours(-1, -1)  # warm the clocks and caches on this shape before timing anything
                 row = {"tp": tp, "shape": name, "M": M, "N": N, "K": K}
                 best = (1e9, None)
-                for wide in ([1, 2] if epi == 1 else [0, 1, 2]):
-                    for splits in (1, 2, 3, 4):  # the tilings the GPU tests cover
-                        if wide == 2 and splits > 3:
-                            continue
-                        try:
-                            t = ours(splits, wide)
-                        except RuntimeError:
-                            continue
-                        if t < best[0]:
-                            best = (t, f"wide{wide}/s{splits}")
+                bns = [-1] + ([64, 128] if M > 64 else [])  # token tiles: automatic, or several per batch
+                for bn in bns:
+                    c.gemm_force_bn(bn)
+                    for wide in ([1, 2] if epi == 1 else [0, 1, 2]):
+                        for splits in (1, 2, 3, 4, 6, 8):  # the tilings the GPU tests cover
+                            if (wide == 2 and splits > 4) or (epi == 1 and splits > 4):
+                                continue
+                            try:
+                                t = ours(splits, wide)
+                            except RuntimeError:
+                                continue
+                            if t < best[0]:
+                                best = (t, f"wide{wide}/s{splits}/bn{bn}")
+                c.gemm_force_bn(-1)
                 row["auto_us"] = round(ours(-1, -1), 2)
                 row["best_us"], row["best"] = round(best[0], 2), best[1]
                 row["cublas_us"] = round(cublas(), 2) if epi == 0 else None

@@ -3,7 +3,8 @@
     python -m minisgl.benchmark.online --model M [--tp 4] [--rates 2,4,8 | --trace FILE --scales ...]
         [-- extra server flags]
 
-Launches ``python -m minisgl`` as a child process group (its own session, stopped at the end),
+Launches ``python -m minisgl`` (this engine, or with ``--impl reference`` the unmodified reference
+from baseline/_ref) as a child process group (its own session, stopped at the end),
 waits until ``/v1/models`` answers, then drives it with the client of ``minisgl.benchmark.client``:
 Poisson arrivals at each rate with lognormal prompt / output lengths and shared prefixes, or a
 Qwen-Bailian / Mooncake trace file replayed at each time scale. Prints one JSON line per load
@@ -38,6 +39,29 @@ def wait_ready(port: int, proc: subprocess.Popen, timeout: float) -> None:
     raise TimeoutError(f"server not ready after {timeout:.0f} s")
 
 
+def _reference_env():
+    """Environment that makes ``python -m minisgl`` resolve to the reference installed in
+    baseline/_ref. Its API server imports prompt_toolkit at load time for the interactive shell,
+    which this image lacks; a stand-in package that only defines the two imported names (and fails
+    if the shell is used) lets the HTTP server start. The reference's code is not modified."""
+    import tempfile
+
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    ref = os.path.join(root, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "minisgl")):
+        raise SystemExit("the reference is not installed in baseline/_ref")
+    stub = tempfile.mkdtemp(prefix="minisgl_ref_stub_")
+    os.makedirs(os.path.join(stub, "prompt_toolkit"))
+    with open(os.path.join(stub, "prompt_toolkit", "__init__.py"), "w") as f:
+        f.write("class PromptSession:\n    def __init__(self, *a, **k):\n"
+                "        raise RuntimeError('interactive shell unavailable: prompt_toolkit is not installed')\n")
+    with open(os.path.join(stub, "prompt_toolkit", "completion.py"), "w") as f:
+        f.write("class WordCompleter:\n    def __init__(self, *a, **k):\n        pass\n")
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join([ref, stub])
+    return env, stub  # run from outside this repository so its package does not shadow the reference
+
+
 def main(argv=None) -> list:
     argv = list(sys.argv[1:] if argv is None else argv)
     extra = []
@@ -59,6 +83,8 @@ def main(argv=None) -> list:
     ap.add_argument("--prefix-len", type=int, default=512, help="length of the shared prompt prefixes")
     ap.add_argument("--startup-timeout", type=float, default=1800)
     ap.add_argument("--seed", type=int, default=42)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours",
+                    help="serve with this engine, or with the unmodified reference installed in baseline/_ref")
     a = ap.parse_args(argv)
 
     from minisgl.benchmark.client import (read_mooncake_trace, read_qwen_trace, run_trace, scale_traces,
@@ -66,11 +92,14 @@ def main(argv=None) -> list:
     from minisgl.utils.hf import load_tokenizer
 
     cmd = [sys.executable, "-m", "minisgl", "--model", a.model, "--tp", str(a.tp), "--port", str(a.port)] + extra
+    env, cwd = None, None
+    if a.impl == "reference":
+        env, cwd = _reference_env()
     from minisgl.utils.proc import die_with_parent
 
     # its own process group (killed as a group below), and killed by the kernel if this launcher dies
     # first (a timeout or a signal skips the finally clause)
-    proc = subprocess.Popen(cmd, start_new_session=True, preexec_fn=die_with_parent)
+    proc = subprocess.Popen(cmd, start_new_session=True, preexec_fn=die_with_parent, env=env, cwd=cwd)
     rows = []
     try:
         wait_ready(a.port, proc, a.startup_timeout)

@@ -39,3 +39,58 @@ def compare_memory_kernel_perf(ours: Callable[[], object], baseline: Callable[[]
            "baseline_gbs": nbytes / t1 / 1e6, "speedup": t1 / t0}
     print(f"{name}: ours {res['ours_gbs']:.0f} GB/s, baseline {res['baseline_gbs']:.0f} GB/s, x{res['speedup']:.2f}")
     return res
+
+
+class ClockSampler:
+    """``nvidia-smi`` samples of the SM clock and the throttle reasons of one GPU every 200 ms
+    between ``start()`` and ``stop()`` (a benchmark's timed region); ``stop()`` returns the median SM
+    clock under load, the maximum clock and every throttle reason that was active."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.path = None
+
+    def start(self) -> None:
+        import os
+        import subprocess
+        import tempfile
+
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        import os
+        import statistics
+
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        sm, mx, reasons = [], [], set()
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(self.REASONS, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}

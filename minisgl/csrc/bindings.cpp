@@ -551,4 +551,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvls_allreduce_rmsnorm", &nvls_allreduce_rmsnorm);
   m.def("num_sms", []() { return msgl_num_sms(); });
   m.def("gemm_splits", [](int64_t M, int64_t N, int64_t K) { return msgl_gemm_pick_splits(M, N, K); });
+  m.def("gemm_force_bn", [](int64_t bn) { msgl_gemm_force_bn((int)bn); });
 }

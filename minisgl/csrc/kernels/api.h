@@ -58,6 +58,8 @@ void msgl_gemm_ex2(void* out, const void* x, const void* w, int w_blocked, const
 void msgl_gemm_ex3(void* out, const void* x, const void* w, int w_blocked, const void* bias, int M, int N,
                    int K, int ldo, int epi, int force_splits, int force_wide, void* workspace, int64_t ws_cap,
                    uint32_t* arrive_ticket, void* arrive_mc, cudaStream_t s);
+// Token-tile override for tiling sweeps and tests (-1 restores the automatic choice).
+void msgl_gemm_force_bn(int bn);
 // LM-head greedy pick fused into the GEMM (out = x @ w^T is never written): part is
 // [ceil(N / 32)][M] float2 {largest value, its row}; msgl_argmax_partials reduces it per token to the
 // row (+ id_offset) and optionally its value. Ties resolve to the lowest row.

@@ -25,6 +25,7 @@
 // receive slots. Owners add them to their TMEM accumulator and run the epilogue. No global
 // atomics, no workspace.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -525,8 +526,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
     }
   }
   if (warp >= 2 && lane == 0) {
-    bulk_wait<0>();
-    if (p.arrive_mc != nullptr) fence_proxy_async_global();
+    // Exiting only needs the staging smem read out (the writes complete before the grid does);
+    // a GEMM that signals other ranks waits for its writes to land first.
+    if (p.arrive_mc != nullptr) {
+      bulk_wait<0>();
+      fence_proxy_async_global();
+    } else {
+      bulk_wait_read<0>();
+    }
   }
 
   tc_fence_before();
@@ -849,8 +856,14 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
     }
   }
   if (warp >= 2 && lane == 0) {
-    bulk_wait<0>();
-    if (p.arrive_mc != nullptr) fence_proxy_async_global();
+    // Exiting only needs the staging smem read out (the writes complete before the grid does);
+    // a GEMM that signals other ranks waits for its writes to land first.
+    if (p.arrive_mc != nullptr) {
+      bulk_wait<0>();
+      fence_proxy_async_global();
+    } else {
+      bulk_wait_read<0>();
+    }
   }
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its pair / cluster peers may still address its smem / TMEM
@@ -962,12 +975,27 @@ struct Plan {
 // tiles with BN = round-up(M) <= 256 tokens; gated outputs use 256-row tiles (128 gate + 128 up)
 // with BN <= 256 for decode and 128 for prefill. Split-K (a cluster of 2 or 4 CTAs per tile,
 // reduced through DSMEM) only pays off for long K with few tiles.
-// Gated outputs of a small weight matrix (a tensor-parallel shard's gate_up: few 256-row tiles):
-// 128-token tiles on one SM, so split-K can spread the weights over every SM (decode-shape sweep on
-// B200: 2.2x faster at TP8, 1.8x at TP4 than one 256-token 2-SM tile per 512 rows).
+// Plans for the decode GEMMs of tensor-parallel shards (few weight tiles), chosen from a sweep of
+// every tiling at Qwen3-14B's TP2/4/8 shapes on B200 (`python -m minisgl.benchmark.kernels
+// gemm-sweep`):
+//  * gated outputs (gate_up) whose 256-row tiles x 128-token tiles fit in one wave: 128-token tiles
+//    on one SM, with split-K while at most half the SMs would be busy (2.2x at TP8, 1.8x at TP4 and
+//    1.6x at TP2 with 256 tokens, against one 256-token 2-SM tile per 512 rows);
+//  * plain outputs of at most 16M weights with more than 64 tokens: 128-token tiles on one SM and
+//    enough K-splits for about one wave (1.2-1.35x for the QKV / o_proj / down_proj shards at
+//    TP4/TP8): several token tiles per weight tile keep each CTA's activation traffic near its
+//    weight traffic instead of streaming all 256 tokens' activations per weight tile.
 static bool small_gated(int M, int N, int epi) {
-  return is_act(epi) && (N / 256) * ((M + 127) / 128) <= num_sms_cached() / 2;
+  const int tiles = (N / 256) * ((M + 127) / 128);
+  return is_act(epi) && tiles <= (M <= 128 ? num_sms_cached() / 2 : num_sms_cached());
 }
+static bool small_plain(int M, int N, int K, int epi) {
+  return !is_act(epi) && epi != kArgmax && M > 64 && (int64_t)N * K <= (16ll << 20);
+}
+
+// Token-tile override for tiling sweeps and tests (-1: automatic). 1-SM kernel: 16/32/64/128/256;
+// 2-SM kernel: 64/128/160/192/224/256. Not for concurrent use.
+static std::atomic<int> g_force_bn{-1};
 
 static Plan make_plan(int M, int N, int K, int epi, int force_splits, int force_wide) {
   Plan pl;
@@ -975,7 +1003,9 @@ static Plan make_plan(int M, int N, int K, int epi, int force_splits, int force_
   if (M <= 256) pl.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
   else pl.bn = act ? 128 : 256;
   const bool gated_split = force_wide < 0 && small_gated(M, N, epi);
-  if (gated_split) pl.bn = std::min(pl.bn, 128);
+  const bool plain_split = force_wide < 0 && small_plain(M, N, K, epi);
+  if (gated_split || plain_split) pl.bn = std::min(pl.bn, 128);
+  if (const int fb = g_force_bn.load(); fb == 16 || fb == 32 || fb == 64 || fb == 128 || fb == 256) pl.bn = fb;
   pl.wide = act || force_wide == 1;
   pl.rows_a = pl.wide ? 256 : 128;
   pl.tiles = ((N + pl.rows_a - 1) / pl.rows_a) * ((M + pl.bn - 1) / pl.bn);
@@ -985,8 +1015,11 @@ static Plan make_plan(int M, int N, int K, int epi, int force_splits, int force_
   const bool can_split = !(pl.rows_a == 256 && pl.bn > 128);
   int splits = 1;
   if (force_splits > 0) splits = force_splits;
-  else if (gated_split && kblocks >= 16) {
+  else if (gated_split && kblocks >= 16 && pl.tiles <= sms / 2) {
     splits = std::max(1, std::min(std::min(sms / pl.tiles, kblocks / 8), 4));
+  } else if (plain_split) {
+    // short K (the TP8 o_proj shard: 10 k-blocks) with up to 128 tokens gains nothing from splits
+    if (kblocks >= 16 || M > 128) splits = std::max(1, std::min(std::min((sms + pl.tiles - 1) / pl.tiles, kblocks / 2), 8));
   } else if (!act && M <= 128 && pl.tiles <= sms / 2 && kblocks >= 16) {
     // weight-streaming regime: use as many K-splits as keep every SM busy in one wave
     splits = std::max(1, std::min(sms / pl.tiles, kblocks / 8));
@@ -1134,7 +1167,7 @@ static bool use_2sm(int M, int N, int K, int epi, int force_wide, int w_blocked)
   if (force_wide >= 0) return false;
   if (const char* e = getenv("MINISGL_GEMM_2SM"))
     if (e[0] == '0') return false;
-  if (small_gated(M, N, epi)) return false;
+  if (small_gated(M, N, epi) || small_plain(M, N, K, epi)) return false;
   return M > 64 && K >= 4096;
 }
 
@@ -1169,6 +1202,8 @@ static void launch_2sm(const void* x, const void* w, const void* bias, void* out
   // those re-read the weight tile from smem twice as often and saturate smem bandwidth.
   int bn = M <= 64 ? 64 : M <= 128 ? 128 : ((M + 31) / 32) * 32;
   if (M > 256) bn = 256;
+  if (const int fb = g_force_bn.load(); fb >= 64 && fb <= 256 && (fb == 64 || fb % 32 == 0) && (fb <= 128 || fb >= 160))
+    bn = fb;
   p.n_tiles = (N + (act ? 511 : 255)) / (act ? 512 : 256);
   p.m_tiles = (M + bn - 1) / bn;
   const int tiles = p.n_tiles * p.m_tiles;
@@ -1197,6 +1232,7 @@ static void gemm_run(void* out, const void* x, const void* w, int w_blocked, con
                      uint32_t* arrive_ticket, void* arrive_mc, float2* argmax_out, cudaStream_t s);
 
 extern "C" int msgl_gemm_pick_splits(int M, int N, int K) { return make_plan(M, N, K, kBf16, -1, -1).splits; }
+extern "C" void msgl_gemm_force_bn(int bn) { g_force_bn.store(bn); }
 
 // split-K exchange buffer of the 2-SM kernel: (pair tiles) x 2 x S(<=4) x 256 rows x 256 tokens fp32
 extern "C" int msgl_gemm_workspace_bytes(int M, int N, int K, int splits) {

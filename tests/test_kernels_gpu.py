@@ -526,3 +526,24 @@ def test_lm_head_argmax(M, N, n_valid, K):
     got = logits.gather(1, (ids.long() - 5).clamp(0, n_valid - 1)[:, None])[:, 0]
     torch.testing.assert_close(got.cpu(), top2[:, 0].cpu(), atol=1e-3, rtol=1e-4)
     torch.testing.assert_close(vals.cpu(), top2[:, 0].cpu(), atol=1e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("M", [100, 256])
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("wide,splits", [(0, 1), (0, 2), (0, 6), (0, 8), (1, 3), (2, 1), (2, 4)])
+def test_gemm_token_tiles(M, bn, wide, splits):
+    """Token-tile overrides (several token tiles per weight tile) with split-K up to 8-CTA clusters:
+    the tilings a tiling sweep may pick, against the fp32 reference."""
+    K, N = 1536, 768
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(N, K, device=DEV, dtype=torch.bfloat16) / math.sqrt(K)
+    expect = x.cpu().float() @ w.cpu().float().t()
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    try:
+        _c().gemm_force_bn(bn)
+        for _ in range(2):
+            out.zero_()
+            _c().gemm_ex(out, x, w, None, 0, splits, wide)
+            _close(out, expect, 3e-2, 3e-2)
+    finally:
+        _c().gemm_force_bn(-1)

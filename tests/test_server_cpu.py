@@ -276,3 +276,23 @@ def test_online_benchmark_launcher(tmp_path, free_port):
                  "--", "--device", "cpu", "--dtype", "float32", "--max-running-requests", "8"])
     assert [r["rate"] for r in rows] == [20.0, 40.0]
     assert all(r["completed"] == 6 and r["ttft_p50"] > 0 for r in rows)
+
+
+def test_online_reference_environment():
+    """``--impl reference``: the child's ``minisgl`` resolves to the reference installed in
+    baseline/_ref, and its API server's prompt_toolkit imports resolve to the stand-in package."""
+    import os
+    import subprocess
+    import sys
+
+    from minisgl.benchmark.online import _reference_env
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    if not os.path.isdir(os.path.join(root, "baseline", "_ref", "minisgl")):
+        pytest.skip("reference not installed in baseline/_ref")
+    env, cwd = _reference_env()
+    code = ("import minisgl, prompt_toolkit; from prompt_toolkit import PromptSession; "
+            "from prompt_toolkit.completion import WordCompleter; print(list(minisgl.__path__))")
+    out = subprocess.run([sys.executable, "-c", code], env=env, cwd=cwd, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    assert os.path.join("baseline", "_ref") in out.stdout
