@@ -9,7 +9,7 @@ times without timing, which is the form to wrap in a profiler.
   gemm          bf16 GEMM  out[M, N] = x[M, K] @ w[N, K]^T  (--epi 0 bf16, 1 SiLU-gated, 3 fp32)
   gemm-sweep    Qwen3-14B decode GEMMs per TP degree: automatic plan vs every forced tiling vs cuBLAS
   decode-attn   paged decode attention over a longest-first work list (page size 64)
-  prefill-attn  ragged causal prefill attention (requests of 100..1024 tokens; --impl tcgen05 | mma)
+  prefill-attn  ragged causal prefill attention (requests of 100..1024 tokens; --impl tcgen05 | mma | trtllm)
   suite         every other hot kernel once at decode shapes (Qwen3-14B, --bs tokens; MoE at
                 Qwen3-30B-A3B shapes): embedding, RMSNorm, fused add+RMSNorm, QK-norm+RoPE+KV
                 store, KV store, SiLU-mul, 1-SM and 2-SM GEMMs, argmax, top-k/top-p sampling and
@@ -136,9 +136,27 @@ def _prefill_attn(a, c) -> None:
     cu = torch.tensor([0] + lens, dtype=torch.int32).cumsum(0).to(torch.int32).cuda()
     q = torch.randn(tot, nq, hd, device="cuda", dtype=torch.bfloat16)
     o = torch.empty_like(q)
+    if a.impl == "trtllm":  # FlashInfer's trtllm-gen context kernel on the same requests (64-token pages)
+        from flashinfer.prefill import trtllm_batch_context_with_kv_cache
+
+        npg = [(n + 63) // 64 for n in lens]
+        kp = torch.randn(sum(npg), 64, nkv, hd, device="cuda", dtype=torch.bfloat16)
+        vp = torch.randn_like(kp)
+        bt = torch.zeros(bs, max(npg), dtype=torch.int32)
+        first = 0
+        for b_, m_ in enumerate(npg):
+            bt[b_, :m_] = torch.arange(first, first + m_)
+            first += m_
+        bt = bt.cuda()
+        fi_ws = torch.empty(128 << 20, dtype=torch.uint8, device="cuda")
 
     def run():
-        if a.impl == "tcgen05":
+        if a.impl == "trtllm":
+            trtllm_batch_context_with_kv_cache(
+                query=q, kv_cache=(kp, vp), workspace_buffer=fi_ws, block_tables=bt, seq_lens=kvl,
+                max_q_len=max(lens), max_kv_len=max(lens), bmm1_scale=1 / math.sqrt(hd), bmm2_scale=1.0,
+                cum_seq_lens_q=cu, cum_seq_lens_kv=cu, kv_layout="NHD", batch_size=bs, out_dtype=q.dtype)
+        elif a.impl == "tcgen05":
             c.attention_prefill_fmha(o, q, kc, vc, pt, rows, cu, kvl, max(lens), 1 / math.sqrt(hd), -1, None, 64)
         else:
             c.attention_prefill(o, q, kc, vc, pt, rows, cu, kvl, max(lens), 1 / math.sqrt(hd), -1, None)
@@ -321,7 +339,8 @@ def main(argv=None) -> None:
     p.add_argument("--nq", type=int, default=40)
     p.add_argument("--nkv", type=int, default=8)
     p.add_argument("--tokens", type=int, default=16384)
-    p.add_argument("--impl", default="tcgen05", choices=["tcgen05", "mma"], help="prefill-attn kernel")
+    p.add_argument("--impl", default="tcgen05", choices=["tcgen05", "mma", "trtllm"],
+                   help="prefill-attn kernel (trtllm: FlashInfer's trtllm-gen kernel, for comparison)")
     p.add_argument("--once", action="store_true", help="run a few times untimed (for profilers)")
     a = p.parse_args(argv)
     from minisgl._native import cuda

@@ -1085,21 +1085,27 @@ int run_paged_decode(const PagedDecodeParams& p, const void* q, int q_rows, cons
 // the tile's TT x G packed (token, head) rows are the MMA M = 128 rows (G = query heads per kv head).
 //
 //   warp 0     TMA: the Q tile once (3-D box 64 dims x G heads x TT tokens, per 64-dim half), then
-//              per 128-key block the K and V pages (3-D boxes over [slots, kv heads, head dim])
-//              into a 2-stage ring; page-table entries are fetched by the warp's lanes in batches.
+//              per 128-key block the K pages and the V pages (3-D boxes over [slots, kv heads, head
+//              dim]) into separate 2-stage rings: a K stage is released as soon as its QK^T MMA
+//              completes, a V stage once its PV MMA does. Page-table entries are fetched by the
+//              warp's lanes in batches of 32 pages.
 //   warp 1     MMA: S_i = Q K_i^T into one of two TMEM S buffers, then O += P_{i-1} V_{i-1} once
 //              the softmax warps have written P_{i-1} (V is an MN-major operand: its 128-byte rows
 //              are keys), so QK of block i overlaps the softmax of block i - 1.
-//   warps 2-5  softmax, one thread per row (TMEM lane): read the S row, mask (causal / length /
-//              window), online max and sum in the log2 domain, P row as bf16 into a 128B-swizzled
-//              smem tile (the A operand of the PV MMA). O is rescaled in TMEM only when a row's
-//              max grows by more than 2^8 (lazy rescaling: P then stays <= 256), and always before
-//              the PV that follows. Epilogue: O / l (with the sink term) stored as bf16.
+//   warps 2-9  softmax: two warps per TMEM lane quadrant (a warp may only address the quadrant
+//              warp % 4), one for keys 0-63 and one for keys 64-127 of each block. Both read the
+//              whole S row to take the same row maximum (no exchange needed), and each turns its
+//              64 keys into P (bf16, 128B-swizzled smem: the A operand of the PV MMA) in one of two
+//              P buffers, so block i's softmax only waits for the PV of block i - 2. Masks (causal,
+//              length, window) are applied only on blocks that cross a row's limits. O is rescaled
+//              in TMEM (each warp its 64 columns) only when a row's max grows by more than 2^8
+//              (lazy rescaling: P then stays <= 256). Epilogue: the two partial row sums are added
+//              through shared memory, O / l (with the sink term) stored as bf16.
 // TMEM: S buffers at columns 0 and 128, O at 256 (512 allocated).
 namespace {
 
 constexpr int kFmKB = 128;  // keys per block
-constexpr int kFmThreads = 192;
+constexpr int kFmThreads = 320;
 
 struct FmhaParams {
   __nv_bfloat16* o;
@@ -1113,21 +1119,36 @@ struct FmhaParams {
   int nq, nkv, group, tt, page;
   float scale_log2;
   int window;
+  int num_reqs;
 };
 
 struct FmSmem {
-  static constexpr int kQ = 2 * 128 * 128;           // two 64-dim halves x 128 rows x 128 B
-  static constexpr int kHalf = 128 * 128;            // one 64-dim half of a 128-key block
-  static constexpr int kKV = 4 * kHalf;              // K (2 halves) + V (2 halves)
-  static constexpr int kP = 2 * 128 * 128;           // P: two 64-key halves x 128 rows x 128 B
-  static constexpr int kOffKV = kQ;
-  static constexpr int kOffP = kQ + 2 * kKV;
-  static constexpr int kOffBar = kOffP + kP;
+  static constexpr int kHalf = 128 * 128;    // one 64-dim half of a 128-row / 128-key tile
+  static constexpr int kQ = 2 * kHalf;       // Q: two 64-dim halves x 128 rows x 128 B
+  static constexpr int kT = 2 * kHalf;       // one K or V stage (two 64-dim halves)
+  static constexpr int kP = 2 * kHalf;       // one P buffer: two 64-key halves x 128 rows x 128 B
+  static constexpr int kOffK = kQ;
+  static constexpr int kOffV = kOffK + 2 * kT;
+  static constexpr int kOffP = kOffV + 2 * kT;
+  static constexpr int kOffBar = kOffP + 2 * kP;
   static constexpr int kBytes = 1024 + kOffBar + 256;
 };
+static_assert(FmSmem::kBytes <= 227 * 1024, "prefill attention shared memory exceeds the per-CTA limit");
 
 __device__ __forceinline__ uint32_t fm_swz(int row, int chunk) {  // 128B swizzle within a half tile
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// Issue the TMA loads of one 128-key block's pages (K or V) into a stage: each page is `g` keys,
+// two 64-dim halves. `slot` holds the page's first KV slot in lane (page index - first) of the warp.
+__device__ __forceinline__ void fm_load_pages(uint8_t* stage, const CUtensorMap* map, uint64_t* bar, int kvh,
+                                              int slot, int first, int gpb, int g, int lane) {
+  for (int sub = 0; sub < gpb; ++sub) {
+    const int s0 = __shfl_sync(0xffffffffu, slot, first + sub);
+    if (lane == 0) {
+      for (int h = 0; h < 2; ++h) tma_load_3d(stage + h * FmSmem::kHalf + sub * g * 128, map, bar, h * 64, kvh, s0);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kFmThreads, 1)
@@ -1136,23 +1157,62 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sKV = smem + FmSmem::kOffKV;
+  uint8_t* sK = smem + FmSmem::kOffK;
+  uint8_t* sV = smem + FmSmem::kOffV;
   uint8_t* sP = smem + FmSmem::kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FmSmem::kOffBar);
   uint64_t* qfull = bars;
-  uint64_t* kvfull = bars + 1;   // [2]
-  uint64_t* kvempty = bars + 3;  // [2]
-  uint64_t* sfull = bars + 5;    // [2]
-  uint64_t* sempty = bars + 7;   // [2]
-  uint64_t* pfull = bars + 9;
-  uint64_t* pvdone = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* kfull = bars + 1;    // [2]
+  uint64_t* kempty = bars + 3;   // [2]
+  uint64_t* vfull = bars + 5;    // [2]
+  uint64_t* vempty = bars + 7;   // [2]
+  uint64_t* sfull = bars + 9;    // [2]
+  uint64_t* sempty = bars + 11;  // [2]
+  uint64_t* pfull = bars + 13;   // [2], one per P buffer
+  uint64_t* pvdone = bars + 15;  // [2], PV of the block that used that P buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
-  const int qb = blockIdx.x, b = blockIdx.y, kvh = blockIdx.z;
+  const int kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.group, TT = p.tt;
   pdl_wait();
   pdl_launch();
+  // blockIdx.x is a linear index over every request's ceil(q_len / TT) query tiles (the grid has a
+  // few spare CTAs, which exit here): warp 0 finds the request with a prefix scan of the tile
+  // counts. Within a request the last tile (the most key blocks) is dispatched first.
+  int* tile_info = reinterpret_cast<int*>(bars + 18);
+  if (warp == 0) {
+    const int tile = blockIdx.x;
+    int fb = -1, fq = 0, before = 0;
+    for (int base = 0; base < p.num_reqs; base += 32) {
+      const int j = base + lane;
+      int c = 0;
+      if (j < p.num_reqs) c = max(0, (p.cu_q[j + 1] - p.cu_q[j] + TT - 1) / TT);
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int tot = __shfl_sync(0xffffffffu, incl, 31);
+      if (tile < before + tot) {  // warp-uniform
+        const int first = __ffs(__ballot_sync(0xffffffffu, tile < before + incl)) - 1;
+        const int excl = __shfl_sync(0xffffffffu, incl - c, first);
+        const int cnt = __shfl_sync(0xffffffffu, c, first);
+        fb = base + first;
+        fq = cnt - 1 - (tile - before - excl);
+        break;
+      }
+      before += tot;
+    }
+    if (lane == 0) {
+      tile_info[0] = fb;
+      tile_info[1] = fq;
+    }
+  }
+  __syncthreads();
+  const int b = tile_info[0], qb = tile_info[1];
+  if (b < 0) return;  // CTA-uniform
   const int q0 = p.cu_q[b], n = p.cu_q[b + 1] - q0;
   const int t0 = qb * TT;
   if (t0 >= n) return;
@@ -1169,13 +1229,15 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   if (threadIdx.x == 0) {
     mbar_init(qfull, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kvfull[i], 1);
-      mbar_init(&kvempty[i], 1);
+      mbar_init(&kfull[i], 1);
+      mbar_init(&kempty[i], 1);
+      mbar_init(&vfull[i], 1);
+      mbar_init(&vempty[i], 1);
       mbar_init(&sfull[i], 1);
-      mbar_init(&sempty[i], 4);
+      mbar_init(&sempty[i], 8);
+      mbar_init(&pfull[i], 8);
+      mbar_init(&pvdone[i], 1);
     }
-    mbar_init(pfull, 4);
-    mbar_init(pvdone, 1);
     fence_barrier_init();
     prefetch_tmap(&tq);
     prefetch_tmap(&tk);
@@ -1200,6 +1262,7 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     const int32_t* pt = p.page_table + (int64_t)p.rows[b] * p.pt_stride;
     const int ngroups = nb * gpb;
     bool ok = true;
+    // 32 pages per batch of page-table reads; 32 is a multiple of the pages per block (2, 4 or 8)
     for (int g0 = 0; ok && g0 < ngroups; g0 += 32) {
       int slot = 0;
       if (g0 + lane < ngroups) {
@@ -1207,109 +1270,127 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         slot = pos < L ? pt[pos] : 0;
         if (!MSGL_IN_BOUNDS(slot >= 0 && slot < p.num_slots, kBcAttnSlot)) slot = 0;
       }
-      const int gend = min(32, ngroups - g0);
-      for (int k = 0; k < gend; ++k) {
-        const int s0 = __shfl_sync(0xffffffffu, slot, k);
-        const int gi = g0 + k, i = gi / gpb, sub = gi % gpb, st = i & 1;
-        if (lane == 0 && ok) {
-          if (sub == 0) {
-            if (!mbar_wait(&kvempty[st], ((i >> 1) & 1) ^ 1, 500)) ok = false;
-            else mbar_expect_tx(&kvfull[st], FmSmem::kKV);
-          }
-          if (ok) {
-            uint8_t* kt = sKV + st * FmSmem::kKV;
-            for (int h = 0; h < 2; ++h) {
-              tma_load_3d(kt + h * FmSmem::kHalf + sub * g * 128, &tk, &kvfull[st], h * 64, kvh, s0);
-              tma_load_3d(kt + (2 + h) * FmSmem::kHalf + sub * g * 128, &tv, &kvfull[st], h * 64, kvh, s0);
-            }
-          }
+      const int bend = min(32, ngroups - g0) / gpb;
+      for (int bi = 0; ok && bi < bend; ++bi) {
+        const int i = g0 / gpb + bi, st = i & 1;
+        const uint32_t par = ((i >> 1) & 1) ^ 1;
+        if (lane == 0) {
+          ok = mbar_wait(&kempty[st], par, 500);
+          if (ok) mbar_expect_tx(&kfull[st], FmSmem::kT);
         }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        fm_load_pages(sK + st * FmSmem::kT, &tk, &kfull[st], kvh, slot, bi * gpb, gpb, g, lane);
+        if (lane == 0) {
+          ok = mbar_wait(&vempty[st], par, 501);
+          if (ok) mbar_expect_tx(&vfull[st], FmSmem::kT);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        fm_load_pages(sV + st * FmSmem::kT, &tv, &vfull[st], kvh, slot, bi * gpb, gpb, g, lane);
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, kFmKB);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128) | kIdescBMajorMN;
-      const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP);
+      const uint32_t q_base = smem_u32(sQ);
       bool ok = mbar_wait(qfull, 0, 510);
-      auto issue_pv = [&](int j) {
+      auto issue_pv = [&](int j) -> bool {
         const int st = j & 1;
-        const uint32_t v_base = smem_u32(sKV + st * FmSmem::kKV + 2 * FmSmem::kHalf);
+        const uint32_t par = (j >> 1) & 1;
+        if (!mbar_wait(&pfull[st], par, 513) || !mbar_wait(&vfull[st], par, 514)) return false;
+        tc_fence_after();
+        const uint32_t p_base = smem_u32(sP + st * FmSmem::kP);
+        const uint32_t v_base = smem_u32(sV + st * FmSmem::kT);
 #pragma unroll
         for (int k = 0; k < kFmKB / 16; ++k) {  // 16 keys per MMA
           const uint64_t a = smem_desc_sw128(p_base + (k >> 2) * 128 * 128 + (k & 3) * 32);
           const uint64_t bd = smem_desc_sw128_mn(v_base + k * 16 * 128, FmSmem::kHalf);
           tc_mma_f16(tmem + 256, a, bd, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
         }
-        tc_commit(&kvempty[st]);
-        tc_commit(pvdone);
+        tc_commit(&vempty[st]);
+        tc_commit(&pvdone[st]);
+        return true;
       };
       for (int i = 0; ok && i < nb; ++i) {
-        const int st = i & 1, sb = i & 1;
-        if (!mbar_wait(&kvfull[st], (i >> 1) & 1, 511)) { ok = false; break; }
-        if (!mbar_wait(&sempty[sb], ((i >> 1) & 1) ^ 1, 512)) { ok = false; break; }
+        const int st = i & 1;
+        const uint32_t par = (i >> 1) & 1;
+        if (!mbar_wait(&kfull[st], par, 511) || !mbar_wait(&sempty[st], par ^ 1, 512)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t k_base = smem_u32(sKV + st * FmSmem::kKV);
+        const uint32_t k_base = smem_u32(sK + st * FmSmem::kT);
 #pragma unroll
         for (int k = 0; k < 128 / 16; ++k) {  // head dim, 16 per MMA
           const uint32_t off = (k >> 2) * 128 * 128 + (k & 3) * 32;
-          tc_mma_f16(tmem + sb * kFmKB, smem_desc_sw128(q_base + off), smem_desc_sw128(k_base + off), idesc_s,
+          tc_mma_f16(tmem + st * kFmKB, smem_desc_sw128(q_base + off), smem_desc_sw128(k_base + off), idesc_s,
                      k > 0 ? 1u : 0u);
         }
-        tc_commit(&sfull[sb]);
-        if (i > 0) {
-          if (!mbar_wait(pfull, (i - 1) & 1, 513)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(i - 1);
-        }
+        tc_commit(&kempty[st]);
+        tc_commit(&sfull[st]);
+        if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
       }
-      if (ok && nb > 0 && mbar_wait(pfull, (nb - 1) & 1, 514)) {
-        tc_fence_after();
-        issue_pv(nb - 1);
-      }
+      if (ok && nb > 0) issue_pv(nb - 1);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // accumulator row == TMEM lane
+    const int half = (warp - 2) >> 2;  // keys / O columns [64 * half, 64 * half + 64)
+    const int r = quad * 32 + lane;    // accumulator row == TMEM lane
     const int t = r / G, gh = r - t * G;
     const bool row_ok = r < TT * G && t0 + t < t1;
     const int qpos = qpos0 + t0 + t;
+    const int kmax = min(qpos + 1, L);  // keys [kmin, kmax) are visible to this row
+    const int kmin = p.window > 0 ? qpos - p.window + 1 : 0;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const uint32_t own_col = half * 64, oth_col = (half ^ 1) * 64;
+    const float sl2 = p.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool dead = false;
     for (int i = 0; i < nb; ++i) {
       const int sb = i & 1;
-      if (!dead && !mbar_wait(&sfull[sb], (i >> 1) & 1, 520)) dead = true;
+      const uint32_t par = (i >> 1) & 1;
+      if (!dead && !mbar_wait(&sfull[sb], par, 520)) dead = true;
       tc_fence_after();
-      float s[kFmKB];
-#pragma unroll
-      for (int c = 0; c < kFmKB / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(lane_base + sb * kFmKB + c * 32, v);
+      float so[64], sx[64];  // this warp's 64 keys, the partner warp's 64 keys
+      {
+        uint32_t u0[32], u1[32], u2[32], u3[32];
+        const uint32_t sa = lane_base + sb * kFmKB;
+        tmem_ld_32x32b_x32(sa + own_col, u0);
+        tmem_ld_32x32b_x32(sa + own_col + 32, u1);
+        tmem_ld_32x32b_x32(sa + oth_col, u2);
+        tmem_ld_32x32b_x32(sa + oth_col + 32, u3);
         tc_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(v[j]);
+        for (int j = 0; j < 32; ++j) {
+          so[j] = __uint_as_float(u0[j]);
+          so[32 + j] = __uint_as_float(u1[j]);
+          sx[j] = __uint_as_float(u2[j]);
+          sx[32 + j] = __uint_as_float(u3[j]);
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sempty[sb]);
+      // visible key range of this row inside the block, relative to each 64-key half
       const int k0 = (blk0 + i) * kFmKB;
+      const int lim = row_ok ? kmax - k0 : 0, lo = kmin - k0;
       float mx = -INFINITY;
+      if (lo <= 0 && lim >= kFmKB) {
 #pragma unroll
-      for (int j = 0; j < kFmKB; ++j) {
-        const int kp = k0 + j;
-        bool valid = row_ok && kp <= qpos && kp < L;
-        if (p.window > 0) valid = valid && kp > qpos - p.window;
-        s[j] = valid ? s[j] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[j]);
+        for (int j = 0; j < 64; ++j) mx = fmaxf(mx, fmaxf(so[j], sx[j]));
+      } else {
+        const int lo_o = lo - (int)own_col, lim_o = lim - (int)own_col;
+        const int lo_x = lo - (int)oth_col, lim_x = lim - (int)oth_col;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          so[j] = (j >= lo_o && j < lim_o) ? so[j] : -INFINITY;
+          const float x = (j >= lo_x && j < lim_x) ? sx[j] : -INFINITY;
+          mx = fmaxf(mx, fmaxf(so[j], x));
+        }
       }
-      // P buffer and O are free once the previous PV has completed
-      if (i > 0 && !dead && !mbar_wait(pvdone, (i - 1) & 1, 521)) dead = true;
-      tc_fence_after();
-      const bool grow = mx > m + 8.f;  // lazy rescale threshold (log2 domain)
+      mx *= sl2;  // log2 domain (the scale is positive, so the max commutes with it)
+      const bool grow = mx > m + 8.f;  // lazy rescale threshold
       float alpha = 1.f;
       if (grow) {
         alpha = m == -INFINITY ? 0.f : exp2f(m - mx);
@@ -1317,56 +1398,63 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         m = mx;
       }
       if (i > 0 && __any_sync(0xffffffffu, grow)) {
+        // O holds PV up to block i - 1: wait for it, then rescale this warp's 64 columns
+        if (!dead && !mbar_wait(&pvdone[(i - 1) & 1], ((i - 1) >> 1) & 1, 521)) dead = true;
+        tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_base + 256 + c * 32, v);
+          tmem_ld_32x32b_x32(lane_base + 256 + own_col + c * 32, v);
           tc_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
-          tmem_st_32x32b_x32(lane_base + 256 + c * 32, v);
+          tmem_st_32x32b_x32(lane_base + 256 + own_col + c * 32, v);
         }
         tc_wait_st();
       }
       const float base = m == -INFINITY ? 0.f : m;
       float sum = 0.f;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint8_t* ph = sP + h * 128 * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float e[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            e[j] = exp2f(s[h * 64 + c * 8 + j] - base);
-            sum += e[j];
-          }
-          *reinterpret_cast<uint4*>(ph + fm_swz(r, c)) =
-              make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]), pack_bf16(e[4], e[5]), pack_bf16(e[6], e[7]));
-        }
+      for (int j = 0; j < 64; ++j) {
+        so[j] = exp2f(fmaf(so[j], sl2, -base));
+        sum += so[j];
       }
       l += sum;
+      // P buffer sb is free once the PV of block i - 2 has completed
+      if (i >= 2 && !dead && !mbar_wait(&pvdone[sb], ((i - 2) >> 1) & 1, 522)) dead = true;
+      uint8_t* ph = sP + sb * FmSmem::kP + half * FmSmem::kHalf;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        *reinterpret_cast<uint4*>(ph + fm_swz(r, c)) =
+            make_uint4(pack_bf16(so[c * 8 + 0], so[c * 8 + 1]), pack_bf16(so[c * 8 + 2], so[c * 8 + 3]),
+                       pack_bf16(so[c * 8 + 4], so[c * 8 + 5]), pack_bf16(so[c * 8 + 6], so[c * 8 + 7]));
+      }
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(pfull);
+      if (lane == 0) mbar_arrive(&pfull[sb]);
     }
-    // epilogue: wait for the last PV, normalise, store
-    if (nb > 0 && !dead) mbar_wait(pvdone, (nb - 1) & 1, 522);
+    // epilogue: wait for the last PV, add the partner's partial row sum, normalise, store
+    if (nb > 0 && !dead) mbar_wait(&pvdone[(nb - 1) & 1], ((nb - 1) >> 1) & 1, 523);
     tc_fence_after();
-    float f = 1.f, ll = l;
+    // every MMA has completed, so the P buffers are free for the row-sum exchange
+    float* xl = reinterpret_cast<float*>(sP);
+    xl[half * 128 + r] = l;
+    named_bar_sync(1 + quad, 64);  // the two warps of this quadrant (both always get here)
+    const float lt = l + xl[(half ^ 1) * 128 + r];
+    float f = 1.f, ll = lt;
     if (p.sinks != nullptr) {
       const float sk = p.sinks[kvh * G + gh] * kLog2e;
       const float mn = fmaxf(m, sk);
       f = exp2f(m - mn);
-      ll = l * f + exp2f(sk - mn);
+      ll = lt * f + exp2f(sk - mn);
     }
     const float inv = ll > 0.f ? f / ll : 0.f;
-    __nv_bfloat16* dst = p.o + ((int64_t)(q0 + t0 + t) * p.nq + kvh * G + gh) * 128;
+    __nv_bfloat16* dst = p.o + ((int64_t)(q0 + t0 + t) * p.nq + kvh * G + gh) * 128 + own_col;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       uint32_t v[32];
-      tmem_ld_32x32b_x32(lane_base + 256 + c * 32, v);
+      tmem_ld_32x32b_x32(lane_base + 256 + own_col + c * 32, v);
       tc_wait_ld();
       if (row_ok) {
 #pragma unroll
@@ -1424,7 +1512,12 @@ extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total
   if (!pd_encode(&tq, q, 3, qdims, qstr, qbox) || !pd_encode(&tk, k_cache, 3, kdims, kstr, kbox) ||
       !pd_encode(&tv, v_cache, 3, kdims, kstr, kbox))
     return 2;
-  const dim3 grid((max_q_len + p.tt - 1) / p.tt, num_reqs, nkv);
+  p.num_reqs = num_reqs;
+  (void)max_q_len;
+  // upper bound of sum(ceil(q_len / tt)) over the requests
+  const int64_t tiles = (total_q + p.tt - 1) / p.tt + num_reqs;
+  if (tiles > INT32_MAX || nkv > 65535) return 3;
+  const dim3 grid((unsigned)tiles, nkv);
   msgl_launch(fmha_prefill_kernel, grid, dim3(kFmThreads), FmSmem::kBytes, s, 1, tq, tk, tv, p);
   return 0;
 }

@@ -701,17 +701,37 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
-      pdl_wait();
       int stage = 0;
       uint32_t phase = 0;
+      bool waited = false;
       for (int t = blockIdx.y; t < tiles; t += gridDim.y) {
         int nt, mt, kb0, kb1;
         tile_coords(t, p.n_tiles, p.m_tiles, nt, mt);
         split_range(ysplit, p.splits, p.kblocks, kb0, kb1);
         const int wrow = nt * 2 * C::kRowsA + x * C::kRowsA;
         const int trow = mt * BN + x * C::kTok;
+        int kb = kb0;
+        if (!waited) {
+          // Weights are static: fetch the first stages' weight tiles before waiting for the
+          // previous kernel (programmatic dependent launch), then the activations.
+          const int npre = min(C::kStages, kb1 - kb0);
+          for (int i = 0; i < npre; ++i) {
+            if (x == 0) mbar_expect_tx(&full[i], 2 * C::kStage);
+            const uint32_t fbar = dsmem_addr(smem_u32(&full[i]), leader);
+            tma_load_2d_2sm(stages + i * C::kStage, &tmap_w, fbar, (kb0 + i) * BK, wrow);
+          }
+          pdl_wait();
+          waited = true;
+          for (int i = 0; i < npre; ++i) {
+            const uint32_t fbar = dsmem_addr(smem_u32(&full[i]), leader);
+            tma_load_2d_2sm(stages + i * C::kStage + C::kA, &tmap_x, fbar, (kb0 + i) * BK, trow);
+          }
+          stage = npre % C::kStages;
+          phase = npre == C::kStages ? 1u : 0u;
+          kb = kb0 + npre;
+        }
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, 110)) { ok = false; break; }
           if (x == 0) mbar_expect_tx(&full[stage], 2 * C::kStage);
           uint8_t* a = stages + stage * C::kStage;
@@ -722,6 +742,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__
         }
         if (!ok) break;
       }
+      if (!waited) pdl_wait();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (leader only)

@@ -242,17 +242,18 @@ def _paged_decode_case(hd, nq, nkv, page, window, sinks, num_ctas, lens_kv):
 
 
 @pytest.mark.parametrize("nq,nkv", [(40, 8), (64, 8), (8, 8), (32, 2)])
-@pytest.mark.parametrize("page", [16, 64])
+@pytest.mark.parametrize("page", [16, 32, 64])
 @pytest.mark.parametrize("window,sinks", [(-1, False), (100, True)])
-def test_attention_prefill_tcgen05(nq, nkv, page, window, sinks):
-    """tcgen05 prefill attention (S / O in TMEM, MN-major V operand, lazy O rescaling) against the
-    fp32 reference: ragged requests, prefix hits (kv longer than q), partial last tiles."""
+def test_attention_prefill_tcgen05(nq, nkv, page, window, sinks, qscale=2.0):
+    """tcgen05 prefill attention (S / O in TMEM, MN-major V operand, lazy O rescaling, two softmax
+    warps per row split by keys) against the fp32 reference: ragged requests, prefix hits (kv
+    longer than q), partial last tiles."""
     hd = 128
     lens_q = [1, 17, 300, 64, 129, 700]
     lens_kv = [1, 40, 300, 400, 129, 1000]
     _, kc, vc, pt, rows, _, kvl = _paged_pages_setup(lens_kv, nq, nkv, hd, page, seed=3)
     g = torch.Generator(device="cpu").manual_seed(4)
-    q = (torch.randn(sum(lens_q), nq, hd, generator=g) * 2).to(DEV, torch.bfloat16)
+    q = (torch.randn(sum(lens_q), nq, hd, generator=g) * qscale).to(DEV, torch.bfloat16)
     cu = torch.zeros(len(lens_q) + 1, dtype=torch.int32)
     cu[1:] = torch.cumsum(torch.tensor(lens_q), 0)
     cu = cu.to(DEV)
@@ -265,6 +266,13 @@ def test_attention_prefill_tcgen05(nq, nkv, page, window, sinks):
     _close(o, e, 2e-2, 2e-2)
     assert _c().get_error() == (0, 0)
 
+
+
+@pytest.mark.parametrize("window", [-1, 300])
+def test_attention_prefill_tcgen05_peaked_scores(window):
+    """Large query norms: row maxima jump by far more than the lazy-rescale threshold from block
+    to block, so O is rescaled in TMEM on most blocks."""
+    test_attention_prefill_tcgen05(40, 8, 64, window, False, qscale=8.0)
 
 def test_argmax_and_greedy_sample():
     from minisgl import ops
