@@ -27,7 +27,7 @@ class _CountingModule:
 
     _NON_LAUNCH = {"get_error", "num_sms", "gemm_splits", "peer_flag_bytes", "peer_alloc", "peer_free",
                    "ipc_handle", "ipc_open", "ipc_close", "peer_grid", "nvls_grid", "nvls_flag_bytes",
-                   "nvls_state_words", "nvls_ticket_offset", "gemm_force_bn"}
+                   "nvls_state_words", "nvls_ticket_offset", "gemm_force_bn", "attention_prefill_trace"}
 
     def __init__(self, mod):
         self._mod = mod

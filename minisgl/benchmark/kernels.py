@@ -167,11 +167,61 @@ def _prefill_attn(a, c) -> None:
         torch.cuda.synchronize()
         print("ok", c.get_error())
         return
+    if a.trace and a.impl == "tcgen05":
+        _prefill_trace(c, run)
+        return
     ms = perf_cuda(run, reps=5, graph_calls=3)
     _, tf = _peaks()
     flops = sum(n * (n + 1) / 2 for n in lens) * nq * hd * 4
     print(f"prefill-attn[{a.impl}] tokens={tot} seqs={bs} nq={nq} nkv={nkv}: {ms * 1e3:.1f} us, {flops / ms / 1e9:.0f} TFLOP/s "
           f"({flops / ms * 1e3 / tf:.2f} of measured)")
+
+
+def _prefill_trace(c, run) -> None:
+    """Median phase durations (SM cycles) of the tcgen05 prefill kernel's CTAs for kv head 0, from
+    the kernel's per-CTA clock stamps (slot map beside ``kFmTrace`` in ``attention.cu``)."""
+    import statistics
+
+    run()  # warm
+    torch.cuda.synchronize()
+    tr = torch.zeros(2048, 96, dtype=torch.int32, device="cuda")
+    c.attention_prefill_trace(tr)
+    run()
+    torch.cuda.synchronize()
+    c.attention_prefill_trace(None)
+    t = tr.cpu().numpy().astype("int64")
+    t = t[t[:, 82] > 0]
+    rows = []
+
+    def med(name, vals):
+        vals = [int(v) for v in vals]
+        if vals:
+            rows.append((name, statistics.median(vals), len(vals)))
+
+    med("set up + tile lookup", t[:, 1])
+    med("Q landed after set-up", t[:, 4] - t[:, 1])
+    med("K0 issued after set-up", t[:, 8] - t[:, 1])
+    med("S0 issued after K0 issue", t[:, 24] - t[:, 8])
+    med("S0 landed in softmax after issue", t[:, 40] - t[:, 24])
+    for i in range(6):
+        sel = t[t[:, 2] > i]
+        if len(sel) == 0:
+            break
+        s0 = 40 + 4 * i
+        med(f"blk{i}: softmax idle before S", (sel[:, s0] - sel[:, s0 - 1]) if i else sel[:, s0] - sel[:, 1])
+        med(f"blk{i}: S load + max", sel[:, s0 + 1] - sel[:, s0])
+        med(f"blk{i}: exp + sum", sel[:, s0 + 2] - sel[:, s0 + 1])
+        med(f"blk{i}: P store + hand-over", sel[:, s0 + 3] - sel[:, s0 + 2])
+        med(f"blk{i}: S issued after K issued", sel[:, 24 + i] - sel[:, 8 + i])
+        med(f"blk{i}: PV issued after P handed", sel[:, 32 + i] - sel[:, s0 + 3])
+        med(f"blk{i}: V issued after K issued", sel[:, 16 + i] - sel[:, 8 + i])
+    last = [int(r[40 + 4 * (int(r[2]) - 1) + 3]) if 0 < r[2] <= 8 else None for r in t]
+    med("last PV done after last P", [r[80] - l for r, l in zip(t, last) if l is not None])
+    med("O stored", t[:, 81] - t[:, 80])
+    med("CTA total", t[:, 82])
+    med("key blocks", t[:, 2])
+    for name, v, n in rows:
+        print(f"{name:40s} {v:10.0f}  (n={n})")
 
 
 def _suite(a, c) -> None:
@@ -342,6 +392,7 @@ def main(argv=None) -> None:
     p.add_argument("--impl", default="tcgen05", choices=["tcgen05", "mma", "trtllm"],
                    help="prefill-attn kernel (trtllm: FlashInfer's trtllm-gen kernel, for comparison)")
     p.add_argument("--once", action="store_true", help="run a few times untimed (for profilers)")
+    p.add_argument("--trace", action="store_true", help="prefill-attn: per-CTA phase stamps of the tcgen05 kernel")
     a = p.parse_args(argv)
     from minisgl._native import cuda
 

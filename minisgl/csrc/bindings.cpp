@@ -304,6 +304,18 @@ void attention_prefill_fmha(at::Tensor o, at::Tensor q, at::Tensor k_cache, at::
   CHECK(rc == 0, "tcgen05 prefill attention failed to launch (code ", rc, ")");
 }
 
+// Profiling: phase stamps of later prefill launches into trace (int32 [ctas, 96], kv head 0); None: off.
+void attention_prefill_trace(c10::optional<at::Tensor> trace) {
+  if (!trace.has_value()) {
+    msgl_attention_prefill_trace(nullptr, 0);
+    return;
+  }
+  check_i32(*trace, "trace");
+  check_contig(*trace, "trace");
+  CHECK(trace->dim() == 2 && trace->size(1) == 96, "trace must be [ctas, 96]");
+  msgl_attention_prefill_trace(reinterpret_cast<uint32_t*>(trace->data_ptr<int32_t>()), (int)trace->size(0));
+}
+
 // Paged decode attention over a host-built work list (page size 16/32/64). work: int32 [>= 8 * entries]
 // (two int4 per entry), n_work: int32 [1] = entries, ws: fp32 partials for ws_slots chunk slots,
 // counters: int32 [>= bs * nkv], zero on entry and left at zero.
@@ -511,6 +523,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("attention_decode_paged", &attention_decode_paged);
   m.def("attention_prefill_fmha", &attention_prefill_fmha);
+  m.def("attention_prefill_trace", &attention_prefill_trace);
   m.def("gemm_ex", &gemm_ex);
   m.def("act_and_mul", &act_and_mul);
   m.def("store_kv", &store_kv);

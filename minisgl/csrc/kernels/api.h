@@ -105,6 +105,9 @@ int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total_q, const v
                                 const int32_t* rows, const int32_t* cu_q, const int32_t* kv_lens, int num_reqs,
                                 int max_q_len, int nq, int nkv, int hd, int page, float sm_scale, int window,
                                 const float* sinks, cudaStream_t s);
+// Profiling: record per-CTA phase stamps of later prefill launches into buf ([ctas][96] uint32, SM
+// clock cycles since each CTA started; kv head 0 only); nullptr turns it off. Not for concurrent use.
+void msgl_attention_prefill_trace(uint32_t* buf, int ctas);
 
 // Persistent paged decode over a host-built work list (page size 16/32/64; see attention.cu).
 // Returns 0 on success, 2 if a tensor map could not be encoded, 3 on unsupported arguments.

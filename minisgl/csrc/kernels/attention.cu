@@ -1081,31 +1081,32 @@ int run_paged_decode(const PagedDecodeParams& p, const void* q, int q_rows, cons
 
 // ================================================================================ prefill (tcgen05)
 // Ragged causal prefill attention on the 5th-generation tensor core, for head_dim 128 and page
-// sizes of 16 / 32 / 64 tokens. One CTA per (request, kv head, tile of TT = 128 / G query tokens):
-// the tile's TT x G packed (token, head) rows are the MMA M = 128 rows (G = query heads per kv head).
+// sizes of 16 / 32 / 64 tokens. One CTA per (query tile, kv head): a tile is TT = 128 / G tokens of
+// one request, whose TT x G packed (token, head) rows are the MMA M = 128 rows (G = query heads per
+// kv head), so every K/V tile fetched serves the whole group. Two CTAs fit on an SM (~112 KB of
+// shared memory and 256 TMEM columns each), so one CTA's set-up, first loads and epilogue overlap
+// the other's main loop.
 //
 //   warp 0     TMA: the Q tile once (3-D box 64 dims x G heads x TT tokens, per 64-dim half), then
-//              per 128-key block the K pages and the V pages (3-D boxes over [slots, kv heads, head
-//              dim]) into separate 2-stage rings: a K stage is released as soon as its QK^T MMA
-//              completes, a V stage once its PV MMA does. Page-table entries are fetched by the
-//              warp's lanes in batches of 32 pages.
-//   warp 1     MMA: S_i = Q K_i^T into one of two TMEM S buffers, then O += P_{i-1} V_{i-1} once
-//              the softmax warps have written P_{i-1} (V is an MN-major operand: its 128-byte rows
-//              are keys), so QK of block i overlaps the softmax of block i - 1.
-//   warps 2-9  softmax: two warps per TMEM lane quadrant (a warp may only address the quadrant
-//              warp % 4), one for keys 0-63 and one for keys 64-127 of each block. Both read the
-//              whole S row to take the same row maximum (no exchange needed), and each turns its
-//              64 keys into P (bf16, 128B-swizzled smem: the A operand of the PV MMA) in one of two
-//              P buffers, so block i's softmax only waits for the PV of block i - 2. Masks (causal,
-//              length, window) are applied only on blocks that cross a row's limits. O is rescaled
-//              in TMEM (each warp its 64 columns) only when a row's max grows by more than 2^8
-//              (lazy rescaling: P then stays <= 256). Epilogue: the two partial row sums are added
-//              through shared memory, O / l (with the sink term) stored as bf16.
-// TMEM: S buffers at columns 0 and 128, O at 256 (512 allocated).
+//              per 64-key block the K pages and the V pages (3-D boxes over [slots, kv heads, head
+//              dim]) into separate 2-stage rings. A K stage is released when its QK^T MMA
+//              completes, a V stage when its PV MMA does; the warp issues whichever load has a free
+//              stage first (K before V), so a V load waiting for a PV never holds back the next K.
+//   warp 1     MMA issuer, out of order between two streams: S_i = Q K_i^T into TMEM buffer i % 2
+//              as soon as K_i has landed and that buffer's previous PV is done; O += P_i V_i as soon
+//              as the softmax has written P_i and V_i has landed. P is read straight from TMEM (the
+//              A operand of the PV MMA), V from shared memory as an MN-major operand.
+//   warps 2-5  softmax, one thread per row (TMEM lane): read the S row, mask (causal / length /
+//              window) only on blocks that cross the row's limits, online max and sum in the log2
+//              domain, and write P as packed bf16 over the first 32 columns of its own S buffer. O
+//              is rescaled in TMEM only when a row's max grows by more than 2^8 (lazy rescaling: P
+//              then stays <= 256). Epilogue: O / l (with the sink term) stored as bf16.
+// TMEM: S / P buffers at columns 0 and 64, O at 128 (256 allocated).
 namespace {
 
-constexpr int kFmKB = 128;  // keys per block
-constexpr int kFmThreads = 320;
+constexpr int kFmKB = 64;  // keys per block
+constexpr int kFmThreads = 192;
+constexpr int kFmKStages = 2, kFmVStages = 2;
 
 struct FmhaParams {
   __nv_bfloat16* o;
@@ -1120,27 +1121,42 @@ struct FmhaParams {
   float scale_log2;
   int window;
   int num_reqs;
+  uint32_t* trace;  // optional per-CTA phase stamps (profiling; kv head 0, first trace_ctas tiles)
+  int trace_ctas;
 };
+
+// trace slots (SM clock cycles since the CTA started): 0 tile found, 1 set up, 2 key blocks,
+// 4 Q landed; per key block i < 8: 8 + i K loads issued, 16 + i V loads issued, 24 + i S_i issued,
+// 32 + i PV_i issued; first softmax warp: 40 + 4i S_i landed, 41 + 4i row max taken, 42 + 4i
+// exponentials done, 43 + 4i P_i handed over; 80 last PV done, 81 O stored, 82 CTA done.
+constexpr int kFmTrace = 96;
 
 struct FmSmem {
-  static constexpr int kHalf = 128 * 128;    // one 64-dim half of a 128-row / 128-key tile
-  static constexpr int kQ = 2 * kHalf;       // Q: two 64-dim halves x 128 rows x 128 B
-  static constexpr int kT = 2 * kHalf;       // one K or V stage (two 64-dim halves)
-  static constexpr int kP = 2 * kHalf;       // one P buffer: two 64-key halves x 128 rows x 128 B
-  static constexpr int kOffK = kQ;
-  static constexpr int kOffV = kOffK + 2 * kT;
-  static constexpr int kOffP = kOffV + 2 * kT;
-  static constexpr int kOffBar = kOffP + 2 * kP;
+  static constexpr int kQHalf = 128 * 128;       // one 64-dim half of the 128-row Q tile
+  static constexpr int kHalf = kFmKB * 128;      // one 64-dim half of a 64-key K / V tile
+  static constexpr int kT = 2 * kHalf;           // one K or V stage
+  static constexpr int kOffK = 2 * kQHalf;
+  static constexpr int kOffV = kOffK + kFmKStages * kT;
+  static constexpr int kOffBar = kOffV + kFmVStages * kT;
   static constexpr int kBytes = 1024 + kOffBar + 256;
 };
-static_assert(FmSmem::kBytes <= 227 * 1024, "prefill attention shared memory exceeds the per-CTA limit");
+static_assert(2 * (FmSmem::kBytes + 1024) <= 228 * 1024, "prefill attention must fit two CTAs per SM");
 
-__device__ __forceinline__ uint32_t fm_swz(int row, int chunk) {  // 128B swizzle within a half tile
-  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+// Page-table batch: lane j holds the first KV slot of page (32 * batch + j) of the tile's key range.
+__device__ __forceinline__ int fm_page_slots(const int32_t* pt, int batch, int ngroups, int blk0, int g, int L,
+                                             int64_t num_slots, int lane) {
+  int slot = 0;
+  const int gi = batch * 32 + lane;
+  if (gi < ngroups) {
+    const int pos = blk0 * kFmKB + gi * g;
+    slot = pos < L ? pt[pos] : 0;
+    if (!MSGL_IN_BOUNDS(slot >= 0 && slot < num_slots, kBcAttnSlot)) slot = 0;
+  }
+  return slot;
 }
 
-// Issue the TMA loads of one 128-key block's pages (K or V) into a stage: each page is `g` keys,
-// two 64-dim halves. `slot` holds the page's first KV slot in lane (page index - first) of the warp.
+// TMA loads of one 64-key block's pages (K or V) into a stage: pages of `g` keys, two 64-dim halves
+// each. Lane (first + sub) of the warp holds the first KV slot of page `sub` of the block.
 __device__ __forceinline__ void fm_load_pages(uint8_t* stage, const CUtensorMap* map, uint64_t* bar, int kvh,
                                               int slot, int first, int gpb, int g, int lane) {
   for (int sub = 0; sub < gpb; ++sub) {
@@ -1151,7 +1167,7 @@ __device__ __forceinline__ void fm_load_pages(uint8_t* stage, const CUtensorMap*
   }
 }
 
-__global__ void __launch_bounds__(kFmThreads, 1)
+__global__ void __launch_bounds__(kFmThreads, 2)
 fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, FmhaParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1159,28 +1175,61 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   uint8_t* sQ = smem;
   uint8_t* sK = smem + FmSmem::kOffK;
   uint8_t* sV = smem + FmSmem::kOffV;
-  uint8_t* sP = smem + FmSmem::kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FmSmem::kOffBar);
   uint64_t* qfull = bars;
-  uint64_t* kfull = bars + 1;    // [2]
-  uint64_t* kempty = bars + 3;   // [2]
-  uint64_t* vfull = bars + 5;    // [2]
-  uint64_t* vempty = bars + 7;   // [2]
-  uint64_t* sfull = bars + 9;    // [2]
-  uint64_t* sempty = bars + 11;  // [2]
-  uint64_t* pfull = bars + 13;   // [2], one per P buffer
-  uint64_t* pvdone = bars + 15;  // [2], PV of the block that used that P buffer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* kfull = bars + 1;                 // [kFmKStages]
+  uint64_t* kempty = kfull + kFmKStages;      // [kFmKStages]
+  uint64_t* vfull = kempty + kFmKStages;      // [kFmVStages]
+  uint64_t* vempty = vfull + kFmVStages;      // [kFmVStages]
+  uint64_t* sfull = vempty + kFmVStages;      // [2] S_i landed in buffer i % 2
+  uint64_t* pfull = sfull + 2;                // [2] P_i written over buffer i % 2 (4 warps)
+  uint64_t* pvdone = pfull + 2;               // [2] PV_i done: buffer i % 2 free, O updated
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pvdone + 2);
+  int* tile_info = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.group, TT = p.tt;
+  const long long c_start = clock64();
+  uint32_t* tr = (p.trace != nullptr && kvh == 0 && (int)blockIdx.x < p.trace_ctas)
+                     ? p.trace + (size_t)blockIdx.x * kFmTrace : nullptr;
+#define FM_STAMP(slot)                                             \
+  do {                                                             \
+    if (tr != nullptr) tr[slot] = (uint32_t)(clock64() - c_start); \
+  } while (0)
+
+  // Set-up runs alongside the tile lookup: barriers (warp 1 lane 0), TMEM (warp 1), tensor maps
+  // (warp 0 lane 0), then warp 0 finds the tile. blockIdx.x is a linear index over every request's
+  // ceil(q_len / TT) query tiles (the grid has a few spare CTAs, which exit); within a request the
+  // last tile (the most key blocks) is dispatched first.
+  if (warp == 1) {
+    if (lane == 0) {
+      mbar_init(qfull, 1);
+      for (int i = 0; i < kFmKStages; ++i) {
+        mbar_init(&kfull[i], 1);
+        mbar_init(&kempty[i], 1);
+      }
+      for (int i = 0; i < kFmVStages; ++i) {
+        mbar_init(&vfull[i], 1);
+        mbar_init(&vempty[i], 1);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&sfull[i], 1);
+        mbar_init(&pfull[i], 4);
+        mbar_init(&pvdone[i], 1);
+      }
+      fence_barrier_init();
+    }
+    __syncwarp();
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  } else if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
+  }
   pdl_wait();
   pdl_launch();
-  // blockIdx.x is a linear index over every request's ceil(q_len / TT) query tiles (the grid has a
-  // few spare CTAs, which exit here): warp 0 finds the request with a prefix scan of the tile
-  // counts. Within a request the last tile (the most key blocks) is dispatched first.
-  int* tile_info = reinterpret_cast<int*>(bars + 18);
   if (warp == 0) {
     const int tile = blockIdx.x;
     int fb = -1, fq = 0, before = 0;
@@ -1210,84 +1259,90 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       tile_info[1] = fq;
     }
   }
-  __syncthreads();
-  const int b = tile_info[0], qb = tile_info[1];
-  if (b < 0) return;  // CTA-uniform
-  const int q0 = p.cu_q[b], n = p.cu_q[b + 1] - q0;
-  const int t0 = qb * TT;
-  if (t0 >= n) return;
-  const int t1 = min(n, t0 + TT);
-  const int L = p.kv_lens[b];
-  if (!MSGL_IN_BOUNDS(p.rows[b] >= 0 && L >= n && L <= p.pt_stride, kBcAttnRow)) return;  // CTA-uniform
-  const int qpos0 = L - n;
-  const int kend = qpos0 + t1;  // exclusive
-  int kbeg = 0;
-  if (p.window > 0) kbeg = max(0, qpos0 + t0 - p.window + 1);
-  const int blk0 = kbeg / kFmKB, blk1 = (kend + kFmKB - 1) / kFmKB;
-  const int nb = blk1 - blk0;
-
-  if (threadIdx.x == 0) {
-    mbar_init(qfull, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&kfull[i], 1);
-      mbar_init(&kempty[i], 1);
-      mbar_init(&vfull[i], 1);
-      mbar_init(&vempty[i], 1);
-      mbar_init(&sfull[i], 1);
-      mbar_init(&sempty[i], 8);
-      mbar_init(&pfull[i], 8);
-      mbar_init(&pvdone[i], 1);
-    }
-    fence_barrier_init();
-    prefetch_tmap(&tq);
-    prefetch_tmap(&tk);
-    prefetch_tmap(&tv);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int b = tile_info[0], qb = tile_info[1];
+  // CTA-uniform: spare CTAs and malformed requests skip every role (and still free TMEM below)
+  bool active = b >= 0;
+  int q0 = 0, n = 0, t0 = 0, t1 = 0, L = 0, qpos0 = 0, blk0 = 0, nb = 0;
+  if (active) {
+    q0 = p.cu_q[b];
+    n = p.cu_q[b + 1] - q0;
+    t0 = qb * TT;
+    t1 = min(n, t0 + TT);
+    L = p.kv_lens[b];
+    active = t0 < n && MSGL_IN_BOUNDS(p.rows[b] >= 0 && L >= n && L <= p.pt_stride, kBcAttnRow);
+  }
+  if (active) {
+    qpos0 = L - n;
+    const int kend = qpos0 + t1;  // exclusive
+    int kbeg = 0;
+    if (p.window > 0) kbeg = max(0, qpos0 + t0 - p.window + 1);
+    blk0 = kbeg / kFmKB;
+    nb = (kend + kFmKB - 1) / kFmKB - blk0;
+    if (threadIdx.x == 0) {
+      FM_STAMP(1);
+      if (tr != nullptr) tr[2] = (uint32_t)nb;
+    }
+  }
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    const int g = p.page, gpb = kFmKB / g;
+  if (!active) {
+    // nothing to do
+  } else if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (Q, K, V)
+    const int32_t* pt = p.page_table + (int64_t)p.rows[b] * p.pt_stride;
+    const int g = p.page, gpb = kFmKB / g, bpb = 32 / gpb;  // pages per block, blocks per batch
+    const int ngroups = nb * gpb;
     if (lane == 0) {
       mbar_expect_tx(qfull, 2 * TT * G * 128);
-      for (int h = 0; h < 2; ++h) tma_load_3d(sQ + h * 128 * 128, &tq, qfull, h * 64, kvh * G, q0 + t0);
+      for (int h = 0; h < 2; ++h) tma_load_3d(sQ + h * FmSmem::kQHalf, &tq, qfull, h * 64, kvh * G, q0 + t0);
     }
-    const int32_t* pt = p.page_table + (int64_t)p.rows[b] * p.pt_stride;
-    const int ngroups = nb * gpb;
-    bool ok = true;
-    // 32 pages per batch of page-table reads; 32 is a multiple of the pages per block (2, 4 or 8)
-    for (int g0 = 0; ok && g0 < ngroups; g0 += 32) {
-      int slot = 0;
-      if (g0 + lane < ngroups) {
-        const int pos = blk0 * kFmKB + (g0 + lane) * g;
-        slot = pos < L ? pt[pos] : 0;
-        if (!MSGL_IN_BOUNDS(slot >= 0 && slot < p.num_slots, kBcAttnSlot)) slot = 0;
+    int nk = 0, nv = 0, batch_k = -1, batch_v = -1, slot_k = 0, slot_v = 0;
+    uint32_t spins = 0;
+    uint64_t t_wait = 0;
+    while (nk < nb || nv < nb) {
+      int act = 0;  // 1: load K_nk, 2: load V_nv, -1: gave up
+      if (lane == 0) {
+        if (nk < nb && mbar_test(&kempty[nk % kFmKStages], ((nk / kFmKStages) & 1) ^ 1)) act = 1;
+        else if (nv < nb && mbar_test(&vempty[nv % kFmVStages], ((nv / kFmVStages) & 1) ^ 1)) act = 2;
+        else if ((++spins & 255) == 0) {
+          const uint64_t now = globaltimer_ns();
+          if (t_wait == 0) t_wait = now;
+          else if (now - t_wait > kWaitTimeoutNs) {
+            report_error(kErrMbarTimeout, 500);
+            act = -1;
+          }
+        }
+        if (act > 0) t_wait = 0;
       }
-      const int bend = min(32, ngroups - g0) / gpb;
-      for (int bi = 0; ok && bi < bend; ++bi) {
-        const int i = g0 / gpb + bi, st = i & 1;
-        const uint32_t par = ((i >> 1) & 1) ^ 1;
-        if (lane == 0) {
-          ok = mbar_wait(&kempty[st], par, 500);
-          if (ok) mbar_expect_tx(&kfull[st], FmSmem::kT);
+      act = __shfl_sync(0xffffffffu, act, 0);
+      if (act < 0) break;
+      if (act == 1) {
+        if (nk / bpb != batch_k) {
+          batch_k = nk / bpb;
+          slot_k = fm_page_slots(pt, batch_k, ngroups, blk0, g, L, p.num_slots, lane);
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        fm_load_pages(sK + st * FmSmem::kT, &tk, &kfull[st], kvh, slot, bi * gpb, gpb, g, lane);
+        const int st = nk % kFmKStages;
         if (lane == 0) {
-          ok = mbar_wait(&vempty[st], par, 501);
-          if (ok) mbar_expect_tx(&vfull[st], FmSmem::kT);
+          mbar_expect_tx(&kfull[st], FmSmem::kT);
+          if (nk < 8) FM_STAMP(8 + nk);
         }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        fm_load_pages(sV + st * FmSmem::kT, &tv, &vfull[st], kvh, slot, bi * gpb, gpb, g, lane);
+        fm_load_pages(sK + st * FmSmem::kT, &tk, &kfull[st], kvh, slot_k, (nk % bpb) * gpb, gpb, g, lane);
+        ++nk;
+      } else if (act == 2) {
+        if (nv / bpb != batch_v) {
+          batch_v = nv / bpb;
+          slot_v = fm_page_slots(pt, batch_v, ngroups, blk0, g, L, p.num_slots, lane);
+        }
+        const int st = nv % kFmVStages;
+        if (lane == 0) {
+          mbar_expect_tx(&vfull[st], FmSmem::kT);
+          if (nv < 8) FM_STAMP(16 + nv);
+        }
+        fm_load_pages(sV + st * FmSmem::kT, &tv, &vfull[st], kvh, slot_v, (nv % bpb) * gpb, gpb, g, lane);
+        ++nv;
       }
     }
   } else if (warp == 1) {
@@ -1297,98 +1352,101 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128) | kIdescBMajorMN;
       const uint32_t q_base = smem_u32(sQ);
       bool ok = mbar_wait(qfull, 0, 510);
-      auto issue_pv = [&](int j) -> bool {
-        const int st = j & 1;
-        const uint32_t par = (j >> 1) & 1;
-        if (!mbar_wait(&pfull[st], par, 513) || !mbar_wait(&vfull[st], par, 514)) return false;
-        tc_fence_after();
-        const uint32_t p_base = smem_u32(sP + st * FmSmem::kP);
-        const uint32_t v_base = smem_u32(sV + st * FmSmem::kT);
+      FM_STAMP(4);
+      int ns = 0, np = 0;  // next S / PV to issue
+      uint32_t spins = 0;
+      uint64_t t_wait = 0;
+      while (ok && np < nb) {
+        bool progress = false;
+        // S_ns: K landed, buffer ns % 2 free (PV_{ns-2} done), at most two S ahead of PV
+        if (ns < nb && ns - np < 2 && mbar_test(&kfull[ns % kFmKStages], (ns / kFmKStages) & 1) &&
+            (ns < 2 || mbar_test(&pvdone[ns & 1], ((ns - 2) >> 1) & 1))) {
+          tc_fence_after();
+          const uint32_t k_base = smem_u32(sK + (ns % kFmKStages) * FmSmem::kT);
 #pragma unroll
-        for (int k = 0; k < kFmKB / 16; ++k) {  // 16 keys per MMA
-          const uint64_t a = smem_desc_sw128(p_base + (k >> 2) * 128 * 128 + (k & 3) * 32);
-          const uint64_t bd = smem_desc_sw128_mn(v_base + k * 16 * 128, FmSmem::kHalf);
-          tc_mma_f16(tmem + 256, a, bd, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < 128 / 16; ++k) {  // head dim, 16 per MMA
+            tc_mma_f16(tmem + (ns & 1) * kFmKB, smem_desc_sw128(q_base + (k >> 2) * FmSmem::kQHalf + (k & 3) * 32),
+                       smem_desc_sw128(k_base + (k >> 2) * FmSmem::kHalf + (k & 3) * 32), idesc_s, k > 0 ? 1u : 0u);
+          }
+          tc_commit(&kempty[ns % kFmKStages]);
+          tc_commit(&sfull[ns & 1]);
+          if (ns < 8) FM_STAMP(24 + ns);
+          ++ns;
+          progress = true;
         }
-        tc_commit(&vempty[st]);
-        tc_commit(&pvdone[st]);
-        return true;
-      };
-      for (int i = 0; ok && i < nb; ++i) {
-        const int st = i & 1;
-        const uint32_t par = (i >> 1) & 1;
-        if (!mbar_wait(&kfull[st], par, 511) || !mbar_wait(&sempty[st], par ^ 1, 512)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(sK + st * FmSmem::kT);
+        // PV_np: P written and V landed
+        if (np < ns && mbar_test(&pfull[np & 1], (np >> 1) & 1) &&
+            mbar_test(&vfull[np % kFmVStages], (np / kFmVStages) & 1)) {
+          tc_fence_after();
+          const uint32_t a_tmem = tmem + (np & 1) * kFmKB;  // P: 64 keys packed in 32 columns
+          const uint32_t v_base = smem_u32(sV + (np % kFmVStages) * FmSmem::kT);
 #pragma unroll
-        for (int k = 0; k < 128 / 16; ++k) {  // head dim, 16 per MMA
-          const uint32_t off = (k >> 2) * 128 * 128 + (k & 3) * 32;
-          tc_mma_f16(tmem + st * kFmKB, smem_desc_sw128(q_base + off), smem_desc_sw128(k_base + off), idesc_s,
-                     k > 0 ? 1u : 0u);
+          for (int k = 0; k < kFmKB / 16; ++k) {  // 16 keys per MMA
+            tc_mma_f16_ts(tmem + 128, a_tmem + k * 8, smem_desc_sw128_mn(v_base + k * 16 * 128, FmSmem::kHalf),
+                          idesc_o, (np > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&vempty[np % kFmVStages]);
+          tc_commit(&pvdone[np & 1]);
+          if (np < 8) FM_STAMP(32 + np);
+          ++np;
+          progress = true;
         }
-        tc_commit(&kempty[st]);
-        tc_commit(&sfull[st]);
-        if (i > 0 && !issue_pv(i - 1)) { ok = false; break; }
+        if (progress) {
+          spins = 0;
+        } else if ((++spins & 255) == 0) {
+          const uint64_t now = globaltimer_ns();
+          if (t_wait == 0) t_wait = now;
+          else if (now - t_wait > kWaitTimeoutNs) {
+            report_error(kErrMbarTimeout, 511);
+            ok = false;
+          }
+        }
+        if (progress) t_wait = 0;
       }
-      if (ok && nb > 0) issue_pv(nb - 1);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;  // keys / O columns [64 * half, 64 * half + 64)
-    const int r = quad * 32 + lane;    // accumulator row == TMEM lane
+    const int r = quad * 32 + lane;  // accumulator row == TMEM lane
     const int t = r / G, gh = r - t * G;
     const bool row_ok = r < TT * G && t0 + t < t1;
     const int qpos = qpos0 + t0 + t;
     const int kmax = min(qpos + 1, L);  // keys [kmin, kmax) are visible to this row
     const int kmin = p.window > 0 ? qpos - p.window + 1 : 0;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const uint32_t own_col = half * 64, oth_col = (half ^ 1) * 64;
     const float sl2 = p.scale_log2;
+    const bool stamp = warp == 2 && lane == 0;
     float m = -INFINITY, l = 0.f;
     bool dead = false;
     for (int i = 0; i < nb; ++i) {
       const int sb = i & 1;
-      const uint32_t par = (i >> 1) & 1;
-      if (!dead && !mbar_wait(&sfull[sb], par, 520)) dead = true;
+      if (!dead && !mbar_wait(&sfull[sb], (i >> 1) & 1, 520)) dead = true;
+      if (stamp && i < 8) FM_STAMP(40 + 4 * i);
       tc_fence_after();
-      float so[64], sx[64];  // this warp's 64 keys, the partner warp's 64 keys
+      float s[kFmKB];
       {
-        uint32_t u0[32], u1[32], u2[32], u3[32];
-        const uint32_t sa = lane_base + sb * kFmKB;
-        tmem_ld_32x32b_x32(sa + own_col, u0);
-        tmem_ld_32x32b_x32(sa + own_col + 32, u1);
-        tmem_ld_32x32b_x32(sa + oth_col, u2);
-        tmem_ld_32x32b_x32(sa + oth_col + 32, u3);
+        uint32_t u0[32], u1[32];
+        tmem_ld_32x32b_x32(lane_base + sb * kFmKB, u0);
+        tmem_ld_32x32b_x32(lane_base + sb * kFmKB + 32, u1);
         tc_wait_ld();
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          so[j] = __uint_as_float(u0[j]);
-          so[32 + j] = __uint_as_float(u1[j]);
-          sx[j] = __uint_as_float(u2[j]);
-          sx[32 + j] = __uint_as_float(u3[j]);
+          s[j] = __uint_as_float(u0[j]);
+          s[32 + j] = __uint_as_float(u1[j]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sempty[sb]);
-      // visible key range of this row inside the block, relative to each 64-key half
+      // visible key range of this row inside the block
       const int k0 = (blk0 + i) * kFmKB;
       const int lim = row_ok ? kmax - k0 : 0, lo = kmin - k0;
-      float mx = -INFINITY;
-      if (lo <= 0 && lim >= kFmKB) {
+      if (!(lo <= 0 && lim >= kFmKB)) {
 #pragma unroll
-        for (int j = 0; j < 64; ++j) mx = fmaxf(mx, fmaxf(so[j], sx[j]));
-      } else {
-        const int lo_o = lo - (int)own_col, lim_o = lim - (int)own_col;
-        const int lo_x = lo - (int)oth_col, lim_x = lim - (int)oth_col;
-#pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          so[j] = (j >= lo_o && j < lim_o) ? so[j] : -INFINITY;
-          const float x = (j >= lo_x && j < lim_x) ? sx[j] : -INFINITY;
-          mx = fmaxf(mx, fmaxf(so[j], x));
-        }
+        for (int j = 0; j < kFmKB; ++j) s[j] = (j >= lo && j < lim) ? s[j] : -INFINITY;
       }
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int j = 0; j < kFmKB; ++j) mx4[j & 3] = fmaxf(mx4[j & 3], s[j]);
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      if (stamp && i < 8) FM_STAMP(41 + 4 * i);
       mx *= sl2;  // log2 domain (the scale is positive, so the max commutes with it)
       const bool grow = mx > m + 8.f;  // lazy rescale threshold
       float alpha = 1.f;
@@ -1398,63 +1456,55 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         m = mx;
       }
       if (i > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds PV up to block i - 1: wait for it, then rescale this warp's 64 columns
+        // O holds PV up to block i - 1: wait for it, then rescale the row
         if (!dead && !mbar_wait(&pvdone[(i - 1) & 1], ((i - 1) >> 1) & 1, 521)) dead = true;
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 4; ++c) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_base + 256 + own_col + c * 32, v);
+          tmem_ld_32x32b_x32(lane_base + 128 + c * 32, v);
           tc_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
-          tmem_st_32x32b_x32(lane_base + 256 + own_col + c * 32, v);
+          tmem_st_32x32b_x32(lane_base + 128 + c * 32, v);
         }
-        tc_wait_st();
       }
       const float base = m == -INFINITY ? 0.f : m;
-      float sum = 0.f;
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[32];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        so[j] = exp2f(fmaf(so[j], sl2, -base));
-        sum += so[j];
+      for (int j = 0; j < kFmKB; j += 2) {
+        const float e0 = exp2f(fmaf(s[j], sl2, -base)), e1 = exp2f(fmaf(s[j + 1], sl2, -base));
+        sum4[(j >> 1) & 3] += e0 + e1;
+        pk[j >> 1] = pack_bf16(e0, e1);
       }
-      l += sum;
-      // P buffer sb is free once the PV of block i - 2 has completed
-      if (i >= 2 && !dead && !mbar_wait(&pvdone[sb], ((i - 2) >> 1) & 1, 522)) dead = true;
-      uint8_t* ph = sP + sb * FmSmem::kP + half * FmSmem::kHalf;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        *reinterpret_cast<uint4*>(ph + fm_swz(r, c)) =
-            make_uint4(pack_bf16(so[c * 8 + 0], so[c * 8 + 1]), pack_bf16(so[c * 8 + 2], so[c * 8 + 3]),
-                       pack_bf16(so[c * 8 + 4], so[c * 8 + 5]), pack_bf16(so[c * 8 + 6], so[c * 8 + 7]));
-      }
-      fence_async_smem();
+      l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      if (stamp && i < 8) FM_STAMP(42 + 4 * i);
+      // P over the first 32 columns of this block's S buffer (S is already in registers)
+      tmem_st_32x32b_x32(lane_base + sb * kFmKB, pk);
+      tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pfull[sb]);
+      if (stamp && i < 8) FM_STAMP(43 + 4 * i);
     }
-    // epilogue: wait for the last PV, add the partner's partial row sum, normalise, store
-    if (nb > 0 && !dead) mbar_wait(&pvdone[(nb - 1) & 1], ((nb - 1) >> 1) & 1, 523);
+    // epilogue: wait for the last PV, normalise, store
+    if (nb > 0 && !dead) mbar_wait(&pvdone[(nb - 1) & 1], ((nb - 1) >> 1) & 1, 522);
+    if (stamp) FM_STAMP(80);
     tc_fence_after();
-    // every MMA has completed, so the P buffers are free for the row-sum exchange
-    float* xl = reinterpret_cast<float*>(sP);
-    xl[half * 128 + r] = l;
-    named_bar_sync(1 + quad, 64);  // the two warps of this quadrant (both always get here)
-    const float lt = l + xl[(half ^ 1) * 128 + r];
-    float f = 1.f, ll = lt;
+    float f = 1.f, ll = l;
     if (p.sinks != nullptr) {
       const float sk = p.sinks[kvh * G + gh] * kLog2e;
       const float mn = fmaxf(m, sk);
       f = exp2f(m - mn);
-      ll = lt * f + exp2f(sk - mn);
+      ll = l * f + exp2f(sk - mn);
     }
     const float inv = ll > 0.f ? f / ll : 0.f;
-    __nv_bfloat16* dst = p.o + ((int64_t)(q0 + t0 + t) * p.nq + kvh * G + gh) * 128 + own_col;
+    __nv_bfloat16* dst = p.o + ((int64_t)(q0 + t0 + t) * p.nq + kvh * G + gh) * 128;
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
+    for (int c = 0; c < 4; ++c) {
       uint32_t v[32];
-      tmem_ld_32x32b_x32(lane_base + 256 + own_col + c * 32, v);
+      tmem_ld_32x32b_x32(lane_base + 128 + c * 32, v);
       tc_wait_ld();
       if (row_ok) {
 #pragma unroll
@@ -1466,16 +1516,28 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
               pack_bf16(__uint_as_float(v[j + 6]) * inv, __uint_as_float(v[j + 7]) * inv));
       }
     }
+    if (stamp) FM_STAMP(81);
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0 && active) FM_STAMP(82);
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 256);
   }
+#undef FM_STAMP
 }
 
+// Profiling hook: phase stamps of the next prefill launches (nullptr: off). Not for concurrent use.
+static uint32_t* g_fmha_trace = nullptr;
+static int g_fmha_trace_ctas = 0;
+
 }  // namespace
+
+extern "C" void msgl_attention_prefill_trace(uint32_t* buf, int ctas) {
+  g_fmha_trace = buf;
+  g_fmha_trace_ctas = buf != nullptr ? ctas : 0;
+}
 
 extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total_q, const void* k_cache,
                                            const void* v_cache, int64_t num_slots, int64_t cache_stride,
@@ -1513,6 +1575,8 @@ extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total
       !pd_encode(&tv, v_cache, 3, kdims, kstr, kbox))
     return 2;
   p.num_reqs = num_reqs;
+  p.trace = g_fmha_trace;
+  p.trace_ctas = g_fmha_trace_ctas;
   (void)max_q_len;
   // upper bound of sum(ceil(q_len / tt)) over the requests
   const int64_t tiles = (total_q + p.tt - 1) / p.tt + num_reqs;
