@@ -168,7 +168,7 @@ def _prefill_attn(a, c) -> None:
         print("ok", c.get_error())
         return
     if a.trace and a.impl == "tcgen05":
-        _prefill_trace(c, run)
+        _prefill_trace(c, run, a.trace_file)
         return
     ms = perf_cuda(run, reps=5, graph_calls=3)
     _, tf = _peaks()
@@ -177,9 +177,10 @@ def _prefill_attn(a, c) -> None:
           f"({flops / ms * 1e3 / tf:.2f} of measured)")
 
 
-def _prefill_trace(c, run) -> None:
-    """Median phase durations (SM cycles) of the tcgen05 prefill kernel's CTAs for kv head 0, from
-    the kernel's per-CTA clock stamps (slot map beside ``kFmTrace`` in ``attention.cu``)."""
+def _prefill_trace(c, run, path=None) -> None:
+    """Median phase durations (SM cycles) of one tile (the third) of each persistent CTA of the
+    tcgen05 prefill kernel, from its clock stamps (slot map beside ``kFmTrace`` in ``attention.cu``),
+    and the spread of the CTAs' total times (load balance)."""
     import statistics
 
     run()  # warm
@@ -189,8 +190,12 @@ def _prefill_trace(c, run) -> None:
     run()
     torch.cuda.synchronize()
     c.attention_prefill_trace(None)
+    import numpy as np
+
     t = tr.cpu().numpy().astype("int64")
     t = t[t[:, 82] > 0]
+    if path:
+        np.save(path, t)
     rows = []
 
     def med(name, vals):
@@ -198,9 +203,14 @@ def _prefill_trace(c, run) -> None:
         if vals:
             rows.append((name, statistics.median(vals), len(vals)))
 
-    med("set up + tile lookup", t[:, 1])
-    med("Q landed after set-up", t[:, 4] - t[:, 1])
-    med("K0 issued after set-up", t[:, 8] - t[:, 1])
+    med("traced tile published", t[:, 1])
+    med("softmax idle at the tile start", t[:, 40] - t[:, 88])
+    med("MMA took the tile, after publish", t[:, 89] - t[:, 1])
+    for k, name in ((90, "Q"), (91, "K0"), (92, "S buffer free"), (93, "PV within 2")):
+        med(f"first S input ready: {name}, after MMA took the tile", t[:, k] - t[:, 89])
+    med("first S issued, after MMA took the tile", t[:, 24] - t[:, 89])
+    med("Q issued after publish", t[:, 3] - t[:, 1])
+    med("K0 issued after publish", t[:, 8] - t[:, 1])
     med("S0 issued after K0 issue", t[:, 24] - t[:, 8])
     med("S0 landed in softmax after issue", t[:, 40] - t[:, 24])
     for i in range(6):
@@ -218,10 +228,33 @@ def _prefill_trace(c, run) -> None:
     last = [int(r[40 + 4 * (int(r[2]) - 1) + 3]) if 0 < r[2] <= 8 else None for r in t]
     med("last PV done after last P", [r[80] - l for r, l in zip(t, last) if l is not None])
     med("O stored", t[:, 81] - t[:, 80])
-    med("CTA total", t[:, 82])
-    med("key blocks", t[:, 2])
+    med("CTA total (all its tiles)", t[:, 82])
+    med("key blocks of the traced tile", t[:, 2])
     for name, v, n in rows:
         print(f"{name:40s} {v:10.0f}  (n={n})")
+    sms = {}
+    for r in t:
+        sms.setdefault(int(r[6]), []).append((int(r[7]), int(r[83])))
+    conc = []
+    for iv in sms.values():  # most CTAs resident on one SM at once
+        ev = sorted([(a, 1) for a, _ in iv] + [(b, -1) for _, b in iv])
+        cur = best = 0
+        for _, d in ev:
+            cur += d
+            best = max(best, cur)
+        conc.append(best)
+    tiles = sorted(int(v) for v in t[:, 84])
+    span = (max(int(v) for v in t[:, 83]) - min(int(v) for v in t[:, 7])) * 32 / 1e3
+    print(f"SMs used {len(sms)}, CTAs resident per SM (max) {max(conc)}, (min) {min(conc)}; tiles per CTA "
+          f"min / median / max {tiles[0]} / {tiles[len(tiles) // 2]} / {tiles[-1]} (sum {sum(tiles)}); "
+          f"first start to last end {span:.1f} us")
+    stuck = t[t[:, 84] == 0]
+    if len(stuck):
+        print(f"CTAs without a tile: {len(stuck)}; their median cycles to TMEM alloc / past the launch wait / "
+              f"first fetch: {np.median(stuck[:, 85]):.0f} / {np.median(stuck[:, 86]):.0f} / {np.median(stuck[:, 87]):.0f}")
+    tot = sorted(int(v) for v in t[:, 82])
+    print(f"CTA totals min / median / max: {tot[0]} / {tot[len(tot) // 2]} / {tot[-1]}; "
+          f"dynamic smem base mod 1024: {sorted(set(int(v) for v in t[:, 5]))}")
 
 
 def _suite(a, c) -> None:
@@ -393,6 +426,7 @@ def main(argv=None) -> None:
                    help="prefill-attn kernel (trtllm: FlashInfer's trtllm-gen kernel, for comparison)")
     p.add_argument("--once", action="store_true", help="run a few times untimed (for profilers)")
     p.add_argument("--trace", action="store_true", help="prefill-attn: per-CTA phase stamps of the tcgen05 kernel")
+    p.add_argument("--trace-file", default=None, help="prefill-attn --trace: also save the raw stamps (.npy)")
     a = p.parse_args(argv)
     from minisgl._native import cuda
 

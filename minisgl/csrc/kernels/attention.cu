@@ -16,6 +16,7 @@
 #include "api.h"
 #include "common.cuh"
 
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -1081,32 +1082,40 @@ int run_paged_decode(const PagedDecodeParams& p, const void* q, int q_rows, cons
 
 // ================================================================================ prefill (tcgen05)
 // Ragged causal prefill attention on the 5th-generation tensor core, for head_dim 128 and page
-// sizes of 16 / 32 / 64 tokens. One CTA per (query tile, kv head): a tile is TT = 128 / G tokens of
-// one request, whose TT x G packed (token, head) rows are the MMA M = 128 rows (G = query heads per
-// kv head), so every K/V tile fetched serves the whole group. Two CTAs fit on an SM (~112 KB of
-// shared memory and 256 TMEM columns each), so one CTA's set-up, first loads and epilogue overlap
-// the other's main loop.
+// sizes of 16 / 32 / 64 tokens. The work items are (query tile, kv head) pairs: a tile is TT = 128 /
+// G tokens of one request, whose TT x G packed (token, head) rows are the MMA M = 128 rows (G =
+// query heads per kv head), so every K/V tile fetched serves the whole group. The kernel is
+// persistent with two CTAs per SM (~113 KB of shared memory and 256 TMEM columns each); a CTA
+// takes work items one at a time from a device counter (largest tile of each request first) and
+// its roles run through them as independent streams, so the loads of the next tile overlap the
+// softmax and epilogue of the current one and the two CTAs of an SM fill each other's gaps.
 //
-//   warp 0     TMA: the Q tile once (3-D box 64 dims x G heads x TT tokens, per 64-dim half), then
+//   warp 0     producer: looks each tile up (a prefix scan of the requests' tile counts), publishes
+//              it in a 4-entry tile ring, and streams TMA loads: the tile's Q (3-D box 64 dims x G
+//              heads x TT tokens, per 64-dim half) once the previous tile's last QK^T is done, then
 //              per 64-key block the K pages and the V pages (3-D boxes over [slots, kv heads, head
-//              dim]) into separate 2-stage rings. A K stage is released when its QK^T MMA
-//              completes, a V stage when its PV MMA does; the warp issues whichever load has a free
-//              stage first (K before V), so a V load waiting for a PV never holds back the next K.
+//              dim]) into a 2-stage K ring and a 3-stage V ring (V waits on the later consumer).
+//              Whichever load can go goes first (a new tile's Q, then K, then V, then the next
+//              tile), so a V load waiting for a PV never holds back K; an idle pass sleeps briefly
+//              so the polling leaves issue slots to the softmax.
 //   warp 1     MMA issuer, out of order between two streams: S_i = Q K_i^T into TMEM buffer i % 2
-//              as soon as K_i has landed and that buffer's previous PV is done; O += P_i V_i as soon
-//              as the softmax has written P_i and V_i has landed. P is read straight from TMEM (the
-//              A operand of the PV MMA), V from shared memory as an MN-major operand.
+//              (i counts key blocks across tiles) once K_i has landed and that buffer's previous PV
+//              is done; O += P_i V_i once the softmax has written P_i and V_i has landed (a tile's
+//              first PV also waits until the softmax has read the previous tile's O). P is read
+//              straight from TMEM (the A operand), V from shared memory as an MN-major operand.
 //   warps 2-5  softmax, one thread per row (TMEM lane): read the S row, mask (causal / length /
 //              window) only on blocks that cross the row's limits, online max and sum in the log2
 //              domain, and write P as packed bf16 over the first 32 columns of its own S buffer. O
 //              is rescaled in TMEM only when a row's max grows by more than 2^8 (lazy rescaling: P
-//              then stays <= 256). Epilogue: O / l (with the sink term) stored as bf16.
+//              then stays <= 256). Epilogue: O is read out of TMEM (and released), then O / l (with
+//              the sink term) stored as bf16.
 // TMEM: S / P buffers at columns 0 and 64, O at 128 (256 allocated).
 namespace {
 
 constexpr int kFmKB = 64;  // keys per block
 constexpr int kFmThreads = 192;
-constexpr int kFmKStages = 2, kFmVStages = 2;
+constexpr int kFmKStages = 2, kFmVStages = 3;
+constexpr int kFmRing = 4;  // tile-info ring entries
 
 struct FmhaParams {
   __nv_bfloat16* o;
@@ -1121,15 +1130,33 @@ struct FmhaParams {
   float scale_log2;
   int window;
   int num_reqs;
-  uint32_t* trace;  // optional per-CTA phase stamps (profiling; kv head 0, first trace_ctas tiles)
+  uint32_t* trace;  // optional per-CTA phase stamps of its first tile (profiling)
   int trace_ctas;
+  uint32_t epoch;   // launch number (picks the work counter slot); 0: static round-robin
 };
 
-// trace slots (SM clock cycles since the CTA started): 0 tile found, 1 set up, 2 key blocks,
-// 4 Q landed; per key block i < 8: 8 + i K loads issued, 16 + i V loads issued, 24 + i S_i issued,
-// 32 + i PV_i issued; first softmax warp: 40 + 4i S_i landed, 41 + 4i row max taken, 42 + 4i
-// exponentials done, 43 + 4i P_i handed over; 80 last PV done, 81 O stored, 82 CTA done.
+// Work distribution: CTAs take work items from a per-device counter with atomicAdd. Launch e uses
+// counter slot e % kFmSlots; the last CTA to finish zeroes that slot and the next one, so a replay
+// of the same launch and the next launch both start from zero (even after a launch that did not
+// finish). Launches of this kernel on one device must be stream-ordered: each fetches only after
+// the programmatic-launch wait, i.e. after the previous launch has completed.
+constexpr int kFmSlots = 64;
+__device__ int g_fmha_work[kFmSlots];
+__device__ int g_fmha_exit[kFmSlots];
+
+// trace slots (SM clock cycles since the CTA started, for the CTA's third tile): 1 tile published,
+// 2 key blocks, 3 Q issued, 4 first QK^T issued, 5 dynamic smem base mod 1024; per key block i < 8: 8 + i K loads issued, 16 + i V loads
+// issued, 24 + i S_i issued, 32 + i PV_i issued; first softmax warp: 40 + 4i S_i landed, 41 + 4i
+// row max taken, 42 + 4i exponentials done, 43 + 4i P_i handed over; 80 last PV done, 81 O stored,
+// 82 CTA done; 6 SM id, 7 / 83 %globaltimer / 32 at start / end, 84 tiles taken, 85 TMEM
+// allocated, 86 past the programmatic-launch wait, 87 first work item fetched, 88 softmax starts
+// the traced tile, 89 MMA takes it, 90-93 its first QK^T inputs ready (Q, K, S buffer, PV lag).
 constexpr int kFmTrace = 96;
+
+// One work item, as published in the tile ring (nb < 0: no more work).
+struct FmTile {
+  int b, q0, t0, t1, L, qpos0, blk0, nb, kvh, row, pad0, pad1;
+};
 
 struct FmSmem {
   static constexpr int kQHalf = 128 * 128;       // one 64-dim half of the 128-row Q tile
@@ -1137,20 +1164,49 @@ struct FmSmem {
   static constexpr int kT = 2 * kHalf;           // one K or V stage
   static constexpr int kOffK = 2 * kQHalf;
   static constexpr int kOffV = kOffK + kFmKStages * kT;
-  static constexpr int kOffBar = kOffV + kFmVStages * kT;
-  static constexpr int kBytes = 1024 + kOffBar + 256;
+  static constexpr int kTiles = kOffV + kFmVStages * kT;  // 1024-aligned operand tiles
+  // tile ring + barriers: in front of the tiles when the alignment gap has room, else behind them
+  static constexpr int kRingBytes = kFmRing * (int)sizeof(FmTile);
+  static constexpr int kMeta = kRingBytes + 256;
+  // the dynamic smem base is 16-byte aligned, so the gap to the next 1 KB boundary is 0..1008
+  static constexpr int kBytes = kTiles + (1008 > 2 * kMeta - 16 ? 1008 : 2 * kMeta - 16);
 };
 static_assert(2 * (FmSmem::kBytes + 1024) <= 228 * 1024, "prefill attention must fit two CTAs per SM");
 
+__device__ __forceinline__ uint32_t fm_swz(int row, int chunk) {  // 128B swizzle within a half tile
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// 2^x on the MUFU unit (flushes results below 2^-126 to zero; 2^-inf = 0)
+__device__ __forceinline__ float fm_exp2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 2^x on the FMA / ALU pipes, to take part of the softmax's exponentials off the MUFU unit: range
+// reduction x = n + f (n = floor(x), f in [0, 1)), 2^f from a cubic through 2^0 = 1 whose other
+// three coefficients are a least-squares fit of 2^f on [0, 1) (computed offline with numpy; max
+// relative error 1.3e-4, below the bf16 rounding of P), and 2^n added to the exponent field.
+// Inputs below -126 (masked keys: -inf) give 2^-126, negligible next to a row sum >= 1.
+__device__ __forceinline__ float fm_exp2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float n = floorf(x);
+  const float f = x - n;
+  const float q = fmaf(fmaf(fmaf(0.07737474f, f, 0.22694686f), f, 0.69542833f), f, 1.f);
+  return __int_as_float(__float_as_int(q) + (__float2int_rz(n) << 23));
+}
+
 // Page-table batch: lane j holds the first KV slot of page (32 * batch + j) of the tile's key range.
-__device__ __forceinline__ int fm_page_slots(const int32_t* pt, int batch, int ngroups, int blk0, int g, int L,
-                                             int64_t num_slots, int lane) {
+__device__ __forceinline__ int fm_page_slots(const FmhaParams& p, const FmTile& T, int batch, int lane) {
+  const int g = p.page;
+  const int ngroups = T.nb * (kFmKB / g);
   int slot = 0;
   const int gi = batch * 32 + lane;
   if (gi < ngroups) {
-    const int pos = blk0 * kFmKB + gi * g;
-    slot = pos < L ? pt[pos] : 0;
-    if (!MSGL_IN_BOUNDS(slot >= 0 && slot < num_slots, kBcAttnSlot)) slot = 0;
+    const int pos = T.blk0 * kFmKB + gi * g;
+    slot = pos < T.L ? p.page_table[(int64_t)T.row * p.pt_stride + pos] : 0;
+    if (!MSGL_IN_BOUNDS(slot >= 0 && slot < p.num_slots, kBcAttnSlot)) slot = 0;
   }
   return slot;
 }
@@ -1167,44 +1223,100 @@ __device__ __forceinline__ void fm_load_pages(uint8_t* stage, const CUtensorMap*
   }
 }
 
+// Warp-wide: the tile of work item w (= tile * nkv + kv head). Tiles are numbered request by
+// request, ceil(q_len / TT) per request, the last tile of a request (the most key blocks) first.
+// The scan state (first request of the current 32-request window, tiles before it) only moves
+// forward, as a CTA's work items increase. Returns false past the last tile; T.nb = 0 marks a
+// malformed request (skipped).
+__device__ __forceinline__ bool fm_lookup(const FmhaParams& p, int w, int& scan_base, int& scan_before, FmTile& T,
+                                          int lane) {
+  const int tile = w / p.nkv;
+  const int TT = p.tt;
+  int b = -1, qb = 0;
+  while (scan_base < p.num_reqs) {
+    const int j = scan_base + lane;
+    int c = 0;
+    if (j < p.num_reqs) c = max(0, (p.cu_q[j + 1] - p.cu_q[j] + TT - 1) / TT);
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int tot = __shfl_sync(0xffffffffu, incl, 31);
+    if (tile < scan_before + tot) {  // warp-uniform
+      const int first = __ffs(__ballot_sync(0xffffffffu, tile < scan_before + incl)) - 1;
+      const int excl = __shfl_sync(0xffffffffu, incl - c, first);
+      const int cnt = __shfl_sync(0xffffffffu, c, first);
+      b = scan_base + first;
+      qb = cnt - 1 - (tile - scan_before - excl);
+      break;
+    }
+    scan_base += 32;
+    scan_before += tot;
+  }
+  if (b < 0) return false;
+  T.b = b;
+  T.kvh = w - tile * p.nkv;
+  T.q0 = p.cu_q[b];
+  const int n = p.cu_q[b + 1] - T.q0;
+  T.t0 = qb * TT;
+  T.t1 = min(n, T.t0 + TT);
+  T.L = p.kv_lens[b];
+  T.row = p.rows[b];
+  T.nb = 0;
+  if (T.t0 < n && MSGL_IN_BOUNDS(T.row >= 0 && T.L >= n && T.L <= p.pt_stride, kBcAttnRow)) {
+    T.qpos0 = T.L - n;
+    const int kend = T.qpos0 + T.t1;  // exclusive
+    const int kbeg = p.window > 0 ? max(0, T.qpos0 + T.t0 - p.window + 1) : 0;
+    T.blk0 = kbeg / kFmKB;
+    T.nb = (kend + kFmKB - 1) / kFmKB - T.blk0;
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kFmThreads, 2)
 fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, FmhaParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t gap = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + gap;
+  uint8_t* meta = gap >= (uint32_t)FmSmem::kMeta ? smem_raw : smem + FmSmem::kTiles;
   uint8_t* sQ = smem;
   uint8_t* sK = smem + FmSmem::kOffK;
   uint8_t* sV = smem + FmSmem::kOffV;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FmSmem::kOffBar);
-  uint64_t* qfull = bars;
-  uint64_t* kfull = bars + 1;                 // [kFmKStages]
+  FmTile* ring = reinterpret_cast<FmTile*>(meta);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(meta + FmSmem::kRingBytes);
+  uint64_t* qfull = bars;                     // Q of a tile landed (one phase per tile)
+  uint64_t* qempty = bars + 1;                // last QK^T of a tile done: Q buffer free
+  uint64_t* ofree = bars + 2;                 // the softmax has read a tile's O (4 warps)
+  uint64_t* kfull = bars + 3;                 // [kFmKStages]
   uint64_t* kempty = kfull + kFmKStages;      // [kFmKStages]
   uint64_t* vfull = kempty + kFmKStages;      // [kFmVStages]
   uint64_t* vempty = vfull + kFmVStages;      // [kFmVStages]
   uint64_t* sfull = vempty + kFmVStages;      // [2] S_i landed in buffer i % 2
   uint64_t* pfull = sfull + 2;                // [2] P_i written over buffer i % 2 (4 warps)
   uint64_t* pvdone = pfull + 2;               // [2] PV_i done: buffer i % 2 free, O updated
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pvdone + 2);
-  int* tile_info = reinterpret_cast<int*>(tmem_slot + 2);
+  uint64_t* tfull = pvdone + 2;               // [kFmRing] tile entry published
+  uint64_t* tempty = tfull + kFmRing;         // [kFmRing] entry released (MMA, 4 softmax, V stream)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kFmRing);
 
-  const int kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.group, TT = p.tt;
   const long long c_start = clock64();
-  uint32_t* tr = (p.trace != nullptr && kvh == 0 && (int)blockIdx.x < p.trace_ctas)
+  uint32_t* tr = (p.trace != nullptr && (int)blockIdx.x < p.trace_ctas)
                      ? p.trace + (size_t)blockIdx.x * kFmTrace : nullptr;
-#define FM_STAMP(slot)                                             \
-  do {                                                             \
-    if (tr != nullptr) tr[slot] = (uint32_t)(clock64() - c_start); \
+  constexpr int TS = 2;  // the traced tile of each CTA (its third: past the start-up transient)
+#define FM_STAMP(cond, slot)                                                   \
+  do {                                                                         \
+    if (tr != nullptr && (cond)) tr[slot] = (uint32_t)(clock64() - c_start);   \
   } while (0)
 
-  // Set-up runs alongside the tile lookup: barriers (warp 1 lane 0), TMEM (warp 1), tensor maps
-  // (warp 0 lane 0), then warp 0 finds the tile. blockIdx.x is a linear index over every request's
-  // ceil(q_len / TT) query tiles (the grid has a few spare CTAs, which exit); within a request the
-  // last tile (the most key blocks) is dispatched first.
   if (warp == 1) {
     if (lane == 0) {
       mbar_init(qfull, 1);
+      mbar_init(qempty, 1);
+      mbar_init(ofree, 4);
       for (int i = 0; i < kFmKStages; ++i) {
         mbar_init(&kfull[i], 1);
         mbar_init(&kempty[i], 1);
@@ -1218,96 +1330,65 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         mbar_init(&pfull[i], 4);
         mbar_init(&pvdone[i], 1);
       }
+      for (int i = 0; i < kFmRing; ++i) {
+        mbar_init(&tfull[i], 1);
+        mbar_init(&tempty[i], 6);
+      }
       fence_barrier_init();
     }
     __syncwarp();
     tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
+    FM_STAMP(lane == 0, 85);
   } else if (warp == 0 && lane == 0) {
     prefetch_tmap(&tq);
     prefetch_tmap(&tk);
     prefetch_tmap(&tv);
+    if (tr != nullptr) {
+      tr[5] = smem_u32(smem_raw) & 1023u;  // alignment of the dynamic smem base
+      uint32_t sm;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+      tr[6] = sm;
+      tr[7] = (uint32_t)(globaltimer_ns() >> 5);  // start, 32 ns units
+    }
   }
   pdl_wait();
+  FM_STAMP(threadIdx.x == 0, 86);
   pdl_launch();
-  if (warp == 0) {
-    const int tile = blockIdx.x;
-    int fb = -1, fq = 0, before = 0;
-    for (int base = 0; base < p.num_reqs; base += 32) {
-      const int j = base + lane;
-      int c = 0;
-      if (j < p.num_reqs) c = max(0, (p.cu_q[j + 1] - p.cu_q[j] + TT - 1) / TT);
-      int incl = c;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
-      }
-      const int tot = __shfl_sync(0xffffffffu, incl, 31);
-      if (tile < before + tot) {  // warp-uniform
-        const int first = __ffs(__ballot_sync(0xffffffffu, tile < before + incl)) - 1;
-        const int excl = __shfl_sync(0xffffffffu, incl - c, first);
-        const int cnt = __shfl_sync(0xffffffffu, c, first);
-        fb = base + first;
-        fq = cnt - 1 - (tile - before - excl);
-        break;
-      }
-      before += tot;
-    }
-    if (lane == 0) {
-      tile_info[0] = fb;
-      tile_info[1] = fq;
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int b = tile_info[0], qb = tile_info[1];
-  // CTA-uniform: spare CTAs and malformed requests skip every role (and still free TMEM below)
-  bool active = b >= 0;
-  int q0 = 0, n = 0, t0 = 0, t1 = 0, L = 0, qpos0 = 0, blk0 = 0, nb = 0;
-  if (active) {
-    q0 = p.cu_q[b];
-    n = p.cu_q[b + 1] - q0;
-    t0 = qb * TT;
-    t1 = min(n, t0 + TT);
-    L = p.kv_lens[b];
-    active = t0 < n && MSGL_IN_BOUNDS(p.rows[b] >= 0 && L >= n && L <= p.pt_stride, kBcAttnRow);
-  }
-  if (active) {
-    qpos0 = L - n;
-    const int kend = qpos0 + t1;  // exclusive
-    int kbeg = 0;
-    if (p.window > 0) kbeg = max(0, qpos0 + t0 - p.window + 1);
-    blk0 = kbeg / kFmKB;
-    nb = (kend + kFmKB - 1) / kFmKB - blk0;
-    if (threadIdx.x == 0) {
-      FM_STAMP(1);
-      if (tr != nullptr) tr[2] = (uint32_t)nb;
-    }
-  }
 
-  if (!active) {
-    // nothing to do
-  } else if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer (Q, K, V)
-    const int32_t* pt = p.page_table + (int64_t)p.rows[b] * p.pt_stride;
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer (tiles, Q, K, V)
     const int g = p.page, gpb = kFmKB / g, bpb = 32 / gpb;  // pages per block, blocks per batch
-    const int ngroups = nb * gpb;
-    if (lane == 0) {
-      mbar_expect_tx(qfull, 2 * TT * G * 128);
-      for (int h = 0; h < 2; ++h) tma_load_3d(sQ + h * FmSmem::kQHalf, &tq, qfull, h * 64, kvh * G, q0 + t0);
-    }
-    int nk = 0, nv = 0, batch_k = -1, batch_v = -1, slot_k = 0, slot_v = 0;
+    int scan_base = 0, scan_before = 0, next_static = blockIdx.x;
+    int k_seq = 0;          // tiles published (the current K tile is k_seq - 1)
+    bool k_have = false, k_done = false, q_issued = false;
+    int ik = 0, gk = 0, batch_k = -1, slot_k = 0;
+    FmTile KT;
+    int v_seq = 0;          // ring entry the V stream reads next
+    bool v_have = false, v_done = false;
+    int iv = 0, gv = 0, batch_v = -1, slot_v = 0;
+    FmTile VT;
     uint32_t spins = 0;
     uint64_t t_wait = 0;
-    while (nk < nb || nv < nb) {
-      int act = 0;  // 1: load K_nk, 2: load V_nv, -1: gave up
+    while (!(k_done && v_done)) {
+      int act = 0;  // 1 K block, 2 V block, 3 Q, 4 publish the next tile, 5 V stream takes a tile
       if (lane == 0) {
-        if (nk < nb && mbar_test(&kempty[nk % kFmKStages], ((nk / kFmKStages) & 1) ^ 1)) act = 1;
-        else if (nv < nb && mbar_test(&vempty[nv % kFmVStages], ((nv / kFmVStages) & 1) ^ 1)) act = 2;
-        else if ((++spins & 255) == 0) {
+        if (k_have && !q_issued && (k_seq == 1 || mbar_test(qempty, (k_seq - 2) & 1)))
+          act = 3;
+        else if (k_have && ik < KT.nb && mbar_test(&kempty[gk % kFmKStages], ((gk / kFmKStages) & 1) ^ 1))
+          act = 1;
+        else if (v_have && iv < VT.nb && mbar_test(&vempty[gv % kFmVStages], ((gv / kFmVStages) & 1) ^ 1))
+          act = 2;
+        else if (!k_done && (!k_have || (ik == KT.nb && q_issued)) &&
+                 mbar_test(&tempty[k_seq % kFmRing], ((k_seq / kFmRing) & 1) ^ 1))
+          act = 4;
+        else if (!v_done && !v_have && mbar_test(&tfull[v_seq % kFmRing], (v_seq / kFmRing) & 1))
+          act = 5;
+        else if ((++spins & 63) == 0) {
           const uint64_t now = globaltimer_ns();
           if (t_wait == 0) t_wait = now;
           else if (now - t_wait > kWaitTimeoutNs) {
@@ -1319,30 +1400,88 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       }
       act = __shfl_sync(0xffffffffu, act, 0);
       if (act < 0) break;
+      if (act == 0) __nanosleep(64);  // idle: leave the issue slots to the softmax warps
       if (act == 1) {
-        if (nk / bpb != batch_k) {
-          batch_k = nk / bpb;
-          slot_k = fm_page_slots(pt, batch_k, ngroups, blk0, g, L, p.num_slots, lane);
+        if (ik / bpb != batch_k) {
+          batch_k = ik / bpb;
+          slot_k = fm_page_slots(p, KT, batch_k, lane);
         }
-        const int st = nk % kFmKStages;
+        const int st = gk % kFmKStages;
         if (lane == 0) {
           mbar_expect_tx(&kfull[st], FmSmem::kT);
-          if (nk < 8) FM_STAMP(8 + nk);
+          FM_STAMP(k_seq == TS + 1 && ik < 8, 8 + ik);
         }
-        fm_load_pages(sK + st * FmSmem::kT, &tk, &kfull[st], kvh, slot_k, (nk % bpb) * gpb, gpb, g, lane);
-        ++nk;
+        fm_load_pages(sK + st * FmSmem::kT, &tk, &kfull[st], KT.kvh, slot_k, (ik % bpb) * gpb, gpb, g, lane);
+        ++ik;
+        ++gk;
       } else if (act == 2) {
-        if (nv / bpb != batch_v) {
-          batch_v = nv / bpb;
-          slot_v = fm_page_slots(pt, batch_v, ngroups, blk0, g, L, p.num_slots, lane);
+        if (iv / bpb != batch_v) {
+          batch_v = iv / bpb;
+          slot_v = fm_page_slots(p, VT, batch_v, lane);
         }
-        const int st = nv % kFmVStages;
+        const int st = gv % kFmVStages;
         if (lane == 0) {
           mbar_expect_tx(&vfull[st], FmSmem::kT);
-          if (nv < 8) FM_STAMP(16 + nv);
+          FM_STAMP(v_seq == TS && iv < 8, 16 + iv);
         }
-        fm_load_pages(sV + st * FmSmem::kT, &tv, &vfull[st], kvh, slot_v, (nv % bpb) * gpb, gpb, g, lane);
-        ++nv;
+        fm_load_pages(sV + st * FmSmem::kT, &tv, &vfull[st], VT.kvh, slot_v, (iv % bpb) * gpb, gpb, g, lane);
+        ++iv;
+        ++gv;
+        if (iv == VT.nb) {  // every V load of the tile issued: release the entry
+          if (lane == 0) mbar_arrive(&tempty[v_seq % kFmRing]);
+          v_have = false;
+          ++v_seq;
+        }
+      } else if (act == 3) {
+        if (lane == 0) {
+          mbar_expect_tx(qfull, 2 * TT * G * 128);
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(sQ + h * FmSmem::kQHalf, &tq, qfull, h * 64, KT.kvh * G, KT.q0 + KT.t0);
+          FM_STAMP(k_seq == TS + 1, 3);
+        }
+        q_issued = true;
+      } else if (act == 4) {
+        // next work item with key blocks (malformed requests are skipped), or the end marker
+        bool more = false;
+        while (true) {
+          int w = next_static;
+          next_static += gridDim.x;
+          if (p.epoch != 0) {
+            if (lane == 0) w = atomicAdd(&g_fmha_work[p.epoch % kFmSlots], 1);
+            w = __shfl_sync(0xffffffffu, w, 0);
+            if (tr != nullptr && lane == 0 && tr[87] == 0) tr[87] = (uint32_t)(clock64() - c_start) | 1u;
+          }
+          more = fm_lookup(p, w, scan_base, scan_before, KT, lane);
+          if (!more || KT.nb > 0) break;
+        }
+        if (!more) KT.nb = -1;
+        if (tr != nullptr && lane == 0 && more) tr[84] += 1;  // tiles taken
+        if (lane == 0) {
+          ring[k_seq % kFmRing] = KT;
+          mbar_arrive(&tfull[k_seq % kFmRing]);  // release: the entry is visible to its readers
+          FM_STAMP(k_seq == TS, 1);
+          if (tr != nullptr && k_seq == TS) tr[2] = (uint32_t)max(KT.nb, 0);
+        }
+        __syncwarp();  // the entry is read back by this warp's V stream
+        ++k_seq;
+        if (more) {
+          k_have = true;
+          q_issued = false;
+          ik = 0;
+          batch_k = -1;
+        } else {
+          k_have = false;
+          k_done = true;
+        }
+      } else if (act == 5) {
+        VT = ring[v_seq % kFmRing];
+        if (VT.nb < 0) {
+          v_done = true;
+        } else {
+          v_have = true;
+          iv = 0;
+          batch_v = -1;
+        }
       }
     }
   } else if (warp == 1) {
@@ -1351,57 +1490,94 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, kFmKB);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128) | kIdescBMajorMN;
       const uint32_t q_base = smem_u32(sQ);
-      bool ok = mbar_wait(qfull, 0, 510);
-      FM_STAMP(4);
-      int ns = 0, np = 0;  // next S / PV to issue
+      int s_seq = 0, s_nb = 0, is = 0, gs = 0;  // S stream: ring entry, its key blocks, block, global block
+      bool s_have = false, s_done = false;
+      int p_seq = 0, p_nb = 0, ip = 0, gp = 0;  // PV stream
+      bool p_have = false, p_done = false;
       uint32_t spins = 0;
       uint64_t t_wait = 0;
-      while (ok && np < nb) {
+      while (!(s_done && p_done)) {
         bool progress = false;
-        // S_ns: K landed, buffer ns % 2 free (PV_{ns-2} done), at most two S ahead of PV
-        if (ns < nb && ns - np < 2 && mbar_test(&kfull[ns % kFmKStages], (ns / kFmKStages) & 1) &&
-            (ns < 2 || mbar_test(&pvdone[ns & 1], ((ns - 2) >> 1) & 1))) {
-          tc_fence_after();
-          const uint32_t k_base = smem_u32(sK + (ns % kFmKStages) * FmSmem::kT);
-#pragma unroll
-          for (int k = 0; k < 128 / 16; ++k) {  // head dim, 16 per MMA
-            tc_mma_f16(tmem + (ns & 1) * kFmKB, smem_desc_sw128(q_base + (k >> 2) * FmSmem::kQHalf + (k & 3) * 32),
-                       smem_desc_sw128(k_base + (k >> 2) * FmSmem::kHalf + (k & 3) * 32), idesc_s, k > 0 ? 1u : 0u);
-          }
-          tc_commit(&kempty[ns % kFmKStages]);
-          tc_commit(&sfull[ns & 1]);
-          if (ns < 8) FM_STAMP(24 + ns);
-          ++ns;
+        if (!s_have && !s_done && mbar_test(&tfull[s_seq % kFmRing], (s_seq / kFmRing) & 1)) {
+          s_nb = ring[s_seq % kFmRing].nb;
+          if (s_nb < 0) s_done = true;
+          else { s_have = true; is = 0; }
+          FM_STAMP(s_seq == TS, 89);
           progress = true;
         }
-        // PV_np: P written and V landed
-        if (np < ns && mbar_test(&pfull[np & 1], (np >> 1) & 1) &&
-            mbar_test(&vfull[np % kFmVStages], (np / kFmVStages) & 1)) {
+        if (tr != nullptr && s_have && is == 0 && s_seq == TS) {  // which input of the tile's first S is late
+          if (tr[90] == 0 && mbar_test(qfull, s_seq & 1)) FM_STAMP(true, 90);
+          if (tr[91] == 0 && mbar_test(&kfull[gs % kFmKStages], (gs / kFmKStages) & 1)) FM_STAMP(true, 91);
+          if (tr[92] == 0 && (gs < 2 || mbar_test(&pvdone[gs & 1], ((gs - 2) >> 1) & 1))) FM_STAMP(true, 92);
+          if (tr[93] == 0 && gs - gp < 2) FM_STAMP(true, 93);
+        }
+        // S_gs: Q and K landed, buffer gs % 2 free (PV_{gs-2} done), at most two S ahead of PV
+        if (s_have && gs - gp < 2 && (is > 0 || mbar_test(qfull, s_seq & 1)) &&
+            mbar_test(&kfull[gs % kFmKStages], (gs / kFmKStages) & 1) &&
+            (gs < 2 || mbar_test(&pvdone[gs & 1], ((gs - 2) >> 1) & 1))) {
           tc_fence_after();
-          const uint32_t a_tmem = tmem + (np & 1) * kFmKB;  // P: 64 keys packed in 32 columns
-          const uint32_t v_base = smem_u32(sV + (np % kFmVStages) * FmSmem::kT);
+          if (is == 0) FM_STAMP(s_seq == TS, 4);
+          const uint32_t k_base = smem_u32(sK + (gs % kFmKStages) * FmSmem::kT);
+#pragma unroll
+          for (int k = 0; k < 128 / 16; ++k) {  // head dim, 16 per MMA
+            tc_mma_f16(tmem + (gs & 1) * kFmKB, smem_desc_sw128(q_base + (k >> 2) * FmSmem::kQHalf + (k & 3) * 32),
+                       smem_desc_sw128(k_base + (k >> 2) * FmSmem::kHalf + (k & 3) * 32), idesc_s, k > 0 ? 1u : 0u);
+          }
+          tc_commit(&kempty[gs % kFmKStages]);
+          tc_commit(&sfull[gs & 1]);
+          FM_STAMP(s_seq == TS && is < 8, 24 + is);
+          ++gs;
+          if (++is == s_nb) {  // the tile's last QK^T: its Q buffer is free once this completes
+            tc_commit(qempty);
+            s_have = false;
+            ++s_seq;
+          }
+          progress = true;
+        }
+        if (!p_have && !p_done && p_seq < s_seq + (s_have ? 1 : 0) + (s_done ? 1 : 0)) {
+          // the PV stream follows the S stream through the ring (the entry is still held)
+          p_nb = ring[p_seq % kFmRing].nb;
+          if (p_nb < 0) p_done = true;
+          else { p_have = true; ip = 0; }
+          progress = true;
+        }
+        // PV_gp: P written, V landed, and for a tile's first block the previous tile's O read out
+        if (p_have && gp < gs && mbar_test(&pfull[gp & 1], (gp >> 1) & 1) &&
+            mbar_test(&vfull[gp % kFmVStages], (gp / kFmVStages) & 1) &&
+            (ip > 0 || mbar_test(ofree, (p_seq & 1) ^ 1))) {
+          tc_fence_after();
+          const uint32_t a_tmem = tmem + (gp & 1) * kFmKB;  // P: 64 keys packed in 32 columns
+          const uint32_t v_base = smem_u32(sV + (gp % kFmVStages) * FmSmem::kT);
 #pragma unroll
           for (int k = 0; k < kFmKB / 16; ++k) {  // 16 keys per MMA
             tc_mma_f16_ts(tmem + 128, a_tmem + k * 8, smem_desc_sw128_mn(v_base + k * 16 * 128, FmSmem::kHalf),
-                          idesc_o, (np > 0 || k > 0) ? 1u : 0u);
+                          idesc_o, (ip > 0 || k > 0) ? 1u : 0u);
           }
-          tc_commit(&vempty[np % kFmVStages]);
-          tc_commit(&pvdone[np & 1]);
-          if (np < 8) FM_STAMP(32 + np);
-          ++np;
+          tc_commit(&vempty[gp % kFmVStages]);
+          tc_commit(&pvdone[gp & 1]);
+          FM_STAMP(p_seq == TS && ip < 8, 32 + ip);
+          ++gp;
+          if (++ip == p_nb) {  // done with the tile's entry
+            mbar_arrive(&tempty[p_seq % kFmRing]);
+            p_have = false;
+            ++p_seq;
+          }
           progress = true;
         }
         if (progress) {
           spins = 0;
-        } else if ((++spins & 255) == 0) {
-          const uint64_t now = globaltimer_ns();
-          if (t_wait == 0) t_wait = now;
-          else if (now - t_wait > kWaitTimeoutNs) {
-            report_error(kErrMbarTimeout, 511);
-            ok = false;
+          t_wait = 0;
+        } else {
+          __nanosleep(32);  // idle: leave the issue slots to the softmax warps
+          if ((++spins & 63) == 0) {
+            const uint64_t now = globaltimer_ns();
+            if (t_wait == 0) t_wait = now;
+            else if (now - t_wait > kWaitTimeoutNs) {
+              report_error(kErrMbarTimeout, 510);
+              break;
+            }
           }
         }
-        if (progress) t_wait = 0;
       }
     }
   } else {
@@ -1409,118 +1585,150 @@ fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // accumulator row == TMEM lane
     const int t = r / G, gh = r - t * G;
-    const bool row_ok = r < TT * G && t0 + t < t1;
-    const int qpos = qpos0 + t0 + t;
-    const int kmax = min(qpos + 1, L);  // keys [kmin, kmax) are visible to this row
-    const int kmin = p.window > 0 ? qpos - p.window + 1 : 0;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const float sl2 = p.scale_log2;
     const bool stamp = warp == 2 && lane == 0;
-    float m = -INFINITY, l = 0.f;
+    int gsm = 0;  // global key block
     bool dead = false;
-    for (int i = 0; i < nb; ++i) {
-      const int sb = i & 1;
-      if (!dead && !mbar_wait(&sfull[sb], (i >> 1) & 1, 520)) dead = true;
-      if (stamp && i < 8) FM_STAMP(40 + 4 * i);
-      tc_fence_after();
-      float s[kFmKB];
-      {
-        uint32_t u0[32], u1[32];
-        tmem_ld_32x32b_x32(lane_base + sb * kFmKB, u0);
-        tmem_ld_32x32b_x32(lane_base + sb * kFmKB + 32, u1);
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          s[j] = __uint_as_float(u0[j]);
-          s[32 + j] = __uint_as_float(u1[j]);
-        }
-      }
-      // visible key range of this row inside the block
-      const int k0 = (blk0 + i) * kFmKB;
-      const int lim = row_ok ? kmax - k0 : 0, lo = kmin - k0;
-      if (!(lo <= 0 && lim >= kFmKB)) {
-#pragma unroll
-        for (int j = 0; j < kFmKB; ++j) s[j] = (j >= lo && j < lim) ? s[j] : -INFINITY;
-      }
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int j = 0; j < kFmKB; ++j) mx4[j & 3] = fmaxf(mx4[j & 3], s[j]);
-      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      if (stamp && i < 8) FM_STAMP(41 + 4 * i);
-      mx *= sl2;  // log2 domain (the scale is positive, so the max commutes with it)
-      const bool grow = mx > m + 8.f;  // lazy rescale threshold
-      float alpha = 1.f;
-      if (grow) {
-        alpha = m == -INFINITY ? 0.f : exp2f(m - mx);
-        l *= alpha;
-        m = mx;
-      }
-      if (i > 0 && __any_sync(0xffffffffu, grow)) {
-        // O holds PV up to block i - 1: wait for it, then rescale the row
-        if (!dead && !mbar_wait(&pvdone[(i - 1) & 1], ((i - 1) >> 1) & 1, 521)) dead = true;
+    for (int seq = 0;; ++seq) {
+      if (!dead && !mbar_wait(&tfull[seq % kFmRing], (seq / kFmRing) & 1, 519)) dead = true;
+      if (dead) break;
+      const FmTile T = ring[seq % kFmRing];
+      if (T.nb < 0) break;
+      FM_STAMP(stamp && seq == TS, 88);
+      const bool row_ok = r < TT * G && T.t0 + t < T.t1;
+      const int qpos = T.qpos0 + T.t0 + t;
+      const int kmax = min(qpos + 1, T.L);  // keys [kmin, kmax) are visible to this row
+      const int kmin = p.window > 0 ? qpos - p.window + 1 : 0;
+      const bool st0 = stamp && seq == TS;
+      float m = -INFINITY, l = 0.f;
+      for (int i = 0; i < T.nb; ++i, ++gsm) {
+        const int sb = gsm & 1;
+        if (!dead && !mbar_wait(&sfull[sb], (gsm >> 1) & 1, 520)) dead = true;
+        if (st0 && i < 8) FM_STAMP(true, 40 + 4 * i);
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(lane_base + 128 + c * 32, v);
+        float s[kFmKB];
+        {
+          uint32_t u0[32], u1[32];
+          tmem_ld_32x32b_x32(lane_base + sb * kFmKB, u0);
+          tmem_ld_32x32b_x32(lane_base + sb * kFmKB + 32, u1);
           tc_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
-          tmem_st_32x32b_x32(lane_base + 128 + c * 32, v);
+          for (int j = 0; j < 32; ++j) {
+            s[j] = __uint_as_float(u0[j]);
+            s[32 + j] = __uint_as_float(u1[j]);
+          }
         }
-      }
-      const float base = m == -INFINITY ? 0.f : m;
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[32];
+        // visible key range of this row inside the block
+        const int k0 = (T.blk0 + i) * kFmKB;
+        const int lim = row_ok ? kmax - k0 : 0, lo = kmin - k0;
+        if (!(lo <= 0 && lim >= kFmKB)) {
 #pragma unroll
-      for (int j = 0; j < kFmKB; j += 2) {
-        const float e0 = exp2f(fmaf(s[j], sl2, -base)), e1 = exp2f(fmaf(s[j + 1], sl2, -base));
-        sum4[(j >> 1) & 3] += e0 + e1;
-        pk[j >> 1] = pack_bf16(e0, e1);
+          for (int j = 0; j < kFmKB; ++j) s[j] = (j >= lo && j < lim) ? s[j] : -INFINITY;
+        }
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int j = 0; j < kFmKB; ++j) mx4[j & 3] = fmaxf(mx4[j & 3], s[j]);
+        float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        if (st0 && i < 8) FM_STAMP(true, 41 + 4 * i);
+        mx *= sl2;  // log2 domain (the scale is positive, so the max commutes with it)
+        const bool grow = mx > m + 8.f;  // lazy rescale threshold
+        float alpha = 1.f;
+        if (grow) {
+          alpha = m == -INFINITY ? 0.f : exp2f(m - mx);
+          l *= alpha;
+          m = mx;
+        }
+        if (i > 0 && __any_sync(0xffffffffu, grow)) {
+          // O holds PV up to the previous block: wait for it, then rescale the row
+          if (!dead && !mbar_wait(&pvdone[(gsm - 1) & 1], ((gsm - 1) >> 1) & 1, 521)) dead = true;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(lane_base + 128 + c * 32, v);
+            tc_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
+            tmem_st_32x32b_x32(lane_base + 128 + c * 32, v);
+          }
+        }
+        const float base = m == -INFINITY ? 0.f : m;
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[32];
+#pragma unroll
+        for (int j = 0; j < kFmKB; j += 2) {
+          // one pair in four on the FMA pipe (the MUFU unit is the softmax's bottleneck)
+          const float x0 = fmaf(s[j], sl2, -base), x1 = fmaf(s[j + 1], sl2, -base);
+          const bool poly = ((j >> 1) & 3) == 3;
+          const float e0 = poly ? fm_exp2_poly(x0) : fm_exp2_mufu(x0);
+          const float e1 = poly ? fm_exp2_poly(x1) : fm_exp2_mufu(x1);
+          sum4[(j >> 1) & 3] += e0 + e1;
+          pk[j >> 1] = pack_bf16(e0, e1);
+        }
+        l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+        if (st0 && i < 8) FM_STAMP(true, 42 + 4 * i);
+        // P over the first 32 columns of this block's S buffer (S is already in registers)
+        tmem_st_32x32b_x32(lane_base + sb * kFmKB, pk);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pfull[sb]);
+        if (st0 && i < 8) FM_STAMP(true, 43 + 4 * i);
       }
-      l += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-      if (stamp && i < 8) FM_STAMP(42 + 4 * i);
-      // P over the first 32 columns of this block's S buffer (S is already in registers)
-      tmem_st_32x32b_x32(lane_base + sb * kFmKB, pk);
-      tc_wait_st();
+      // epilogue: wait for the tile's last PV, read O out of TMEM and release it, normalise, store
+      if (!dead && !mbar_wait(&pvdone[(gsm - 1) & 1], ((gsm - 1) >> 1) & 1, 522)) dead = true;
+      FM_STAMP(st0, 80);
+      tc_fence_after();
+      uint32_t ov[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(lane_base + 128 + c * 32, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ov[c * 32 + j] = v[j];
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&pfull[sb]);
-      if (stamp && i < 8) FM_STAMP(43 + 4 * i);
-    }
-    // epilogue: wait for the last PV, normalise, store
-    if (nb > 0 && !dead) mbar_wait(&pvdone[(nb - 1) & 1], ((nb - 1) >> 1) & 1, 522);
-    if (stamp) FM_STAMP(80);
-    tc_fence_after();
-    float f = 1.f, ll = l;
-    if (p.sinks != nullptr) {
-      const float sk = p.sinks[kvh * G + gh] * kLog2e;
-      const float mn = fmaxf(m, sk);
-      f = exp2f(m - mn);
-      ll = l * f + exp2f(sk - mn);
-    }
-    const float inv = ll > 0.f ? f / ll : 0.f;
-    __nv_bfloat16* dst = p.o + ((int64_t)(q0 + t0 + t) * p.nq + kvh * G + gh) * 128;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(lane_base + 128 + c * 32, v);
-      tc_wait_ld();
-      if (row_ok) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8)
-          *reinterpret_cast<uint4*>(dst + c * 32 + j) = make_uint4(
-              pack_bf16(__uint_as_float(v[j]) * inv, __uint_as_float(v[j + 1]) * inv),
-              pack_bf16(__uint_as_float(v[j + 2]) * inv, __uint_as_float(v[j + 3]) * inv),
-              pack_bf16(__uint_as_float(v[j + 4]) * inv, __uint_as_float(v[j + 5]) * inv),
-              pack_bf16(__uint_as_float(v[j + 6]) * inv, __uint_as_float(v[j + 7]) * inv));
+      if (lane == 0) mbar_arrive(ofree);
+      float f = 1.f, ll = l;
+      if (p.sinks != nullptr) {
+        const float sk = p.sinks[T.kvh * G + gh] * kLog2e;
+        const float mn = fmaxf(m, sk);
+        f = exp2f(m - mn);
+        ll = l * f + exp2f(sk - mn);
       }
+      const float inv = ll > 0.f ? f / ll : 0.f;
+      if (row_ok) {
+        __nv_bfloat16* dst = p.o + ((int64_t)(T.q0 + T.t0 + t) * p.nq + T.kvh * G + gh) * 128;
+#pragma unroll
+        for (int j = 0; j < 128; j += 8)
+          *reinterpret_cast<uint4*>(dst + j) = make_uint4(
+              pack_bf16(__uint_as_float(ov[j]) * inv, __uint_as_float(ov[j + 1]) * inv),
+              pack_bf16(__uint_as_float(ov[j + 2]) * inv, __uint_as_float(ov[j + 3]) * inv),
+              pack_bf16(__uint_as_float(ov[j + 4]) * inv, __uint_as_float(ov[j + 5]) * inv),
+              pack_bf16(__uint_as_float(ov[j + 6]) * inv, __uint_as_float(ov[j + 7]) * inv));
+      }
+      FM_STAMP(st0, 81);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[seq % kFmRing]);
     }
-    if (stamp) FM_STAMP(81);
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && active) FM_STAMP(82);
+  FM_STAMP(threadIdx.x == 0, 82);
+  if (tr != nullptr && threadIdx.x == 0) tr[83] = (uint32_t)(globaltimer_ns() >> 5);  // end, 32 ns units
+  if (threadIdx.x == 0 && p.epoch != 0) {
+    __threadfence();
+    const int slot = p.epoch % kFmSlots, next = (slot + 1) % kFmSlots;
+    if (atomicAdd(&g_fmha_exit[slot], 1) == (int)gridDim.x - 1) {  // last CTA out: reset
+      atomicExch(&g_fmha_work[slot], 0);
+      atomicExch(&g_fmha_exit[slot], 0);
+      atomicExch(&g_fmha_work[next], 0);
+      atomicExch(&g_fmha_exit[next], 0);
+    }
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
@@ -1575,14 +1783,30 @@ extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total
       !pd_encode(&tv, v_cache, 3, kdims, kstr, kbox))
     return 2;
   p.num_reqs = num_reqs;
+  static std::atomic<uint32_t> launches{0};
+  static const bool static_rr = [] {
+    const char* e = getenv("MINISGL_FMHA_STATIC");
+    return e != nullptr && e[0] == '1';
+  }();
+  p.epoch = ++launches;
+  if (p.epoch == 0) p.epoch = ++launches;
+  if (static_rr) p.epoch = 0;
   p.trace = g_fmha_trace;
   p.trace_ctas = g_fmha_trace_ctas;
   (void)max_q_len;
-  // upper bound of sum(ceil(q_len / tt)) over the requests
-  const int64_t tiles = (total_q + p.tt - 1) / p.tt + num_reqs;
-  if (tiles > INT32_MAX || nkv > 65535) return 3;
-  const dim3 grid((unsigned)tiles, nkv);
-  msgl_launch(fmha_prefill_kernel, grid, dim3(kFmThreads), FmSmem::kBytes, s, 1, tq, tk, tv, p);
+  // persistent: two CTAs per SM, at most one per work item (upper bound of sum(ceil(q_len / tt))
+  // over the requests, times the kv heads)
+  const int64_t work = ((total_q + p.tt - 1) / p.tt + num_reqs) * nkv;
+  if (work > INT32_MAX) return 3;
+  static std::once_flag carveout;
+  std::call_once(carveout, [] {
+    cudaFuncSetAttribute(fmha_prefill_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  });
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = (int)std::min<int64_t>(work, 2 * (int64_t)sms);
+  msgl_launch(fmha_prefill_kernel, dim3(grid), dim3(kFmThreads), FmSmem::kBytes, s, 1, tq, tk, tv, p);
   return 0;
 }
 
