@@ -371,6 +371,35 @@ void gemm_grouped(at::Tensor out, at::Tensor xs, at::Tensor w, c10::optional<at:
                     tile_count.data_ptr<int32_t>(), work.data_ptr(), max_tiles, bn, (int)epi, stream());
 }
 
+// Grouped GEMM over MXFP4 experts: q uint8 [E, K/64, n_pad, 32] (e2m1 pairs), s uint8
+// [E, K/64, n_pad, 2] (e8m0 scales), n = logical rows (gated: gate / up interleaved in 128-row blocks).
+void gemm_grouped_fp4(at::Tensor out, at::Tensor xs, at::Tensor q, at::Tensor s, int64_t n,
+                      c10::optional<at::Tensor> bias, at::Tensor tile_count, at::Tensor work, int64_t bn, int64_t epi) {
+  check_bf16(out, "out"); check_bf16(xs, "xs");
+  check_contig(xs, "xs"); check_contig(out, "out"); check_contig(q, "q"); check_contig(s, "s");
+  check_cuda(q, "q"); check_cuda(s, "s");
+  check_dtype(q, at::kByte, "q"); check_dtype(s, at::kByte, "s");
+  check_i32(tile_count, "tile_count"); check_i32(work, "work");
+  CHECK(q.dim() == 4 && q.size(3) == 32 && s.dim() == 4 && s.size(3) == 2, "fp4 experts must be [E, K/64, Np, 32|2]");
+  CHECK(q.size(0) == s.size(0) && q.size(1) == s.size(1) && q.size(2) == s.size(2), "fp4 blocks / scales mismatch");
+  CHECK(epi == 0 || epi == 1 || epi == 2 || epi == 4, "grouped gemm epilogue must be 0, 1, 2 or 4");
+  const int64_t E = q.size(0), K = q.size(1) * 64, n_pad = q.size(2);
+  const int64_t n_out = epi == 0 ? n : n / 2;
+  CHECK(n <= n_pad && n_pad % 128 == 0, "fp4 rows padded to whole tiles");
+  if (epi != 0) CHECK(n % 256 == 0 && n_pad == n, "gated grouped gemm needs 2I to be a multiple of 256");
+  CHECK(xs.size(1) == K && out.size(1) == n_out && out.size(0) == xs.size(0), "grouped gemm shapes");
+  CHECK(bn == 16 || bn == 32 || bn == 64 || bn == 128, "bn must be 16/32/64/128");
+  CHECK(xs.size(0) % bn == 0, "row capacity must be a multiple of bn");
+  if (bias.has_value()) { check_bf16(*bias, "bias"); CHECK(bias->numel() == E * n, "bias must be [E, N]"); }
+  CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(s.data_ptr()) % 16 == 0,
+        "fp4 experts must be 16-byte aligned");
+  const int max_tiles = work.numel() / 2;
+  const int rc = msgl_gemm_grouped_fp4(out.data_ptr(), xs.data_ptr(), q.data_ptr(), s.data_ptr(), opt_ptr(bias),
+                                       xs.size(0), n, n_pad, K, out.stride(0), E, tile_count.data_ptr<int32_t>(),
+                                       work.data_ptr(), max_tiles, bn, (int)epi, stream());
+  CHECK(rc == 0, "fp4 grouped gemm: unsupported shape (code ", rc, ")");
+}
+
 void moe_route(at::Tensor logits, int64_t topk, bool renorm, bool softmax_after, at::Tensor weights, at::Tensor ids) {
   check_cuda(logits, "logits"); check_dtype(logits, at::kFloat, "logits"); check_contig(logits, "logits");
   check_dtype(weights, at::kFloat, "weights"); check_i32(ids, "ids");
@@ -524,6 +553,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_decode_paged", &attention_decode_paged);
   m.def("attention_prefill_fmha", &attention_prefill_fmha);
   m.def("attention_prefill_trace", &attention_prefill_trace);
+  m.def("gemm_grouped_fp4", &gemm_grouped_fp4);
   m.def("gemm_ex", &gemm_ex);
   m.def("act_and_mul", &act_and_mul);
   m.def("store_kv", &store_kv);

@@ -74,6 +74,12 @@ void msgl_argmax_partials(int32_t* out, float* out_val, const void* part, int n_
 void msgl_gemm_grouped(void* out, const void* x, const void* w, const void* bias, int rows_cap, int N, int K,
                        int ldo, int E, const int* tile_count, const void* work, int max_tiles, int bn, int epi,
                        cudaStream_t s);
+// msgl_gemm_grouped with MXFP4 expert weights kept in HBM (k-block-major: q [E][K/64][n_pad][32]
+// e2m1 bytes, sc [E][K/64][n_pad][2] e8m0 scales; N logical rows, K % 64 == 0). Returns 0, or 3 for
+// an unsupported shape.
+int msgl_gemm_grouped_fp4(void* out, const void* x, const void* q, const void* sc, const void* bias, int rows_cap,
+                          int N, int n_pad, int K, int ldo, int E, const int* tile_count, const void* work,
+                          int max_tiles, int bn, int epi, cudaStream_t s);
 void msgl_moe_route(const float* logits, int T, int E, int topk, int renorm, int softmax_after, float* weights,
                     int32_t* ids, cudaStream_t s);
 // experts [e0, e0 + E) are local (expert parallelism); other assignments get inv = -1

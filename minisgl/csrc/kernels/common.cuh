@@ -288,6 +288,14 @@ MSGL_DEVICE void bulk_push_dsmem(uint32_t remote_dst, const void* src, uint32_t 
                : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory, completing on a local mbarrier (no
+// multicast). Both addresses 16-byte aligned, bytes a multiple of 16.
+MSGL_DEVICE void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 MSGL_DEVICE float4 ld_dsmem_v4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"

@@ -547,6 +547,239 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 
 
 // =================================================================================================
+// MXFP4 weights (grouped / MoE mode): experts stay in HBM as e2m1 values (two per byte, low nibble
+// first) with one e8m0 scale per 32 values along K, in a k-block-major layout
+//   q [E][K/64][Np][32] bytes, s [E][K/64][Np][2] bytes   (Np = rows padded to whole weight tiles)
+// so one (expert, 64-K block, weight tile) is a single contiguous bulk copy of each. Four
+// converter warps turn every landed fp4 tile into the bf16 operand tile (128B-swizzled, the layout
+// the TMA writes for bf16 weights) and the rest of the pipeline is the bf16 kernel's: the MMA warp
+// waits for the converted tile, epilogue warps 2..9 as in gemm_kernel. Conversion: a 1 KB table
+// maps each byte (two e2m1 codes) to their bf16 pair at scale 1, replicated once per lane so a
+// warp's lookups hit 32 different banks; one bf16x2 multiply applies the block scale (a power of
+// two, so the product is exact: the same bf16 values as dequantising at load).
+// =================================================================================================
+constexpr int kConvWarps = 4;
+constexpr int kThreadsF4 = kThreads + kConvWarps * 32;
+
+template <int BN, int EPI, bool WIDE>
+struct CfgF4 {
+  using C = Cfg<BN, EPI, WIDE>;
+  static constexpr int kQ = C::kRowsA * 32;                   // fp4 bytes of one stage
+  static constexpr int kS = C::kRowsA * 2;                    // scale bytes of one stage
+  static constexpr int kRaw = (kQ + kS + 1023) / 1024 * 1024;
+  static constexpr int kStage = C::kA + C::kB + kRaw;         // {bf16 weight tile, activations, raw}
+  static constexpr int kLut = 256 * 32 * 4;
+  static constexpr int kStages = std::min(6, (220 * 1024 - C::kEpiSmem - kLut) / kStage);
+  static constexpr int kSmem = 1024 + kStages * kStage + C::kEpiSmem + kLut + 256;
+  static_assert(kStages >= 2, "fp4 GEMM stages do not fit");
+};
+
+// bf16 bits of an e2m1 code at scale 1 (sign bit 3; 0, 0.5, 1, 1.5, 2, 3, 4, 6)
+__device__ __forceinline__ uint32_t e2m1_bf16(uint32_t c) {
+  constexpr uint32_t kMag[8] = {0x0000, 0x3F00, 0x3F80, 0x3FC0, 0x4000, 0x4040, 0x4080, 0x40C0};
+  return kMag[c & 7] | ((c & 8) << 12);
+}
+
+// bf16 of 2^(e - 127) for an e8m0 scale byte, in both halves
+__device__ __forceinline__ uint32_t e8m0_bf16x2(uint32_t e) {
+  const uint32_t b = e == 0 ? 0x0040u : (e << 7);  // 2^-127 is a bf16 subnormal
+  return b | (b << 16);
+}
+
+template <int BN, int EPI, bool WIDE>
+__global__ void __launch_bounds__(kThreadsF4, 1)
+gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_out,
+                const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wsc, int n_pad, Params p) {
+  using C = Cfg<BN, EPI, WIDE>;
+  using F = CfgF4<BN, EPI, WIDE>;
+  constexpr int W = C::kChunk;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* epi_smem = smem + F::kStages * F::kStage;
+  uint32_t* lut = reinterpret_cast<uint32_t*>(epi_smem + C::kEpiSmem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(lut) + F::kLut);
+  uint64_t* full = bars;                  // raw fp4 + scales + activations landed
+  uint64_t* conv = bars + F::kStages;     // bf16 weight tile written (converter threads)
+  uint64_t* empty = bars + 2 * F::kStages;
+  uint64_t* tfull = bars + 3 * F::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = p.n_tiles * p.m_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < F::kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&conv[i], kConvWarps * 32);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], kEpiWarps);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_out);
+  }
+  // byte -> bf16x2 table, entry (byte, copy) at word byte * 32 + copy (lane L reads copy L)
+  for (int i = threadIdx.x; i < 256 * 32; i += kThreadsF4) {
+    const uint32_t b = (uint32_t)i >> 5;
+    lut[i] = e2m1_bf16(b & 15) | (e2m1_bf16(b >> 4) << 16);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  pdl_launch();
+  pdl_wait();  // every role reads the device work list
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        int nt, row0, expert;
+        if (!unit_coords(p, u, BN, nt, row0, expert)) continue;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, 150)) { ok = false; break; }
+          uint8_t* st = stages + stage * F::kStage;
+          uint8_t* raw = st + C::kA + C::kB;
+          mbar_expect_tx(&full[stage], F::kQ + F::kS + C::kB);
+          const size_t blk = ((size_t)expert * p.kblocks + kb) * n_pad + (size_t)nt * C::kRowsA;
+          bulk_load(raw, wq + blk * 32, F::kQ, &full[stage]);
+          bulk_load(raw + F::kQ, wsc + blk * 2, F::kS, &full[stage]);
+          tma_load_2d(st + C::kA, &tmap_x, &full[stage], kb * BK, row0);
+          if (++stage == F::kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, BN);
+      int stage = 0, use = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        int nt_, row0_, ex_;
+        if (!unit_coords(p, u, BN, nt_, row0_, ex_)) continue;
+        const int acc = C::kBufs == 2 ? (use & 1) : 0;
+        const uint32_t par = C::kBufs == 2 ? ((use >> 1) & 1) : (use & 1);
+        if (!mbar_wait(&tempty[acc], par ^ 1, 250)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * C::kAccCols;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&conv[stage], phase, 251)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a = smem_u32(stages + stage * F::kStage);
+          const uint32_t b = a + C::kA;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint64_t bd = smem_desc_sw128(b + k * 32);
+            tc_mma_f16(d, smem_desc_sw128(a + k * 32), bd, idesc, accum);
+            if constexpr (C::kTwo) tc_mma_f16(d + BN, smem_desc_sw128(a + 128 * 128 + k * 32), bd, idesc, accum);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == F::kStages) { stage = 0; phase ^= 1; }
+        }
+        tc_commit(&tfull[acc]);
+        ++use;
+      }
+    }
+  } else if (warp >= 2 + kEpiWarps) {
+    // ------------------------------------------------------------------ fp4 -> bf16 converters
+    const int ct = threadIdx.x - kThreads;  // 0..127: weight row (and row + 128 when 256 rows)
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      int nt_, row0_, ex_;
+      if (!unit_coords(p, u, BN, nt_, row0_, ex_)) continue;
+      for (int kb = 0; kb < p.kblocks; ++kb) {
+        if (!mbar_wait(&full[stage], phase, 350)) { ok = false; break; }
+        uint8_t* st = stages + stage * F::kStage;
+        const uint8_t* raw = st + C::kA + C::kB;
+#pragma unroll
+        for (int h = 0; h < C::kRowsA / 128; ++h) {
+          const int r = h * 128 + ct;
+          const uint4 q0 = *reinterpret_cast<const uint4*>(raw + r * 32);
+          const uint4 q1 = *reinterpret_cast<const uint4*>(raw + r * 32 + 16);
+          const uint32_t sc = *reinterpret_cast<const uint16_t*>(raw + F::kQ + r * 2);
+          const uint32_t sb0 = e8m0_bf16x2(sc & 0xFF), sb1 = e8m0_bf16x2(sc >> 8);
+          const __nv_bfloat162 s0 = *reinterpret_cast<const __nv_bfloat162*>(&sb0);
+          const __nv_bfloat162 s1 = *reinterpret_cast<const __nv_bfloat162*>(&sb1);
+          const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          uint8_t* dst = st + h * 128 * 128 + (r & 127) * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {  // 16-byte chunk c: values 8c .. 8c + 7
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t byte = __byte_perm(words[c], 0, 0x4440 + j);
+              const uint32_t v = lut[byte * 32 + lane];
+              __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(&v);
+              x = __hmul2(x, c < 4 ? s0 : s1);
+              o[j] = *reinterpret_cast<const uint32_t*>(&x);
+            }
+            *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        }
+        fence_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
+        mbar_arrive(&conv[stage]);
+        if (++stage == F::kStages) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* stage_out = epi_smem + (warp - 2) * C::kStageOut;
+    constexpr int kChunks = BN / W;
+    constexpr int kParts = (C::kTwo && !C::kAct) ? 2 : 1;
+    constexpr int kItems = kParts * kChunks;
+    int use = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      int nt, row0, expert;
+      if (!unit_coords(p, u, BN, nt, row0, expert)) continue;
+      const __nv_bfloat16* bias = p.bias == nullptr ? nullptr : p.bias + (int64_t)expert * p.bias_stride;
+      const int use_now = use++;
+      const int acc = C::kBufs == 2 ? (use_now & 1) : 0;
+      const uint32_t par = C::kBufs == 2 ? ((use_now >> 1) & 1) : (use_now & 1);
+      if (!mbar_wait(&tfull[acc], par, 352)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + acc * C::kAccCols + ((uint32_t)(q * 32) << 16);
+      for (int it = half; it < kItems; it += 2) {
+        const int part = it / kChunks, c = it % kChunks;
+        float v[32], g2[32];
+        tmem_load_cols<W>(tb + part * BN + c * W, v);
+        if constexpr (C::kAct) tmem_load_cols<W>(tb + BN + c * W, g2);
+        store_item<BN, EPI, WIDE>(v, g2, p, bias, nt, row0, part, c, q, lane, stage_out, &tmap_out);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (lane == 0) bulk_wait_read<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// =================================================================================================
 // 2-SM variant (tcgen05.mma.cta_group::2): a CTA pair computes one 256-weight-row tile. Each CTA
 // loads its own 128 weight rows (256 for gated outputs: 128 gate + 128 up) and HALF of the token
 // tile into its own smem; the loads complete on the pair leader's barrier; the leader's single MMA
@@ -1389,6 +1622,69 @@ extern "C" void msgl_gemm_grouped(void* out, const void* x, const void* w, const
     case kSwiglu: launch_grouped_bn<kSwiglu>(bn, p, x, w, out, E, N, K, ldo, s); break;
     default: launch_grouped_bn<kBf16>(bn, p, x, w, out, E, N, K, ldo, s); break;
   }
+}
+
+template <int BN, int EPI>
+static void launch_grouped_fp4(const Params& p, const void* x, const uint8_t* q, const uint8_t* sc, int n_pad,
+                               void* out, int K, int ldo, cudaStream_t s) {
+  constexpr bool kGated = EPI != kBf16;
+  using C = Cfg<BN, EPI, kGated>;
+  using F = CfgF4<BN, EPI, kGated>;
+  msgl_set_smem<gemm_fp4_kernel<BN, EPI, kGated>>(F::kSmem);
+  const CUtensorMap mx = make_map(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, K, K, BK, BN, true);
+  const CUtensorMap mo = make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, C::kChunk, false);
+  const int units = p.n_tiles * p.m_tiles;
+  msgl_launch(gemm_fp4_kernel<BN, EPI, kGated>, dim3(std::min(units, num_sms_cached())), dim3(kThreadsF4), F::kSmem,
+              s, 1, mx, mo, q, sc, n_pad, p);
+}
+
+template <int EPI>
+static void launch_grouped_fp4_bn(int bn, const Params& p, const void* x, const uint8_t* q, const uint8_t* sc,
+                                  int n_pad, void* out, int K, int ldo, cudaStream_t s) {
+  switch (bn) {
+    case 16: launch_grouped_fp4<16, EPI>(p, x, q, sc, n_pad, out, K, ldo, s); break;
+    case 32: launch_grouped_fp4<32, EPI>(p, x, q, sc, n_pad, out, K, ldo, s); break;
+    case 64: launch_grouped_fp4<64, EPI>(p, x, q, sc, n_pad, out, K, ldo, s); break;
+    default: launch_grouped_fp4<128, EPI>(p, x, q, sc, n_pad, out, K, ldo, s); break;
+  }
+}
+
+// msgl_gemm_grouped with MXFP4 expert weights in the k-block-major layout (see gemm_fp4_kernel):
+// q [E][K/64][n_pad][32] e2m1 bytes, sc [E][K/64][n_pad][2] e8m0 scales; N logical rows (gated:
+// gate / up interleaved in 128-row blocks, N % 256 == 0), n_pad >= N a multiple of the weight tile
+// (256 gated, 128 otherwise), K % 64 == 0.
+extern "C" int msgl_gemm_grouped_fp4(void* out, const void* x, const void* q, const void* sc, const void* bias,
+                                     int rows_cap, int N, int n_pad, int K, int ldo, int E, const int* tile_count,
+                                     const void* work, int max_tiles, int bn, int epi, cudaStream_t s) {
+  if (rows_cap <= 0 || N <= 0 || max_tiles <= 0) return 0;
+  const bool gated = epi != kBf16;
+  if (K % BK != 0 || (gated && (N % 256 != 0 || n_pad != N)) || (!gated && (n_pad % 128 != 0 || n_pad < N)) ||
+      E <= 0)
+    return 3;
+  Params p;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.arrive_ticket = nullptr;
+  p.arrive_mc = nullptr;
+  p.argmax_out = nullptr;
+  p.bias_stride = N;
+  p.w_blocked = 0;
+  p.grp_count = tile_count;
+  p.grp_work = reinterpret_cast<const int2*>(work);
+  p.M = rows_cap;
+  p.n_out = gated ? N / 2 : N;
+  p.n_tiles = gated ? N / 256 : (N + 127) / 128;
+  p.m_tiles = max_tiles;
+  p.kblocks = K / BK;
+  p.splits = 1;
+  const uint8_t* q8 = reinterpret_cast<const uint8_t*>(q);
+  const uint8_t* s8 = reinterpret_cast<const uint8_t*>(sc);
+  switch (epi) {
+    case kSilu: launch_grouped_fp4_bn<kSilu>(bn, p, x, q8, s8, n_pad, out, K, ldo, s); break;
+    case kGelu: launch_grouped_fp4_bn<kGelu>(bn, p, x, q8, s8, n_pad, out, K, ldo, s); break;
+    case kSwiglu: launch_grouped_fp4_bn<kSwiglu>(bn, p, x, q8, s8, n_pad, out, K, ldo, s); break;
+    default: launch_grouped_fp4_bn<kBf16>(bn, p, x, q8, s8, n_pad, out, K, ldo, s); break;
+  }
+  return 0;
 }
 
 namespace {

@@ -59,6 +59,7 @@ _FLAGS = {
     "NVLS_LL_BYTES": _Flag(2 << 20, parse_mem_bytes),  # largest world x T x H x 4 sent in the LL form
     "NVLS_GEMM_FUSION": _Flag(True, _as_bool),  # row-parallel GEMMs write the NVLS staging region
     "FUSED_LM_HEAD": _Flag(True, _as_bool),  # greedy batches take the argmax in the LM-head GEMM epilogue
+    "MXFP4_RESIDENT": _Flag(True, _as_bool),  # keep MXFP4 experts in fp4 on the GPU (fp4 grouped GEMM)
 }
 
 

@@ -70,16 +70,44 @@ class MoELayer(BaseOP):
     _interleaved = False  # gate_up_proj in the gated grouped-GEMM layout (CUDA)
 
     def load_state_dict(self, state_dict, *, prefix: str = "", _internal: bool = False) -> None:
-        super().load_state_dict(state_dict, prefix=prefix, _internal=_internal)
-        if self.gate_up_proj.is_cuda:
-            # gate / up rows interleaved in 128-row blocks (intermediate size padded to a whole
-            # block) so the first grouped GEMM applies the activation in its epilogue; the public
-            # tensors then hold the GPU layout
-            from minisgl.ops.moe import interleave_experts
+        from minisgl.moe.mxfp4 import Mxfp4Experts, dequant_mxfp4, interleave_rows, pad_k
 
+        # MXFP4 experts (``<proj>_blocks`` / ``<proj>_scales``, see models/weight.py): kept in fp4
+        # on the GPU for the fp4 grouped GEMM, dequantised elsewhere
+        key = (lambda n: f"{prefix}.{n}") if prefix else (lambda n: n)
+        fp4 = {}
+        for proj in ("gate_up_proj", "down_proj"):
+            if key(f"{proj}_blocks") in state_dict:
+                blocks, scales = state_dict.pop(key(f"{proj}_blocks")), state_dict.pop(key(f"{proj}_scales"))
+                if blocks.is_cuda:
+                    fp4[proj] = (blocks, scales)
+                    setattr(self, proj, None)  # not a tensor: the state-dict walk skips it
+                else:
+                    state_dict[key(proj)] = dequant_mxfp4(blocks, scales, getattr(self, proj).dtype)
+        super().load_state_dict(state_dict, prefix=prefix, _internal=_internal)
+        if not fp4 and not self.gate_up_proj.is_cuda:
+            return
+        # GPU layout: gate / up rows interleaved in 128-row blocks (intermediate size padded to a
+        # whole block) so the first grouped GEMM applies the activation in its epilogue
+        from minisgl.ops.moe import interleave_experts
+
+        if "gate_up_proj" in fp4:
+            blocks, scales = fp4["gate_up_proj"]
+            self.gate_up_proj = Mxfp4Experts.pack(interleave_rows(blocks), interleave_rows(scales), 256)
+            if self.gate_up_proj_bias is not None:
+                self.gate_up_proj_bias = interleave_rows(self.gate_up_proj_bias)
+            ip = self.gate_up_proj.n // 2
+            if "down_proj" in fp4:
+                blocks, scales = fp4["down_proj"]
+                self.down_proj = Mxfp4Experts.pack(*pad_k(blocks, scales, ip), 128)
+            elif self.down_proj.shape[2] != ip:
+                w2 = torch.zeros(*self.down_proj.shape[:2], ip, dtype=self.down_proj.dtype, device=self.down_proj.device)
+                w2[:, :, : self.down_proj.shape[2]] = self.down_proj
+                self.down_proj = w2
+        else:
             self.gate_up_proj, self.down_proj, self.gate_up_proj_bias = interleave_experts(
                 self.gate_up_proj, self.down_proj, self.gate_up_proj_bias)
-            self._interleaved = True
+        self._interleaved = True
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         be = get_global_ctx().moe_backend

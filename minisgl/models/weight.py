@@ -27,6 +27,7 @@ from typing import Dict, Iterator, Tuple
 
 import torch
 
+from minisgl.moe.mxfp4 import dequant_mxfp4  # noqa: F401  (re-exported for checkpoint tools)
 from minisgl.ops.reference import GATE_UP_BLOCK, interleave_gate_up
 from minisgl.parallel import get_tp_info
 from minisgl.utils import div_ceil
@@ -37,26 +38,10 @@ _QKV = {".q_proj.": "q", ".k_proj.": "k", ".v_proj.": "v"}
 _GU = {".gate_proj.": "gate", ".up_proj.": "up"}
 _EXPERT = re.compile(r"^(?P<pre>.+\.experts)\.(?P<idx>\d+)\.(?P<name>.+)$")
 
-# e2m1 code -> value (sign bit 3, exponent bits 2..1, mantissa bit 0)
-_E2M1 = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0)
+def _keep_mxfp4() -> bool:
+    from minisgl.env import ENV
 
-
-def dequant_mxfp4(blocks: torch.Tensor, scales: torch.Tensor, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
-    """``blocks [..., G, 16]`` uint8 (32 e2m1 values per block, low nibble first), ``scales [..., G]``
-    uint8 e8m0 -> ``[..., G * 32]``. Processed one leading index at a time to bound temporaries."""
-    if blocks.shape[:-1] != scales.shape or blocks.shape[-1] != 16:
-        raise ValueError(f"mxfp4 blocks {tuple(blocks.shape)} / scales {tuple(scales.shape)} mismatch")
-    lut = torch.tensor(_E2M1, dtype=torch.float32, device=blocks.device)
-    out = torch.empty(blocks.shape[:-2] + (blocks.shape[-2] * 32,), dtype=dtype, device=blocks.device)
-    flat_b = blocks.reshape(-1, *blocks.shape[-2:])
-    flat_s = scales.reshape(-1, scales.shape[-1])
-    flat_o = out.view(-1, out.shape[-1])
-    for i in range(flat_b.shape[0]):
-        b = flat_b[i].to(torch.uint8)
-        v = torch.stack([lut[(b & 0x0F).long()], lut[(b >> 4).long()]], dim=-1).reshape(b.shape[0], 32)
-        v = torch.ldexp(v, (flat_s[i].to(torch.int32) - 127).unsqueeze(-1).to(torch.float32))
-        flat_o[i] = v.reshape(-1).to(dtype)
-    return out
+    return bool(ENV.MXFP4_RESIDENT)
 
 
 def _split_gate_up_rows(w: torch.Tensor, rank: int, size: int) -> torch.Tensor:
@@ -71,7 +56,8 @@ def _split_gate_up_rows(w: torch.Tensor, rank: int, size: int) -> torch.Tensor:
 def _fused_expert(key: str, t: torch.Tensor, pending: Dict[str, torch.Tensor], rank: int, size: int, dtype,
                   experts: tuple | None = None):
     """Convert one gpt-oss fused-expert tensor; returns ``(name, tensor)``, ``None`` while an MXFP4
-    blocks / scales pair is incomplete, or ``False`` if ``key`` is not such a tensor. With
+    blocks / scales pair is incomplete (a list of two: the pair kept as MXFP4), or ``False`` if
+    ``key`` is not such a tensor. With
     ``experts = (first, count)`` (expert parallelism) only those experts are kept, whole."""
     if experts is not None and t.dim() >= 2 and ".experts." in key:
         t = t[experts[0] : experts[0] + experts[1]]
@@ -83,7 +69,19 @@ def _fused_expert(key: str, t: torch.Tensor, pending: Dict[str, torch.Tensor], r
                 pending[key] = t
                 if f"{base}_blocks" not in pending or f"{base}_scales" not in pending:
                     return None
-                w = dequant_mxfp4(pending.pop(f"{base}_blocks"), pending.pop(f"{base}_scales"), dtype)
+                blocks, scales = pending.pop(f"{base}_blocks"), pending.pop(f"{base}_scales")
+                if _keep_mxfp4():
+                    # kept as MXFP4 (the MoE layer packs it for the fp4 grouped GEMM): rows permuted
+                    # and split as the bf16 weights would be; the down projection's input dim splits
+                    # across ranks in whole 32-value blocks only
+                    if proj == "gate_up_proj":  # [E, 2I, H/32, 16], rows interleaved
+                        return [(f"{base}_blocks", _split_gate_up_rows(blocks, rank, size)),
+                                (f"{base}_scales", _split_gate_up_rows(scales, rank, size))]
+                    if size == 1 or scales.shape[-1] % size == 0:  # [E, H, I/32, 16]
+                        if size > 1:
+                            blocks, scales = blocks.chunk(size, dim=2)[rank], scales.chunk(size, dim=2)[rank]
+                        return [(f"{base}_blocks", blocks.contiguous()), (f"{base}_scales", scales.contiguous())]
+                w = dequant_mxfp4(blocks, scales, dtype)
                 if proj == "gate_up_proj":  # [E, 2I, H], rows interleaved
                     return base, _split_gate_up_rows(w, rank, size)
                 return base, (w.chunk(size, dim=-1)[rank] if size > 1 else w).contiguous()  # [E, H, I]
@@ -207,6 +205,9 @@ def load_weight(model_path: str, device: torch.device, config=None) -> Iterator[
                 if ".experts." in key and em is None:
                     conv = _fused_expert(key, raw, pending, info.rank, info.size, dtype, ep)
                     if conv is None:
+                        continue
+                    if isinstance(conv, list):
+                        yield from conv
                         continue
                     if conv is not False:
                         yield conv

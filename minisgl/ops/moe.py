@@ -3,7 +3,8 @@
 route (softmax top-k) -> align (counting sort into per-expert segments padded to ``bn`` rows,
 device work list) -> gather permuted activations -> grouped tcgen05 GEMM (gate|up, activation in
 its epilogue when the weights are gate/up interleaved) -> grouped GEMM (down) -> weighted top-k
-combine.
+combine. Expert weights are bf16 ``[E, N, K]`` tensors or MXFP4 ``Mxfp4Experts`` (fp4 in HBM,
+converted to bf16 tile by tile inside the grouped GEMM).
 
 Behaviour matches ``moe/grouped.py:moe_reference`` (and the reference's fused MoE,
 python/minisgl/moe/fused.py:127-227).
@@ -63,6 +64,16 @@ def pick_bn(pairs: int, experts: int) -> int:
     return 128
 
 
+def _grouped(out, xs, w, bias, count, work, bn, epi):
+    """Grouped GEMM over bf16 experts ``[E, N, K]`` or MXFP4 experts kept in fp4 (``Mxfp4Experts``)."""
+    from minisgl.moe.mxfp4 import Mxfp4Experts
+
+    if isinstance(w, Mxfp4Experts):
+        _cuda().gemm_grouped_fp4(out, xs, w.q, w.s, w.n, bias, count, work, bn, epi)
+    else:
+        _cuda().gemm_grouped(out, xs, w, bias, count, work, bn, epi)
+
+
 def moe_forward(x, w1, w2, gating, topk, renormalize, activation, w1_bias=None, w2_bias=None,
                 softmax_after_topk=False, expert_offset: int = 0, w1_interleaved: bool = False):
     """``w1``/``w2`` hold experts [expert_offset, expert_offset + E) of the ``gating`` columns
@@ -91,13 +102,13 @@ def moe_forward(x, w1, w2, gating, topk, renormalize, activation, w1_bias=None, 
     c.moe_gather(xs, x.contiguous(), perm, topk)
     a = torch.empty(rows, inter, dtype=x.dtype, device=dev)
     if w1_interleaved:
-        c.gemm_grouped(a, xs, w1, w1_bias, count, work, bn, _GATED_EPI[activation])
+        _grouped(a, xs, w1, w1_bias, count, work, bn, _GATED_EPI[activation])
     else:
         y1 = torch.empty(rows, two_i, dtype=x.dtype, device=dev)
-        c.gemm_grouped(y1, xs, w1, w1_bias, count, work, bn, 0)
+        _grouped(y1, xs, w1, w1_bias, count, work, bn, 0)
         c.moe_act(a, y1, _ACT[activation], perm)
     y2 = torch.empty(rows, H, dtype=x.dtype, device=dev)
-    c.gemm_grouped(y2, a, w2, w2_bias, count, work, bn, 0)
+    _grouped(y2, a, w2, w2_bias, count, work, bn, 0)
     out = torch.empty(T, H, dtype=x.dtype, device=dev)
     c.moe_combine(out, y2, weights, inv, topk)
     return out
