@@ -25,8 +25,9 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
-# gpt-oss-120b (MoE, bf16 experts: ~240 GB of weights) needs TP >= 2; with MINISGL_MOE_PARALLEL=ep
-# each rank holds whole experts
+# gpt-oss-120b (MoE): its experts stay MXFP4 in HBM (~65 GB of weights in all, so one GPU holds it);
+# with MINISGL_MXFP4_RESIDENT=0 they are bf16 (~240 GB: TP >= 2); with MINISGL_MOE_PARALLEL=ep each
+# rank holds whole experts
 MODELS = {"qwen3-14b": "qwen3-14b", "qwen3-0.6b": "qwen3-0.6b", "qwen3-32b": "qwen3-32b",
           "gpt-oss-120b": "gpt-oss-120b"}
 CONFIG = dict(max_running_req=256, cuda_graph_max_bs=256, page_size=64, max_seq_len_override=4096,

@@ -10,6 +10,7 @@ times without timing, which is the form to wrap in a profiler.
   gemm-sweep    Qwen3-14B decode GEMMs per TP degree: automatic plan vs every forced tiling vs cuBLAS
   decode-attn   paged decode attention over a longest-first work list (page size 64)
   prefill-attn  ragged causal prefill attention (requests of 100..1024 tokens; --impl tcgen05 | mma | trtllm)
+  moe           one gpt-oss-style MoE layer, experts bf16 vs MXFP4 kept in fp4
   suite         every other hot kernel once at decode shapes (Qwen3-14B, --bs tokens; MoE at
                 Qwen3-30B-A3B shapes): embedding, RMSNorm, fused add+RMSNorm, QK-norm+RoPE+KV
                 store, KV store, SiLU-mul, 1-SM and 2-SM GEMMs, argmax, top-k/top-p sampling and
@@ -257,6 +258,53 @@ def _prefill_trace(c, run, path=None) -> None:
           f"dynamic smem base mod 1024: {sorted(set(int(v) for v in t[:, 5]))}")
 
 
+def _moe(a, c) -> None:
+    """One gpt-oss-style MoE layer (swiglu_oai, biases, top-k after softmax) on ``--bs`` tokens:
+    experts as bf16 vs MXFP4 kept in fp4 (converted inside the grouped GEMM). Reports CUDA-event
+    time per layer and the expert bytes read per call (experts hit by the routing, all of their
+    rows) as a fraction of the measured HBM bandwidth."""
+    from minisgl.moe.mxfp4 import Mxfp4Experts, interleave_rows, pad_k
+    from minisgl.ops.moe import interleave_experts, moe_forward
+
+    E, H, inter, T, topk = a.experts, a.hidden, a.inter, a.bs, a.topk
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    b1 = torch.randint(0, 256, (E, 2 * inter, H // 32, 16), generator=g, device=dev, dtype=torch.uint8)
+    s1 = torch.randint(119, 124, (E, 2 * inter, H // 32), generator=g, device=dev, dtype=torch.uint8)
+    b2 = torch.randint(0, 256, (E, H, inter // 32, 16), generator=g, device=dev, dtype=torch.uint8)
+    s2 = torch.randint(119, 124, (E, H, inter // 32), generator=g, device=dev, dtype=torch.uint8)
+    q1 = Mxfp4Experts.pack(interleave_rows(b1), interleave_rows(s1), 256)
+    ip = q1.n // 2
+    q2 = Mxfp4Experts.pack(*pad_k(b2, s2, ip), 128)
+    del b1, s1, b2, s2
+    x = torch.randn(T, H, device=dev, dtype=torch.bfloat16)
+    gating = torch.randn(T, E, device=dev)
+    bias1 = torch.zeros(E, 2 * ip, device=dev, dtype=torch.bfloat16)
+    bias2 = torch.zeros(E, H, device=dev, dtype=torch.bfloat16)
+    hit = int(torch.topk(gating, topk, dim=-1).indices.unique().numel())
+    hbm, _ = _peaks()
+    impls = {"mxfp4": (q1, q2)}
+    if not a.once:
+        w1 = q1.dequant()
+        w2 = q2.dequant()
+        impls["bf16"] = (w1, w2)
+    for name, (w1, w2) in impls.items():
+        def run():
+            moe_forward(x, w1, w2, gating, topk, True, "swiglu_oai", bias1, bias2, True, 0, True)
+
+        if a.once:
+            for _ in range(3):
+                run()
+            torch.cuda.synchronize()
+            print("ok", c.get_error())
+            return
+        ms = perf_cuda(run, reps=10, graph_calls=5)
+        per_expert = (q1.nbytes() + q2.nbytes()) / E if name == "mxfp4" else (w1.numel() + w2.numel()) * 2 / E
+        nbytes = per_expert * hit
+        print(f"moe[{name}] tokens={T} experts={E} hit={hit} H={H} I={inter} top{topk}: {ms * 1e3:.1f} us, "
+              f"{nbytes / ms / 1e6:.0f} GB/s of expert weights ({nbytes / ms * 1e3 / hbm:.2f} of measured)")
+
+
 def _suite(a, c) -> None:
     """One table row per kernel: CUDA-event time (graph replay) and bytes the kernel must move.
     Weight-streaming entries rotate over copies larger than L2; activation-sized entries are
@@ -411,7 +459,7 @@ def _gemm_sweep(a, c) -> None:
 
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    p.add_argument("op", choices=["gemm", "gemm-sweep", "decode-attn", "prefill-attn", "suite"])
+    p.add_argument("op", choices=["gemm", "gemm-sweep", "decode-attn", "prefill-attn", "suite", "moe"])
     p.add_argument("--tps", default="1,2,4,8", help="gemm-sweep: TP degrees")
     p.add_argument("--ms", default="16,64,128,256", help="gemm-sweep: token counts")
     p.add_argument("--m", type=int, default=128)
@@ -422,6 +470,10 @@ def main(argv=None) -> None:
     p.add_argument("--nq", type=int, default=40)
     p.add_argument("--nkv", type=int, default=8)
     p.add_argument("--tokens", type=int, default=16384)
+    p.add_argument("--experts", type=int, default=128, help="moe: experts on this GPU")
+    p.add_argument("--hidden", type=int, default=2880, help="moe: hidden size")
+    p.add_argument("--inter", type=int, default=2880, help="moe: expert intermediate size")
+    p.add_argument("--topk", type=int, default=4, help="moe: experts per token")
     p.add_argument("--impl", default="tcgen05", choices=["tcgen05", "mma", "trtllm"],
                    help="prefill-attn kernel (trtllm: FlashInfer's trtllm-gen kernel, for comparison)")
     p.add_argument("--once", action="store_true", help="run a few times untimed (for profilers)")
@@ -431,7 +483,7 @@ def main(argv=None) -> None:
     from minisgl._native import cuda
 
     c = cuda()
-    {"gemm": _gemm, "gemm-sweep": _gemm_sweep, "decode-attn": _decode_attn, "prefill-attn": _prefill_attn,
+    {"gemm": _gemm, "gemm-sweep": _gemm_sweep, "decode-attn": _decode_attn, "prefill-attn": _prefill_attn, "moe": _moe,
      "suite": _suite}[a.op](a, c)
 
 

@@ -550,35 +550,48 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ 
 // MXFP4 weights (grouped / MoE mode): experts stay in HBM as e2m1 values (two per byte, low nibble
 // first) with one e8m0 scale per 32 values along K, in a k-block-major layout
 //   q [E][K/64][Np][32] bytes, s [E][K/64][Np][2] bytes   (Np = rows padded to whole weight tiles)
-// so one (expert, 64-K block, weight tile) is a single contiguous bulk copy of each. Four
-// converter warps turn every landed fp4 tile into the bf16 operand tile (128B-swizzled, the layout
-// the TMA writes for bf16 weights) and the rest of the pipeline is the bf16 kernel's: the MMA warp
-// waits for the converted tile, epilogue warps 2..9 as in gemm_kernel. Conversion: a 1 KB table
-// maps each byte (two e2m1 codes) to their bf16 pair at scale 1, replicated once per lane so a
-// warp's lookups hit 32 different banks; one bf16x2 multiply applies the block scale (a power of
-// two, so the product is exact: the same bf16 values as dequantising at load).
+// so one (expert, 64-K block, weight tile) is a single contiguous bulk copy of each. Converter
+// warps (8, or 4 for 128-token tiles whose epilogue needs the registers) turn every landed fp4
+// tile into the bf16 operand tile (128B-swizzled, the layout the TMA writes for bf16 weights) and
+// the rest of the pipeline is the bf16 kernel's: the MMA warp waits for the converted tile,
+// epilogue warps 2..9 as in gemm_kernel. Conversion in registers (fp4_to_bf16x8): byte-permute
+// lookups into 8-entry tables of the bf16 high and low bytes of |e2m1| at scale 1, the sign bits
+// spread by the permute's sign-replicate mode, then one bf16x2 multiply by the block scale (a
+// power of two, so the product is exact: the same bf16 values as dequantising at load).
 // =================================================================================================
-constexpr int kConvWarps = 4;
-constexpr int kThreadsF4 = kThreads + kConvWarps * 32;
+template <int BN>
+constexpr int conv_warps() { return BN <= 64 ? 8 : 4; }
+template <int BN>
+constexpr int threads_f4() { return kThreads + conv_warps<BN>() * 32; }
+
+// Eight e2m1 values (x: byte k = codes 2k (low nibble) and 2k + 1) -> four bf16x2 words at scale 1
+__device__ __forceinline__ void fp4_to_bf16x8(uint32_t x, uint32_t (&o)[4]) {
+  // bf16 of |e2m1| 0, 0.5, 1, 1.5, 2, 3, 4, 6: low bytes 00 00 80 C0 00 40 80 C0, high 00 3F 3F 3F 40 40 40 40
+  constexpr uint32_t kLbLo = 0xC0800000u, kLbHi = 0xC0804000u, kHbLo = 0x3F3F3F00u, kHbHi = 0x40404040u;
+  const uint32_t x4 = x << 4;  // each low nibble's sign bit becomes its byte's top bit
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {  // values 4h .. 4h + 3 (bytes 2h, 2h + 1 of x)
+    const uint32_t sel = (h == 0 ? x : __byte_perm(x, 0, 0x4432)) & 0x7777u;  // magnitude codes
+    const uint32_t lo = __byte_perm(kLbLo, kLbHi, sel), hi = __byte_perm(kHbLo, kHbHi, sel);
+    // signs: byte 1 <- top bit of byte (2h + j) of x4 (low nibble), byte 3 <- of x (high nibble)
+    const uint32_t s0 = __byte_perm(x4, x, h == 0 ? 0xC080u : 0xE0A0u);
+    const uint32_t s1 = __byte_perm(x4, x, h == 0 ? 0xD090u : 0xF0B0u);
+    o[2 * h] = __byte_perm(lo, hi, 0x5140u) | (s0 & 0x80008000u);
+    o[2 * h + 1] = __byte_perm(lo, hi, 0x7362u) | (s1 & 0x80008000u);
+  }
+}
 
 template <int BN, int EPI, bool WIDE>
 struct CfgF4 {
   using C = Cfg<BN, EPI, WIDE>;
-  static constexpr int kQ = C::kRowsA * 32;                   // fp4 bytes of one stage
-  static constexpr int kS = C::kRowsA * 2;                    // scale bytes of one stage
+  static constexpr int kQ = C::kRowsA * 32;                   // fp4 bytes of one k-block of a tile
+  static constexpr int kS = C::kRowsA * 2;                    // its scale bytes
   static constexpr int kRaw = (kQ + kS + 1023) / 1024 * 1024;
   static constexpr int kStage = C::kA + C::kB + kRaw;         // {bf16 weight tile, activations, raw}
-  static constexpr int kLut = 256 * 32 * 4;
-  static constexpr int kStages = std::min(6, (220 * 1024 - C::kEpiSmem - kLut) / kStage);
-  static constexpr int kSmem = 1024 + kStages * kStage + C::kEpiSmem + kLut + 256;
+  static constexpr int kStages = std::min(8, (220 * 1024 - C::kEpiSmem) / kStage);
+  static constexpr int kSmem = 1024 + kStages * kStage + C::kEpiSmem + 256;
   static_assert(kStages >= 2, "fp4 GEMM stages do not fit");
 };
-
-// bf16 bits of an e2m1 code at scale 1 (sign bit 3; 0, 0.5, 1, 1.5, 2, 3, 4, 6)
-__device__ __forceinline__ uint32_t e2m1_bf16(uint32_t c) {
-  constexpr uint32_t kMag[8] = {0x0000, 0x3F00, 0x3F80, 0x3FC0, 0x4000, 0x4040, 0x4080, 0x40C0};
-  return kMag[c & 7] | ((c & 8) << 12);
-}
 
 // bf16 of 2^(e - 127) for an e8m0 scale byte, in both halves
 __device__ __forceinline__ uint32_t e8m0_bf16x2(uint32_t e) {
@@ -586,19 +599,24 @@ __device__ __forceinline__ uint32_t e8m0_bf16x2(uint32_t e) {
   return b | (b << 16);
 }
 
+// Pipeline: one ring of stages {bf16 weight tile, activation tile, raw fp4 + scales}; the producer
+// lane loads the raw weights and the activations, converter threads write the bf16 tile from the
+// raw bytes of the same stage, the MMA lane waits for the converted tile and releases the stage.
+// A ring split into a deep raw ring and a short operand ring (converters loading the activations)
+// measured slower: the activations' load latency then sits between conversion and MMA.
 template <int BN, int EPI, bool WIDE>
-__global__ void __launch_bounds__(kThreadsF4, 1)
+__global__ void __launch_bounds__(threads_f4<BN>(), 1)
 gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_out,
                 const uint8_t* __restrict__ wq, const uint8_t* __restrict__ wsc, int n_pad, Params p) {
   using C = Cfg<BN, EPI, WIDE>;
   using F = CfgF4<BN, EPI, WIDE>;
   constexpr int W = C::kChunk;
+  constexpr int kConv = conv_warps<BN>();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
   uint8_t* epi_smem = smem + F::kStages * F::kStage;
-  uint32_t* lut = reinterpret_cast<uint32_t*>(epi_smem + C::kEpiSmem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(lut) + F::kLut);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + C::kEpiSmem);
   uint64_t* full = bars;                  // raw fp4 + scales + activations landed
   uint64_t* conv = bars + F::kStages;     // bf16 weight tile written (converter threads)
   uint64_t* empty = bars + 2 * F::kStages;
@@ -612,7 +630,7 @@ gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   if (threadIdx.x == 0) {
     for (int i = 0; i < F::kStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&conv[i], kConvWarps * 32);
+      mbar_init(&conv[i], kConv * 32);
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -622,11 +640,6 @@ gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     fence_barrier_init();
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_out);
-  }
-  // byte -> bf16x2 table, entry (byte, copy) at word byte * 32 + copy (lane L reads copy L)
-  for (int i = threadIdx.x; i < 256 * 32; i += kThreadsF4) {
-    const uint32_t b = (uint32_t)i >> 5;
-    lut[i] = e2m1_bf16(b & 15) | (e2m1_bf16(b >> 4) << 16);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -697,7 +710,9 @@ gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     }
   } else if (warp >= 2 + kEpiWarps) {
     // ------------------------------------------------------------------ fp4 -> bf16 converters
-    const int ct = threadIdx.x - kThreads;  // 0..127: weight row (and row + 128 when 256 rows)
+    // work item = (row, 32-value half): one e8m0 scale, four 16-byte output chunks
+    constexpr int kHalves = C::kRowsA * 2;
+    const int ct = threadIdx.x - kThreads;
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -706,31 +721,27 @@ gemm_fp4_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       if (!unit_coords(p, u, BN, nt_, row0_, ex_)) continue;
       for (int kb = 0; kb < p.kblocks; ++kb) {
         if (!mbar_wait(&full[stage], phase, 350)) { ok = false; break; }
-        uint8_t* st = stages + stage * F::kStage;
-        const uint8_t* raw = st + C::kA + C::kB;
+        uint8_t* op = stages + stage * F::kStage;
+        const uint8_t* raw = op + C::kA + C::kB;
 #pragma unroll
-        for (int h = 0; h < C::kRowsA / 128; ++h) {
-          const int r = h * 128 + ct;
-          const uint4 q0 = *reinterpret_cast<const uint4*>(raw + r * 32);
-          const uint4 q1 = *reinterpret_cast<const uint4*>(raw + r * 32 + 16);
-          const uint32_t sc = *reinterpret_cast<const uint16_t*>(raw + F::kQ + r * 2);
-          const uint32_t sb0 = e8m0_bf16x2(sc & 0xFF), sb1 = e8m0_bf16x2(sc >> 8);
-          const __nv_bfloat162 s0 = *reinterpret_cast<const __nv_bfloat162*>(&sb0);
-          const __nv_bfloat162 s1 = *reinterpret_cast<const __nv_bfloat162*>(&sb1);
-          const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-          uint8_t* dst = st + h * 128 * 128 + (r & 127) * 128;
+        for (int it = ct; it < kHalves; it += kConv * 32) {
+          const int r = it >> 1, hv = it & 1;
+          const uint4 qv = *reinterpret_cast<const uint4*>(raw + r * 32 + hv * 16);
+          const uint32_t sb = e8m0_bf16x2(raw[F::kQ + r * 2 + hv]);
+          const __nv_bfloat162 sc = *reinterpret_cast<const __nv_bfloat162*>(&sb);
+          const uint32_t words[4] = {qv.x, qv.y, qv.z, qv.w};
+          uint8_t* dst = op + (r >> 7) * 128 * 128 + (r & 127) * 128;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {  // 16-byte chunk c: values 8c .. 8c + 7
+          for (int c = 0; c < 4; ++c) {  // 16-byte chunk 4 hv + c: values 8 (4 hv + c) .. + 7
             uint32_t o[4];
+            fp4_to_bf16x8(words[c], o);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint32_t byte = __byte_perm(words[c], 0, 0x4440 + j);
-              const uint32_t v = lut[byte * 32 + lane];
-              __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(&v);
-              x = __hmul2(x, c < 4 ? s0 : s1);
-              o[j] = *reinterpret_cast<const uint32_t*>(&x);
+              __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&o[j]);
+              v = __hmul2(v, sc);
+              o[j] = *reinterpret_cast<const uint32_t*>(&v);
             }
-            *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(dst + (((4 * hv + c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
         fence_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
@@ -1634,7 +1645,7 @@ static void launch_grouped_fp4(const Params& p, const void* x, const uint8_t* q,
   const CUtensorMap mx = make_map(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, K, K, BK, BN, true);
   const CUtensorMap mo = make_map(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.M, p.n_out, ldo, 32, C::kChunk, false);
   const int units = p.n_tiles * p.m_tiles;
-  msgl_launch(gemm_fp4_kernel<BN, EPI, kGated>, dim3(std::min(units, num_sms_cached())), dim3(kThreadsF4), F::kSmem,
+  msgl_launch(gemm_fp4_kernel<BN, EPI, kGated>, dim3(std::min(units, num_sms_cached())), dim3(threads_f4<BN>()), F::kSmem,
               s, 1, mx, mo, q, sc, n_pad, p);
 }
 

@@ -197,7 +197,15 @@ class Engine:
         if config.use_dummy_weight:
             g = torch.Generator(device=self.device).manual_seed(config.seed + config.tp_info.rank)
             out = {}
+            fp4 = self._dummy_mxfp4()
             for k, v in self.model.state_dict().items():
+                if fp4 and k.endswith((".experts.gate_up_proj", ".experts.down_proj")) and v.shape[2] % 64 == 0:
+                    # MXFP4 checkpoint kept in fp4: random e2m1 bytes, scales near 2^-6 (|w| ~ 0.02)
+                    blocks = torch.empty(*v.shape[:2], v.shape[2] // 32, 16, dtype=torch.uint8, device=self.device)
+                    out[k + "_blocks"] = blocks.random_(0, 256, generator=g)
+                    scales = torch.empty(*v.shape[:2], v.shape[2] // 32, dtype=torch.uint8, device=self.device)
+                    out[k + "_scales"] = scales.random_(119, 123, generator=g)
+                    continue
                 if k.endswith(("norm.weight",)):
                     out[k] = torch.ones(v.shape, dtype=v.dtype, device=self.device)
                 else:
@@ -210,6 +218,13 @@ class Engine:
             return out
         return {k: v.to(self.dtype) if v.is_floating_point() and not k.endswith("sinks") else v
                 for k, v in load_weight(config.model_path, self.device, self.model_config)}
+
+    def _dummy_mxfp4(self) -> bool:
+        """Dummy weights for an MXFP4 checkpoint's experts are generated in fp4 (kept that way on
+        the GPU) instead of bf16."""
+        from minisgl.env import ENV
+
+        return self.is_cuda and bool(ENV.MXFP4_RESIDENT) and getattr(self.model_config, "quant_method", None) == "mxfp4"
 
     def _sync_free_memory(self) -> Tuple[int, int]:
         if not self.is_cuda:

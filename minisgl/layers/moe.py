@@ -57,8 +57,9 @@ class MoELayer(BaseOP):
         self._e0, local = expert_range(num_experts)
         self._ep = info.size > 1 and local < num_experts
         inter = intermediate_size if self._ep else div_even(intermediate_size, info.size)
-        self.gate_up_proj = torch.empty(local, 2 * inter, hidden_size)
-        self.down_proj = torch.empty(local, hidden_size, inter)
+        # shape / dtype placeholders (no memory: the loaded tensors replace them)
+        self.gate_up_proj = torch.empty(local, 2 * inter, hidden_size, device="meta")
+        self.down_proj = torch.empty(local, hidden_size, inter, device="meta")
         self.gate_up_proj_bias = torch.empty(local, 2 * inter) if has_bias else None
         self.down_proj_bias = torch.empty(local, hidden_size) if has_bias else None
         self._comm = DistributedCommunicator()

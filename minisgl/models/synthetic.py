@@ -79,6 +79,7 @@ PRESETS: Dict[str, dict] = {
         layer_types=["sliding_attention", "full_attention"] * 18,
         rope_scaling=dict(rope_type="yarn", factor=32.0, beta_fast=32.0, beta_slow=1.0,
                           original_max_position_embeddings=4096, truncate=False),
+        quantization_config=dict(quant_method="mxfp4"),
     ),
 }
 

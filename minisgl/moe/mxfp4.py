@@ -28,19 +28,21 @@ E2M1 = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3
 
 def dequant_mxfp4(blocks: torch.Tensor, scales: torch.Tensor, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     """``blocks [..., G, 16]`` uint8 (32 e2m1 values per block, low nibble first), ``scales [..., G]``
-    uint8 e8m0 -> ``[..., G * 32]``. Processed one leading index at a time to bound temporaries."""
+    uint8 e8m0 -> ``[..., G * 32]``. Processed in chunks of rows to bound temporaries."""
     if blocks.shape[:-1] != scales.shape or blocks.shape[-1] != 16:
         raise ValueError(f"mxfp4 blocks {tuple(blocks.shape)} / scales {tuple(scales.shape)} mismatch")
     lut = torch.tensor(E2M1, dtype=torch.float32, device=blocks.device)
-    out = torch.empty(blocks.shape[:-2] + (blocks.shape[-2] * 32,), dtype=dtype, device=blocks.device)
-    flat_b = blocks.reshape(-1, *blocks.shape[-2:])
-    flat_s = scales.reshape(-1, scales.shape[-1])
-    flat_o = out.view(-1, out.shape[-1])
-    for i in range(flat_b.shape[0]):
-        b = flat_b[i].to(torch.uint8)
-        v = torch.stack([lut[(b & 0x0F).long()], lut[(b >> 4).long()]], dim=-1).reshape(b.shape[0], 32)
-        v = torch.ldexp(v, (flat_s[i].to(torch.int32) - 127).unsqueeze(-1).to(torch.float32))
-        flat_o[i] = v.reshape(-1).to(dtype)
+    G = blocks.shape[-2]
+    out = torch.empty(blocks.shape[:-2] + (G * 32,), dtype=dtype, device=blocks.device)
+    flat_b = blocks.reshape(-1, G, 16)
+    flat_s = scales.reshape(-1, G)
+    flat_o = out.view(-1, G * 32)
+    step = max(1, (1 << 22) // (G * 32))  # rows per chunk: ~4M values
+    for i in range(0, flat_b.shape[0], step):
+        b = flat_b[i : i + step].to(torch.uint8)
+        v = torch.stack([lut[(b & 0x0F).long()], lut[(b >> 4).long()]], dim=-1).reshape(b.shape[0], G, 32)
+        v = torch.ldexp(v, (flat_s[i : i + step].to(torch.int32) - 127).unsqueeze(-1).to(torch.float32))
+        flat_o[i : i + step] = v.reshape(b.shape[0], -1).to(dtype)
     return out
 
 

@@ -166,6 +166,22 @@ def test_gpu_decode_tracks_oracle(tmp_path, preset, free_port):
     assert exact >= 0.9, (worst, exact)  # near-ties are rare; most steps pick the oracle's exact argmax
 
 
+def test_gpu_mxfp4_experts_track_oracle(tmp_path, free_port):
+    """gpt-oss with MXFP4 experts kept in fp4 on the GPU (fp4 grouped GEMM) against the fp32 CPU
+    oracle, which dequantises the same checkpoint: 16 greedy tokens per prompt, teacher forced."""
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    path = make_checkpoint("tiny-gpt-oss", str(tmp_path / "mxfp4"), dtype=torch.bfloat16, expert_format="mxfp4")
+    prompts = _prompts(12, 1024, seed=6)
+    sp = SamplingParams(max_tokens=16, ignore_eos=True)
+    outs, rows = _run(path, prompts, sp, free_port, tap=True, dtype=torch.bfloat16, max_running_req=32,
+                      num_page_override=4096, cuda_graph_max_bs=16)
+    assert all(len(o) == 16 for o in outs)
+    worst, exact = _check_against_oracle(path, prompts, outs, free_port + 1, gpu_rows=rows,
+                                         outliers=_outliers_allowed("tiny-gpt-oss", 12 * 16))
+    assert exact >= 0.9, (worst, exact)
+
+
 @pytest.mark.parametrize("preset", ["tiny-qwen3", "tiny-gpt-oss"])
 def test_fused_greedy_lm_head_tracks_oracle(tmp_path, preset, free_port):
     """Greedy decoding with the argmax taken inside the LM-head GEMM (the default; no logits are

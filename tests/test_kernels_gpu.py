@@ -555,3 +555,44 @@ def test_gemm_token_tiles(M, bn, wide, splits):
             _close(out, expect, 3e-2, 3e-2)
     finally:
         _c().gemm_force_bn(-1)
+
+
+@pytest.mark.parametrize("T", [5, 64, 300])
+@pytest.mark.parametrize("H,inter,act,bias", [(512, 384, "swiglu_oai", True), (2880, 256, "silu", False)])
+def test_moe_mxfp4_experts_match_dequantised(T, H, inter, act, bias):
+    """MoE forward with MXFP4 experts kept in fp4 (the grouped GEMM converts each tile to bf16 in
+    shared memory) equals the bf16 path on the dequantised weights bit for bit (power-of-two scales
+    make the conversion exact; the MMA sequence is the same), and the fp32 reference within bf16
+    tolerance. H = 2880 leaves a partial last 128-row tile of the down projection."""
+    from minisgl.moe.grouped import moe_reference
+    from minisgl.moe.mxfp4 import Mxfp4Experts, dequant_mxfp4, interleave_rows, pad_k
+    from minisgl.ops.moe import interleave_experts, moe_forward
+
+    E, topk = 8, 4
+    g = torch.Generator().manual_seed(T + H)
+    b1 = torch.randint(0, 256, (E, 2 * inter, H // 32, 16), generator=g, dtype=torch.int32).to(torch.uint8)
+    s1 = torch.randint(116, 120, (E, 2 * inter, H // 32), generator=g, dtype=torch.int32).to(torch.uint8)
+    b2 = torch.randint(0, 256, (E, H, inter // 32, 16), generator=g, dtype=torch.int32).to(torch.uint8)
+    s2 = torch.randint(116, 120, (E, H, inter // 32), generator=g, dtype=torch.int32).to(torch.uint8)
+    bias1 = (torch.randn(E, 2 * inter, generator=g) * 0.1).to(DEV, torch.bfloat16) if bias else None
+    bias2 = (torch.randn(E, H, generator=g) * 0.1).to(DEV, torch.bfloat16) if bias else None
+    x = (torch.randn(T, H, generator=g)).to(DEV, torch.bfloat16)
+    gating = torch.randn(T, E, generator=g).to(DEV)
+    w1 = dequant_mxfp4(b1, s1, torch.bfloat16).to(DEV)
+    w2 = dequant_mxfp4(b2, s2, torch.bfloat16).to(DEV)
+    w1i, w2i, b1i = interleave_experts(w1, w2, bias1)
+    ip = w1i.shape[1] // 2
+    q1 = Mxfp4Experts.pack(interleave_rows(b1.to(DEV)), interleave_rows(s1.to(DEV)), 256)
+    q2 = Mxfp4Experts.pack(*pad_k(b2.to(DEV), s2.to(DEV), ip), 128)
+    soft_after = act == "swiglu_oai"
+    ref16 = moe_forward(x, w1i, w2i, gating, topk, True, act, b1i, bias2, soft_after, 0, True)
+    out = moe_forward(x, q1, q2, gating, topk, True, act, b1i, bias2, soft_after, 0, True)
+    torch.cuda.synchronize()
+    assert _c().get_error() == (0, 0)
+    assert torch.equal(out, ref16)
+    ref = moe_reference(x.cpu().float(), w1.cpu().float(), w2.cpu().float(), gating.cpu(), topk, True, act,
+                        None if bias1 is None else bias1.cpu().float(), None if bias2 is None else bias2.cpu().float(),
+                        soft_after)
+    # bf16 activations between the two GEMMs: errors scale with the output's range
+    tol = 2e-2 * float(ref.abs().max())
+    _close(out, ref.to(DEV), tol, 2e-2)

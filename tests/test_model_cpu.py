@@ -118,17 +118,33 @@ def test_gpt_oss_mxfp4_checkpoint_loads_like_dequantized(tmp_path, tp):
         d = make_checkpoint("tiny-gpt-oss", str(tmp_path / fmt), weights=False)
         save_file({k: v.contiguous() for k, v in sd.items()}, str(tmp_path / fmt / "model.safetensors"))
         dirs[fmt] = d
-    for rank in range(tp):
-        set_tp_info(rank, tp)
+    from minisgl.env import ENV
+
+    def decoded(d):
+        """Loaded tensors with MXFP4 pairs kept by the loader (``<proj>_blocks`` / ``_scales``)
+        dequantised, as the MoE layer does off the GPU."""
+        out = dict(load_weight(d, torch.device("cpu")))
+        for k in [k for k in out if k.endswith("_blocks")]:
+            base = k[: -len("_blocks")]
+            out[base] = dequant_mxfp4(out.pop(k), out.pop(base + "_scales"), torch.float32)
+        return {k: v.float() for k, v in out.items()}
+
+    for keep in (True, False):
+        ENV.MXFP4_RESIDENT = keep
         try:
-            loaded = {f: {k: v.float() for k, v in load_weight(d, torch.device("cpu"))} for f, d in dirs.items()}
+            for rank in range(tp):
+                set_tp_info(rank, tp)
+                try:
+                    loaded = {f: decoded(d) for f, d in dirs.items()}
+                finally:
+                    reset_tp_info()
+                ref = loaded["per_expert"]
+                for f in ("fused", "mxfp4"):
+                    assert loaded[f].keys() == ref.keys(), f
+                    for k in ref:
+                        assert torch.equal(loaded[f][k], ref[k]), (f, k, rank, keep)
         finally:
-            reset_tp_info()
-        ref = loaded["per_expert"]
-        for f in ("fused", "mxfp4"):
-            assert loaded[f].keys() == ref.keys(), f
-            for k in ref:
-                assert torch.equal(loaded[f][k], ref[k]), (f, k, rank)
+            ENV.reload()
 
 
 def test_mistral3_layout_loads_like_the_text_model(tmp_path, free_port):
