@@ -1771,7 +1771,7 @@ extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total
   p.page = page;
   p.scale_log2 = sm_scale * kLog2e;
   p.window = window;
-  msgl_set_smem<fmha_prefill_kernel>(FmSmem::kBytes);
+  msgl_set_smem<fmha_prefill_kernel>(FmSmem::kBytes, 100);  // two CTAs per SM need all of it
   CUtensorMap tq, tk, tv;
   const cuuint64_t qdims[3] = {(cuuint64_t)hd, (cuuint64_t)nq, (cuuint64_t)total_q};
   const cuuint64_t qstr[2] = {(cuuint64_t)hd * 2, (cuuint64_t)nq * hd * 2};
@@ -1798,10 +1798,6 @@ extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total
   // over the requests, times the kv heads)
   const int64_t work = ((total_q + p.tt - 1) / p.tt + num_reqs) * nkv;
   if (work > INT32_MAX) return 3;
-  static std::once_flag carveout;
-  std::call_once(carveout, [] {
-    cudaFuncSetAttribute(fmha_prefill_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-  });
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

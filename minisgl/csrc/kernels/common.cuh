@@ -529,8 +529,10 @@ inline cudaError_t msgl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, 
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for one kernel, done once per (kernel, device):
 // the attribute belongs to the device's context, so a process that launches on several GPUs sets it
 // on each. Thread-safe; returns the CUDA error of the attribute call (cudaSuccess once it is set).
+// carveout >= 0 also sets the preferred shared-memory carveout (percent of the unified L1 /
+// shared storage), e.g. 100 for kernels that rely on two large CTAs fitting on one SM.
 template <auto Kernel>
-inline cudaError_t msgl_set_smem(int bytes) {
+inline cudaError_t msgl_set_smem(int bytes, int carveout = -1) {
   static std::mutex mu;
   static std::atomic<uint64_t> done{0};  // bit d: set on device d (devices 0..63)
   int dev = 0;
@@ -541,6 +543,9 @@ inline cudaError_t msgl_set_smem(int bytes) {
   std::lock_guard<std::mutex> g(mu);
   if (bit != 0 && (done.load(std::memory_order_relaxed) & bit)) return cudaSuccess;
   e = cudaFuncSetAttribute(reinterpret_cast<const void*>(Kernel), cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && carveout >= 0)
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(Kernel), cudaFuncAttributePreferredSharedMemoryCarveout,
+                             carveout);
   if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
   return e;
 }
