@@ -1783,6 +1783,9 @@ extern "C" int msgl_attention_prefill_fmha(void* o, const void* q, int64_t total
       !pd_encode(&tv, v_cache, 3, kdims, kstr, kbox))
     return 2;
   p.num_reqs = num_reqs;
+  // Work distribution: the device counter (default), or with MINISGL_FMHA_STATIC=1 the static
+  // round-robin blockIdx.x + k * gridDim.x (kept for load-balance comparisons; 10-15 % slower on the
+  // benchmark step because its slowest CTA ends well after the median one).
   static std::atomic<uint32_t> launches{0};
   static const bool static_rr = [] {
     const char* e = getenv("MINISGL_FMHA_STATIC");
