@@ -1173,10 +1173,6 @@ struct FmSmem {
 };
 static_assert(2 * (FmSmem::kBytes + 1024) <= 228 * 1024, "prefill attention must fit two CTAs per SM");
 
-__device__ __forceinline__ uint32_t fm_swz(int row, int chunk) {  // 128B swizzle within a half tile
-  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
-}
-
 // 2^x on the MUFU unit (flushes results below 2^-126 to zero; 2^-inf = 0)
 __device__ __forceinline__ float fm_exp2_mufu(float x) {
   float y;

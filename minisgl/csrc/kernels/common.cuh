@@ -190,13 +190,6 @@ MSGL_DEVICE void tma_store_2d(const CUtensorMap* map, const void* smem_src, int 
       "r"(smem_u32(smem_src)), "r"(x), "r"(y)
       : "memory");
 }
-MSGL_DEVICE void tma_store_3d(const CUtensorMap* map, const void* smem_src, int x, int y, int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
 MSGL_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 template <int N>
 MSGL_DEVICE void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
